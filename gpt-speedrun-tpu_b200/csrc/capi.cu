@@ -1,0 +1,30 @@
+// Library-level entry points: version, status strings, device error flags.
+#include "common.cuh"
+#include "gemm.cuh"
+
+namespace gptb200 {
+int attention_read_error(int clear);
+}
+
+extern "C" const char* gptb200_version(void) { return "gptb200 0.1.0 (sm_100a)"; }
+
+extern "C" const char* gptb200_status_string(int status) {
+  switch (status) {
+    case GPTB200_OK: return "ok";
+    case GPTB200_EINVAL: return "invalid argument";
+    case GPTB200_ESHAPE: return "unsupported shape or alignment";
+    case GPTB200_EUNSUPPORTED: return "unsupported option combination";
+    case GPTB200_EDEVICE: return "a kernel reported a device-side error";
+    case GPTB200_ERANGE: return "token id outside the vocabulary";
+    default:
+      if (status < 0) return cudaGetErrorString(static_cast<cudaError_t>(-status));
+      return "unknown status";
+  }
+}
+
+extern "C" int gptb200_device_error(int clear) {
+  cudaDeviceSynchronize();
+  int e = gptb200::gemm_read_error(clear);
+  e |= gptb200::attention_read_error(clear);
+  return e ? GPTB200_EDEVICE : GPTB200_OK;
+}

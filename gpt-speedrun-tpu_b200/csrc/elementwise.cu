@@ -1,0 +1,375 @@
+// Memory-bound kernels of the step: RMSNorm forward/backward, embedding
+// gather/scatter, RoPE tables, bias-gradient column sums and the fp32->bf16
+// cast. All of them move 16-byte vectors (8 bf16 / 4 fp32) per thread access,
+// reduce with warp shuffles and size their grids from the SM count.
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace gptb200 {
+
+static int sms() {
+  int dev = 0, n = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n;
+}
+
+__device__ __forceinline__ void ld8(const bf16* p, float* v) {
+  uint4 q = *reinterpret_cast<const uint4*>(p);
+  unpack_bf16x2(q.x, v[0], v[1]);
+  unpack_bf16x2(q.y, v[2], v[3]);
+  unpack_bf16x2(q.z, v[4], v[5]);
+  unpack_bf16x2(q.w, v[6], v[7]);
+}
+__device__ __forceinline__ void st8(bf16* p, const float* v) {
+  uint4 q;
+  q.x = pack_bf16x2(v[0], v[1]);
+  q.y = pack_bf16x2(v[2], v[3]);
+  q.z = pack_bf16x2(v[4], v[5]);
+  q.w = pack_bf16x2(v[6], v[7]);
+  *reinterpret_cast<uint4*>(p) = q;
+}
+
+// ------------------------------------------------------------------ RMSNorm
+// One warp per row; each lane keeps CH 8-element chunks of the row in
+// registers (CH = ceil(d / 256)), so x is read once.
+template <int CH>
+__global__ void __launch_bounds__(256) rms_fwd_kernel(const bf16* __restrict__ x,
+                                                      const bf16* __restrict__ scale,
+                                                      bf16* __restrict__ y,
+                                                      float* __restrict__ rstd_out, int64_t rows,
+                                                      int d) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int nch = d >> 3;
+  for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows;
+       r += warps) {
+    const bf16* xr = x + r * d;
+    float v[CH][8];
+    float ss = 0.f;
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      int ch = lane + 32 * c;
+      if (ch < nch) {
+        ld8(xr + ch * 8, v[c]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ss += v[c][j] * v[c][j];
+      }
+    }
+    ss = warp_sum(ss);
+    const float rstd = rsqrtf(ss / (float)d + 1.0e-5f);
+    if (lane == 0) rstd_out[r] = rstd;
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      int ch = lane + 32 * c;
+      if (ch < nch) {
+        float s[8], o[8];
+        ld8(scale + ch * 8, s);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = bf16r(v[c][j] * rstd) * s[j];
+        st8(y + r * d + ch * 8, o);
+      }
+    }
+  }
+}
+
+// Backward: dn = dy*scale; xhat = x*rstd;
+// dx = rstd * (dn - xhat * mean(dn * xhat)); dscale += dy * bf16(xhat).
+template <int CH>
+__global__ void __launch_bounds__(256) rms_bwd_kernel(
+    const bf16* __restrict__ x, const bf16* __restrict__ scale, const float* __restrict__ rstd_in,
+    const bf16* __restrict__ dy, const bf16* dx_in, bf16* dx_out, float* __restrict__ dscale,
+    int64_t rows, int d) {
+  extern __shared__ float red[];  // [warps_per_block][d]
+  const int lane = threadIdx.x & 31;
+  const int wib = threadIdx.x >> 5;
+  const int wpb = blockDim.x >> 5;
+  const int64_t warps = (int64_t)gridDim.x * wpb;
+  const int nch = d >> 3;
+  float ds[CH][8];
+#pragma unroll
+  for (int c = 0; c < CH; ++c)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ds[c][j] = 0.f;
+
+  for (int64_t r = (int64_t)blockIdx.x * wpb + wib; r < rows; r += warps) {
+    const float rstd = rstd_in[r];
+    float xh[CH][8], dn[CH][8];
+    float dot = 0.f;
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      int ch = lane + 32 * c;
+      if (ch < nch) {
+        float xv[8], g[8], s[8];
+        ld8(x + r * d + ch * 8, xv);
+        ld8(dy + r * d + ch * 8, g);
+        ld8(scale + ch * 8, s);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          xh[c][j] = xv[j] * rstd;
+          dn[c][j] = g[j] * s[j];
+          ds[c][j] += g[j] * bf16r(xh[c][j]);
+          dot += dn[c][j] * xh[c][j];
+        }
+      }
+    }
+    dot = warp_sum(dot) / (float)d;
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      int ch = lane + 32 * c;
+      if (ch < nch) {
+        float o[8], prev[8];
+        if (dx_in) {
+          ld8(dx_in + r * d + ch * 8, prev);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) prev[j] = 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = prev[j] + bf16r(rstd * (dn[c][j] - xh[c][j] * dot));
+        st8(dx_out + r * d + ch * 8, o);
+      }
+    }
+  }
+  // Reduce the per-warp dscale partials inside the block, then one atomic per column.
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    int ch = lane + 32 * c;
+    if (ch < nch)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) red[wib * d + ch * 8 + j] = ds[c][j];
+  }
+  __syncthreads();
+  for (int col = threadIdx.x; col < d; col += blockDim.x) {
+    float s = 0.f;
+    for (int w = 0; w < wpb; ++w) s += red[w * d + col];
+    atomicAdd(dscale + col, s);
+  }
+}
+
+template <int CH>
+static int rms_fwd_launch(const bf16* x, const bf16* s, bf16* y, float* rstd, int64_t rows, int d,
+                          cudaStream_t st) {
+  int64_t blocks = std::min<int64_t>((rows + 7) / 8, (int64_t)sms() * 8);
+  rms_fwd_kernel<CH><<<(int)blocks, 256, 0, st>>>(x, s, y, rstd, rows, d);
+  GPTB200_CHECK_LAUNCH();
+  return 0;
+}
+
+template <int CH>
+static int rms_bwd_launch(const bf16* x, const bf16* s, const float* rstd, const bf16* dy,
+                          const bf16* dxi, bf16* dxo, float* dscale, int64_t rows, int d,
+                          cudaStream_t st) {
+  const int threads = 256;
+  int64_t blocks = std::min<int64_t>((rows + 7) / 8, (int64_t)sms() * 2);
+  size_t smem = (size_t)(threads / 32) * d * sizeof(float);
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(rms_bwd_kernel<CH>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return -static_cast<int>(e);
+  }
+  rms_bwd_kernel<CH><<<(int)blocks, threads, smem, st>>>(x, s, rstd, dy, dxi, dxo, dscale, rows, d);
+  GPTB200_CHECK_LAUNCH();
+  return 0;
+}
+
+}  // namespace gptb200
+
+using namespace gptb200;
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+extern "C" int gptb200_rms_norm_fwd(const void* x, const void* scale, void* y, float* rstd,
+                                    int64_t rows, int64_t d, void* stream) {
+  if (!x || !scale || !y || !rstd || rows <= 0 || d <= 0) return GPTB200_EINVAL;
+  if (d % 8 || d > 4096 || !aligned16(x) || !aligned16(y) || !aligned16(scale)) return GPTB200_ESHAPE;
+  auto st = reinterpret_cast<cudaStream_t>(stream);
+  auto X = reinterpret_cast<const bf16*>(x);
+  auto S = reinterpret_cast<const bf16*>(scale);
+  auto Y = reinterpret_cast<bf16*>(y);
+  int ch = (int)((d / 8 + 31) / 32);
+  if (ch <= 1) return rms_fwd_launch<1>(X, S, Y, rstd, rows, (int)d, st);
+  if (ch <= 2) return rms_fwd_launch<2>(X, S, Y, rstd, rows, (int)d, st);
+  if (ch <= 3) return rms_fwd_launch<3>(X, S, Y, rstd, rows, (int)d, st);
+  if (ch <= 4) return rms_fwd_launch<4>(X, S, Y, rstd, rows, (int)d, st);
+  if (ch <= 8) return rms_fwd_launch<8>(X, S, Y, rstd, rows, (int)d, st);
+  return rms_fwd_launch<16>(X, S, Y, rstd, rows, (int)d, st);
+}
+
+extern "C" int gptb200_rms_norm_bwd(const void* x, const void* scale, const float* rstd,
+                                    const void* dy, const void* dx_in, void* dx_out,
+                                    float* dscale, int64_t rows, int64_t d, void* stream) {
+  if (!x || !scale || !rstd || !dy || !dx_out || !dscale || rows <= 0 || d <= 0)
+    return GPTB200_EINVAL;
+  if (d % 8 || d > 2048 || !aligned16(x) || !aligned16(dy) || !aligned16(dx_out) ||
+      (dx_in && !aligned16(dx_in)))
+    return GPTB200_ESHAPE;
+  auto st = reinterpret_cast<cudaStream_t>(stream);
+  auto X = reinterpret_cast<const bf16*>(x);
+  auto S = reinterpret_cast<const bf16*>(scale);
+  auto DY = reinterpret_cast<const bf16*>(dy);
+  auto DXI = reinterpret_cast<const bf16*>(dx_in);
+  auto DXO = reinterpret_cast<bf16*>(dx_out);
+  int ch = (int)((d / 8 + 31) / 32);
+  if (ch <= 1) return rms_bwd_launch<1>(X, S, rstd, DY, DXI, DXO, dscale, rows, (int)d, st);
+  if (ch <= 2) return rms_bwd_launch<2>(X, S, rstd, DY, DXI, DXO, dscale, rows, (int)d, st);
+  if (ch <= 3) return rms_bwd_launch<3>(X, S, rstd, DY, DXI, DXO, dscale, rows, (int)d, st);
+  if (ch <= 4) return rms_bwd_launch<4>(X, S, rstd, DY, DXI, DXO, dscale, rows, (int)d, st);
+  return rms_bwd_launch<8>(X, S, rstd, DY, DXI, DXO, dscale, rows, (int)d, st);
+}
+
+// ------------------------------------------------------------------ embedding
+__global__ void embed_fwd_kernel(const int32_t* __restrict__ tok, const bf16* __restrict__ table,
+                                 bf16* __restrict__ out, int64_t n, int d, int64_t vocab) {
+  const int nch = d >> 3;
+  const int64_t total = n * nch;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t r = i / nch;
+    int c = (int)(i - r * nch);
+    int64_t t = tok[r];
+    t = t < 0 ? 0 : (t >= vocab ? vocab - 1 : t);
+    *reinterpret_cast<uint4*>(out + r * d + c * 8) =
+        *reinterpret_cast<const uint4*>(table + t * d + c * 8);
+  }
+}
+
+__global__ void embed_bwd_kernel(const int32_t* __restrict__ tok, const bf16* __restrict__ dout,
+                                 float* __restrict__ dtable, int64_t n, int d, int64_t vocab) {
+  const int nch = d >> 2;
+  const int64_t total = n * nch;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t r = i / nch;
+    int c = (int)(i - r * nch);
+    int64_t t = tok[r];
+    if (t < 0 || t >= vocab) continue;
+    uint2 q = *reinterpret_cast<const uint2*>(dout + r * d + c * 4);
+    float a, b, e, f;
+    unpack_bf16x2(q.x, a, b);
+    unpack_bf16x2(q.y, e, f);
+    atomicAdd(reinterpret_cast<float4*>(dtable + t * d + c * 4), make_float4(a, b, e, f));
+  }
+}
+
+extern "C" int gptb200_embedding_fwd(const int32_t* tokens, const void* table, void* out, int64_t n,
+                                     int64_t d, int64_t vocab, void* stream) {
+  if (!tokens || !table || !out || n <= 0 || d <= 0 || vocab <= 0) return GPTB200_EINVAL;
+  if (d % 8 || !aligned16(table) || !aligned16(out)) return GPTB200_ESHAPE;
+  int64_t total = n * (d / 8);
+  int blocks = (int)std::min<int64_t>((total + 255) / 256, (int64_t)sms() * 16);
+  embed_fwd_kernel<<<blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      tokens, reinterpret_cast<const bf16*>(table), reinterpret_cast<bf16*>(out), n, (int)d, vocab);
+  GPTB200_CHECK_LAUNCH();
+  return 0;
+}
+
+extern "C" int gptb200_embedding_bwd(const int32_t* tokens, const void* dout, float* dtable,
+                                     int64_t n, int64_t d, int64_t vocab, void* stream) {
+  if (!tokens || !dout || !dtable || n <= 0 || d <= 0 || vocab <= 0) return GPTB200_EINVAL;
+  if (d % 4 || !aligned16(dtable)) return GPTB200_ESHAPE;
+  int64_t total = n * (d / 4);
+  int blocks = (int)std::min<int64_t>((total + 255) / 256, (int64_t)sms() * 16);
+  embed_bwd_kernel<<<blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      tokens, reinterpret_cast<const bf16*>(dout), dtable, n, (int)d, vocab);
+  GPTB200_CHECK_LAUNCH();
+  return 0;
+}
+
+// ------------------------------------------------------------------ RoPE tables
+__global__ void rope_tables_kernel(bf16* cos_out, bf16* sin_out, int64_t seq, int half, int hd) {
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= seq * half) return;
+  int64_t t = i / half;
+  int k = (int)(i - t * half);
+  // fraction = arange(0, hd, 2) / hd ; inv = 10000^-fraction ; angle = t * inv (all fp32)
+  float fraction = (float)(2 * k) / (float)hd;
+  float inv = powf(10000.0f, -fraction);
+  float angle = (float)t * inv;
+  cos_out[i] = __float2bfloat16(cosf(angle));
+  sin_out[i] = __float2bfloat16(sinf(angle));
+}
+
+extern "C" int gptb200_rope_tables(void* cos_out, void* sin_out, int64_t seq, int64_t head_dim,
+                                   void* stream) {
+  if (!cos_out || !sin_out || seq <= 0 || head_dim <= 0 || head_dim % 2) return GPTB200_EINVAL;
+  int half = (int)(head_dim / 2);
+  int64_t total = seq * half;
+  rope_tables_kernel<<<(int)((total + 255) / 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<bf16*>(cos_out), reinterpret_cast<bf16*>(sin_out), seq, half, (int)head_dim);
+  GPTB200_CHECK_LAUNCH();
+  return 0;
+}
+
+// ------------------------------------------------------------------ column sums
+// Block = 8 warps. Lane l of every warp owns columns [8l, 8l+8) of a 256-wide
+// strip; the warps of the block split the rows of the block's row range.
+__global__ void __launch_bounds__(256) colsum_kernel(const bf16* __restrict__ x, int64_t rows,
+                                                     int n, int64_t rows_per_block, float alpha,
+                                                     float* __restrict__ out) {
+  __shared__ float red[8][256];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int col = blockIdx.x * 256 + lane * 8;
+  const int64_t r0 = (int64_t)blockIdx.y * rows_per_block;
+  const int64_t r1 = min(rows, r0 + rows_per_block);
+  float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  if (col < n) {
+    for (int64_t r = r0 + w; r < r1; r += 8) {
+      float v[8];
+      ld8(x + r * n + col, v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] += v[j];
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) red[w][lane * 8 + j] = acc[j];
+  __syncthreads();
+  int c = threadIdx.x;  // 256 threads -> 256 columns of the strip
+  if (blockIdx.x * 256 + c < n) {
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) s += red[k][c];
+    atomicAdd(out + blockIdx.x * 256 + c, alpha * s);
+  }
+}
+
+extern "C" int gptb200_colsum(const void* x, int64_t rows, int64_t n, float alpha, float* out,
+                              void* stream) {
+  if (!x || !out || rows <= 0 || n <= 0) return GPTB200_EINVAL;
+  if (n % 8 || !aligned16(x)) return GPTB200_ESHAPE;
+  int strips = (int)((n + 255) / 256);
+  int64_t want = std::max<int64_t>(1, (int64_t)sms() * 4 / strips);
+  int64_t rpb = std::max<int64_t>(64, (rows + want - 1) / want);
+  int ysplit = (int)((rows + rpb - 1) / rpb);
+  dim3 grid(strips, ysplit);
+  colsum_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const bf16*>(x), rows, (int)n, rpb, alpha, out);
+  GPTB200_CHECK_LAUNCH();
+  return 0;
+}
+
+// ------------------------------------------------------------------ cast
+__global__ void cast_bf16_kernel(const float* __restrict__ src, bf16* __restrict__ dst, int64_t n) {
+  int64_t n4 = n >> 2;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float4 v = reinterpret_cast<const float4*>(src)[i];
+    uint2 q;
+    q.x = pack_bf16x2(v.x, v.y);
+    q.y = pack_bf16x2(v.z, v.w);
+    reinterpret_cast<uint2*>(dst)[i] = q;
+  }
+  int64_t tail = (n4 << 2) + blockIdx.x * blockDim.x + threadIdx.x;
+  if (tail < n && blockIdx.x == 0) dst[tail] = __float2bfloat16(src[tail]);
+}
+
+extern "C" int gptb200_cast_bf16(const float* src, void* dst, int64_t n, void* stream) {
+  if (!src || !dst || n <= 0) return GPTB200_EINVAL;
+  if (!aligned16(src) || (reinterpret_cast<uintptr_t>(dst) & 7)) return GPTB200_ESHAPE;
+  int blocks = (int)std::min<int64_t>((n / 4 + 255) / 256 + 1, (int64_t)sms() * 16);
+  cast_bf16_kernel<<<blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      src, reinterpret_cast<bf16*>(dst), n);
+  GPTB200_CHECK_LAUNCH();
+  return 0;
+}

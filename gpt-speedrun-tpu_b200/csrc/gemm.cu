@@ -1,0 +1,585 @@
+// Persistent, warp-specialized tcgen05 GEMM for sm_100a.
+//
+//   C[M,N] = epilogue( sum_k A[m,k] B[n,k] )   bf16 operands, fp32 accumulation in TMEM
+//
+// One CTA per SM loops over output tiles (128 x BN) and, for weight gradients,
+// over K splits. Roles inside the CTA (192 threads):
+//   warp 0  lane 0 : TMA producer. Each pipeline stage holds a 128x64 A tile and
+//                    a BNx64 B tile in 128-byte-swizzled shared memory. K-major
+//                    operands are one box; MN-major operands are 64-wide boxes.
+//   warp 1  lane 0 : MMA issuer. 4 tcgen05.mma (K=16 each) per stage into one of
+//                    two TMEM accumulators (2 x BN fp32 columns), so the
+//                    epilogue of tile i overlaps the main loop of tile i+1.
+//   warps 2-5      : epilogue. Each warp owns the 32 TMEM lanes (= tile rows) of
+//                    its quadrant (warp % 4), reads 32 columns at a time with
+//                    tcgen05.ld and applies the fused epilogue (bias, residual,
+//                    GELU, dGELU, fp32 store or atomic add, and the two
+//                    cross-entropy epilogues used by lce.cu).
+// Every wait is bounded (common.cuh); a wait that runs out raises the CTA's
+// abort flag so all roles leave their loops, TMEM is freed and the error is
+// visible through gptb200_device_error().
+#include <algorithm>
+#include <mutex>
+#include <vector>
+
+#include "common.cuh"
+#include "gemm.cuh"
+
+namespace gptb200 {
+
+static __device__ int g_gemm_error;
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int kThreads = 192;
+
+template <int BN, int STAGES>
+struct GemmSmem {
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int BAR_OFFSET = STAGES * STAGE_BYTES;
+  static constexpr int TOTAL = BAR_OFFSET + 256 + 1024;  // barriers + alignment slack
+};
+
+struct TileCoord {
+  int tm, tn, ks;
+};
+
+__device__ __forceinline__ TileCoord decode_unit(const GemmParams& p, int u) {
+  TileCoord c;
+  int per_split = p.tiles_m * p.tiles_n;
+  c.ks = u / per_split;
+  int r = u - c.ks * per_split;
+  c.tm = r / p.tiles_n;
+  c.tn = r - c.tm * p.tiles_n;
+  return c;
+}
+
+// ------------------------------------------------------------------ epilogues
+template <int EPI>
+struct EpilogueRowState {
+  float run_max = -INFINITY;
+  float run_sum = 0.f;
+};
+
+// Writes 8 consecutive bf16 values (one 16-byte store).
+__device__ __forceinline__ void store_bf16x8(bf16* dst, const float* v) {
+  uint4 q;
+  q.x = pack_bf16x2(v[0], v[1]);
+  q.y = pack_bf16x2(v[2], v[3]);
+  q.z = pack_bf16x2(v[4], v[5]);
+  q.w = pack_bf16x2(v[6], v[7]);
+  *reinterpret_cast<uint4*>(dst) = q;
+}
+
+__device__ __forceinline__ void load_bf16x8(const bf16* src, float* v) {
+  uint4 q = *reinterpret_cast<const uint4*>(src);
+  unpack_bf16x2(q.x, v[0], v[1]);
+  unpack_bf16x2(q.y, v[2], v[3]);
+  unpack_bf16x2(q.z, v[4], v[5]);
+  unpack_bf16x2(q.w, v[6], v[7]);
+}
+
+// Applies the epilogue to 32 accumulator columns [col, col+32) of one row.
+template <int EPI>
+__device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int row, int col, float* v,
+                                               EpilogueRowState<EPI>& st, int target,
+                                               float lse, float cot) {
+  const bool row_ok = row < p.M;
+  if constexpr (EPI == EPI_BF16_) {
+    if (!row_ok) return;
+    bf16* C = reinterpret_cast<bf16*>(p.C);
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      int c0 = col + 8 * g;
+      if (c0 >= p.N) break;
+      float t[8], b[8], r[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) t[j] = bf16r(v[8 * g + j]);
+      if (p.bias) {
+        load_bf16x8(p.bias + c0, b);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) t[j] = bf16r(t[j] + b[j]);
+      }
+      if (p.alpha != 1.0f) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) t[j] = bf16r(p.alpha * t[j]);
+      }
+      if (p.resid) {
+        load_bf16x8(p.resid + (int64_t)row * p.ld_resid + c0, r);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) t[j] = r[j] + t[j];
+      }
+      store_bf16x8(C + (int64_t)row * p.ldc + c0, t);
+    }
+  } else if constexpr (EPI == EPI_BIAS_GELU_) {
+    if (!row_ok) return;
+    bf16* C = reinterpret_cast<bf16*>(p.C);
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      int c0 = col + 8 * g;
+      if (c0 >= p.N) break;
+      float u[8], b[8], o[8];
+      load_bf16x8(p.bias + c0, b);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        u[j] = bf16r(bf16r(v[8 * g + j]) + b[j]);
+        o[j] = gelu_tanh(u[j]);
+      }
+      store_bf16x8(p.aux + (int64_t)row * p.ld_aux + c0, u);
+      store_bf16x8(C + (int64_t)row * p.ldc + c0, o);
+    }
+  } else if constexpr (EPI == EPI_DGELU_) {
+    if (!row_ok) return;
+    bf16* C = reinterpret_cast<bf16*>(p.C);
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      int c0 = col + 8 * g;
+      if (c0 >= p.N) break;
+      float u[8], o[8];
+      load_bf16x8(p.aux + (int64_t)row * p.ld_aux + c0, u);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = bf16r(p.alpha * v[8 * g + j]) * gelu_tanh_grad(u[j]);
+      store_bf16x8(C + (int64_t)row * p.ldc + c0, o);
+    }
+  } else if constexpr (EPI == EPI_F32_) {
+    if (!row_ok) return;
+    float* C = reinterpret_cast<float*>(p.C);
+#pragma unroll
+    for (int g = 0; g < 8; ++g) {
+      int c0 = col + 4 * g;
+      if (c0 >= p.N) break;
+      float4* dst = reinterpret_cast<float4*>(C + (int64_t)row * p.ldc + c0);
+      float4 w = make_float4(p.alpha * v[4 * g], p.alpha * v[4 * g + 1], p.alpha * v[4 * g + 2],
+                             p.alpha * v[4 * g + 3]);
+      if (p.accumulate) {
+        float4 o = *dst;
+        w.x += o.x;
+        w.y += o.y;
+        w.z += o.z;
+        w.w += o.w;
+      }
+      *dst = w;
+    }
+  } else if constexpr (EPI == EPI_F32_ATOMIC_) {
+    if (!row_ok) return;
+    float* C = reinterpret_cast<float*>(p.C);
+#pragma unroll
+    for (int g = 0; g < 8; ++g) {
+      int c0 = col + 4 * g;
+      if (c0 >= p.N) break;
+      float4* dst = reinterpret_cast<float4*>(C + (int64_t)row * p.ldc + c0);
+      atomicAdd(dst, make_float4(p.alpha * v[4 * g], p.alpha * v[4 * g + 1],
+                                 p.alpha * v[4 * g + 2], p.alpha * v[4 * g + 3]));
+    }
+  } else if constexpr (EPI == EPI_LCE_FWD_) {
+    // Online log-sum-exp over the semantic vocabulary, plus the target logit.
+    float m = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if (col + j >= p.v_sem) v[j] = -INFINITY;
+      m = fmaxf(m, v[j]);
+    }
+    if (target >= col && target < col + 32) {
+      float tv = 0.f;
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col + j == target) tv = v[j];
+      if (row_ok) p.tgt_logit[row] = tv;
+    }
+    if (m == -INFINITY) return;
+    float nm = fmaxf(st.run_max, m);
+    const float kLog2e = 1.4426950408889634f;
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) s += exp2f((v[j] - nm) * kLog2e);
+    st.run_sum = st.run_sum * exp2f((st.run_max - nm) * kLog2e) + s;
+    st.run_max = nm;
+  } else if constexpr (EPI == EPI_LCE_BWD_) {
+    // G = (softmax - onehot(target)) * cotangent, rounded to bf16.
+    if (!row_ok) return;
+    bf16* C = reinterpret_cast<bf16*>(p.C);
+    const float kLog2e = 1.4426950408889634f;
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      int c0 = col + 8 * g;
+      if (c0 >= p.N) break;
+      float o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        int c = c0 + j;
+        float pr = (c < p.v_sem) ? exp2f((v[8 * g + j] - lse) * kLog2e) : 0.f;
+        o[j] = (pr - (c == target ? 1.f : 0.f)) * cot;
+      }
+      store_bf16x8(C + (int64_t)row * p.ldc + c0, o);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ kernel
+template <int BN, int STAGES, int EPI, int A_MN, int B_MN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const GemmParams p) {
+  using L = GemmSmem<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::BAR_OFFSET);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 2 * BN);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  int* err = &g_gemm_error;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int u = blockIdx.x; u < p.num_units; u += gridDim.x) {
+        TileCoord tc = decode_unit(p, u);
+        const int m0 = tc.tm * BM, n0 = tc.tn * BN;
+        const int kb0 = tc.ks * p.kb_per_split;
+        const int kb1 = min(p.num_kb, kb0 + p.kb_per_split);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, err)) goto producer_done;
+          uint8_t* sa = smem + stage * L::STAGE_BYTES;
+          uint8_t* sb = sa + L::A_BYTES;
+          mbar_arrive_expect_tx(&full[stage], L::STAGE_BYTES);
+          const int k0 = kb * BK;
+          if constexpr (!A_MN) {
+            tma_load_2d(sa, &tmA, &full[stage], k0, m0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BM / 64; ++j)
+              tma_load_2d(sa + j * 64 * BK * 2, &tmA, &full[stage], m0 + 64 * j, k0);
+          }
+          if constexpr (!B_MN) {
+            tma_load_2d(sb, &tmB, &full[stage], k0, n0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_2d(sb + j * 64 * BK * 2, &tmB, &full[stage], n0 + 64 * j, k0);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    producer_done:;
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer
+      constexpr uint32_t idesc = umma_idesc_bf16(BM, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int u = blockIdx.x; u < p.num_units; u += gridDim.x) {
+        TileCoord tc = decode_unit(p, u);
+        const int kb0 = tc.ks * p.kb_per_split;
+        const int kb1 = min(p.num_kb, kb0 + p.kb_per_split);
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, err)) break;
+        tc_fence_after();
+        const uint32_t dtmem = tmem_base + acc * BN;
+        bool ok = true;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * L::STAGE_BYTES);
+          const uint32_t sb = sa + L::A_BYTES;
+#pragma unroll
+          for (int ki = 0; ki < BK / 16; ++ki) {
+            // K-major SW128: rows of 128 B, 8-row atoms 1024 B apart; a K step
+            // of 16 bf16 advances the start address by 32 B inside the atom.
+            // MN-major SW128: 64-wide MN blocks (LBO apart), 8-k-row atoms
+            // 1024 B apart (SBO); a K step of 16 rows advances 2048 B.
+            const uint64_t ad = A_MN ? umma_smem_desc(sa + ki * 2048, 64 * BK * 2, 1024)
+                                     : umma_smem_desc(sa + ki * 32, 16, 1024);
+            const uint64_t bd = B_MN ? umma_smem_desc(sb + ki * 2048, 64 * BK * 2, 1024)
+                                     : umma_smem_desc(sb + ki * 32, 16, 1024);
+            umma_bf16(dtmem, ad, bd, idesc, (kb > kb0 || ki > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+    }
+  } else {
+    // ---------------- epilogue warps 2..5
+    const int quad = warp & 3;
+    const int r_in_tile = quad * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int u = blockIdx.x; u < p.num_units; u += gridDim.x) {
+      TileCoord tc = decode_unit(p, u);
+      const int row = tc.tm * BM + r_in_tile;
+      const int n0 = tc.tn * BN;
+      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, err)) break;
+      tc_fence_after();
+      int target = -1;
+      float lse = 0.f, cot = 0.f;
+      if constexpr (EPI == EPI_LCE_FWD_ || EPI == EPI_LCE_BWD_) {
+        if (row < p.M) {
+          target = p.targets[row];
+          if (target < 0 || target >= p.v_sem) target = -1;
+          if constexpr (EPI == EPI_LCE_BWD_) {
+            lse = p.lse[row];
+            cot = (target >= 0) ? p.cot[row] : 0.f;
+          }
+        }
+      }
+      EpilogueRowState<EPI> st;
+      const uint32_t trow = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        float v[32];
+        tmem_ld32(trow + c * 32, v);
+        epilogue_chunk<EPI>(p, row, n0 + c * 32, v, st, target, lse, cot);
+      }
+      if constexpr (EPI == EPI_LCE_FWD_) {
+        if (row < p.M)
+          p.partial[(int64_t)row * p.tiles_n + tc.tn] = make_float2(st.run_max, st.run_sum);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 2 * BN);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, []() {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+// 2-D bf16 tensor map: `inner` contiguous elements per row, `outer` rows,
+// row stride `ld` elements, box {64, box_outer}, 128-byte swizzle.
+static bool make_map(CUtensorMap* map, const void* base, int64_t inner, int64_t outer, int64_t ld,
+                     int box_outer) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+static int sm_count() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static int cache[64] = {0};
+  if (dev < 64 && cache[dev]) return cache[dev];
+  int n = 148;
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  if (dev < 64) cache[dev] = n;
+  return n;
+}
+
+template <int BN, int STAGES, int EPI, int A_MN, int B_MN>
+static int launch_variant(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
+                          cudaStream_t stream) {
+  using L = GemmSmem<BN, STAGES>;
+  auto kern = gemm_tc_kernel<BN, STAGES, EPI, A_MN, B_MN>;
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 64 || !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
+    if (e != cudaSuccess) return -static_cast<int>(e);
+    if (dev < 64) configured[dev] = true;
+  }
+  int grid = std::min<int64_t>(p.num_units, sm_count());
+  kern<<<grid, kThreads, L::TOTAL, stream>>>(ta, tb, p);
+  GPTB200_CHECK_LAUNCH();
+  return GPTB200_OK;
+}
+
+constexpr int kBN = 256;
+constexpr int kStages = 4;
+
+template <int EPI>
+static int dispatch_layout(int a_mn, int b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
+                           const GemmParams& p, cudaStream_t s) {
+  if (a_mn == 0 && b_mn == 0) return launch_variant<kBN, kStages, EPI, 0, 0>(ta, tb, p, s);
+  if (a_mn == 0 && b_mn == 1) return launch_variant<kBN, kStages, EPI, 0, 1>(ta, tb, p, s);
+  if (a_mn == 1 && b_mn == 0) return launch_variant<kBN, kStages, EPI, 1, 0>(ta, tb, p, s);
+  return launch_variant<kBN, kStages, EPI, 1, 1>(ta, tb, p, s);
+}
+
+int gemm_launch(const void* a, int a_mn, int64_t lda, const void* b, int b_mn, int64_t ldb,
+                int64_t M, int64_t N, int64_t K, int epi, GemmParams p, cudaStream_t stream) {
+  if (!a || !b || !p.C) return GPTB200_EINVAL;
+  if (M <= 0 || N <= 0 || K <= 0) return GPTB200_EINVAL;
+  if (M > INT32_MAX / 2 || N > INT32_MAX / 2 || K > INT32_MAX / 2) return GPTB200_ESHAPE;
+  if ((lda % 8) || (ldb % 8) || (N % 8)) return GPTB200_ESHAPE;
+  if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) |
+       reinterpret_cast<uintptr_t>(p.C)) & 15)
+    return GPTB200_ESHAPE;
+  if (a_mn ? lda < M : lda < K) return GPTB200_ESHAPE;
+  if (b_mn ? ldb < N : ldb < K) return GPTB200_ESHAPE;
+  if (p.ldc < N || (p.ldc % 8)) return GPTB200_ESHAPE;
+
+  CUtensorMap ta, tb;
+  bool ok = a_mn ? make_map(&ta, a, M, K, lda, BK) : make_map(&ta, a, K, M, lda, BM);
+  ok = ok && (b_mn ? make_map(&tb, b, N, K, ldb, BK) : make_map(&tb, b, K, N, ldb, kBN));
+  if (!ok) return GPTB200_ESHAPE;
+
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.tiles_m = (int)((M + BM - 1) / BM);
+  p.tiles_n = (int)((N + kBN - 1) / kBN);
+  p.num_kb = (int)((K + BK - 1) / BK);
+  int splits = 1;
+  if (epi == EPI_F32_ATOMIC_) {
+    // Split K until there are about three units per SM, keeping >= 8 k-blocks each.
+    const int tiles = p.tiles_m * p.tiles_n;
+    const int target = 3 * sm_count();
+    while (tiles * splits < target && p.num_kb / (splits * 2) >= 8) splits *= 2;
+  }
+  p.kb_per_split = (p.num_kb + splits - 1) / splits;
+  p.splits = (p.num_kb + p.kb_per_split - 1) / p.kb_per_split;
+  p.num_units = p.tiles_m * p.tiles_n * p.splits;
+
+  switch (epi) {
+    case EPI_BF16_: return dispatch_layout<EPI_BF16_>(a_mn, b_mn, ta, tb, p, stream);
+    case EPI_F32_: return dispatch_layout<EPI_F32_>(a_mn, b_mn, ta, tb, p, stream);
+    case EPI_F32_ATOMIC_: return dispatch_layout<EPI_F32_ATOMIC_>(a_mn, b_mn, ta, tb, p, stream);
+    case EPI_BIAS_GELU_:
+      if (a_mn || !b_mn) return GPTB200_EUNSUPPORTED;
+      return launch_variant<kBN, kStages, EPI_BIAS_GELU_, 0, 1>(ta, tb, p, stream);
+    case EPI_DGELU_:
+      if (a_mn || b_mn) return GPTB200_EUNSUPPORTED;
+      return launch_variant<kBN, kStages, EPI_DGELU_, 0, 0>(ta, tb, p, stream);
+    case EPI_LCE_FWD_:
+      if (a_mn || b_mn) return GPTB200_EUNSUPPORTED;
+      return launch_variant<kBN, kStages, EPI_LCE_FWD_, 0, 0>(ta, tb, p, stream);
+    case EPI_LCE_BWD_:
+      if (a_mn || b_mn) return GPTB200_EUNSUPPORTED;
+      return launch_variant<kBN, kStages, EPI_LCE_BWD_, 0, 0>(ta, tb, p, stream);
+    default: return GPTB200_EUNSUPPORTED;
+  }
+}
+
+int gemm_tile_n() { return kBN; }
+
+int gemm_read_error(int clear) {
+  int h = 0;
+  cudaMemcpyFromSymbol(&h, g_gemm_error, sizeof(int));
+  if (clear) {
+    int z = 0;
+    cudaMemcpyToSymbol(g_gemm_error, &z, sizeof(int));
+  }
+  return h;
+}
+
+}  // namespace gptb200
+
+extern "C" int gptb200_gemm(const void* a, int a_mn_major, int64_t lda, const void* b,
+                            int b_mn_major, int64_t ldb, void* c, int64_t ldc, int64_t m,
+                            int64_t n, int64_t k, const gptb200_epilogue* e, void* stream) {
+  using namespace gptb200;
+  if (!e) return GPTB200_EINVAL;
+  GemmParams p = {};
+  p.C = c;
+  p.ldc = ldc;
+  p.alpha = e->alpha;
+  p.accumulate = e->accumulate;
+  p.bias = reinterpret_cast<const bf16*>(e->bias);
+  p.resid = reinterpret_cast<const bf16*>(e->residual);
+  p.ld_resid = e->ld_residual;
+  p.aux = reinterpret_cast<bf16*>(e->aux);
+  p.ld_aux = e->ld_aux;
+  int kind;
+  switch (e->kind) {
+    case GPTB200_EPI_BF16: kind = EPI_BF16_; break;
+    case GPTB200_EPI_BIAS_GELU:
+      if (!e->bias || !e->aux || e->ld_aux < n || (e->ld_aux % 8)) return GPTB200_EINVAL;
+      kind = EPI_BIAS_GELU_;
+      break;
+    case GPTB200_EPI_DGELU:
+      if (!e->aux || e->ld_aux < n || (e->ld_aux % 8)) return GPTB200_EINVAL;
+      kind = EPI_DGELU_;
+      break;
+    case GPTB200_EPI_F32: kind = EPI_F32_; break;
+    case GPTB200_EPI_F32_ATOMIC: kind = EPI_F32_ATOMIC_; break;
+    default: return GPTB200_EUNSUPPORTED;
+  }
+  if (e->residual && (e->ld_residual < n || (e->ld_residual % 8))) return GPTB200_EINVAL;
+  if (kind == EPI_F32_ || kind == EPI_F32_ATOMIC_) {
+    if (ldc % 4) return GPTB200_ESHAPE;
+  }
+  return gemm_launch(a, a_mn_major, lda, b, b_mn_major, ldb, m, n, k, kind, p,
+                     reinterpret_cast<cudaStream_t>(stream));
+}

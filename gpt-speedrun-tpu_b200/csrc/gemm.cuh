@@ -1,0 +1,49 @@
+// Internal interface of the tcgen05 GEMM (gemm.cu), shared with lce.cu.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace gptb200 {
+
+enum {
+  EPI_BF16_ = 0,
+  EPI_BIAS_GELU_ = 1,
+  EPI_DGELU_ = 2,
+  EPI_F32_ = 3,
+  EPI_F32_ATOMIC_ = 4,
+  EPI_LCE_FWD_ = 10,  // per (row, N-tile) partial (max, sum exp) + target logit
+  EPI_LCE_BWD_ = 11,  // bf16 (softmax - onehot) * cotangent
+};
+
+struct GemmParams {
+  // filled by gemm_launch
+  int M, N, K;
+  int tiles_m, tiles_n, num_kb, kb_per_split, splits, num_units;
+  // output + generic epilogue operands
+  void* C;
+  int64_t ldc;
+  float alpha;
+  int accumulate;
+  const __nv_bfloat16* bias;
+  const __nv_bfloat16* resid;
+  int64_t ld_resid;
+  __nv_bfloat16* aux;
+  int64_t ld_aux;
+  // cross-entropy epilogues
+  const int32_t* targets;
+  const float* lse;
+  const float* cot;
+  float2* partial;    // [M, tiles_n]
+  float* tgt_logit;   // [M]
+  int v_sem;
+};
+
+// Validates shapes, encodes the TMA maps and launches the persistent kernel.
+int gemm_launch(const void* a, int a_mn, int64_t lda, const void* b, int b_mn, int64_t ldb,
+                int64_t M, int64_t N, int64_t K, int epi, GemmParams p, cudaStream_t stream);
+int gemm_tile_n();
+int gemm_read_error(int clear);
+
+}  // namespace gptb200

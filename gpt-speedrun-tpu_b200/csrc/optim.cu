@@ -1,0 +1,239 @@
+// CompleteP AdamW over one flat fp32 parameter buffer (three launches):
+//   1. sqnorm_partial : per-block partial sums of grad^2 (fixed grid, deterministic)
+//   2. adamw_scalars  : one block -> global grad norm, step+1, learning rate
+//                       (warmup + cosine, train.py:1219-1236), bias
+//                       corrections, clip scale, history row
+//   3. adamw_update   : the element-wise m/v/param update with per-tensor
+//                       lr/eps/decay multipliers looked up from the group
+//                       table, plus the bf16 compute copy of the new params.
+// The step counter lives on the device, so a captured CUDA graph of the whole
+// step replays correctly.
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace gptb200 {
+
+constexpr int kNormBlocks = 1184;  // 8 x 148
+constexpr int kNormThreads = 512;
+
+struct AdamScalars {
+  float lr;
+  float bc1;
+  float bc2;
+  float gscale;     // grad_scale * clip scale
+  float grad_norm;
+  int step;
+};
+
+__global__ void __launch_bounds__(kNormThreads) sqnorm_partial_kernel(const float* __restrict__ g,
+                                                                      int64_t n,
+                                                                      double* __restrict__ part) {
+  __shared__ double red[kNormThreads / 32];
+  double acc = 0.0;
+  float accf = 0.f;
+  const int64_t n4 = n >> 2;
+  int cnt = 0;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float4 v = reinterpret_cast<const float4*>(g)[i];
+    accf += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    if (++cnt == 64) {
+      acc += accf;
+      accf = 0.f;
+      cnt = 0;
+    }
+  }
+  if (blockIdx.x == 0 && threadIdx.x < (n & 3)) {
+    float t = g[(n4 << 2) + threadIdx.x];
+    accf += t * t;
+  }
+  acc += accf;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double s = 0.0;
+    for (int w = 0; w < kNormThreads / 32; ++w) s += red[w];
+    part[blockIdx.x] = s;
+  }
+}
+
+__global__ void adamw_scalars_kernel(const double* __restrict__ part, int nparts,
+                                     const gptb200_adamw_config cfg, int32_t* step_io,
+                                     const float* loss, float* history, AdamScalars* out) {
+  __shared__ double red[32];
+  double s = 0.0;
+  for (int i = threadIdx.x; i < nparts; i += blockDim.x) s += part[i];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x != 0) return;
+  double tot = 0.0;
+  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) tot += red[w];
+  // Gradients are scaled by grad_scale before the norm (1.0 for the reference step).
+  const float gs = cfg.grad_scale;
+  const float grad_norm = (float)sqrt(tot) * gs;
+  float clip = 1.0f;
+  if (cfg.grad_clip > 0.f) clip = fminf(1.0f, cfg.grad_clip / (grad_norm + 1.0e-6f));
+  const int step = *step_io + 1;
+  const float stepf = (float)step;
+  float warm = 1.0f;
+  if (cfg.warmup_steps > 0) warm = fminf(1.0f, stepf / (float)cfg.warmup_steps);
+  const int span = max(1, cfg.total_steps - cfg.warmup_steps);
+  float prog = (stepf - (float)cfg.warmup_steps) / (float)span;
+  prog = fminf(fmaxf(prog, 0.0f), 1.0f);
+  const float cosine = 0.5f * (1.0f + cosf(3.14159265358979323846f * prog));
+  const float mult = cfg.min_lr_ratio + (1.0f - cfg.min_lr_ratio) * cosine;
+  const float lr = (cfg.learning_rate * cfg.horizon_lr_scale) * warm * mult;
+  AdamScalars a;
+  a.lr = lr;
+  a.bc1 = 1.0f - powf(cfg.beta1, stepf);
+  a.bc2 = 1.0f - powf(cfg.beta2, stepf);
+  a.gscale = gs * clip;
+  a.grad_norm = grad_norm;
+  a.step = step;
+  *out = a;
+  *step_io = step;
+  if (history && step >= 1 && step <= cfg.total_steps) {
+    float* row = history + (int64_t)(step - 1) * 3;
+    row[0] = loss ? *loss : 0.f;
+    row[1] = lr;
+    row[2] = grad_norm;
+  }
+}
+
+__global__ void __launch_bounds__(256) adamw_update_kernel(
+    float* __restrict__ p, float* __restrict__ m, float* __restrict__ v,
+    const float* __restrict__ g, int64_t n, const gptb200_tensor_group* __restrict__ groups,
+    int ngroups, const gptb200_adamw_config cfg, const AdamScalars* __restrict__ sc,
+    bf16* __restrict__ pbf) {
+  extern __shared__ gptb200_tensor_group sg[];
+  for (int i = threadIdx.x; i < ngroups; i += blockDim.x) sg[i] = groups[i];
+  __syncthreads();
+  const AdamScalars s = *sc;
+  const float b1 = cfg.beta1, b2 = cfg.beta2;
+  const float omb1 = 1.0f - b1, omb2 = 1.0f - b2;
+  const float eps_base = cfg.eps * cfg.eps_horizon_scale;
+  const float wd_base = cfg.weight_decay * cfg.wd_horizon_scale;
+  const int64_t n4 = (n + 3) >> 2;
+  int gi = 0;
+  for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < n4;
+       q += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t e0 = q << 2;
+    // Locate the group holding element e0 (offsets are increasing). Groups
+    // start on multiples of 4 elements, so a float4 never straddles two.
+    if (gi >= ngroups || e0 < sg[gi].offset || e0 >= sg[gi].offset + sg[gi].size) {
+      int lo = 0, hi = ngroups - 1, f = -1;
+      while (lo <= hi) {
+        int mid = (lo + hi) >> 1;
+        if (sg[mid].offset <= e0) {
+          f = mid;
+          lo = mid + 1;
+        } else {
+          hi = mid - 1;
+        }
+      }
+      if (f < 0 || e0 >= sg[f].offset + sg[f].size) continue;  // padding between tensors
+      gi = f;
+    }
+    const gptb200_tensor_group G = sg[gi];
+    const float lr = s.lr * G.lr_mult;
+    const float eps = eps_base * G.eps_mult;
+    const float wd = G.decay ? wd_base * G.wd_mult : 0.f;
+    int64_t lim = G.offset + G.size;
+    if (lim > n) lim = n;
+    const int cnt = (int)((lim - e0) < 4 ? (lim - e0) : 4);
+    if (cnt == 4) {
+      float4 P = reinterpret_cast<float4*>(p)[q];
+      float4 M = reinterpret_cast<float4*>(m)[q];
+      float4 V = reinterpret_cast<float4*>(v)[q];
+      float4 Gr = reinterpret_cast<const float4*>(g)[q];
+      float* pp = &P.x;
+      float* mm = &M.x;
+      float* vv = &V.x;
+      const float* gg = &Gr.x;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float gr = gg[j] * s.gscale;
+        mm[j] = b1 * mm[j] + omb1 * gr;
+        vv[j] = b2 * vv[j] + omb2 * (gr * gr);
+        float adam = (mm[j] / s.bc1) / (sqrtf(vv[j] / s.bc2) + eps);
+        float dec = wd * pp[j];
+        pp[j] = pp[j] - lr * (adam + dec);
+      }
+      reinterpret_cast<float4*>(p)[q] = P;
+      reinterpret_cast<float4*>(m)[q] = M;
+      reinterpret_cast<float4*>(v)[q] = V;
+      if (pbf) {
+        uint2 o;
+        o.x = pack_bf16x2(P.x, P.y);
+        o.y = pack_bf16x2(P.z, P.w);
+        reinterpret_cast<uint2*>(pbf)[q] = o;
+      }
+    } else {
+      for (int j = 0; j < cnt; ++j) {
+        int64_t e = e0 + j;
+        float gr = g[e] * s.gscale;
+        float mj = b1 * m[e] + omb1 * gr;
+        float vj = b2 * v[e] + omb2 * (gr * gr);
+        float adam = (mj / s.bc1) / (sqrtf(vj / s.bc2) + eps);
+        float pj = p[e] - lr * (adam + wd * p[e]);
+        m[e] = mj;
+        v[e] = vj;
+        p[e] = pj;
+        if (pbf) pbf[e] = __float2bfloat16(pj);
+      }
+    }
+  }
+}
+
+}  // namespace gptb200
+
+using namespace gptb200;
+
+extern "C" size_t gptb200_adamw_workspace_size(int64_t n) {
+  (void)n;
+  return kNormBlocks * sizeof(double) + 256;
+}
+
+extern "C" int gptb200_adamw_step(float* params, float* m, float* v, const float* grads, int64_t n,
+                                  const gptb200_tensor_group* groups, int32_t n_groups,
+                                  const gptb200_adamw_config* cfg, int32_t* step, const float* loss,
+                                  float* history, void* params_bf16, void* workspace,
+                                  void* stream) {
+  if (!params || !m || !v || !grads || !groups || !cfg || !step || !workspace || n <= 0 ||
+      n_groups <= 0)
+    return GPTB200_EINVAL;
+  if (n_groups > 4096) return GPTB200_EUNSUPPORTED;
+  if (((reinterpret_cast<uintptr_t>(params) | reinterpret_cast<uintptr_t>(m) |
+        reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(grads) |
+        reinterpret_cast<uintptr_t>(workspace)) & 15) ||
+      (params_bf16 && (reinterpret_cast<uintptr_t>(params_bf16) & 7)))
+    return GPTB200_ESHAPE;
+  auto st = reinterpret_cast<cudaStream_t>(stream);
+  double* part = reinterpret_cast<double*>(workspace);
+  AdamScalars* sc = reinterpret_cast<AdamScalars*>(reinterpret_cast<char*>(workspace) +
+                                                   kNormBlocks * sizeof(double));
+  sqnorm_partial_kernel<<<kNormBlocks, kNormThreads, 0, st>>>(grads, n, part);
+  GPTB200_CHECK_LAUNCH();
+  adamw_scalars_kernel<<<1, 1024, 0, st>>>(part, kNormBlocks, *cfg, step, loss, history, sc);
+  GPTB200_CHECK_LAUNCH();
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int64_t n4 = (n + 3) / 4;
+  int blocks = (int)std::min<int64_t>((n4 + 255) / 256, (int64_t)sms * 8);
+  size_t smem = (size_t)n_groups * sizeof(gptb200_tensor_group);
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(adamw_update_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return -static_cast<int>(e);
+  }
+  adamw_update_kernel<<<blocks, 256, smem, st>>>(params, m, v, grads, n, groups, n_groups, *cfg, sc,
+                                                 reinterpret_cast<bf16*>(params_bf16));
+  GPTB200_CHECK_LAUNCH();
+  return 0;
+}

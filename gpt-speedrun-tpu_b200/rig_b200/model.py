@@ -1,0 +1,413 @@
+"""The GPT training step on one GPU (and its data-parallel replicas).
+
+`GPTTrainer` replaces the reference's jitted ``train_step``
+(recipes/reference/train.py:1460-1472, wiring of `gpt_hidden` :1096-1176,
+loss :1194-1216, update :1362-1457). It owns:
+
+* one flat fp32 buffer each for parameters, gradients and the two Adam
+  moments, with every tensor at a 64-element-aligned offset (so any tensor
+  view is 16-byte aligned for TMA and 128-bit accesses), plus a bf16 mirror
+  of the parameters that the update kernel rewrites every step (the
+  ``weight.astype(dtype)`` of rig/nn.py:56);
+* every activation the backward pass reads, preallocated once for the local
+  batch (the step is static-shaped, so nothing is allocated per step);
+* the explicit forward/backward kernel schedule below. There is no autograd
+  on the hot path: each launch is a libgptb200 kernel on the current stream.
+
+Forward, per block (activations bf16, rows = local tokens):
+  rms_norm -> GEMM(+bias) -> qkv -> attention (RoPE on load) -> GEMM(+bias,
+  x branch multiplier, + residual) -> rms_norm -> GEMM(+bias, GELU) ->
+  GEMM(+bias, x multiplier, + residual); then the final rms_norm and the fused
+  linear cross-entropy (no logits in HBM).
+Backward mirrors it with dgrad GEMMs (dGELU fused), weight-gradient GEMMs that
+accumulate into the fp32 gradient buffer with split-K atomics, bias-gradient
+column sums, RMSNorm backward fused with the residual-gradient add, and the
+attention backward writing dq/dk/dv straight into the packed qkv gradient.
+With data parallelism each block's gradient slice is all-reduced on NCCL as
+soon as its backward has been enqueued, overlapping the remaining backward.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import dataclasses
+from typing import Iterable
+
+import numpy as np
+import torch
+
+from . import _lib, ops
+from .config import (
+    Config,
+    decay_for_name,
+    effective_adam_betas,
+    horizon_scales,
+    tensor_multipliers,
+)
+
+BLOCK_FIELDS = (
+    "ln1_scale", "qkv_w", "qkv_b", "attn_w", "attn_b",
+    "ln2_scale", "mlp_up_w", "mlp_up_b", "mlp_down_w", "mlp_down_b",
+)
+ALIGN = 64
+
+
+def block_shapes(config: Config) -> dict[str, tuple[int, ...]]:
+    d, h = config.d_model, config.hidden
+    return {
+        "ln1_scale": (d,),
+        "qkv_w": (d, 3 * d),
+        "qkv_b": (3 * d,),
+        "attn_w": (d, d),
+        "attn_b": (d,),
+        "ln2_scale": (d,),
+        "mlp_up_w": (d, h),
+        "mlp_up_b": (h,),
+        "mlp_down_w": (h, d),
+        "mlp_down_b": (d,),
+    }
+
+
+@dataclasses.dataclass(frozen=True)
+class Slot:
+    name: str          # "blocks/3/qkv_w", "token_embedding", ...
+    leaf: str          # "qkv_w"
+    block: int         # -1 outside the blocks
+    shape: tuple[int, ...]
+    offset: int
+
+    @property
+    def size(self) -> int:
+        return int(np.prod(self.shape))
+
+
+class ParamLayout:
+    """Flat layout: blocks 0..L-1, then final_ln_scale, token/output embedding."""
+
+    def __init__(self, config: Config):
+        self.config = config
+        slots: list[Slot] = []
+        off = 0
+
+        def add(name, leaf, block, shape):
+            nonlocal off
+            slots.append(Slot(name, leaf, block, tuple(shape), off))
+            off += int(np.prod(shape))
+            off = (off + ALIGN - 1) // ALIGN * ALIGN
+
+        shapes = block_shapes(config)
+        self.block_ranges: list[tuple[int, int]] = []
+        for b in range(config.layers):
+            start = off
+            for leaf in BLOCK_FIELDS:
+                add(f"blocks/{b}/{leaf}", leaf, b, shapes[leaf])
+            self.block_ranges.append((start, off))
+        tail = off
+        add("final_ln_scale", "final_ln_scale", -1, (config.d_model,))
+        add("token_embedding", "token_embedding", -1, (config.vocab_size, config.d_model))
+        if not config.tied:
+            add("output_embedding", "output_embedding", -1, (config.vocab_size, config.d_model))
+        self.tail_range = (tail, off)
+        self.slots = slots
+        self.by_name = {s.name: s for s in slots}
+        self.numel = off
+
+    def parameter_count(self) -> int:
+        return sum(s.size for s in self.slots)
+
+
+def init_params(config: Config, seed: int) -> dict[str, np.ndarray]:
+    """Initial parameters with the reference's draw order (train.py:865-901).
+
+    numpy PCG64 `default_rng(seed)`; per block qkv_w, attn_w, mlp_up_w,
+    mlp_down_w ~ N(0, sigma_h) (rig/nn.py:20-23: float32 standard normal times
+    float32 scale), biases 0, scales 1; then token_embedding ~ N(0, init_std),
+    then output_embedding ~ N(0, init_std / m_N) when untied.
+    """
+
+    rng = np.random.default_rng(seed)
+    hidden_scale = (
+        config.init_std / np.sqrt(config.width_multiplier)
+        if config.parameterization == "completep_fixed_tpp_v1"
+        else 0.02
+    )
+
+    def normal(shape, scale):
+        return rng.standard_normal(shape, dtype=np.float32) * np.float32(scale)
+
+    shapes = block_shapes(config)
+    out: dict[str, np.ndarray] = {}
+    for b in range(config.layers):
+        for leaf in BLOCK_FIELDS:
+            shape = shapes[leaf]
+            if leaf.endswith("_scale"):
+                value = np.ones(shape, dtype=np.float32)
+            elif leaf.endswith("_b"):
+                value = np.zeros(shape, dtype=np.float32)
+            else:
+                value = normal(shape, hidden_scale)
+            out[f"blocks/{b}/{leaf}"] = value
+    out["token_embedding"] = normal((config.vocab_size, config.d_model), config.init_std)
+    out["final_ln_scale"] = np.ones((config.d_model,), dtype=np.float32)
+    if not config.tied:
+        out["output_embedding"] = normal(
+            (config.vocab_size, config.d_model), config.init_std / config.width_multiplier
+        )
+    return out
+
+
+class _Block:
+    """Views of one block's parameters, bf16 mirrors and gradients."""
+
+    def __init__(self, trainer: "GPTTrainer", b: int):
+        for leaf in BLOCK_FIELDS:
+            name = f"blocks/{b}/{leaf}"
+            setattr(self, leaf, trainer.param_view(name, bf16=True))
+            setattr(self, "g_" + leaf, trainer.grad_view(name))
+
+
+class GPTTrainer:
+    """Holds the model state on one GPU and runs the training step."""
+
+    def __init__(
+        self,
+        config: Config,
+        local_batch: int,
+        device: torch.device | str = "cuda",
+        *,
+        process_group=None,
+        world_size: int = 1,
+        history_steps: int | None = None,
+    ):
+        if config.dtype_name != "bfloat16":
+            raise ValueError("the B200 step computes in bfloat16")
+        if config.head_dim != 64:
+            raise ValueError("the attention kernels need head_dim 64")
+        self.config = config
+        self.device = torch.device(device)
+        if self.device.type != "cuda":
+            raise ValueError("GPTTrainer needs a CUDA device (there is no CPU path)")
+        self.B = int(local_batch)
+        self.T = config.seq_len
+        self.N = self.B * self.T
+        self.world_size = int(world_size)
+        self.pg = process_group
+        self.layout = ParamLayout(config)
+        dev = self.device
+        n = self.layout.numel
+        self.params = torch.zeros(n, dtype=torch.float32, device=dev)
+        self.grads = torch.zeros(n, dtype=torch.float32, device=dev)
+        self.m = torch.zeros(n, dtype=torch.float32, device=dev)
+        self.v = torch.zeros(n, dtype=torch.float32, device=dev)
+        self.params_bf16 = torch.zeros(n, dtype=torch.bfloat16, device=dev)
+        self.step_dev = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.history = torch.zeros(max(1, history_steps or config.steps), 3,
+                                   dtype=torch.float32, device=dev)
+        self.blocks = [_Block(self, b) for b in range(config.layers)]
+        self.final_scale = self.param_view("final_ln_scale", bf16=True)
+        self.g_final_scale = self.grad_view("final_ln_scale")
+        self.tok_emb = self.param_view("token_embedding", bf16=True)
+        self.g_tok_emb = self.grad_view("token_embedding")
+        if config.tied:
+            self.out_emb, self.g_out_emb = self.tok_emb, self.g_tok_emb
+        else:
+            self.out_emb = self.param_view("output_embedding", bf16=True)
+            self.g_out_emb = self.grad_view("output_embedding")
+        self._alloc_activations()
+        self._build_optimizer()
+        self.rope = ops.rope_tables(self.T, config.head_dim, dev)
+
+    # ------------------------------------------------------------ state views
+    def param_view(self, name: str, bf16: bool = False) -> torch.Tensor:
+        s = self.layout.by_name[name]
+        buf = self.params_bf16 if bf16 else self.params
+        return buf[s.offset : s.offset + s.size].view(s.shape)
+
+    def grad_view(self, name: str) -> torch.Tensor:
+        s = self.layout.by_name[name]
+        return self.grads[s.offset : s.offset + s.size].view(s.shape)
+
+    def load_params(self, values: dict[str, np.ndarray]) -> None:
+        for s in self.layout.slots:
+            arr = np.asarray(values[s.name], dtype=np.float32).reshape(s.shape)
+            self.params[s.offset : s.offset + s.size].copy_(
+                torch.from_numpy(np.ascontiguousarray(arr)).reshape(-1))
+        ops.cast_bf16(self.params, self.params_bf16)
+        self.m.zero_()
+        self.v.zero_()
+        self.step_dev.zero_()
+
+    def export(self, buf: torch.Tensor | None = None) -> dict[str, np.ndarray]:
+        buf = self.params if buf is None else buf
+        host = buf.detach().float().cpu().numpy()
+        return {s.name: host[s.offset : s.offset + s.size].reshape(s.shape).copy()
+                for s in self.layout.slots}
+
+    # ------------------------------------------------------------ buffers
+    def _alloc_activations(self) -> None:
+        c, dev, N = self.config, self.device, self.N
+        d, h, L = c.d_model, c.hidden, c.layers
+        bf = dict(dtype=torch.bfloat16, device=dev)
+        f32 = dict(dtype=torch.float32, device=dev)
+        self.x = [torch.empty(N, d, **bf) for _ in range(L + 1)]
+        self.ln1 = [torch.empty(N, d, **bf) for _ in range(L)]
+        self.rstd1 = [torch.empty(N, **f32) for _ in range(L)]
+        self.qkv = [torch.empty(N, 3 * d, **bf) for _ in range(L)]
+        self.att = [torch.empty(N, d, **bf) for _ in range(L)]
+        self.lse = [torch.empty(self.B, c.heads, self.T, **f32) for _ in range(L)]
+        self.xm = [torch.empty(N, d, **bf) for _ in range(L)]
+        self.ln2 = [torch.empty(N, d, **bf) for _ in range(L)]
+        self.rstd2 = [torch.empty(N, **f32) for _ in range(L)]
+        self.u = [torch.empty(N, h, **bf) for _ in range(L)]
+        self.g = [torch.empty(N, h, **bf) for _ in range(L)]
+        self.lnf = torch.empty(N, d, **bf)
+        self.rstdf = torch.empty(N, **f32)
+        self.losses = torch.empty(N, **f32)
+        self.lse_ce = torch.empty(N, **f32)
+        self.loss = torch.zeros(1, **f32)
+        self.cot = torch.full((N,), 1.0 / (N * self.world_size), **f32)
+        # backward scratch
+        self.dx = torch.empty(N, d, **bf)
+        self.dln = torch.empty(N, d, **bf)
+        self.du = torch.empty(N, h, **bf)
+        self.datt = torch.empty(N, d, **bf)
+        self.dqkv = torch.empty(N, 3 * d, **bf)
+        self.attn_ws = ops.attention_workspace(self.B, c.heads, self.T, dev)
+        self.lce_fwd_ws = ops.lce_fwd_workspace(N, c.vocab_size, dev)
+        self.lce_bwd_ws = ops.lce_bwd_workspace(N, c.vocab_size, dev)
+        self.tokens = torch.empty(self.B, self.T, dtype=torch.int32, device=dev)
+        self.targets = torch.empty(self.B, self.T, dtype=torch.int32, device=dev)
+
+    def _build_optimizer(self) -> None:
+        c = self.config
+        groups = []
+        for s in self.layout.slots:
+            lr_m, eps_m, wd_m = tensor_multipliers(s.leaf, s.block >= 0, c)
+            groups.append(_lib.TensorGroup(
+                offset=s.offset, size=s.size, lr_mult=lr_m, eps_mult=eps_m, wd_mult=wd_m,
+                decay=int(decay_for_name(s.leaf))))
+        arr = (_lib.TensorGroup * len(groups))(*groups)
+        raw = bytes(arr)
+        self.groups_dev = torch.frombuffer(bytearray(raw), dtype=torch.uint8).to(self.device)
+        self.n_groups = len(groups)
+        b1, b2 = effective_adam_betas(c)
+        lr_h, eps_h, wd_h = horizon_scales(c)
+        self.adam_cfg = _lib.AdamWConfig(
+            learning_rate=c.learning_rate, horizon_lr_scale=lr_h, min_lr_ratio=c.min_lr_ratio,
+            warmup_steps=c.warmup_steps, total_steps=c.steps, beta1=b1, beta2=b2,
+            eps=c.adam_epsilon, eps_horizon_scale=eps_h, weight_decay=c.weight_decay,
+            wd_horizon_scale=wd_h, grad_clip=c.grad_clip, grad_scale=1.0)
+        self.adam_ws = ops.adamw_workspace(self.layout.numel, self.device)
+
+    # ------------------------------------------------------------ views
+    def _qkv_views(self, buf: torch.Tensor):
+        c = self.config
+        t5 = buf.view(self.B, self.T, 3, c.heads, c.head_dim)
+        return t5[:, :, 0], t5[:, :, 1], t5[:, :, 2]
+
+    def _bthd(self, buf: torch.Tensor):
+        c = self.config
+        return buf.view(self.B, self.T, c.heads, c.head_dim)
+
+    # ------------------------------------------------------------ step
+    def set_batch(self, x: torch.Tensor, y: torch.Tensor) -> None:
+        """Copies a [B, T] int32 batch (host pinned or device) into the step's buffers."""
+
+        self.tokens.copy_(x, non_blocking=True)
+        self.targets.copy_(y, non_blocking=True)
+
+    def forward(self) -> torch.Tensor:
+        c = self.config
+        d, h, N = c.d_model, c.hidden, self.N
+        a = c.branch_scale
+        ops.embedding_fwd(self.tokens.view(-1), self.tok_emb, self.x[0])
+        for l, blk in enumerate(self.blocks):
+            ops.rms_norm_fwd(self.x[l], blk.ln1_scale, self.ln1[l], self.rstd1[l])
+            ops.matmul(self.ln1[l], blk.qkv_w, bias=blk.qkv_b, out=self.qkv[l])
+            q, k, v = self._qkv_views(self.qkv[l])
+            ops.attention_fwd(q, k, v, self._bthd(self.att[l]), self.lse[l], scale=c.softmax_scale,
+                              layout="bthd", rope=self.rope)
+            ops.matmul(self.att[l], blk.attn_w, bias=blk.attn_b, alpha=a, residual=self.x[l],
+                       out=self.xm[l])
+            ops.rms_norm_fwd(self.xm[l], blk.ln2_scale, self.ln2[l], self.rstd2[l])
+            ops.matmul(self.ln2[l], blk.mlp_up_w, bias=blk.mlp_up_b, kind=_lib.EPI_BIAS_GELU,
+                       aux=self.u[l], out=self.g[l])
+            ops.matmul(self.g[l], blk.mlp_down_w, bias=blk.mlp_down_b, alpha=a,
+                       residual=self.xm[l], out=self.x[l + 1])
+        ops.rms_norm_fwd(self.x[c.layers], self.final_scale, self.lnf, self.rstdf)
+        ops.lce_fwd(self.lnf, self.out_emb, self.targets.view(-1), c.semantic_vocab_size,
+                    self.losses, self.lse_ce, self.loss, workspace=self.lce_fwd_ws)
+        return self.loss
+
+    def _wgrad(self, act: torch.Tensor, dy: torch.Tensor, gview: torch.Tensor, alpha: float):
+        """gview[K_in, N_out] += alpha * act^T dy (fp32, split-K atomics)."""
+
+        m, n = act.shape[1], dy.shape[1]
+        ops.gemm(act, dy, gview, a_mn_major=True, b_mn_major=True, m=m, n=n, k=self.N,
+                 kind=_lib.EPI_F32_ATOMIC, alpha=alpha)
+
+    def _dgrad(self, dy: torch.Tensor, w: torch.Tensor, out: torch.Tensor, **kw):
+        """out[N, in] = epilogue(dy[N, out] @ w[in, out]^T)."""
+
+        ops.gemm(dy, w, out, m=self.N, n=w.shape[0], k=w.shape[1], **kw)
+
+    def backward(self, reduce_hook=None) -> None:
+        c = self.config
+        a = c.branch_scale
+        self.grads.zero_()
+        ops.lce_bwd(self.lnf, self.out_emb, self.targets.view(-1), self.lse_ce, self.cot,
+                    c.semantic_vocab_size, self.dln, self.g_out_emb, workspace=self.lce_bwd_ws)
+        ops.rms_norm_bwd(self.x[c.layers], self.final_scale, self.rstdf, self.dln, None, self.dx,
+                         self.g_final_scale)
+        dx = self.dx
+        for l in reversed(range(c.layers)):
+            blk = self.blocks[l]
+            # MLP: x[l+1] = xm + a * (gelu(ln2 Wu + bu) Wd + bd)
+            self._dgrad(dx, blk.mlp_down_w, self.du, kind=_lib.EPI_DGELU, alpha=a, aux=self.u[l])
+            self._wgrad(self.g[l], dx, blk.g_mlp_down_w, a)
+            ops.colsum(dx, blk.g_mlp_down_b, a)
+            self._wgrad(self.ln2[l], self.du, blk.g_mlp_up_w, 1.0)
+            ops.colsum(self.du, blk.g_mlp_up_b, 1.0)
+            self._dgrad(self.du, blk.mlp_up_w, self.dln)
+            ops.rms_norm_bwd(self.xm[l], blk.ln2_scale, self.rstd2[l], self.dln, dx, dx,
+                             blk.g_ln2_scale)
+            # attention: xm = x + a * (att Wo + bo)
+            self._dgrad(dx, blk.attn_w, self.datt, alpha=a)
+            self._wgrad(self.att[l], dx, blk.g_attn_w, a)
+            ops.colsum(dx, blk.g_attn_b, a)
+            q, k, v = self._qkv_views(self.qkv[l])
+            dq, dk, dv = self._qkv_views(self.dqkv)
+            ops.attention_bwd(q, k, v, self._bthd(self.att[l]), self._bthd(self.datt), self.lse[l],
+                              dq, dk, dv, scale=c.softmax_scale, layout="bthd", rope=self.rope,
+                              workspace=self.attn_ws)
+            self._wgrad(self.ln1[l], self.dqkv, blk.g_qkv_w, 1.0)
+            ops.colsum(self.dqkv, blk.g_qkv_b, 1.0)
+            self._dgrad(self.dqkv, blk.qkv_w, self.dln)
+            ops.rms_norm_bwd(self.x[l], blk.ln1_scale, self.rstd1[l], self.dln, dx, dx,
+                             blk.g_ln1_scale)
+            if reduce_hook is not None:
+                reduce_hook(*self.layout.block_ranges[l])
+        ops.embedding_bwd(self.tokens.view(-1), dx, self.g_tok_emb)
+        if reduce_hook is not None:
+            reduce_hook(*self.layout.tail_range)
+
+    def optimizer_step(self) -> None:
+        ops.adamw_step(self.params, self.m, self.v, self.grads, self.groups_dev, self.n_groups,
+                       self.adam_cfg, self.step_dev, self.loss, self.history, self.params_bf16,
+                       self.adam_ws)
+
+    def train_step(self, x: torch.Tensor | None = None, y: torch.Tensor | None = None) -> None:
+        """One full step: forward, backward, (all-reduce), AdamW. Asynchronous."""
+
+        if x is not None:
+            self.set_batch(x, y)
+        self.forward()
+        if self.world_size > 1:
+            from .mesh import GradientReducer
+
+            reducer = GradientReducer(self.grads, self.pg)
+            self.backward(reduce_hook=reducer.launch)
+            reducer.finish(self.loss)
+        else:
+            self.backward()
+        self.optimizer_step()

@@ -1,0 +1,262 @@
+"""Tensor-level wrappers over the libgptb200 C ABI.
+
+Each function takes CUDA torch tensors (PyTorch is used for device memory and
+streams only), checks dtypes/shapes/contiguity on the host, and launches the
+kernel on the current torch stream. No function here has a CPU path: a CPU
+tensor raises ``ValueError``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+from ._lib import Epilogue, call
+
+BF16 = torch.bfloat16
+F32 = torch.float32
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream() -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _cuda(*ts: torch.Tensor | None) -> None:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("rig_b200 kernels need CUDA tensors (there is no CPU path)")
+
+
+def _row_major(t: torch.Tensor, name: str) -> int:
+    """Returns the leading dimension of a 2-D tensor with unit inner stride."""
+
+    if t.dim() != 2 or t.stride(1) != 1:
+        raise ValueError(f"{name} must be a 2-D tensor with contiguous rows, got {tuple(t.stride())}")
+    return t.stride(0)
+
+
+# ----------------------------------------------------------------- GEMM
+def gemm(
+    a: torch.Tensor,
+    b: torch.Tensor,
+    out: torch.Tensor,
+    *,
+    a_mn_major: bool = False,
+    b_mn_major: bool = False,
+    m: int,
+    n: int,
+    k: int,
+    kind: int = _lib.EPI_BF16,
+    alpha: float = 1.0,
+    bias: torch.Tensor | None = None,
+    residual: torch.Tensor | None = None,
+    aux: torch.Tensor | None = None,
+    accumulate: bool = False,
+) -> torch.Tensor:
+    """out[m, n] = epilogue(sum_k A[m, k] B[n, k]); see include/gptb200.h."""
+
+    _cuda(a, b, out, bias, residual, aux)
+    if a.dtype != BF16 or b.dtype != BF16:
+        raise TypeError("GEMM operands must be bfloat16")
+    lda, ldb, ldc = _row_major(a, "a"), _row_major(b, "b"), _row_major(out, "out")
+    epi = Epilogue(
+        kind=kind,
+        accumulate=int(accumulate),
+        alpha=float(alpha),
+        bias=_ptr(bias),
+        residual=_ptr(residual),
+        ld_residual=0 if residual is None else _row_major(residual, "residual"),
+        aux=_ptr(aux),
+        ld_aux=0 if aux is None else _row_major(aux, "aux"),
+    )
+    call(
+        "gptb200_gemm",
+        a.data_ptr(), int(a_mn_major), lda, b.data_ptr(), int(b_mn_major), ldb,
+        out.data_ptr(), ldc, m, n, k, ctypes.byref(epi), _stream(),
+    )
+    return out
+
+
+def matmul(x: torch.Tensor, w: torch.Tensor, *, bias=None, out=None, kind=_lib.EPI_BF16,
+           alpha=1.0, residual=None, aux=None) -> torch.Tensor:
+    """y[M, N] = x[M, K] @ w[K, N] (w in the reference's [in, out] layout)."""
+
+    m, k = x.shape
+    n = w.shape[1]
+    if out is None:
+        out = torch.empty(m, n, device=x.device, dtype=BF16)
+    return gemm(x, w, out, b_mn_major=True, m=m, n=n, k=k, kind=kind, alpha=alpha, bias=bias,
+                residual=residual, aux=aux)
+
+
+# ----------------------------------------------------------------- RMSNorm
+def rms_norm_fwd(x: torch.Tensor, scale: torch.Tensor, y: torch.Tensor, rstd: torch.Tensor):
+    _cuda(x, scale, y, rstd)
+    rows, d = x.shape
+    call("gptb200_rms_norm_fwd", x.data_ptr(), scale.data_ptr(), y.data_ptr(), rstd.data_ptr(),
+         rows, d, _stream())
+    return y, rstd
+
+
+def rms_norm_bwd(x, scale, rstd, dy, dx_in, dx_out, dscale):
+    _cuda(x, scale, rstd, dy, dx_in, dx_out, dscale)
+    rows, d = x.shape
+    call("gptb200_rms_norm_bwd", x.data_ptr(), scale.data_ptr(), rstd.data_ptr(), dy.data_ptr(),
+         _ptr(dx_in), dx_out.data_ptr(), dscale.data_ptr(), rows, d, _stream())
+    return dx_out
+
+
+# ----------------------------------------------------------------- embedding
+def embedding_fwd(tokens: torch.Tensor, table: torch.Tensor, out: torch.Tensor):
+    _cuda(tokens, table, out)
+    if tokens.dtype != torch.int32:
+        raise TypeError("token ids must be int32")
+    call("gptb200_embedding_fwd", tokens.data_ptr(), table.data_ptr(), out.data_ptr(),
+         tokens.numel(), table.shape[1], table.shape[0], _stream())
+    return out
+
+
+def embedding_bwd(tokens: torch.Tensor, dout: torch.Tensor, dtable: torch.Tensor):
+    _cuda(tokens, dout, dtable)
+    call("gptb200_embedding_bwd", tokens.data_ptr(), dout.data_ptr(), dtable.data_ptr(),
+         tokens.numel(), dtable.shape[1], dtable.shape[0], _stream())
+    return dtable
+
+
+def rope_tables(seq: int, head_dim: int, device) -> tuple[torch.Tensor, torch.Tensor]:
+    cos = torch.empty(seq, head_dim // 2, device=device, dtype=BF16)
+    sin = torch.empty_like(cos)
+    call("gptb200_rope_tables", cos.data_ptr(), sin.data_ptr(), seq, head_dim, _stream())
+    return cos, sin
+
+
+# ----------------------------------------------------------------- attention
+def _strides4(t: torch.Tensor, layout: str) -> tuple[int, int, int]:
+    """Element strides (batch, head, time) of a rank-4 view, inner dim contiguous."""
+
+    if t.stride(3) != 1:
+        raise ValueError("attention tensors need a contiguous head dimension")
+    if layout == "bhsd":
+        return t.stride(0), t.stride(1), t.stride(2)
+    return t.stride(0), t.stride(2), t.stride(1)  # bthd
+
+
+def attention_fwd(q, k, v, o, lse, *, scale: float, layout: str = "bhsd", rope=None):
+    """Causal attention; q/k/v/o are rank-4 views in `layout` ('bhsd' or 'bthd')."""
+
+    _cuda(q, k, v, o, lse)
+    sb, sh, st = _strides4(q, layout)
+    if _strides4(k, layout) != (sb, sh, st) or _strides4(v, layout) != (sb, sh, st):
+        raise ValueError("q, k and v must share strides")
+    osb, osh, ost = _strides4(o, layout)
+    if layout == "bhsd":
+        b, h, t, dh = q.shape
+    else:
+        b, t, h, dh = q.shape
+    cos, sin = rope if rope is not None else (None, None)
+    call("gptb200_attention_fwd", q.data_ptr(), k.data_ptr(), v.data_ptr(), sb, sh, st,
+         o.data_ptr(), osb, osh, ost, lse.data_ptr(), b, h, t, dh, float(scale), _ptr(cos),
+         _ptr(sin), _stream())
+    return o, lse
+
+
+def attention_workspace(b: int, h: int, t: int, device) -> torch.Tensor:
+    n = _lib.load().gptb200_attention_bwd_workspace_size(b, h, t)
+    return torch.empty(n, dtype=torch.uint8, device=device)
+
+
+def attention_bwd(q, k, v, o, do, lse, dq, dk, dv, *, scale: float, layout="bhsd", rope=None,
+                  workspace=None):
+    _cuda(q, k, v, o, do, lse, dq, dk, dv)
+    sb, sh, st = _strides4(q, layout)
+    for t_ in (k, v, dq, dk, dv):
+        if _strides4(t_, layout) != (sb, sh, st):
+            raise ValueError("q, k, v, dq, dk, dv must share strides")
+    osb, osh, ost = _strides4(o, layout)
+    if _strides4(do, layout) != (osb, osh, ost):
+        raise ValueError("o and do must share strides")
+    if layout == "bhsd":
+        b, h, t, dh = q.shape
+    else:
+        b, t, h, dh = q.shape
+    if workspace is None:
+        workspace = attention_workspace(b, h, t, q.device)
+    cos, sin = rope if rope is not None else (None, None)
+    call("gptb200_attention_bwd", q.data_ptr(), k.data_ptr(), v.data_ptr(), sb, sh, st,
+         o.data_ptr(), do.data_ptr(), osb, osh, ost, lse.data_ptr(), dq.data_ptr(),
+         dk.data_ptr(), dv.data_ptr(), b, h, t, dh, float(scale), _ptr(cos), _ptr(sin),
+         workspace.data_ptr(), _stream())
+    return dq, dk, dv
+
+
+# ----------------------------------------------------------------- cross entropy
+def lce_fwd_workspace(n: int, v: int, device) -> torch.Tensor:
+    size = _lib.load().gptb200_lce_fwd_workspace_size(n, v)
+    return torch.empty(size, dtype=torch.uint8, device=device)
+
+
+def lce_bwd_workspace(n: int, v: int, device) -> torch.Tensor:
+    size = _lib.load().gptb200_lce_bwd_workspace_size(n, v)
+    return torch.empty(size, dtype=torch.uint8, device=device)
+
+
+def lce_fwd(hidden, embedding, targets, v_semantic, losses, lse, mean=None, workspace=None):
+    _cuda(hidden, embedding, targets, losses, lse, mean)
+    n, d = hidden.shape
+    v = embedding.shape[0]
+    if workspace is None:
+        workspace = lce_fwd_workspace(n, v, hidden.device)
+    call("gptb200_lce_fwd", hidden.data_ptr(), embedding.data_ptr(), targets.data_ptr(), n, d, v,
+         v_semantic, losses.data_ptr(), lse.data_ptr(), _ptr(mean), workspace.data_ptr(),
+         _stream())
+    return losses
+
+
+def lce_bwd(hidden, embedding, targets, lse, dlosses, v_semantic, dhidden, dembedding,
+            workspace=None):
+    _cuda(hidden, embedding, targets, lse, dlosses, dhidden, dembedding)
+    n, d = hidden.shape
+    v = embedding.shape[0]
+    if workspace is None:
+        workspace = lce_bwd_workspace(n, v, hidden.device)
+    call("gptb200_lce_bwd", hidden.data_ptr(), embedding.data_ptr(), targets.data_ptr(),
+         lse.data_ptr(), dlosses.data_ptr(), n, d, v, v_semantic, dhidden.data_ptr(),
+         dembedding.data_ptr(), workspace.data_ptr(), _stream())
+    return dhidden, dembedding
+
+
+# ----------------------------------------------------------------- misc
+def colsum(x: torch.Tensor, out: torch.Tensor, alpha: float = 1.0):
+    _cuda(x, out)
+    rows, n = x.shape
+    call("gptb200_colsum", x.data_ptr(), rows, n, float(alpha), out.data_ptr(), _stream())
+    return out
+
+
+def cast_bf16(src: torch.Tensor, dst: torch.Tensor):
+    _cuda(src, dst)
+    call("gptb200_cast_bf16", src.data_ptr(), dst.data_ptr(), src.numel(), _stream())
+    return dst
+
+
+def adamw_workspace(n: int, device) -> torch.Tensor:
+    size = _lib.load().gptb200_adamw_workspace_size(n)
+    return torch.empty(size, dtype=torch.uint8, device=device)
+
+
+def adamw_step(params, m, v, grads, groups_dev, n_groups, cfg, step, loss, history, params_bf16,
+               workspace):
+    _cuda(params, m, v, grads, groups_dev, step, loss, history, params_bf16, workspace)
+    call("gptb200_adamw_step", params.data_ptr(), m.data_ptr(), v.data_ptr(), grads.data_ptr(),
+         params.numel(), groups_dev.data_ptr(), n_groups, ctypes.byref(cfg), step.data_ptr(),
+         _ptr(loss), _ptr(history), _ptr(params_bf16), workspace.data_ptr(), _stream())
+
+
+def device_error(clear: bool = True) -> int:
+    return _lib.load().gptb200_device_error(int(clear))

@@ -1,0 +1,246 @@
+/*
+ * libgptb200 — C ABI of the B200 (sm_100a) kernels behind the GPT training step
+ * of the GPT-speedrun rig (recipes/reference/train.py, train_step at :1460-1472).
+ *
+ * Conventions (every entry point):
+ *   - Pointers are device pointers unless the parameter says "host".
+ *   - bf16 tensors are passed as `void*` (IEEE bfloat16, row-major).
+ *   - `stream` is a cudaStream_t passed as `void*` (NULL = legacy stream).
+ *   - Return value: 0 on success, a positive GPTB200_E* code for an argument or
+ *     shape error (checked before anything is launched), or the negated
+ *     cudaError_t of a failed launch. Nothing throws across this boundary.
+ *   - No entry point allocates device memory. Scratch space that a kernel needs
+ *     is passed in as `workspace`, sized by the matching *_workspace_size().
+ *   - All work is stream-ordered and asynchronous; entry points are reentrant.
+ *
+ * Each declaration names the reference interface it replaces (file:line within
+ * the reference project honglu2875/GPT-speedrun-TPU).
+ */
+#ifndef GPTB200_H_
+#define GPTB200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GPTB200_OK 0
+#define GPTB200_EINVAL 1       /* bad argument: null pointer, non-positive size */
+#define GPTB200_ESHAPE 2       /* unsupported shape / alignment */
+#define GPTB200_EUNSUPPORTED 3 /* unsupported combination of options */
+#define GPTB200_EDEVICE 4      /* a kernel reported a device-side error (bounded wait ran out) */
+#define GPTB200_ERANGE 5       /* token id outside the vocabulary */
+
+/* Library identification; no reference counterpart. */
+const char* gptb200_version(void);
+const char* gptb200_status_string(int status);
+
+/* Reads (and with clear != 0 resets) the device-side error flags of every
+ * kernel family on the current device. Returns 0 when no kernel reported an
+ * error, else GPTB200_EDEVICE. Synchronizes the device. */
+int gptb200_device_error(int clear);
+
+/* ------------------------------------------------------------------ GEMM
+ * C[M,N] = epilogue( sum_k A[m,k] * B[n,k] ), bf16 operands, fp32 accumulate
+ * in tensor memory (tcgen05.mma, TMA-fed).
+ *   a_mn_major = 0: A stored [M, K] (row stride lda >= K)
+ *   a_mn_major = 1: A stored [K, M] (row stride lda >= M)
+ *   b_mn_major = 0: B stored [N, K] (row stride ldb >= K)
+ *   b_mn_major = 1: B stored [K, N] (row stride ldb >= N)
+ * Replaces rig/nn.py:55-56 (`linear`: einsum("...d,df->...f", x, W) + b) and
+ * the projections of recipes/reference/train.py:1136,1164-1166,1170-1174, with
+ * their XLA-generated transposes for the backward pass. Leading dimensions and
+ * N must be multiples of 8 elements; pointers 16-byte aligned.
+ */
+#define GPTB200_EPI_BF16 0       /* C bf16 = resid + alpha*(bf16(acc) + bias), each step rounded to bf16 */
+#define GPTB200_EPI_BIAS_GELU 1  /* aux bf16 = bf16(acc)+bias; C bf16 = gelu_tanh(aux) */
+#define GPTB200_EPI_DGELU 2      /* C bf16 = bf16(alpha*acc) * gelu_tanh'(aux) */
+#define GPTB200_EPI_F32 3        /* C fp32 = alpha*acc (accumulate=1: C += alpha*acc) */
+#define GPTB200_EPI_F32_ATOMIC 4 /* C fp32 += alpha*acc with atomics; K may be split across CTAs */
+
+typedef struct gptb200_epilogue {
+  int kind;              /* GPTB200_EPI_* */
+  int accumulate;        /* EPI_F32 only */
+  float alpha;           /* 1.0f for none */
+  const void* bias;      /* bf16 [N] or NULL (EPI_BF16, required for EPI_BIAS_GELU) */
+  const void* residual;  /* bf16 [M, ld_residual] or NULL (EPI_BF16) */
+  int64_t ld_residual;
+  void* aux;             /* bf16 [M, ld_aux]: written by BIAS_GELU, read by DGELU */
+  int64_t ld_aux;
+} gptb200_epilogue;
+
+int gptb200_gemm(const void* a, int a_mn_major, int64_t lda, const void* b, int b_mn_major,
+                 int64_t ldb, void* c, int64_t ldc, int64_t m, int64_t n, int64_t k,
+                 const gptb200_epilogue* epilogue, void* stream);
+
+/* ------------------------------------------------------------------ RMSNorm
+ * y = bf16(x * rsqrt(mean(x^2) + 1e-5)) * scale   (fp32 statistics)
+ * Replaces rig/nn.py:26-33 (`rms_norm`). x, y, scale bf16; rstd fp32 [rows]
+ * (saved for the backward pass). d must be a multiple of 8 and <= 4096
+ * (<= 2048 for the backward).
+ */
+int gptb200_rms_norm_fwd(const void* x, const void* scale, void* y, float* rstd, int64_t rows,
+                         int64_t d, void* stream);
+
+/* Backward of rms_norm. dx_out (bf16) = dx_in (bf16 residual-stream gradient,
+ * may be NULL for zero, may alias dx_out) + d(rms_norm)/dx · dy.
+ * dscale (fp32 [d]) is accumulated into (+=). Replaces the XLA autodiff of
+ * rig/nn.py:26-33. */
+int gptb200_rms_norm_bwd(const void* x, const void* scale, const float* rstd, const void* dy,
+                         const void* dx_in, void* dx_out, float* dscale, int64_t rows, int64_t d,
+                         void* stream);
+
+/* ------------------------------------------------------------------ embedding
+ * out[i, :] = bf16(table[tokens[i], :]); Replaces recipes/reference/train.py:1107
+ * (`params["token_embedding"][tokens].astype(dtype)`). table bf16 [vocab, d].
+ * Token ids outside [0, vocab) are clamped (the step validates ids on the host,
+ * rig/tokens.py:262-268). */
+int gptb200_embedding_fwd(const int32_t* tokens, const void* table, void* out, int64_t n,
+                          int64_t d, int64_t vocab, void* stream);
+/* dtable[tokens[i], :] += dout[i, :] (fp32 atomics). Backward of the gather. */
+int gptb200_embedding_bwd(const int32_t* tokens, const void* dout, float* dtable, int64_t n,
+                          int64_t d, int64_t vocab, void* stream);
+
+/* ------------------------------------------------------------------ RoPE
+ * Tables of the interleaved base-10000 rotary embedding of rig/nn.py:36-52:
+ * angle[t, i] = t * 10000^(-2i/head_dim) in fp32, cos/sin rounded to bf16.
+ * cos_out, sin_out: bf16 [seq, head_dim/2]. */
+int gptb200_rope_tables(void* cos_out, void* sin_out, int64_t seq, int64_t head_dim,
+                        void* stream);
+
+/* ------------------------------------------------------------------ attention
+ * Causal softmax attention, fp32 statistics, bf16 P before P·V, with optional
+ * interleaved RoPE applied to q and k as they are loaded (rope_cos/rope_sin
+ * from gptb200_rope_tables, or NULL for none).
+ * Tensors are addressed as base + b*stride_b + h*stride_h + t*stride_t + e
+ * (element strides); q, k, v share (stride_b, stride_h, stride_t), o and do
+ * share (o_stride_*). lse: fp32 [batch, heads, seq] (natural-log units of the
+ * scaled scores). head_dim must be 64.
+ * Replaces rig/kernels/tpu_flash_attention.py:236-348 (forward kernel) behind
+ * make_causal_attention (:962-1164); semantics of reference_causal_attention
+ * (:171-207) and, with rope, of rig/nn.py:36-52 applied first.
+ */
+int gptb200_attention_fwd(const void* q, const void* k, const void* v, int64_t stride_b,
+                          int64_t stride_h, int64_t stride_t, void* o, int64_t o_stride_b,
+                          int64_t o_stride_h, int64_t o_stride_t, float* lse, int64_t batch,
+                          int64_t heads, int64_t seq, int64_t head_dim, float softmax_scale,
+                          const void* rope_cos, const void* rope_sin, void* stream);
+
+size_t gptb200_attention_bwd_workspace_size(int64_t batch, int64_t heads, int64_t seq);
+
+/* Backward: dq, dk, dv are written (not accumulated) with the q/k/v strides;
+ * with rope, dq and dk are gradients with respect to the pre-rotation inputs.
+ * Replaces rig/kernels/tpu_flash_attention.py:479-575 (dQ) and :578-701 (dK/dV). */
+int gptb200_attention_bwd(const void* q, const void* k, const void* v, int64_t stride_b,
+                          int64_t stride_h, int64_t stride_t, const void* o, const void* dout,
+                          int64_t o_stride_b, int64_t o_stride_h, int64_t o_stride_t,
+                          const float* lse, void* dq, void* dk, void* dv, int64_t batch,
+                          int64_t heads, int64_t seq, int64_t head_dim, float softmax_scale,
+                          const void* rope_cos, const void* rope_sin, void* workspace,
+                          void* stream);
+
+/* ------------------------------------------------------------------ linear cross-entropy
+ * Tied-embedding cross entropy without materializing [n, vocab] logits:
+ * loss[i] = logsumexp_{v < v_semantic}(h_i · E_v) - h_i · E_{target_i}
+ * (+inf for a target outside [0, v_semantic)). hidden bf16 [n, d], embedding
+ * bf16 [v_storage, d], targets int32 [n]. Outputs: losses fp32 [n], lse fp32
+ * [n] (saved for the backward), mean_loss fp32 [1] = mean(losses).
+ * Replaces rig/kernels/linear_cross_entropy.py:115-179 and :349-368
+ * (`tiled_tied_cross_entropy` / `_losses`).
+ */
+size_t gptb200_lce_fwd_workspace_size(int64_t n, int64_t v_storage);
+int gptb200_lce_fwd(const void* hidden, const void* embedding, const int32_t* targets, int64_t n,
+                    int64_t d, int64_t v_storage, int64_t v_semantic, float* losses, float* lse,
+                    float* mean_loss, void* workspace, void* stream);
+
+/* Backward with per-token cotangent dlosses (fp32 [n]; for the mean this is
+ * 1/n everywhere). dhidden bf16 [n, d] is written; dembedding fp32
+ * [v_storage, d] is accumulated into (+=); rows >= v_semantic receive nothing.
+ * Targets outside [0, v_semantic) contribute no gradient.
+ * Replaces rig/kernels/linear_cross_entropy.py:220-302. */
+size_t gptb200_lce_bwd_workspace_size(int64_t n, int64_t v_storage);
+int gptb200_lce_bwd(const void* hidden, const void* embedding, const int32_t* targets,
+                    const float* lse, const float* dlosses, int64_t n, int64_t d,
+                    int64_t v_storage, int64_t v_semantic, void* dhidden, float* dembedding,
+                    void* workspace, void* stream);
+
+/* ------------------------------------------------------------------ reductions
+ * out[j] += sum_i x[i, j] for bf16 x [rows, n] (bias gradients), scaled by alpha. */
+int gptb200_colsum(const void* x, int64_t rows, int64_t n, float alpha, float* out, void* stream);
+
+/* ------------------------------------------------------------------ optimizer
+ * CompleteP AdamW over one flat fp32 parameter buffer, replacing
+ * recipes/reference/train.py:1362-1457 (`_apply_training_update` after the
+ * gradients: global grad norm, optional clip, m/v update, bias correction,
+ * per-tensor lr/eps/decay multipliers of :1274-1333, history row).
+ */
+typedef struct gptb200_tensor_group {
+  int64_t offset;        /* first element in the flat buffers */
+  int64_t size;          /* element count */
+  float lr_mult;
+  float eps_mult;
+  float wd_mult;
+  int32_t decay;         /* 1 when weight decay applies (train.py:1252-1271) */
+} gptb200_tensor_group;
+
+typedef struct gptb200_adamw_config {
+  float learning_rate;       /* base lr (config.learning_rate) */
+  float horizon_lr_scale;    /* sqrt(batch_multiplier / data_multiplier) */
+  float min_lr_ratio;
+  int32_t warmup_steps;
+  int32_t total_steps;
+  float beta1, beta2;        /* effective betas (train.py:1336-1345) */
+  float eps;                 /* config.adam_epsilon */
+  float eps_horizon_scale;   /* sqrt(data_multiplier / batch_multiplier) */
+  float weight_decay;
+  float wd_horizon_scale;    /* sqrt(batch_multiplier / data_multiplier) */
+  float grad_clip;           /* <= 0: disabled */
+  float grad_scale;          /* gradients are multiplied by this first (1.0) */
+} gptb200_adamw_config;
+
+/* Device scalars of the optimizer: step (int32, incremented by the update),
+ * plus the per-step values written for the history row. */
+size_t gptb200_adamw_workspace_size(int64_t n);
+
+/* One update. groups: DEVICE array of n_groups gptb200_tensor_group covering
+ * [0, n) in increasing offset order. step: device int32 (read, then +1).
+ * loss: device fp32 scalar (the step's mean loss) for the history row.
+ * history: device fp32 [total_steps, 3] rows (loss, lr, grad_norm); may be NULL.
+ * params_bf16: optional bf16 mirror of params written after the update. */
+int gptb200_adamw_step(float* params, float* m, float* v, const float* grads, int64_t n,
+                       const gptb200_tensor_group* groups, int32_t n_groups,
+                       const gptb200_adamw_config* cfg, int32_t* step, const float* loss,
+                       float* history, void* params_bf16, void* workspace, void* stream);
+
+/* fp32 -> bf16 copy of n elements (the compute-dtype cast of train.py's
+ * `weight.astype(dtype)`). */
+int gptb200_cast_bf16(const float* src, void* dst, int64_t n, void* stream);
+
+/* ------------------------------------------------------------------ data loader (host)
+ * Native core of rig/tokens.py:171-272 (`ShuffledEpochBatchStream`). All
+ * pointers in this section are HOST pointers; these functions run on the CPU.
+ */
+/* SplitMix64 avalanche of rig/tokens.py:127-133. */
+uint64_t gptb200_mix_uint64(uint64_t value);
+/* Keyed bounded Feistel permutation of rig/tokens.py:136-168. Returns the
+ * image of `value` in [0, size), or UINT64_MAX for value >= size. */
+uint64_t gptb200_permute_bounded(uint64_t value, uint64_t size, uint64_t key);
+/* Copies `rows` windows of seq_len+1 tokens for global ordinals
+ * first_ordinal.. into out (int32 [rows, seq_len+1]), given one epoch's plan:
+ * ordered_shards[i] / ordered_cumulative[i] (int64, n_shards entries) from
+ * rig/tokens.py:222-236, and the shard data pointers/lengths (uint16 tokens).
+ * All ordinals must belong to the epoch `epoch_ordinal_base / windows_per_epoch`
+ * whose key is epoch_key. Returns 0, or GPTB200_ERANGE if a token is >= vocab. */
+int gptb200_gather_windows(const uint16_t* const* shard_data, const int64_t* shard_lengths,
+                           const int64_t* ordered_shards, const int64_t* ordered_cumulative,
+                           int64_t n_shards, int64_t windows_per_epoch, uint64_t epoch_key,
+                           int64_t first_epoch_ordinal, int64_t rows, int64_t seq_len,
+                           int64_t vocab, int32_t* out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GPTB200_H_ */

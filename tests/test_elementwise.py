@@ -1,0 +1,88 @@
+"""Memory-bound kernels vs fp32 PyTorch restatements of rig/nn.py and train.py."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import reference_step as ref
+from rig_b200 import ops
+
+pytestmark = pytest.mark.gpu
+
+
+def _rel(x, y):
+    return ((x.float() - y.float()).norm() / y.float().norm()).item()
+
+
+@pytest.mark.parametrize("rows,d", [(1000, 768), (37, 256), (8, 2048), (5, 3072)])
+def test_rms_norm_fwd(cuda, rows, d):
+    x = torch.randn(rows, d).bfloat16()
+    s = (1 + 0.1 * torch.randn(d)).bfloat16()
+    y = torch.empty(rows, d, device=cuda, dtype=torch.bfloat16)
+    r = torch.empty(rows, device=cuda)
+    ops.rms_norm_fwd(x.to(cuda), s.to(cuda), y, r)
+    expect = ref.rms_norm(x, s)
+    assert _rel(y.cpu(), expect) < 5e-3
+    x32 = x.float()
+    assert torch.allclose(r.cpu(), torch.rsqrt((x32 * x32).mean(-1) + 1e-5), rtol=1e-5)
+
+
+@pytest.mark.parametrize("rows,d", [(1000, 768), (64, 256), (8, 2048)])
+def test_rms_norm_bwd(cuda, rows, d):
+    x = torch.randn(rows, d).bfloat16()
+    s = (1 + 0.1 * torch.randn(d)).bfloat16()
+    dy = torch.randn(rows, d).bfloat16()
+    dres = torch.randn(rows, d).bfloat16()
+    # autograd of the restatement, fp32 end to end
+    xx = x.float().requires_grad_(True)
+    ss = s.float().requires_grad_(True)
+    y = xx * torch.rsqrt((xx * xx).mean(-1, keepdim=True) + 1e-5) * ss
+    (y * dy.float()).sum().backward()
+    xd, sd, dyd = x.to(cuda), s.to(cuda), dy.to(cuda)
+    yy = torch.empty_like(xd)
+    r = torch.empty(rows, device=cuda)
+    ops.rms_norm_fwd(xd, sd, yy, r)
+    dx = dres.to(cuda).clone()
+    dscale = torch.zeros(d, device=cuda)
+    ops.rms_norm_bwd(xd, sd, r, dyd, dx, dx, dscale)
+    assert _rel(dx.cpu().float() - dres.float(), xx.grad) < 1e-2
+    assert _rel(dscale.cpu(), ss.grad) < 1e-2
+
+
+def test_embedding(cuda):
+    v, d, n = 1000, 256, 4096
+    table = torch.randn(v, d).bfloat16()
+    tok = torch.randint(0, v, (n,), dtype=torch.int32)
+    out = torch.empty(n, d, device=cuda, dtype=torch.bfloat16)
+    ops.embedding_fwd(tok.to(cuda), table.to(cuda), out)
+    assert torch.equal(out.cpu(), table[tok.long()])
+    dout = torch.randn(n, d).bfloat16()
+    dt = torch.zeros(v, d, device=cuda)
+    ops.embedding_bwd(tok.to(cuda), dout.to(cuda), dt)
+    expect = torch.zeros(v, d).index_add_(0, tok.long(), dout.float())
+    assert torch.allclose(dt.cpu(), expect, atol=1e-4)
+
+
+def test_rope_tables(cuda):
+    cos, sin = ops.rope_tables(1024, 64, cuda)
+    ec, es = ref.rope_tables(1024, 64)
+    # cos/sin are rounded to bf16 exactly like the restatement (one-ulp ties allowed)
+    assert (cos.cpu().float() - ec.float()).abs().max().item() <= 2 ** -8
+    assert (sin.cpu().float() - es.float()).abs().max().item() <= 2 ** -8
+    assert (cos.cpu() != ec).float().mean().item() < 1e-3
+
+
+@pytest.mark.parametrize("rows,n", [(131, 768), (4096, 2304), (10, 8)])
+def test_colsum(cuda, rows, n):
+    x = torch.randn(rows, n).bfloat16()
+    out = torch.full((n,), 1.0, device=cuda)
+    ops.colsum(x.to(cuda), out, alpha=0.5)
+    assert torch.allclose(out.cpu(), 1.0 + 0.5 * x.float().sum(0), atol=1e-3, rtol=1e-4)
+
+
+@pytest.mark.parametrize("n", [1, 7, 4096, 100003])
+def test_cast(cuda, n):
+    x = torch.randn(n)
+    y = torch.empty(n, device=cuda, dtype=torch.bfloat16)
+    ops.cast_bf16(x.to(cuda), y)
+    assert torch.equal(y.cpu(), x.bfloat16())

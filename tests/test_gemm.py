@@ -1,0 +1,103 @@
+"""tcgen05 GEMM vs a plain fp32 PyTorch reference, every operand layout and epilogue."""
+
+import pytest
+import torch
+
+from rig_b200 import _lib, ops
+
+pytestmark = pytest.mark.gpu
+
+
+def _operands(m, n, k, a_mn, b_mn, dev, seed=0):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    a = torch.randn(m, k, generator=g).to(dev).bfloat16()
+    b = torch.randn(n, k, generator=g).to(dev).bfloat16()
+    a_st = a.t().contiguous() if a_mn else a
+    b_st = b.t().contiguous() if b_mn else b
+    return a, b, a_st, b_st
+
+
+def _rel(x, ref):
+    return ((x.float() - ref).norm() / ref.norm()).item()
+
+
+@pytest.mark.parametrize("a_mn", [0, 1])
+@pytest.mark.parametrize("b_mn", [0, 1])
+@pytest.mark.parametrize("shape", [(128, 256, 64), (256, 512, 128), (1024, 768, 768),
+                                   (384, 264, 200), (136, 40, 24)])
+def test_layouts_bf16(cuda, a_mn, b_mn, shape):
+    m, n, k = shape
+    a, b, a_st, b_st = _operands(m, n, k, a_mn, b_mn, cuda)
+    c = torch.empty(m, n, device=cuda, dtype=torch.bfloat16)
+    ops.gemm(a_st, b_st, c, a_mn_major=bool(a_mn), b_mn_major=bool(b_mn), m=m, n=n, k=k)
+    ref = a.float() @ b.float().t()
+    assert _rel(c, ref) < 4e-3
+    assert ops.device_error() == 0
+
+
+def test_bias_alpha_residual(cuda):
+    m, n, k = 300, 768, 256
+    a, b, _, b_st = _operands(m, n, k, 0, 1, cuda, 1)
+    bias = torch.randn(n, device=cuda).bfloat16()
+    res = torch.randn(m, n, device=cuda).bfloat16()
+    c = torch.empty(m, n, device=cuda, dtype=torch.bfloat16)
+    ops.gemm(a, b_st, c, b_mn_major=True, m=m, n=n, k=k, bias=bias, alpha=0.25, residual=res)
+    t = (a.float() @ b.float().t()).bfloat16().float()
+    t = (t + bias.float()).bfloat16().float()
+    t = (0.25 * t).bfloat16().float()
+    ref = res.float() + t
+    assert _rel(c, ref) < 4e-3
+
+
+def test_gelu_and_dgelu(cuda):
+    m, n, k = 512, 1024, 256
+    a, b, _, b_st = _operands(m, n, k, 0, 1, cuda, 2)
+    bias = (0.1 * torch.randn(n, device=cuda)).bfloat16()
+    u = torch.empty(m, n, device=cuda, dtype=torch.bfloat16)
+    g = torch.empty_like(u)
+    ops.gemm(a, b_st, g, b_mn_major=True, m=m, n=n, k=k, kind=_lib.EPI_BIAS_GELU, bias=bias, aux=u)
+    u_ref = ((a.float() @ b.float().t()).bfloat16().float() + bias.float()).bfloat16().float()
+    assert _rel(u, u_ref) < 4e-3
+    g_ref = torch.nn.functional.gelu(u.float(), approximate="tanh")
+    assert _rel(g, g_ref) < 4e-3
+    # dgelu: C = bf16(alpha * dy @ w^T) * gelu'(u)
+    dy = torch.randn(m, 256, device=cuda).bfloat16()
+    w = torch.randn(n, 256, device=cuda).bfloat16()  # [N, K] K-major
+    du = torch.empty(m, n, device=cuda, dtype=torch.bfloat16)
+    ops.gemm(dy, w, du, m=m, n=n, k=256, kind=_lib.EPI_DGELU, alpha=0.5, aux=u)
+    x = u.float().requires_grad_(True)
+    gl = torch.nn.functional.gelu(x, approximate="tanh")
+    up = (0.5 * (dy.float() @ w.float().t())).bfloat16().float()
+    (gl * up).sum().backward()
+    assert _rel(du, x.grad) < 5e-3
+
+
+@pytest.mark.parametrize("k", [64, 4096, 20000])
+def test_f32_atomic_split_k(cuda, k):
+    m, n = 768, 2304
+    a, b, a_st, b_st = _operands(m, n, k, 1, 1, cuda, 3)
+    c = torch.ones(m, n, device=cuda)
+    ops.gemm(a_st, b_st, c, a_mn_major=True, b_mn_major=True, m=m, n=n, k=k,
+             kind=_lib.EPI_F32_ATOMIC, alpha=0.5)
+    ref = 1.0 + 0.5 * (a.float() @ b.float().t())
+    assert _rel(c, ref) < 1e-5
+
+
+def test_f32_store_and_accumulate(cuda):
+    m, n, k = 600, 768, 512
+    a, b, a_st, b_st = _operands(m, n, k, 1, 1, cuda, 4)
+    c = torch.full((m, n), 2.0, device=cuda)
+    ops.gemm(a_st, b_st, c, a_mn_major=True, b_mn_major=True, m=m, n=n, k=k, kind=_lib.EPI_F32,
+             accumulate=True)
+    ref = 2.0 + a.float() @ b.float().t()
+    assert _rel(c, ref) < 1e-5
+    ops.gemm(a_st, b_st, c, a_mn_major=True, b_mn_major=True, m=m, n=n, k=k, kind=_lib.EPI_F32)
+    assert _rel(c, ref - 2.0) < 1e-5
+
+
+def test_rejects_bad_arguments(cuda):
+    a = torch.zeros(64, 60, device=cuda, dtype=torch.bfloat16)  # lda % 8 != 0
+    b = torch.zeros(64, 60, device=cuda, dtype=torch.bfloat16)
+    c = torch.zeros(64, 64, device=cuda, dtype=torch.bfloat16)
+    with pytest.raises(_lib.GptB200Error):
+        ops.gemm(a, b, c, m=64, n=64, k=60)
