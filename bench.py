@@ -1,0 +1,314 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 GPT training step (BASELINE metric: train tokens/s and
+MFU of the 125M tier, bf16, seq 1024, global batch 128, at 1/2/4/8 GPUs).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+One process per GPU (torchrun for N > 1). A "step" is one full training step
+(forward, backward, gradient all-reduce, AdamW) over the rank's share of the
+128 x 1024-token global batch (strong scaling: the global batch is fixed).
+
+Printed by rank 0 as one JSON line:
+  value        whole-job tokens/s with the step's inputs already in HBM
+  e2e          the same through the public API with the batch copied from
+               pinned host memory and the loss read back every step
+  roofline     the GEMM kernel family (the dominant kernel) timed with CUDA
+               events around its launches in instrumented steps
+  cpu_baseline the CPU restatement of the reference step (oracle/) on this
+               host's cores, on a bounded sample (rank 0, N = 1 only)
+`--impl reference` times that CPU restatement alone as the reference arm (the
+reference itself is JAX, which this image does not have).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "gpt-speedrun-tpu_b200"))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "train tokens/sec + MFU, GPT-125M bf16 seq1024"
+UNIT = "tokens/s"
+NOMINAL_BF16_TFLOPS = 2250.0
+
+
+def flops_per_token(cfg) -> int:
+    """Reference MFU convention (docs/FLOPS.md:9-24 of the rig): 6 x matmul
+    parameters (incl. the tied head) + full-square attention 12*L*H*T*Dh."""
+
+    d, L = cfg.d_model, cfg.layers
+    return 6 * (L * 12 * d * d + cfg.vocab_size * d) + 12 * L * cfg.heads * cfg.seq_len * cfg.head_dim
+
+
+def measured_peaks() -> dict:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return {"hbm_gbs": data["hbm_gbs"], "bf16": data["bf16_tflops"],
+                "bf16_sustained": data["bf16_tflops_sustained"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16": 1590.0, "bf16_sustained": 1400.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples every 200 ms while running."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(gpu_index), f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.file, stderr=subprocess.DEVNULL)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        self.proc.wait(timeout=10)
+        self.file.flush()
+        rows = []
+        for line in pathlib.Path(self.file.name).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.file.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
+
+
+def make_stream(cfg, rank: int, world: int, steps: int, seed: int):
+    """Synthetic Zipf(1.1) tokens (seed 3) in an llm.c shard, read through the
+    shuffled-epoch stream like the reference trainer (stream seed = seed + 1)."""
+
+    from rig_b200.tokens import (ShardedTokens, ShuffledEpochBatchStream, load_token_file,
+                                 write_llmc_shard, zipf_tokens)
+
+    n_tokens = (steps + 2) * cfg.batch_size * (cfg.seq_len + 1)
+    path = pathlib.Path(tempfile.gettempdir()) / f"gptb200_zipf_s{seed}_{n_tokens}_r{rank}.bin"
+    if not path.exists():
+        write_llmc_shard(path, zipf_tokens(n_tokens, cfg.vocab_size, seed))
+    shard = np.ascontiguousarray(load_token_file(path, data_format="llmc"))
+    return ShuffledEpochBatchStream(ShardedTokens([shard]), global_batch_size=cfg.batch_size,
+                                    seq_len=cfg.seq_len, vocab_size=cfg.vocab_size, seed=seed + 1,
+                                    process_index=rank, process_count=world)
+
+
+def cpu_oracle_rate(cfg, tokens: int, steps: int, threads: int) -> tuple[float, str]:
+    """Tokens/s of the CPU restatement of the reference step on `tokens`-token
+    samples (one sequence each), `steps` timed steps after one warm-up."""
+
+    from oracle import reference_step as ref
+    from rig_b200.tokens import zipf_tokens
+
+    torch.set_num_threads(threads)
+    seqs = max(1, tokens // cfg.seq_len)
+    small = cfg.replace(batch_size=seqs)
+    params = ref.init_params(small, 3)
+    trainer = ref.OracleTrainer(small, params)
+    toks = zipf_tokens((steps + 1) * seqs * (cfg.seq_len + 1), cfg.vocab_size, 7).astype(np.int32)
+    w = toks.reshape(steps + 1, seqs, cfg.seq_len + 1)
+    trainer.train_step(w[0][:, :-1], w[0][:, 1:])
+    t0 = time.perf_counter()
+    for i in range(1, steps + 1):
+        trainer.train_step(w[i][:, :-1], w[i][:, 1:])
+    dt = time.perf_counter() - t0
+    sample = (f"{steps} step(s) of {seqs} x {cfg.seq_len} tokens of the {cfg.tier} step "
+              "(forward, backward, AdamW over all parameters)")
+    return steps * seqs * cfg.seq_len / dt, sample
+
+
+def run_reference(args, cfg, rank: int, world: int) -> None:
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    rate, sample = cpu_oracle_rate(cfg, cfg.seq_len, max(1, args.steps), threads)
+    line = {
+        "metric": METRIC, "value": rate, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1000.0 * cfg.seq_len / rate,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic Zipf(1.1) tokens", "impl": "reference",
+        "config": {"workload": f"{cfg.tier} training step, CPU restatement", "seq_len": cfg.seq_len},
+        "cpu_baseline": {"value": rate, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": rate, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "reference is JAX (not installable offline); its step is timed as the "
+                "oracle/ CPU restatement",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--config", default="baseline_125m")
+    ap.add_argument("--seed", type=int, default=3)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+
+    from rig_b200.config import load_config
+    from rig_b200.mesh import initialize_distributed_runtime
+
+    cfg = load_config(args.config)
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        run_reference(args, cfg, rank, int(os.environ.get("WORLD_SIZE", "1")))
+        return
+
+    import torch.distributed as dist
+
+    from rig_b200 import ops
+    from rig_b200.model import GPTTrainer, init_params
+
+    rank, world, local = initialize_distributed_runtime("nccl")
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    local_batch = cfg.batch_size // world
+    total_steps = args.warmup + 2 * args.steps + 1
+    stream = make_stream(cfg, rank, world, total_steps, args.seed)
+    batches = [stream.next_batch() for _ in range(total_steps)]
+    pinned = [(torch.from_numpy(x).pin_memory(), torch.from_numpy(y).pin_memory())
+              for x, y in batches]
+    dev_batches = [(x.to(device), y.to(device)) for x, y in pinned[: args.warmup + args.steps]]
+
+    trainer = GPTTrainer(cfg, local_batch, device, process_group=None, world_size=world,
+                         history_steps=max(cfg.steps, total_steps + 1))
+    trainer.load_params(init_params(cfg, args.seed))
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(ms: float) -> float:
+        if world == 1:
+            return ms
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for i in range(args.warmup):
+        trainer.train_step(*dev_batches[i])
+    barrier()
+
+    # ---- value: inputs resident in HBM
+    clocks = ClockSampler(local)
+    launches0 = ops.launch_count()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    start.record()
+    for i in range(args.steps):
+        trainer.train_step(*dev_batches[args.warmup + i])
+    end.record()
+    barrier()
+    launches = ops.launch_count() - launches0
+    clock_info = clocks.stop()
+    ms = max_over_ranks(start.elapsed_time(end))
+    global_tokens = cfg.batch_size * cfg.seq_len
+    value = global_tokens * args.steps / (ms / 1000.0)
+
+    # ---- e2e: H2D of each step's batch from pinned host memory + D2H of the loss
+    loss_host = torch.empty(args.steps, dtype=torch.float32).pin_memory()
+    off = args.warmup + args.steps
+    barrier()
+    start.record()
+    for i in range(args.steps):
+        x, y = pinned[off + i]
+        trainer.set_batch(x, y)
+        trainer.train_step()
+        loss_host[i : i + 1].copy_(trainer.loss, non_blocking=True)
+    end.record()
+    barrier()
+    ms_e2e = max_over_ranks(start.elapsed_time(end))
+    e2e_value = global_tokens * args.steps / (ms_e2e / 1000.0)
+    if not np.all(np.isfinite(loss_host.numpy())):
+        raise FloatingPointError(f"non-finite loss during the benchmark: {loss_host.tolist()}")
+
+    # ---- roofline of the dominant kernel family (tcgen05 GEMM), instrumented steps
+    peaks = measured_peaks()
+    ops.gemm_timer = []
+    gstart, gend = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    gstart.record()
+    trainer.train_step(*dev_batches[-1])
+    gend.record()
+    torch.cuda.synchronize()
+    timed = ops.gemm_timer
+    ops.gemm_timer = None
+    gemm_ms = sum(s.elapsed_time(e) for s, e, _ in timed)
+    gemm_flops = sum(f for _, _, f in timed)
+    step_ms_instr = gstart.elapsed_time(gend)
+    achieved = gemm_flops / (gemm_ms / 1000.0) / 1e12
+    roofline = {
+        "bound": "tensor", "kernel": "gemm_tc_kernel (tcgen05 GEMM, all launches of one step)",
+        "achieved": achieved, "peak": peaks["bf16_sustained"], "unit": "TFLOP/s",
+        "frac": achieved / peaks["bf16_sustained"],
+        "peak_source": f"{peaks['source']} sustained bf16 (kernel timed inside a long step)",
+        "traffic": None, "launches_per_step": len(timed), "share_of_step": gemm_ms / step_ms_instr,
+        "algorithmic_flops_per_step": gemm_flops,
+    }
+
+    fpt = flops_per_token(cfg)
+    mfu = value * fpt / (world * peaks["bf16"] * 1e12)
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: Zipf(s=1.1) token ids (seed 3) in an llm.c uint16 shard, read "
+                "through the shuffled-epoch stream; random-init weights (CompleteP init)",
+        "config": {"workload": f"{cfg.tier} training step (fwd+bwd+allreduce+AdamW)",
+                   "model": f"GPT {cfg.layers}L/{cfg.d_model}d/{cfg.heads}H tied vocab "
+                            f"{cfg.vocab_size}", "global_batch": cfg.batch_size,
+                   "seq_len": cfg.seq_len, "parallelism": f"dp{world}",
+                   "l2": "working set (activations ~40 GB/GPU at dp1) far larger than L2"},
+        "mfu": mfu, "mfu_peak_tflops": peaks["bf16"], "mfu_peak_source": peaks["source"],
+        "mfu_vs_nominal_2250": value * fpt / (world * NOMINAL_BF16_TFLOPS * 1e12),
+        "flops_per_token": fpt,
+        "e2e": {"value": e2e_value, "unit": UNIT,
+                "h2d_bytes_per_step": 2 * local_batch * cfg.seq_len * 4,
+                "d2h_bytes_per_step": 4, "ms_per_step": ms_e2e / args.steps},
+        "roofline": roofline,
+        "clocks": clock_info,
+        "gpu_launches": int(launches),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        rate, sample = cpu_oracle_rate(cfg, cfg.seq_len, 1, threads)
+        line["cpu_baseline"] = {"value": rate, "unit": UNIT, "cores": threads, "kind": "port",
+                                "sample": sample}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -2,8 +2,16 @@
 #include "common.cuh"
 #include "gemm.cuh"
 
+#include <atomic>
+
 namespace gptb200 {
 int attention_read_error(int clear);
+static std::atomic<uint64_t> g_launches{0};
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+}  // namespace gptb200
+
+extern "C" uint64_t gptb200_launch_count(void) {
+  return gptb200::g_launches.load(std::memory_order_relaxed);
 }
 
 extern "C" const char* gptb200_version(void) { return "gptb200 0.1.0 (sm_100a)"; }

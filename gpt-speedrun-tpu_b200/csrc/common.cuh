@@ -227,9 +227,15 @@ GPTB200_DEV float warp_max(float v) {
   return v;
 }
 
-// Host-side status helpers shared by the translation units.
+// Host-side status helpers shared by the translation units. Every kernel
+// launch is followed by GPTB200_CHECK_LAUNCH, which also counts it (the
+// count is what gptb200_launch_count() reports).
+namespace gptb200 {
+void count_launch();
+}
 #define GPTB200_CHECK_LAUNCH()                                   \
   do {                                                           \
     cudaError_t e_ = cudaGetLastError();                         \
     if (e_ != cudaSuccess) return -static_cast<int>(e_);         \
+    gptb200::count_launch();                                     \
   } while (0)

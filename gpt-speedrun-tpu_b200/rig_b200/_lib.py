@@ -74,6 +74,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "gptb200_version": (ctypes.c_char_p, []),
     "gptb200_status_string": (ctypes.c_char_p, [c_int]),
     "gptb200_device_error": (c_int, [c_int]),
+    "gptb200_launch_count": (ctypes.c_uint64, []),
     "gptb200_gemm": (
         c_int,
         [c_vp, c_int, c_i64, c_vp, c_int, c_i64, c_vp, c_i64, c_i64, c_i64, c_i64,

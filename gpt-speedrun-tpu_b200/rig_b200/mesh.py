@@ -72,12 +72,16 @@ class GradientReducer:
         )
 
     def finish(self, loss: torch.Tensor | None = None) -> None:
+        """Waits for every bucket; `loss` (this rank's mean) becomes the global mean."""
+
         if loss is not None:
             self.works.append(
-                dist.all_reduce(loss, op=dist.ReduceOp.AVG, group=self.group, async_op=True))
+                dist.all_reduce(loss, op=dist.ReduceOp.SUM, group=self.group, async_op=True))
         for w in self.works:
             w.wait()
         self.works.clear()
+        if loss is not None:
+            loss.div_(dist.get_world_size(self.group))
 
 
 def barrier() -> None:

@@ -75,12 +75,31 @@ def gemm(
         aux=_ptr(aux),
         ld_aux=0 if aux is None else _row_major(aux, "aux"),
     )
+    if gemm_timer is not None:
+        start = torch.cuda.Event(enable_timing=True)
+        start.record()
     call(
         "gptb200_gemm",
         a.data_ptr(), int(a_mn_major), lda, b.data_ptr(), int(b_mn_major), ldb,
         out.data_ptr(), ldc, m, n, k, ctypes.byref(epi), _stream(),
     )
+    if gemm_timer is not None:
+        end = torch.cuda.Event(enable_timing=True)
+        end.record()
+        gemm_timer.append((start, end, 2.0 * m * n * k))
     return out
+
+
+# When set to a list, every gemm() call appends (start_event, end_event, flops)
+# recorded on the launching stream; the benchmark uses it to time the GEMM
+# launches inside its measured steps.
+gemm_timer: list | None = None
+
+
+def launch_count() -> int:
+    """Kernels launched by libgptb200 in this process so far."""
+
+    return int(_lib.load().gptb200_launch_count())
 
 
 def matmul(x: torch.Tensor, w: torch.Tensor, *, bias=None, out=None, kind=_lib.EPI_BF16,

@@ -42,6 +42,11 @@ const char* gptb200_status_string(int status);
  * error, else GPTB200_EDEVICE. Synchronizes the device. */
 int gptb200_device_error(int clear);
 
+/* Number of kernels this library has launched in this process (all devices).
+ * Used by the benchmark to report how many native launches a step makes; no
+ * reference counterpart. */
+uint64_t gptb200_launch_count(void);
+
 /* ------------------------------------------------------------------ GEMM
  * C[M,N] = epilogue( sum_k A[m,k] * B[n,k] ), bf16 operands, fp32 accumulate
  * in tensor memory (tcgen05.mma, TMA-fed).
