@@ -169,6 +169,7 @@ def main() -> None:
     ap.add_argument("--config", default="baseline_125m")
     ap.add_argument("--seed", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--eager", action="store_true", help="no CUDA graph replay")
     args = ap.parse_args()
 
     from rig_b200.config import load_config
@@ -217,6 +218,8 @@ def main() -> None:
 
     for i in range(args.warmup):
         trainer.train_step(*dev_batches[i])
+        if i == 0 and world == 1 and not args.eager:
+            trainer.capture()  # after one eager step; replays the same launches
     barrier()
 
     # ---- value: inputs resident in HBM
@@ -230,6 +233,8 @@ def main() -> None:
     end.record()
     barrier()
     launches = ops.launch_count() - launches0
+    if trainer.graph is not None:  # replays do not pass through the host launch counter
+        launches += trainer.graph_launches * args.steps
     clock_info = clocks.stop()
     ms = max_over_ranks(start.elapsed_time(end))
     global_tokens = cfg.batch_size * cfg.seq_len
@@ -254,6 +259,7 @@ def main() -> None:
 
     # ---- roofline of the dominant kernel family (tcgen05 GEMM), instrumented steps
     peaks = measured_peaks()
+    graph, trainer.graph = trainer.graph, None  # instrumented step runs eagerly
     ops.gemm_timer = []
     gstart, gend = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     gstart.record()
@@ -262,6 +268,7 @@ def main() -> None:
     torch.cuda.synchronize()
     timed = ops.gemm_timer
     ops.gemm_timer = None
+    trainer.graph = graph
     gemm_ms = sum(s.elapsed_time(e) for s, e, _ in timed)
     gemm_flops = sum(f for _, _, f in timed)
     step_ms_instr = gstart.elapsed_time(gend)

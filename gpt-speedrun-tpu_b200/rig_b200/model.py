@@ -396,11 +396,43 @@ class GPTTrainer:
                        self.adam_cfg, self.step_dev, self.loss, self.history, self.params_bf16,
                        self.adam_ws)
 
+    def capture(self) -> None:
+        """Records one whole step (forward, backward, AdamW) as a CUDA graph.
+
+        The step is static-shaped and allocates nothing, so after one eager
+        warm-up step (which also sets every kernel's shared-memory attribute)
+        the graph replays the identical launch sequence; the batch is read from
+        `self.tokens` / `self.targets` and the step counter lives on the device.
+        Single-process only: with data parallelism the step runs eagerly.
+        """
+
+        if self.world_size != 1:
+            raise ValueError("graph capture is used for the single-GPU step only")
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        graph = torch.cuda.CUDAGraph()
+        before = ops.launch_count()
+        with torch.cuda.stream(side):
+            with torch.cuda.graph(graph, stream=side):
+                self._eager_step()
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        self.graph = graph
+        self.graph_launches = ops.launch_count() - before
+
+    graph: "torch.cuda.CUDAGraph | None" = None
+    graph_launches: int = 0  # libgptb200 kernels inside one replay
+
     def train_step(self, x: torch.Tensor | None = None, y: torch.Tensor | None = None) -> None:
         """One full step: forward, backward, (all-reduce), AdamW. Asynchronous."""
 
         if x is not None:
             self.set_batch(x, y)
+        if self.graph is not None:
+            self.graph.replay()
+            return
+        self._eager_step()
+
+    def _eager_step(self) -> None:
         self.forward()
         if self.world_size > 1:
             from .mesh import GradientReducer
