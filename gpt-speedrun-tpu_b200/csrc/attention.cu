@@ -1,21 +1,32 @@
-// Causal flash attention (head_dim 64) with RoPE applied on the Q/K loads.
+// Causal flash attention (head_dim 64) on the Blackwell tensor cores.
 //
-// Forward: one CTA per (128-query block, batch*head); 8 warps x 16 query rows.
-// K/V tiles of 64 keys stream through double-buffered, XOR-swizzled shared
-// memory with cp.async; RoPE rotates the Q tile and every K tile in shared
-// memory right after arrival (interleaved pairs, bf16 cos/sin tables). Scores,
-// online softmax (fp32, base-2 exponent) and P·V (bf16 P) stay in registers.
-// Output O and the natural-log LSE per row are written for the backward.
-//
-// Backward: delta = rowsum(dO ∘ O); a dK/dV kernel (one CTA per 64-key block,
-// looping over the query blocks at or below the diagonal) and a dQ kernel (one
-// CTA per 64-query block, looping over key blocks up to the diagonal) recompute
-// P from the LSE, so no atomics are needed. Gradients of rotated q/k are
-// rotated back (transpose of the RoPE rotation) before the bf16 store.
-//
-// The tensor-core instructions are warp-level mma.sync m16n8k16 (bf16 in,
-// fp32 accumulate). Semantics: rig/kernels/tpu_flash_attention.py:171-207
-// (reference_causal_attention) and rig/nn.py:36-52 (apply_rotary).
+// Forward (attn_fwd_tc): one CTA per (128-query tile, batch*head), 6 warps:
+//   warp 0  TMA: the Q tile once, then 128-key K/V tiles into a 2-stage ring
+//           (4-D tensor maps over (e, t, h, b), so any [b, t, h, e] strides work
+//           and rows past the sequence end arrive as zeros);
+//   warp 1  one thread issues tcgen05.mma: S = Q·Kᵀ (128x128, fp32 in TMEM),
+//           then O += P·V (128x64, fp32 in TMEM, V as an MN-major operand);
+//   warps 2-5 softmax: thread r owns query row r (TMEM lane r). It copies its
+//           S row to registers (freeing TMEM for the next S while it computes),
+//           applies scale·log2(e) and the causal mask, and keeps a running max
+//           that is only raised when the row max grows by more than 2^8, in
+//           which case O is rescaled in TMEM (tcgen05.ld/st) — otherwise the
+//           stale max is exact because O and the row sum use the same one.
+//           P = exp2(s - m) is written as bf16 into a 128-byte-swizzled K-major
+//           shared tile that the next P·V MMA reads.
+//   Two CTAs fit on an SM (112 KB shared memory, 256 TMEM columns each).
+// Backward (attn_bwd_tc): one CTA per (128-key tile, batch*head), looping over
+// query tiles from the diagonal down. Per query tile the MMA thread computes
+// Sᵀ = K·Qᵀ and dPᵀ = V·dOᵀ into TMEM; the softmax warps (thread = key row)
+// form Pᵀ = exp2(Sᵀ·c - lse) and dSᵀ = Pᵀ∘(dPᵀ - δ) in 32-column chunks,
+// writing both as bf16 swizzled tiles; then dQ = dS·K (dSᵀ read as an
+// MN-major A operand), dV += Pᵀ·dO and dK += dSᵀ·Q run on the tensor cores.
+// dQ is read back from TMEM and added to an fp32 accumulator with vector
+// atomics; dK, dV leave TMEM once at the end. q and k arrive already rotated
+// (RoPE runs in the QKV projection epilogue); with RoPE tables the backward
+// rotates dq and dk back so they are gradients of the unrotated inputs.
+// Every mbarrier wait is bounded (common.cuh). Semantics follow
+// rig/kernels/tpu_flash_attention.py:171-207 (fp32 statistics, bf16 P).
 #include <algorithm>
 
 #include "common.cuh"
@@ -25,585 +36,614 @@ namespace gptb200 {
 static __device__ int g_attn_error;
 
 constexpr int HD = 64;
+constexpr int TILE = 128;          // queries per forward CTA / keys per backward CTA
+constexpr int TILE_BYTES = TILE * 128;  // 128 rows x 64 bf16 (128 B)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
+constexpr int kThreads = 192;
 
-struct AttnArgs {
-  const bf16* q;
-  const bf16* k;
-  const bf16* v;
-  int64_t sb, sh, st;
-  const bf16* o;
-  bf16* o_out;
-  const bf16* dout;
-  int64_t osb, osh, ost;
-  float* lse_out;
-  const float* lse;
-  const float* delta;
-  bf16* dq;
-  bf16* dk;
-  bf16* dv;
+struct AttnParams {
   int B, H, T;
   float scale;
-  const bf16* rcos;
+  // output / saved tensors
+  bf16* o;
+  int64_t osb, osh, ost;
+  float* lse;          // [B, H, T], natural log
+  const bf16* dout;
+  const float* delta;  // [B, H, T]
+  float* dq_acc;       // [B, H, T, 64] fp32
+  bf16* dk;
+  bf16* dv;
+  int64_t sb, sh, st;  // q/k/v (and dq/dk/dv) strides
+  const bf16* rcos;    // RoPE tables [T, 32] or null
   const bf16* rsin;
 };
 
-// ------------------------------------------------------------------ helpers
-__device__ __forceinline__ uint32_t swz(int row, int chunk) {
+__device__ __forceinline__ uint32_t swz128(int row, int chunk) {
   return (uint32_t)(row * 128 + (((chunk ^ (row & 7)) & 7) << 4));
 }
 
-__device__ __forceinline__ void cp_async16(uint32_t saddr, const void* g) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr), "l"(g) : "memory");
-}
-__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
-                                        uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
-                                          uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-
-__device__ __forceinline__ void mma16816(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
-      "{%8,%9}, {%0,%1,%2,%3};"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-// Asynchronously copies `rows` x 64 bf16 rows (row r at base + (r0+r)*stride)
-// into a swizzled tile; rows at or beyond T are zero-filled.
-__device__ __forceinline__ void load_tile_async(uint8_t* s, const bf16* base, int64_t stride, int r0,
-                                                int rows, int T, int tid, int nthreads) {
-  const uint32_t sa = smem_u32(s);
-  for (int i = tid; i < rows * 8; i += nthreads) {
-    int r = i >> 3, c = i & 7;
-    if (r0 + r < T) {
-      cp_async16(sa + swz(r, c), base + (int64_t)(r0 + r) * stride + c * 8);
-    } else {
-      *reinterpret_cast<uint4*>(s + swz(r, c)) = make_uint4(0, 0, 0, 0);
-    }
-  }
-}
-
-// Rotates a swizzled tile in place: pair i of row r at position r0+r.
-__device__ __forceinline__ void rope_tile(uint8_t* s, const bf16* rcos, const bf16* rsin, int r0,
-                                          int rows, int T, int tid, int nthreads) {
-  for (int i = tid; i < rows * 8; i += nthreads) {
-    int r = i >> 3, c = i & 7;
-    int t = r0 + r;
-    if (t >= T) continue;
-    uint4* p = reinterpret_cast<uint4*>(s + swz(r, c));
-    uint4 q = *p;
-    uint32_t* w = &q.x;
-    const bf16* cs = rcos + (int64_t)t * (HD / 2) + c * 4;
-    const bf16* sn = rsin + (int64_t)t * (HD / 2) + c * 4;
+// Rotates 4 interleaved pairs (one 16-byte chunk holding elements 8c..8c+7 of
+// position t) by the transpose of the RoPE rotation.
+__device__ __forceinline__ void rope_back(float* v, const bf16* rcos, const bf16* rsin, int t,
+                                          int c) {
+  const bf16* cs = rcos + (int64_t)t * (HD / 2) + c * 4;
+  const bf16* sn = rsin + (int64_t)t * (HD / 2) + c * 4;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      float e, o;
-      unpack_bf16x2(w[j], e, o);
-      float cv = __bfloat162float(cs[j]), sv = __bfloat162float(sn[j]);
-      w[j] = pack_bf16x2(e * cv - o * sv, e * sv + o * cv);
-    }
-    *p = q;
-  }
-}
-
-// Loads the A fragments (16 rows x 64 dims, 4 k-steps) of rows [row0, row0+16)
-// of a swizzled 64-wide tile.
-__device__ __forceinline__ void load_a_frags(const uint8_t* s, int row0, int lane, uint32_t (*a)[4]) {
-  const uint32_t sa = smem_u32(s);
-#pragma unroll
-  for (int kk = 0; kk < 4; ++kk) {
-    int r = row0 + (lane & 7) + 8 * ((lane >> 3) & 1);
-    int c = kk * 2 + (lane >> 4);
-    ldsm_x4(sa + swz(r, c), a[kk][0], a[kk][1], a[kk][2], a[kk][3]);
-  }
-}
-
-// acc[16 x 64] (8 n-tiles) += A[16 x 64] · Tile^T, where Tile is 64 rows
-// (the n dimension) x 64 dims (the k dimension), non-transposed ldmatrix.
-__device__ __forceinline__ void mma_a_tileT(float (*acc)[4], const uint32_t (*a)[4], const uint8_t* s,
-                                            int lane) {
-  const uint32_t sa = smem_u32(s);
-#pragma unroll
-  for (int kk = 0; kk < 4; ++kk) {
-#pragma unroll
-    for (int np = 0; np < 4; ++np) {
-      uint32_t b0, b1, b2, b3;
-      int r = np * 16 + (lane & 7) + 8 * (lane >> 4);
-      int c = kk * 2 + ((lane >> 3) & 1);
-      ldsm_x4(sa + swz(r, c), b0, b1, b2, b3);
-      mma16816(acc[2 * np], a[kk], b0, b1);
-      mma16816(acc[2 * np + 1], a[kk], b2, b3);
-    }
-  }
-}
-
-// acc[16 x 64 dims] += P[16 x 64 rows-of-tile] · Tile, where Tile is 64 rows
-// (the k dimension) x 64 dims (the n dimension), transposed ldmatrix. P is
-// given as fp32 accumulator fragments (8 n-tiles) and rounded to bf16 here.
-__device__ __forceinline__ void mma_p_tile(float (*acc)[4], const float (*p)[4], const uint8_t* s,
-                                           int lane) {
-  const uint32_t sa = smem_u32(s);
-#pragma unroll
-  for (int kk = 0; kk < 4; ++kk) {
-    uint32_t a[4];
-    a[0] = pack_bf16x2(p[2 * kk][0], p[2 * kk][1]);
-    a[1] = pack_bf16x2(p[2 * kk][2], p[2 * kk][3]);
-    a[2] = pack_bf16x2(p[2 * kk + 1][0], p[2 * kk + 1][1]);
-    a[3] = pack_bf16x2(p[2 * kk + 1][2], p[2 * kk + 1][3]);
-#pragma unroll
-    for (int np = 0; np < 4; ++np) {
-      uint32_t b0, b1, b2, b3;
-      int r = kk * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);
-      int c = np * 2 + (lane >> 4);
-      ldsm_x4_t(sa + swz(r, c), b0, b1, b2, b3);
-      mma16816(acc[2 * np], a, b0, b1);
-      mma16816(acc[2 * np + 1], a, b2, b3);
-    }
-  }
-}
-
-// Writes a warp's 16 x 64 fp32 accumulator (scaled) as bf16 rows into a
-// swizzled smem tile, optionally rotating pairs back (inverse RoPE) for
-// positions pos0 + row.
-__device__ __forceinline__ void stage_rows(uint8_t* s, int row0, const float (*acc)[4], float mul,
-                                           int lane) {
-#pragma unroll
-  for (int nt = 0; nt < 8; ++nt) {
-    int col = nt * 8 + (lane & 3) * 2;
-    int r = row0 + (lane >> 2);
-    uint32_t off0 = swz(r, col >> 3) + (col & 7) * 2;
-    uint32_t off1 = swz(r + 8, col >> 3) + (col & 7) * 2;
-    *reinterpret_cast<uint32_t*>(s + off0) = pack_bf16x2(acc[nt][0] * mul, acc[nt][1] * mul);
-    *reinterpret_cast<uint32_t*>(s + off1) = pack_bf16x2(acc[nt][2] * mul, acc[nt][3] * mul);
-  }
-}
-
-// Copies `rows` swizzled smem rows to global (row r -> base + (r0+r)*stride),
-// skipping rows >= T; with rcos != NULL applies the transpose RoPE rotation
-// (d_even = g_e*c + g_o*s, d_odd = -g_e*s + g_o*c) on the way out.
-__device__ __forceinline__ void store_tile(const uint8_t* s, bf16* base, int64_t stride, int r0,
-                                           int rows, int T, const bf16* rcos, const bf16* rsin,
-                                           int tid, int nthreads) {
-  for (int i = tid; i < rows * 8; i += nthreads) {
-    int r = i >> 3, c = i & 7;
-    int t = r0 + r;
-    if (t >= T) continue;
-    uint4 q = *reinterpret_cast<const uint4*>(s + swz(r, c));
-    if (rcos) {
-      uint32_t* w = &q.x;
-      const bf16* cs = rcos + (int64_t)t * (HD / 2) + c * 4;
-      const bf16* sn = rsin + (int64_t)t * (HD / 2) + c * 4;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        float ge, go;
-        unpack_bf16x2(w[j], ge, go);
-        float cv = __bfloat162float(cs[j]), sv = __bfloat162float(sn[j]);
-        w[j] = pack_bf16x2(ge * cv + go * sv, -ge * sv + go * cv);
-      }
-    }
-    *reinterpret_cast<uint4*>(base + (int64_t)t * stride + c * 8) = q;
+  for (int j = 0; j < 4; ++j) {
+    float cv = __bfloat162float(cs[j]), sv = __bfloat162float(sn[j]);
+    float ge = v[2 * j], go = v[2 * j + 1];
+    v[2 * j] = ge * cv + go * sv;
+    v[2 * j + 1] = -ge * sv + go * cv;
   }
 }
 
 // ------------------------------------------------------------------ forward
-constexpr int FWD_BR = 128, FWD_BC = 64, FWD_THREADS = 256;
-constexpr int TILE_BYTES = 64 * 128;  // 64 rows x 64 bf16
+struct FwdSmem {
+  static constexpr int Q = 0;
+  static constexpr int K = Q + TILE_BYTES;        // 2 stages
+  static constexpr int V = K + 2 * TILE_BYTES;    // 2 stages
+  static constexpr int P = V + 2 * TILE_BYTES;    // 2 blocks of 64 keys
+  static constexpr int BAR = P + 2 * TILE_BYTES;
+  static constexpr int TOTAL = BAR + 256 + 1024;
+};
 
-__global__ void __launch_bounds__(FWD_THREADS, 2) attn_fwd_kernel(const AttnArgs a) {
-  extern __shared__ __align__(128) uint8_t sm[];
-  uint8_t* sQ = sm;                        // 128 rows
-  uint8_t* sK = sm + 2 * TILE_BYTES;       // 2 buffers
-  uint8_t* sV = sK + 2 * TILE_BYTES;       // 2 buffers
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int nqb = (a.T + FWD_BR - 1) / FWD_BR;
-  const int qb = nqb - 1 - blockIdx.x;  // heaviest blocks first
+__global__ void __launch_bounds__(kThreads, 2)
+    attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                           ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + FwdSmem::BAR);
+  uint64_t* q_full = bars + 0;
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;
+  uint64_t* s_free = bars + 6;
+  uint64_t* p_full = bars + 7;
+  uint64_t* pv_done = bars + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nqt = (p.T + TILE - 1) / TILE;
+  const int qt = nqt - 1 - (int)blockIdx.x;  // heaviest tiles first
   const int bh = blockIdx.y;
-  const int b = bh / a.H, h = bh - b * a.H;
-  const int q0 = qb * FWD_BR;
-  const bf16* Q = a.q + b * a.sb + h * a.sh;
-  const bf16* K = a.k + b * a.sb + h * a.sh;
-  const bf16* V = a.v + b * a.sb + h * a.sh;
+  const int b = bh / p.H, h = bh - b * p.H;
+  const int q0 = qt * TILE;
+  const int nkv = qt + 1;
+  int* err = &g_attn_error;
 
-  load_tile_async(sQ, Q, a.st, q0, FWD_BR, a.T, tid, FWD_THREADS);
-  cp_commit();
-  const int kv_end = min(a.T, q0 + FWD_BR);
-  const int ntiles = (kv_end + FWD_BC - 1) / FWD_BC;
-  load_tile_async(sK, K, a.st, 0, FWD_BC, a.T, tid, FWD_THREADS);
-  load_tile_async(sV, V, a.st, 0, FWD_BC, a.T, tid, FWD_THREADS);
-  cp_commit();
-  cp_wait<1>();
-  __syncthreads();
-  if (a.rcos) {
-    rope_tile(sQ, a.rcos, a.rsin, q0, FWD_BR, a.T, tid, FWD_THREADS);
-    __syncthreads();
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(s_free, 4);
+    mbar_init(p_full, 4);
+    mbar_init(pv_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
   }
-  uint32_t qf[4][4];
-  load_a_frags(sQ, warp * 16, lane, qf);
+  if (warp == 1) tmem_alloc(tmem_slot, 256);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem, tO = tmem + 128;
 
-  float o[8][4];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-  const float sl2 = a.scale * kLog2e;
-  const int row_a = q0 + warp * 16 + (lane >> 2);
-  const int row_b = row_a + 8;
-
-  for (int j = 0; j < ntiles; ++j) {
-    const int buf = j & 1;
-    if (j + 1 < ntiles) {
-      load_tile_async(sK + (buf ^ 1) * TILE_BYTES, K, a.st, (j + 1) * FWD_BC, FWD_BC, a.T, tid,
-                      FWD_THREADS);
-      load_tile_async(sV + (buf ^ 1) * TILE_BYTES, V, a.st, (j + 1) * FWD_BC, FWD_BC, a.T, tid,
-                      FWD_THREADS);
-      cp_commit();
-      cp_wait<1>();
-    } else {
-      cp_wait<0>();
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(q_full, TILE_BYTES);
+      tma_load_4d(sm + FwdSmem::Q, &tmQ, q_full, 0, q0, h, b);
+      for (int j = 0; j < nkv; ++j) {
+        const int s = j & 1;
+        if (!mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1, abort_flag, err)) break;
+        mbar_arrive_expect_tx(&kv_full[s], 2 * TILE_BYTES);
+        tma_load_4d(sm + FwdSmem::K + s * TILE_BYTES, &tmK, &kv_full[s], 0, j * TILE, h, b);
+        tma_load_4d(sm + FwdSmem::V + s * TILE_BYTES, &tmV, &kv_full[s], 0, j * TILE, h, b);
+      }
     }
-    __syncthreads();
-    uint8_t* kt = sK + buf * TILE_BYTES;
-    uint8_t* vt = sV + buf * TILE_BYTES;
-    if (a.rcos) {
-      rope_tile(kt, a.rcos, a.rsin, j * FWD_BC, FWD_BC, a.T, tid, FWD_THREADS);
-      __syncthreads();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idS = umma_idesc_bf16(128, 128, 0, 0);
+      constexpr uint32_t idO = umma_idesc_bf16(128, 64, 0, 1);
+      const uint32_t sQ = smem_u32(sm + FwdSmem::Q);
+      const uint32_t sP = smem_u32(sm + FwdSmem::P);
+      bool ok = mbar_wait(q_full, 0, abort_flag, err);
+      for (int j = 0; ok && j < nkv; ++j) {
+        const int s = j & 1;
+        if (!mbar_wait(&kv_full[s], (j >> 1) & 1, abort_flag, err)) break;
+        if (j > 0 && !mbar_wait(s_free, (j - 1) & 1, abort_flag, err)) break;
+        tc_fence_after();
+        const uint32_t sK = smem_u32(sm + FwdSmem::K + s * TILE_BYTES);
+        const uint32_t sV = smem_u32(sm + FwdSmem::V + s * TILE_BYTES);
+#pragma unroll
+        for (int k = 0; k < HD / 16; ++k)
+          umma_bf16(tS, umma_smem_desc(sQ + k * 32, 16, 1024), umma_smem_desc(sK + k * 32, 16, 1024),
+                    idS, k > 0);
+        umma_commit(s_full);
+        if (!mbar_wait(p_full, j & 1, abort_flag, err)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < TILE / 16; ++k)
+          umma_bf16(tO, umma_smem_desc(sP + (k >> 2) * TILE_BYTES + (k & 3) * 32, 16, 1024),
+                    umma_smem_desc(sV + k * 2048, TILE_BYTES, 1024), idO, (j > 0 || k > 0));
+        umma_commit(pv_done);
+        umma_commit(&kv_empty[s]);
+      }
     }
-    const int k0 = j * FWD_BC;
-    if (k0 <= q0 + warp * 16 + 15) {  // the warp sees at least one key of this tile
-      float s[8][4];
+  } else {
+    // softmax warps: thread owns row r of the tile (TMEM lane r)
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;
+    const int qrow = q0 + r;
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const float c = p.scale * kLog2e;
+    float m_used = -INFINITY, l = 0.f;
+    uint8_t* sP = sm + FwdSmem::P;
+    bool ok = true;
+    for (int j = 0; j < nkv && ok; ++j) {
+      if (!mbar_wait(s_full, j & 1, abort_flag, err)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float s[TILE];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
-      mma_a_tileT(s, qf, kt, lane);
-      const bool diag = k0 + FWD_BC - 1 > q0 + warp * 16;
-      float mx0 = -INFINITY, mx1 = -INFINITY;
+      for (int cc = 0; cc < TILE / 32; ++cc) tmem_ld32(tS + lane_off + cc * 32, s + cc * 32);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(s_free);
+      const bool diag = (j == qt);
+      float mx = -INFINITY;
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          int key = k0 + nt * 8 + (lane & 3) * 2 + e;
-          float va = s[nt][e] * sl2, vb = s[nt][2 + e] * sl2;
-          if (diag) {
-            if (key > row_a) va = -INFINITY;
-            if (key > row_b) vb = -INFINITY;
+      for (int i = 0; i < TILE; ++i) {
+        float v = s[i] * c;
+        if (diag && i > r) v = -INFINITY;
+        s[i] = v;
+        mx = fmaxf(mx, v);
+      }
+      bool waited_pv = false;
+      if (mx > m_used + 8.0f) {
+        const float m_new = mx;
+        if (j > 0) {
+          const float alpha = ex2(m_used - m_new);
+          l *= alpha;
+          if (!mbar_wait(pv_done, (j - 1) & 1, abort_flag, err)) {
+            ok = false;
+            break;
           }
-          s[nt][e] = va;
-          s[nt][2 + e] = vb;
-          mx0 = fmaxf(mx0, va);
-          mx1 = fmaxf(mx1, vb);
+          waited_pv = true;
+          tc_fence_after();
+          float o[32];
+#pragma unroll
+          for (int cc = 0; cc < HD / 32; ++cc) {
+            tmem_ld32(tO + lane_off + cc * 32, o);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] *= alpha;
+            tmem_st32(tO + lane_off + cc * 32, o);
+          }
+        }
+        m_used = m_new;
+      }
+      float sum = 0.f;
+#pragma unroll
+      for (int i = 0; i < TILE; ++i) {
+        s[i] = ex2(s[i] - m_used);
+        sum += s[i];
+      }
+      l += sum;
+      // P_{j-1} must have been consumed by its P·V MMA before P_j overwrites it.
+      if (j > 0 && !waited_pv) {
+        if (!mbar_wait(pv_done, (j - 1) & 1, abort_flag, err)) {
+          ok = false;
+          break;
         }
       }
-      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-      const float nm0 = fmaxf(m0, mx0), nm1 = fmaxf(m1, mx1);
-      const float c0 = (nm0 == -INFINITY) ? 0.f : nm0;
-      const float c1 = (nm1 == -INFINITY) ? 0.f : nm1;
-      const float al0 = exp2f(m0 - c0), al1 = exp2f(m1 - c1);
-      float rs0 = 0.f, rs1 = 0.f;
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
-        s[nt][0] = exp2f(s[nt][0] - c0);
-        s[nt][1] = exp2f(s[nt][1] - c0);
-        s[nt][2] = exp2f(s[nt][2] - c1);
-        s[nt][3] = exp2f(s[nt][3] - c1);
-        rs0 += s[nt][0] + s[nt][1];
-        rs1 += s[nt][2] + s[nt][3];
-      }
-      l0 = l0 * al0 + rs0;
-      l1 = l1 * al1 + rs1;
-      m0 = nm0;
-      m1 = nm1;
+      for (int blk = 0; blk < 2; ++blk) {
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
-        o[nt][0] *= al0;
-        o[nt][1] *= al0;
-        o[nt][2] *= al1;
-        o[nt][3] *= al1;
+        for (int ch = 0; ch < 8; ++ch) {
+          const float* v = s + blk * 64 + ch * 8;
+          uint4 q;
+          q.x = pack_bf16x2(v[0], v[1]);
+          q.y = pack_bf16x2(v[2], v[3]);
+          q.z = pack_bf16x2(v[4], v[5]);
+          q.w = pack_bf16x2(v[6], v[7]);
+          *reinterpret_cast<uint4*>(sP + blk * TILE_BYTES + swz128(r, ch)) = q;
+        }
       }
-      mma_p_tile(o, s, vt, lane);
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
     }
-    __syncthreads();
-  }
-  // Finish: row sums across the quad, normalize, LSE.
-  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
-  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
-  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
-  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
-  const float inv0 = 1.f / l0, inv1 = 1.f / l1;
+    if (ok && mbar_wait(pv_done, (nkv - 1) & 1, abort_flag, err)) {
+      tc_fence_after();
+      const float inv = 1.f / l;
+      float o[32];
+      bf16* orow = p.o + b * p.osb + h * p.osh + (int64_t)qrow * p.ost;
 #pragma unroll
-  for (int nt = 0; nt < 8; ++nt) {
-    o[nt][0] *= inv0;
-    o[nt][1] *= inv0;
-    o[nt][2] *= inv1;
-    o[nt][3] *= inv1;
+      for (int cc = 0; cc < HD / 32; ++cc) {
+        tmem_ld32(tO + lane_off + cc * 32, o);
+        if (qrow < p.T) {
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            uint4 q;
+            q.x = pack_bf16x2(o[8 * g] * inv, o[8 * g + 1] * inv);
+            q.y = pack_bf16x2(o[8 * g + 2] * inv, o[8 * g + 3] * inv);
+            q.z = pack_bf16x2(o[8 * g + 4] * inv, o[8 * g + 5] * inv);
+            q.w = pack_bf16x2(o[8 * g + 6] * inv, o[8 * g + 7] * inv);
+            *reinterpret_cast<uint4*>(orow + cc * 32 + 8 * g) = q;
+          }
+        }
+      }
+      if (qrow < p.T) p.lse[(int64_t)bh * p.T + qrow] = (m_used + __log2f(l)) * kLn2;
+    }
   }
-  if ((lane & 3) == 0) {
-    float* L = a.lse_out + (int64_t)bh * a.T;
-    if (row_a < a.T) L[row_a] = (m0 + log2f(l0)) * kLn2;
-    if (row_b < a.T) L[row_b] = (m1 + log2f(l1)) * kLn2;
-  }
-  // Stage O through shared memory (the Q tile is no longer needed).
-  stage_rows(sQ, warp * 16, o, 1.f, lane);
+  tc_fence_before();
   __syncthreads();
-  store_tile(sQ, a.o_out + b * a.osb + h * a.osh, a.ost, q0, FWD_BR, a.T, nullptr, nullptr, tid,
-             FWD_THREADS);
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
 }
 
 // ------------------------------------------------------------------ backward
-__global__ void attn_delta_kernel(const AttnArgs a) {
-  // One warp per row: delta = sum_e dO * O (fp32).
-  const int64_t rows = (int64_t)a.B * a.H * a.T;
+struct BwdSmem {
+  static constexpr int K = 0;
+  static constexpr int V = K + TILE_BYTES;
+  static constexpr int Q = V + TILE_BYTES;       // 2 stages
+  static constexpr int DO = Q + 2 * TILE_BYTES;  // 2 stages
+  static constexpr int PT = DO + 2 * TILE_BYTES; // 2 blocks of 64 queries
+  static constexpr int DST = PT + 2 * TILE_BYTES;
+  static constexpr int LSE = DST + 2 * TILE_BYTES;  // 128 floats
+  static constexpr int DEL = LSE + 512;
+  static constexpr int BAR = DEL + 512;
+  static constexpr int TOTAL = BAR + 256 + 1024;
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_bwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                const AttnParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                           ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + BwdSmem::BAR);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* q_full = bars + 1;   // [2]
+  uint64_t* q_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;
+  uint64_t* s_free = bars + 6;
+  uint64_t* p_full = bars + 7;
+  uint64_t* dq_full = bars + 8;
+  uint64_t* dq_free = bars + 9;
+  uint64_t* ps_free = bars + 10;
+  uint64_t* fin = bars + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* sLse = reinterpret_cast<float*>(sm + BwdSmem::LSE);
+  float* sDel = reinterpret_cast<float*>(sm + BwdSmem::DEL);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nt = (p.T + TILE - 1) / TILE;
+  const int kt = (int)blockIdx.x;
+  const int bh = blockIdx.y;
+  const int b = bh / p.H, h = bh - b * p.H;
+  const int k0 = kt * TILE;
+  const int nq = nt - kt;  // query tiles kt .. nt-1
+  int* err = &g_attn_error;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&q_full[s], 1);
+      mbar_init(&q_empty[s], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(s_free, 4);
+    mbar_init(p_full, 4);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_free, 4);
+    mbar_init(ps_free, 1);
+    mbar_init(fin, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem, tDP = tmem + 128, tDV = tmem + 256, tDK = tmem + 320,
+                 tDQ = tmem + 384;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(kv_full, 2 * TILE_BYTES);
+      tma_load_4d(sm + BwdSmem::K, &tmK, kv_full, 0, k0, h, b);
+      tma_load_4d(sm + BwdSmem::V, &tmV, kv_full, 0, k0, h, b);
+      for (int it = 0; it < nq; ++it) {
+        const int s = it & 1;
+        if (!mbar_wait(&q_empty[s], ((it >> 1) & 1) ^ 1, abort_flag, err)) break;
+        mbar_arrive_expect_tx(&q_full[s], 2 * TILE_BYTES);
+        const int qq = (kt + it) * TILE;
+        tma_load_4d(sm + BwdSmem::Q + s * TILE_BYTES, &tmQ, &q_full[s], 0, qq, h, b);
+        tma_load_4d(sm + BwdSmem::DO + s * TILE_BYTES, &tmDO, &q_full[s], 0, qq, h, b);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idS = umma_idesc_bf16(128, 128, 0, 0);
+      constexpr uint32_t idKN = umma_idesc_bf16(128, 64, 0, 1);  // A K-major, B MN-major
+      constexpr uint32_t idMN = umma_idesc_bf16(128, 64, 1, 1);  // A MN-major, B MN-major
+      const uint32_t sK = smem_u32(sm + BwdSmem::K), sV = smem_u32(sm + BwdSmem::V);
+      const uint32_t sPt = smem_u32(sm + BwdSmem::PT), sdSt = smem_u32(sm + BwdSmem::DST);
+      bool ok = mbar_wait(kv_full, 0, abort_flag, err);
+      for (int it = 0; ok && it < nq; ++it) {
+        const int s = it & 1;
+        const uint32_t sQ = smem_u32(sm + BwdSmem::Q + s * TILE_BYTES);
+        const uint32_t sDO = smem_u32(sm + BwdSmem::DO + s * TILE_BYTES);
+        if (!mbar_wait(&q_full[s], (it >> 1) & 1, abort_flag, err)) break;
+        if (it > 0 && !mbar_wait(s_free, (it - 1) & 1, abort_flag, err)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < HD / 16; ++k) {
+          umma_bf16(tS, umma_smem_desc(sK + k * 32, 16, 1024), umma_smem_desc(sQ + k * 32, 16, 1024),
+                    idS, k > 0);
+          umma_bf16(tDP, umma_smem_desc(sV + k * 32, 16, 1024),
+                    umma_smem_desc(sDO + k * 32, 16, 1024), idS, k > 0);
+        }
+        umma_commit(s_full);
+        if (!mbar_wait(p_full, it & 1, abort_flag, err)) break;
+        if (it > 0 && !mbar_wait(dq_free, (it - 1) & 1, abort_flag, err)) break;
+        tc_fence_after();
+        // dQ = dS · K: A = dSᵀ tile read MN-major (M = queries in two 64-wide
+        // blocks 16 KB apart), B = K tile MN-major (N = head dim).
+#pragma unroll
+        for (int k = 0; k < TILE / 16; ++k)
+          umma_bf16(tDQ, umma_smem_desc(sdSt + k * 2048, TILE_BYTES, 1024),
+                    umma_smem_desc(sK + k * 2048, TILE_BYTES, 1024), idMN, k > 0);
+        umma_commit(dq_full);
+        // dV += Pᵀ · dO ; dK += dSᵀ · Q  (A K-major over queries, B MN-major)
+#pragma unroll
+        for (int k = 0; k < TILE / 16; ++k) {
+          const uint32_t aoff = (k >> 2) * TILE_BYTES + (k & 3) * 32;
+          umma_bf16(tDV, umma_smem_desc(sPt + aoff, 16, 1024),
+                    umma_smem_desc(sDO + k * 2048, TILE_BYTES, 1024), idKN, (it > 0 || k > 0));
+          umma_bf16(tDK, umma_smem_desc(sdSt + aoff, 16, 1024),
+                    umma_smem_desc(sQ + k * 2048, TILE_BYTES, 1024), idKN, (it > 0 || k > 0));
+        }
+        umma_commit(ps_free);
+        umma_commit(&q_empty[s]);
+      }
+      umma_commit(fin);
+    }
+  } else {
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;  // key row of this CTA (and query row for dQ)
+    const int key = k0 + r;
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const float c = p.scale * kLog2e;
+    const int tid = threadIdx.x - 64;
+    uint8_t* sPt = sm + BwdSmem::PT;
+    uint8_t* sdSt = sm + BwdSmem::DST;
+    const float* Lg = p.lse + (int64_t)bh * p.T;
+    const float* Dg = p.delta + (int64_t)bh * p.T;
+    bool ok = true;
+    for (int it = 0; it < nq && ok; ++it) {
+      const int qq0 = (kt + it) * TILE;
+      named_bar_sync(1, 128);  // previous iteration's readers of sLse/sDel are done
+      {
+        const int t = qq0 + tid;
+        sLse[tid] = (t < p.T) ? Lg[t] * kLog2e : INFINITY;  // rows past T: P = 0
+        sDel[tid] = (t < p.T) ? Dg[t] : 0.f;
+      }
+      named_bar_sync(1, 128);
+      if (!mbar_wait(s_full, it & 1, abort_flag, err)) {
+        ok = false;
+        break;
+      }
+      if (it > 0 && !mbar_wait(ps_free, (it - 1) & 1, abort_flag, err)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const bool diag = (it == 0);
+#pragma unroll 1
+      for (int cc = 0; cc < TILE / 32; ++cc) {
+        float sv[32], dp[32];
+        tmem_ld32(tS + lane_off + cc * 32, sv);
+        tmem_ld32(tDP + lane_off + cc * 32, dp);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int qc = cc * 32 + i;
+          float pv = ex2(sv[i] * c - sLse[qc]);
+          if (diag && r > qc) pv = 0.f;
+          sv[i] = pv;
+          dp[i] = pv * (dp[i] - sDel[qc]);
+        }
+        const int blk = cc >> 1;
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          const int ch = (cc & 1) * 4 + g;
+          uint4 qa, qb;
+          qa.x = pack_bf16x2(sv[8 * g], sv[8 * g + 1]);
+          qa.y = pack_bf16x2(sv[8 * g + 2], sv[8 * g + 3]);
+          qa.z = pack_bf16x2(sv[8 * g + 4], sv[8 * g + 5]);
+          qa.w = pack_bf16x2(sv[8 * g + 6], sv[8 * g + 7]);
+          qb.x = pack_bf16x2(dp[8 * g], dp[8 * g + 1]);
+          qb.y = pack_bf16x2(dp[8 * g + 2], dp[8 * g + 3]);
+          qb.z = pack_bf16x2(dp[8 * g + 4], dp[8 * g + 5]);
+          qb.w = pack_bf16x2(dp[8 * g + 6], dp[8 * g + 7]);
+          *reinterpret_cast<uint4*>(sPt + blk * TILE_BYTES + swz128(r, ch)) = qa;
+          *reinterpret_cast<uint4*>(sdSt + blk * TILE_BYTES + swz128(r, ch)) = qb;
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(s_free);
+        mbar_arrive(p_full);
+      }
+      // dQ rows of this query tile: lane r of TMEM holds query qq0 + r.
+      if (!mbar_wait(dq_full, it & 1, abort_flag, err)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int qrow = qq0 + r;
+      float* dst = p.dq_acc + ((int64_t)bh * p.T + qrow) * HD;
+#pragma unroll
+      for (int cc = 0; cc < HD / 32; ++cc) {
+        float v[32];
+        tmem_ld32(tDQ + lane_off + cc * 32, v);
+        if (qrow < p.T) {
+#pragma unroll
+          for (int g = 0; g < 8; ++g)
+            atomicAdd(reinterpret_cast<float4*>(dst + cc * 32 + 4 * g),
+                      make_float4(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]));
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dq_free);
+    }
+    if (ok && mbar_wait(fin, 0, abort_flag, err)) {
+      tc_fence_after();
+      bf16* dkrow = p.dk + b * p.sb + h * p.sh + (int64_t)key * p.st;
+      bf16* dvrow = p.dv + b * p.sb + h * p.sh + (int64_t)key * p.st;
+#pragma unroll
+      for (int cc = 0; cc < HD / 32; ++cc) {
+        float kk[32], vv[32];
+        // warp-collective TMEM loads stay outside the per-row guard
+        tmem_ld32(tDK + lane_off + cc * 32, kk);
+        tmem_ld32(tDV + lane_off + cc * 32, vv);
+        if (key < p.T) {
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            float* kv = kk + 8 * g;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) kv[i] *= p.scale;
+            if (p.rcos) rope_back(kv, p.rcos, p.rsin, key, cc * 4 + g);
+            uint4 qk, qv;
+            qk.x = pack_bf16x2(kv[0], kv[1]);
+            qk.y = pack_bf16x2(kv[2], kv[3]);
+            qk.z = pack_bf16x2(kv[4], kv[5]);
+            qk.w = pack_bf16x2(kv[6], kv[7]);
+            const float* w = vv + 8 * g;
+            qv.x = pack_bf16x2(w[0], w[1]);
+            qv.y = pack_bf16x2(w[2], w[3]);
+            qv.z = pack_bf16x2(w[4], w[5]);
+            qv.w = pack_bf16x2(w[6], w[7]);
+            *reinterpret_cast<uint4*>(dkrow + cc * 32 + 8 * g) = qk;
+            *reinterpret_cast<uint4*>(dvrow + cc * 32 + 8 * g) = qv;
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// delta[bh, t] = sum_e dO * O, and zero the dQ accumulator row. One warp per row.
+__global__ void attn_delta_kernel(const bf16* __restrict__ o, const bf16* __restrict__ dout,
+                                  int64_t osb, int64_t osh, int64_t ost, int B, int H, int T,
+                                  float* __restrict__ delta, float* __restrict__ dq_acc) {
+  const int64_t rows = (int64_t)B * H * T;
   const int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (r >= rows) return;
-  const int64_t bh = r / a.T;
-  const int t = (int)(r - bh * a.T);
-  const int b = (int)(bh / a.H), h = (int)(bh - (int64_t)b * a.H);
-  const int64_t off = b * a.osb + h * a.osh + (int64_t)t * a.ost + lane * 2;
+  const int64_t bh = r / T;
+  const int t = (int)(r - bh * T);
+  const int b = (int)(bh / H), h = (int)(bh - (int64_t)b * H);
+  const int64_t off = b * osb + h * osh + (int64_t)t * ost + lane * 2;
   float o0, o1, g0, g1;
-  unpack_bf16x2(*reinterpret_cast<const uint32_t*>(a.o + off), o0, o1);
-  unpack_bf16x2(*reinterpret_cast<const uint32_t*>(a.dout + off), g0, g1);
+  unpack_bf16x2(*reinterpret_cast<const uint32_t*>(o + off), o0, o1);
+  unpack_bf16x2(*reinterpret_cast<const uint32_t*>(dout + off), g0, g1);
   float s = warp_sum(o0 * g0 + o1 * g1);
-  if (lane == 0) const_cast<float*>(a.delta)[r] = s;
+  if (lane == 0) delta[r] = s;
+  reinterpret_cast<float2*>(dq_acc + r * HD)[lane] = make_float2(0.f, 0.f);
 }
 
-constexpr int BWD_B = 64, BWD_THREADS = 128;
-
-// dK, dV for one 64-key block. Warp w owns keys [k0 + 16w, k0 + 16w + 16).
-__global__ void __launch_bounds__(BWD_THREADS) attn_bwd_dkdv_kernel(const AttnArgs a) {
-  extern __shared__ __align__(128) uint8_t sm[];
-  uint8_t* sK = sm;                    // K block (rotated), later dK staging
-  uint8_t* sV = sK + TILE_BYTES;       // V block, later dV staging
-  uint8_t* sQ = sV + TILE_BYTES;       // 2 buffers
-  uint8_t* sD = sQ + 2 * TILE_BYTES;   // dO, 2 buffers
-  float* sL = reinterpret_cast<float*>(sD + 2 * TILE_BYTES);  // lse (log2 units), 2 x 64
-  float* sDl = sL + 2 * BWD_B;                                  // delta, 2 x 64
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int nkb = (a.T + BWD_B - 1) / BWD_B;
-  const int kb = blockIdx.x;
-  const int bh = blockIdx.y;
-  const int b = bh / a.H, h = bh - b * a.H;
-  const int k0 = kb * BWD_B;
-  const bf16* Q = a.q + b * a.sb + h * a.sh;
-  const bf16* K = a.k + b * a.sb + h * a.sh;
-  const bf16* V = a.v + b * a.sb + h * a.sh;
-  const bf16* dO = a.dout + b * a.osb + h * a.osh;
-  const float* L = a.lse + (int64_t)bh * a.T;
-  const float* Dl = a.delta + (int64_t)bh * a.T;
-
-  load_tile_async(sK, K, a.st, k0, BWD_B, a.T, tid, BWD_THREADS);
-  load_tile_async(sV, V, a.st, k0, BWD_B, a.T, tid, BWD_THREADS);
-  cp_commit();
-  auto load_q = [&](int qi, int buf) {
-    const int q0 = qi * BWD_B;
-    load_tile_async(sQ + buf * TILE_BYTES, Q, a.st, q0, BWD_B, a.T, tid, BWD_THREADS);
-    load_tile_async(sD + buf * TILE_BYTES, dO, a.ost, q0, BWD_B, a.T, tid, BWD_THREADS);
-    for (int i = tid; i < BWD_B; i += BWD_THREADS) {
-      int t = q0 + i;
-      sL[buf * BWD_B + i] = (t < a.T) ? L[t] * kLog2e : 0.f;
-      sDl[buf * BWD_B + i] = (t < a.T) ? Dl[t] : 0.f;
-    }
-  };
-  load_q(kb, 0);
-  cp_commit();
-  cp_wait<1>();
-  __syncthreads();
-  if (a.rcos) {
-    rope_tile(sK, a.rcos, a.rsin, k0, BWD_B, a.T, tid, BWD_THREADS);
-    __syncthreads();
+// dq = bf16(scale * dq_acc), rotated back by RoPE when tables are given.
+__global__ void attn_dq_store_kernel(const float* __restrict__ dq_acc, bf16* __restrict__ dq,
+                                     int64_t sb, int64_t sh, int64_t st, int B, int H, int T,
+                                     float scale, const bf16* rcos, const bf16* rsin) {
+  const int64_t chunks = (int64_t)B * H * T * (HD / 8);
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < chunks;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = i >> 3;
+    const int c = (int)(i & 7);
+    const int64_t bh = row / T;
+    const int t = (int)(row - bh * T);
+    const int b = (int)(bh / H), h = (int)(bh - (int64_t)b * H);
+    const float4* src = reinterpret_cast<const float4*>(dq_acc + row * HD + c * 8);
+    float4 a = src[0], e = src[1];
+    float v[8] = {a.x * scale, a.y * scale, a.z * scale, a.w * scale,
+                  e.x * scale, e.y * scale, e.z * scale, e.w * scale};
+    if (rcos) rope_back(v, rcos, rsin, t, c);
+    uint4 q;
+    q.x = pack_bf16x2(v[0], v[1]);
+    q.y = pack_bf16x2(v[2], v[3]);
+    q.z = pack_bf16x2(v[4], v[5]);
+    q.w = pack_bf16x2(v[6], v[7]);
+    *reinterpret_cast<uint4*>(dq + b * sb + h * sh + (int64_t)t * st + c * 8) = q;
   }
-  uint32_t kf[4][4], vf[4][4];
-  load_a_frags(sK, warp * 16, lane, kf);
-  load_a_frags(sV, warp * 16, lane, vf);
-
-  float dk[8][4], dv[8][4];
-#pragma unroll
-  for (int i = 0; i < 8; ++i)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) dk[i][e] = dv[i][e] = 0.f;
-  const float sl2 = a.scale * kLog2e;
-  const int key_a = k0 + warp * 16 + (lane >> 2);
-  const int key_b = key_a + 8;
-
-  for (int qi = kb; qi < nkb; ++qi) {
-    const int buf = (qi - kb) & 1;
-    if (qi + 1 < nkb) {
-      load_q(qi + 1, buf ^ 1);
-      cp_commit();
-      cp_wait<1>();
-    } else {
-      cp_wait<0>();
-    }
-    __syncthreads();
-    uint8_t* qt = sQ + buf * TILE_BYTES;
-    uint8_t* dt = sD + buf * TILE_BYTES;
-    const int q0 = qi * BWD_B;
-    if (a.rcos) {
-      rope_tile(qt, a.rcos, a.rsin, q0, BWD_B, a.T, tid, BWD_THREADS);
-      __syncthreads();
-    }
-    const float* lq = sL + buf * BWD_B;
-    const float* dq = sDl + buf * BWD_B;
-    // S^T = K_w Q^T  (rows = keys, cols = queries)
-    float s[8][4], dp[8][4];
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) s[i][e] = dp[i][e] = 0.f;
-    mma_a_tileT(s, kf, qt, lane);
-    mma_a_tileT(dp, vf, dt, lane);
-    const bool diag = (qi == kb);
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int qc = nt * 8 + (lane & 3) * 2 + e;
-        const int query = q0 + qc;
-        const float lv = lq[qc], dl = dq[qc];
-        float pa = exp2f(s[nt][e] * sl2 - lv);
-        float pb = exp2f(s[nt][2 + e] * sl2 - lv);
-        if ((diag && key_a > query) || query >= a.T) pa = 0.f;
-        if ((diag && key_b > query) || query >= a.T) pb = 0.f;
-        s[nt][e] = pa;
-        s[nt][2 + e] = pb;
-        dp[nt][e] = pa * (dp[nt][e] - dl);
-        dp[nt][2 + e] = pb * (dp[nt][2 + e] - dl);
-      }
-    }
-    mma_p_tile(dv, s, dt, lane);   // dV += P^T dO
-    mma_p_tile(dk, dp, qt, lane);  // dK += dS^T Q
-    __syncthreads();
-  }
-  // Stage and store: dK (scaled, inverse RoPE), dV.
-  stage_rows(sK, warp * 16, dk, a.scale, lane);
-  stage_rows(sV, warp * 16, dv, 1.f, lane);
-  __syncthreads();
-  store_tile(sK, a.dk + b * a.sb + h * a.sh, a.st, k0, BWD_B, a.T, a.rcos, a.rsin, tid, BWD_THREADS);
-  store_tile(sV, a.dv + b * a.sb + h * a.sh, a.st, k0, BWD_B, a.T, nullptr, nullptr, tid,
-             BWD_THREADS);
-}
-
-// dQ for one 64-query block. Warp w owns queries [q0 + 16w, q0 + 16w + 16).
-__global__ void __launch_bounds__(BWD_THREADS) attn_bwd_dq_kernel(const AttnArgs a) {
-  extern __shared__ __align__(128) uint8_t sm[];
-  uint8_t* sQ = sm;                   // Q block (rotated), later dQ staging
-  uint8_t* sD = sQ + TILE_BYTES;      // dO block
-  uint8_t* sK = sD + TILE_BYTES;      // 2 buffers
-  uint8_t* sV = sK + 2 * TILE_BYTES;  // 2 buffers
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int nqb = (a.T + BWD_B - 1) / BWD_B;
-  const int qb = nqb - 1 - blockIdx.x;
-  const int bh = blockIdx.y;
-  const int b = bh / a.H, h = bh - b * a.H;
-  const int q0 = qb * BWD_B;
-  const bf16* Q = a.q + b * a.sb + h * a.sh;
-  const bf16* K = a.k + b * a.sb + h * a.sh;
-  const bf16* V = a.v + b * a.sb + h * a.sh;
-  const bf16* dO = a.dout + b * a.osb + h * a.osh;
-
-  load_tile_async(sQ, Q, a.st, q0, BWD_B, a.T, tid, BWD_THREADS);
-  load_tile_async(sD, dO, a.ost, q0, BWD_B, a.T, tid, BWD_THREADS);
-  cp_commit();
-  load_tile_async(sK, K, a.st, 0, BWD_B, a.T, tid, BWD_THREADS);
-  load_tile_async(sV, V, a.st, 0, BWD_B, a.T, tid, BWD_THREADS);
-  cp_commit();
-  cp_wait<1>();
-  __syncthreads();
-  if (a.rcos) {
-    rope_tile(sQ, a.rcos, a.rsin, q0, BWD_B, a.T, tid, BWD_THREADS);
-    __syncthreads();
-  }
-  uint32_t qf[4][4], df[4][4];
-  load_a_frags(sQ, warp * 16, lane, qf);
-  load_a_frags(sD, warp * 16, lane, df);
-  const int row_a = q0 + warp * 16 + (lane >> 2);
-  const int row_b = row_a + 8;
-  const float* L = a.lse + (int64_t)bh * a.T;
-  const float* Dl = a.delta + (int64_t)bh * a.T;
-  const float la = (row_a < a.T) ? L[row_a] * kLog2e : 0.f;
-  const float lb = (row_b < a.T) ? L[row_b] * kLog2e : 0.f;
-  const float da = (row_a < a.T) ? Dl[row_a] : 0.f;
-  const float db = (row_b < a.T) ? Dl[row_b] : 0.f;
-  const float sl2 = a.scale * kLog2e;
-
-  float dq[8][4];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) dq[i][0] = dq[i][1] = dq[i][2] = dq[i][3] = 0.f;
-
-  for (int j = 0; j <= qb; ++j) {
-    const int buf = j & 1;
-    if (j + 1 <= qb) {
-      load_tile_async(sK + (buf ^ 1) * TILE_BYTES, K, a.st, (j + 1) * BWD_B, BWD_B, a.T, tid,
-                      BWD_THREADS);
-      load_tile_async(sV + (buf ^ 1) * TILE_BYTES, V, a.st, (j + 1) * BWD_B, BWD_B, a.T, tid,
-                      BWD_THREADS);
-      cp_commit();
-      cp_wait<1>();
-    } else {
-      cp_wait<0>();
-    }
-    __syncthreads();
-    uint8_t* kt = sK + buf * TILE_BYTES;
-    uint8_t* vt = sV + buf * TILE_BYTES;
-    const int k0 = j * BWD_B;
-    if (a.rcos) {
-      rope_tile(kt, a.rcos, a.rsin, k0, BWD_B, a.T, tid, BWD_THREADS);
-      __syncthreads();
-    }
-    float s[8][4], dp[8][4];
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) s[i][e] = dp[i][e] = 0.f;
-    mma_a_tileT(s, qf, kt, lane);
-    mma_a_tileT(dp, df, vt, lane);
-    const bool diag = (j == qb);
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int key = k0 + nt * 8 + (lane & 3) * 2 + e;
-        float pa = exp2f(s[nt][e] * sl2 - la);
-        float pb = exp2f(s[nt][2 + e] * sl2 - lb);
-        if (diag && key > row_a) pa = 0.f;
-        if (diag && key > row_b) pb = 0.f;
-        s[nt][e] = pa * (dp[nt][e] - da);
-        s[nt][2 + e] = pb * (dp[nt][2 + e] - db);
-      }
-    }
-    mma_p_tile(dq, s, kt, lane);  // dQ += dS K
-    __syncthreads();
-  }
-  stage_rows(sQ, warp * 16, dq, a.scale, lane);
-  __syncthreads();
-  store_tile(sQ, a.dq + b * a.sb + h * a.sh, a.st, q0, BWD_B, a.T, a.rcos, a.rsin, tid,
-             BWD_THREADS);
 }
 
 int attention_read_error(int clear) {
-  int h = 0;
-  cudaMemcpyFromSymbol(&h, g_attn_error, sizeof(int));
+  int hv = 0;
+  cudaMemcpyFromSymbol(&hv, g_attn_error, sizeof(int));
   if (clear) {
     int z = 0;
     cudaMemcpyToSymbol(g_attn_error, &z, sizeof(int));
   }
-  return h;
+  return hv;
+}
+
+// ------------------------------------------------------------------ host
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+// 4-D map over a [b, t, h, e] tensor with element strides (sb, st, sh), box
+// 64 (e) x 128 (t), 128-byte swizzle.
+static bool make_map4(CUtensorMap* m, const void* base, int B, int H, int T, int64_t sb,
+                      int64_t sh, int64_t st) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[4] = {HD, (cuuint64_t)T, (cuuint64_t)H, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)st * 2, (cuuint64_t)sh * 2, (cuuint64_t)sb * 2};
+  cuuint32_t box[4] = {HD, TILE, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box,
+             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 }  // namespace gptb200
@@ -616,7 +656,7 @@ static int check_attn(const void* q, const void* k, const void* v, int64_t sb, i
   if (!q || !k || !v) return GPTB200_EINVAL;
   if (batch <= 0 || heads <= 0 || seq <= 0) return GPTB200_EINVAL;
   if (hd != HD) return GPTB200_EUNSUPPORTED;
-  if (batch * heads > 65535 * 1024LL || seq > (1 << 24)) return GPTB200_ESHAPE;
+  if (batch * heads > 65535 || seq > (1 << 24)) return GPTB200_ESHAPE;
   if ((sb | sh | st | osb | osh | ost) % 8) return GPTB200_ESHAPE;
   if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
        reinterpret_cast<uintptr_t>(v)) & 15)
@@ -628,46 +668,47 @@ extern "C" int gptb200_attention_fwd(const void* q, const void* k, const void* v
                                      int64_t stride_h, int64_t stride_t, void* o,
                                      int64_t o_stride_b, int64_t o_stride_h, int64_t o_stride_t,
                                      float* lse, int64_t batch, int64_t heads, int64_t seq,
-                                     int64_t head_dim, float softmax_scale, const void* rope_cos,
-                                     const void* rope_sin, void* stream) {
+                                     int64_t head_dim, float softmax_scale, void* stream) {
   int s = check_attn(q, k, v, stride_b, stride_h, stride_t, o_stride_b, o_stride_h, o_stride_t,
                      batch, heads, seq, head_dim);
   if (s) return s;
   if (!o || !lse || !(softmax_scale > 0.f)) return GPTB200_EINVAL;
-  if ((rope_cos == nullptr) != (rope_sin == nullptr)) return GPTB200_EINVAL;
-  AttnArgs a = {};
-  a.q = reinterpret_cast<const bf16*>(q);
-  a.k = reinterpret_cast<const bf16*>(k);
-  a.v = reinterpret_cast<const bf16*>(v);
-  a.sb = stride_b;
-  a.sh = stride_h;
-  a.st = stride_t;
-  a.o_out = reinterpret_cast<bf16*>(o);
-  a.osb = o_stride_b;
-  a.osh = o_stride_h;
-  a.ost = o_stride_t;
-  a.lse_out = lse;
-  a.B = (int)batch;
-  a.H = (int)heads;
-  a.T = (int)seq;
-  a.scale = softmax_scale;
-  a.rcos = reinterpret_cast<const bf16*>(rope_cos);
-  a.rsin = reinterpret_cast<const bf16*>(rope_sin);
-  const int smem = 6 * TILE_BYTES;
-  static bool cfg = false;
-  if (!cfg) {
-    cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    cfg = true;
+  if (reinterpret_cast<uintptr_t>(o) & 15) return GPTB200_ESHAPE;
+  CUtensorMap mq, mk, mv;
+  if (!make_map4(&mq, q, (int)batch, (int)heads, (int)seq, stride_b, stride_h, stride_t) ||
+      !make_map4(&mk, k, (int)batch, (int)heads, (int)seq, stride_b, stride_h, stride_t) ||
+      !make_map4(&mv, v, (int)batch, (int)heads, (int)seq, stride_b, stride_h, stride_t))
+    return GPTB200_ESHAPE;
+  AttnParams p = {};
+  p.B = (int)batch;
+  p.H = (int)heads;
+  p.T = (int)seq;
+  p.scale = softmax_scale;
+  p.o = reinterpret_cast<bf16*>(o);
+  p.osb = o_stride_b;
+  p.osh = o_stride_h;
+  p.ost = o_stride_t;
+  p.lse = lse;
+  static bool cfg[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 64 || !cfg[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(attn_fwd_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         FwdSmem::TOTAL);
+    if (e != cudaSuccess) return -static_cast<int>(e);
+    if (dev < 64) cfg[dev] = true;
   }
-  dim3 grid((unsigned)((seq + FWD_BR - 1) / FWD_BR), (unsigned)(batch * heads));
-  attn_fwd_kernel<<<grid, FWD_THREADS, smem, reinterpret_cast<cudaStream_t>(stream)>>>(a);
+  dim3 grid((unsigned)((seq + TILE - 1) / TILE), (unsigned)(batch * heads));
+  attn_fwd_tc<<<grid, kThreads, FwdSmem::TOTAL, reinterpret_cast<cudaStream_t>(stream)>>>(mq, mk,
+                                                                                          mv, p);
   GPTB200_CHECK_LAUNCH();
   return 0;
 }
 
 extern "C" size_t gptb200_attention_bwd_workspace_size(int64_t batch, int64_t heads, int64_t seq) {
   if (batch <= 0 || heads <= 0 || seq <= 0) return 0;
-  return (size_t)((batch * heads * seq * 4 + 255) / 256 * 256);
+  const int64_t rows = batch * heads * seq;
+  return (size_t)((rows * 4 + 255) / 256 * 256 + rows * HD * 4);
 }
 
 extern "C" int gptb200_attention_bwd(const void* q, const void* k, const void* v, int64_t stride_b,
@@ -684,47 +725,60 @@ extern "C" int gptb200_attention_bwd(const void* q, const void* k, const void* v
     return GPTB200_EINVAL;
   if ((rope_cos == nullptr) != (rope_sin == nullptr)) return GPTB200_EINVAL;
   if ((reinterpret_cast<uintptr_t>(dout) | reinterpret_cast<uintptr_t>(dq) |
-       reinterpret_cast<uintptr_t>(dk) | reinterpret_cast<uintptr_t>(dv)) & 15)
+       reinterpret_cast<uintptr_t>(dk) | reinterpret_cast<uintptr_t>(dv) |
+       reinterpret_cast<uintptr_t>(o) | reinterpret_cast<uintptr_t>(workspace)) & 15)
     return GPTB200_ESHAPE;
   auto st = reinterpret_cast<cudaStream_t>(stream);
-  AttnArgs a = {};
-  a.q = reinterpret_cast<const bf16*>(q);
-  a.k = reinterpret_cast<const bf16*>(k);
-  a.v = reinterpret_cast<const bf16*>(v);
-  a.sb = stride_b;
-  a.sh = stride_h;
-  a.st = stride_t;
-  a.o = reinterpret_cast<const bf16*>(o);
-  a.dout = reinterpret_cast<const bf16*>(dout);
-  a.osb = o_stride_b;
-  a.osh = o_stride_h;
-  a.ost = o_stride_t;
-  a.lse = lse;
-  a.delta = reinterpret_cast<float*>(workspace);
-  a.dq = reinterpret_cast<bf16*>(dq);
-  a.dk = reinterpret_cast<bf16*>(dk);
-  a.dv = reinterpret_cast<bf16*>(dv);
-  a.B = (int)batch;
-  a.H = (int)heads;
-  a.T = (int)seq;
-  a.scale = softmax_scale;
-  a.rcos = reinterpret_cast<const bf16*>(rope_cos);
-  a.rsin = reinterpret_cast<const bf16*>(rope_sin);
+  const int B = (int)batch, H = (int)heads, T = (int)seq;
+  CUtensorMap mq, mk, mv, mdo;
+  if (!make_map4(&mq, q, B, H, T, stride_b, stride_h, stride_t) ||
+      !make_map4(&mk, k, B, H, T, stride_b, stride_h, stride_t) ||
+      !make_map4(&mv, v, B, H, T, stride_b, stride_h, stride_t) ||
+      !make_map4(&mdo, dout, B, H, T, o_stride_b, o_stride_h, o_stride_t))
+    return GPTB200_ESHAPE;
   const int64_t rows = batch * heads * seq;
-  attn_delta_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(a);
+  float* delta = reinterpret_cast<float*>(workspace);
+  float* dq_acc = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) +
+                                           (rows * 4 + 255) / 256 * 256);
+  attn_delta_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(
+      reinterpret_cast<const bf16*>(o), reinterpret_cast<const bf16*>(dout), o_stride_b,
+      o_stride_h, o_stride_t, B, H, T, delta, dq_acc);
   GPTB200_CHECK_LAUNCH();
-  const int smem_kv = 6 * TILE_BYTES + 4 * BWD_B * (int)sizeof(float);
-  const int smem_q = 6 * TILE_BYTES;
-  static bool cfg = false;
-  if (!cfg) {
-    cudaFuncSetAttribute(attn_bwd_dkdv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_kv);
-    cudaFuncSetAttribute(attn_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_q);
-    cfg = true;
+  AttnParams p = {};
+  p.B = B;
+  p.H = H;
+  p.T = T;
+  p.scale = softmax_scale;
+  p.lse = const_cast<float*>(lse);
+  p.delta = delta;
+  p.dq_acc = dq_acc;
+  p.dk = reinterpret_cast<bf16*>(dk);
+  p.dv = reinterpret_cast<bf16*>(dv);
+  p.sb = stride_b;
+  p.sh = stride_h;
+  p.st = stride_t;
+  p.rcos = reinterpret_cast<const bf16*>(rope_cos);
+  p.rsin = reinterpret_cast<const bf16*>(rope_sin);
+  static bool cfg[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 64 || !cfg[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(attn_bwd_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         BwdSmem::TOTAL);
+    if (e != cudaSuccess) return -static_cast<int>(e);
+    if (dev < 64) cfg[dev] = true;
   }
-  dim3 grid((unsigned)((seq + BWD_B - 1) / BWD_B), (unsigned)(batch * heads));
-  attn_bwd_dkdv_kernel<<<grid, BWD_THREADS, smem_kv, st>>>(a);
+  dim3 grid((unsigned)((seq + TILE - 1) / TILE), (unsigned)(batch * heads));
+  attn_bwd_tc<<<grid, kThreads, BwdSmem::TOTAL, st>>>(mq, mk, mv, mdo, p);
   GPTB200_CHECK_LAUNCH();
-  attn_bwd_dq_kernel<<<grid, BWD_THREADS, smem_q, st>>>(a);
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t chunks = rows * (HD / 8);
+  int blocks = (int)std::min<int64_t>((chunks + 255) / 256, (int64_t)sms * 8);
+  attn_dq_store_kernel<<<blocks, 256, 0, st>>>(dq_acc, reinterpret_cast<bf16*>(dq), stride_b,
+                                               stride_h, stride_t, B, H, T, softmax_scale,
+                                               reinterpret_cast<const bf16*>(rope_cos),
+                                               reinterpret_cast<const bf16*>(rope_sin));
   GPTB200_CHECK_LAUNCH();
   return 0;
 }

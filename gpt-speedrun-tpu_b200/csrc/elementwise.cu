@@ -373,3 +373,52 @@ extern "C" int gptb200_cast_bf16(const float* src, void* dst, int64_t n, void* s
   GPTB200_CHECK_LAUNCH();
   return 0;
 }
+
+// ------------------------------------------------------------------ standalone RoPE
+// One thread per 8-element chunk (4 interleaved pairs) of a [b, t, h, 64] view.
+__global__ void rope_apply_kernel(bf16* __restrict__ x, int64_t sb, int64_t st, int64_t sh, int B,
+                                  int T, int H, int hd, const bf16* __restrict__ rcos,
+                                  const bf16* __restrict__ rsin, int inverse) {
+  const int cph = hd / 8;
+  const int64_t total = (int64_t)B * T * H * cph;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t r = i / cph;
+    const int c = (int)(i - r * cph);
+    const int h = (int)(r % H);
+    r /= H;
+    const int t = (int)(r % T);
+    const int b = (int)(r / T);
+    bf16* p = x + b * sb + (int64_t)t * st + h * sh + c * 8;
+    float v[8];
+    ld8(p, v);
+    const bf16* cs = rcos + (int64_t)t * (hd / 2) + c * 4;
+    const bf16* sn = rsin + (int64_t)t * (hd / 2) + c * 4;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float cv = __bfloat162float(cs[j]);
+      const float sv = inverse ? -__bfloat162float(sn[j]) : __bfloat162float(sn[j]);
+      const float e = v[2 * j], o = v[2 * j + 1];
+      v[2 * j] = e * cv - o * sv;
+      v[2 * j + 1] = e * sv + o * cv;
+    }
+    st8(p, v);
+  }
+}
+
+extern "C" int gptb200_rope_apply(void* x, int64_t stride_b, int64_t stride_t, int64_t stride_h,
+                                  int64_t batch, int64_t seq, int64_t heads, int64_t head_dim,
+                                  const void* rope_cos, const void* rope_sin, int inverse,
+                                  void* stream) {
+  if (!x || !rope_cos || !rope_sin || batch <= 0 || seq <= 0 || heads <= 0 || head_dim <= 0)
+    return GPTB200_EINVAL;
+  if (head_dim % 8 || (stride_b | stride_t | stride_h) % 8 || !aligned16(x)) return GPTB200_ESHAPE;
+  const int64_t total = batch * seq * heads * (head_dim / 8);
+  int blocks = (int)std::min<int64_t>((total + 255) / 256, (int64_t)sms() * 16);
+  rope_apply_kernel<<<blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<bf16*>(x), stride_b, stride_t, stride_h, (int)batch, (int)seq, (int)heads,
+      (int)head_dim, reinterpret_cast<const bf16*>(rope_cos), reinterpret_cast<const bf16*>(rope_sin),
+      inverse);
+  GPTB200_CHECK_LAUNCH();
+  return 0;
+}

@@ -31,7 +31,8 @@ static __device__ int g_gemm_error;
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;                   // two per TMEM lane quadrant
+constexpr int kThreads = 64 + 32 * kEpiWarps;  // TMA warp + MMA warp + epilogue
 
 template <int BN, int STAGES>
 struct GemmSmem {
@@ -110,6 +111,38 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int row, int
         load_bf16x8(p.resid + (int64_t)row * p.ld_resid + c0, r);
 #pragma unroll
         for (int j = 0; j < 8; ++j) t[j] = r[j] + t[j];
+      }
+      store_bf16x8(C + (int64_t)row * p.ldc + c0, t);
+    }
+  } else if constexpr (EPI == EPI_BIAS_ROPE_) {
+    // bias, then the interleaved RoPE rotation of q/k columns at this row's
+    // position (rig/nn.py:36-52), one bf16 rounding per value as in the reference.
+    if (!row_ok) return;
+    bf16* C = reinterpret_cast<bf16*>(p.C);
+    const int pos = row % p.rope_seq;
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      int c0 = col + 8 * g;
+      if (c0 >= p.N) break;
+      float t[8], b[8];
+      load_bf16x8(p.bias + c0, b);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) t[j] = bf16r(bf16r(v[8 * g + j]) + b[j]);
+      if (c0 < p.rope_cols) {
+        const int pair0 = (c0 & 63) >> 1;
+        uint2 cq = *reinterpret_cast<const uint2*>(p.rope_cos + (int64_t)pos * 32 + pair0);
+        uint2 sq = *reinterpret_cast<const uint2*>(p.rope_sin + (int64_t)pos * 32 + pair0);
+        float cs[4], sn[4];
+        unpack_bf16x2(cq.x, cs[0], cs[1]);
+        unpack_bf16x2(cq.y, cs[2], cs[3]);
+        unpack_bf16x2(sq.x, sn[0], sn[1]);
+        unpack_bf16x2(sq.y, sn[2], sn[3]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float e = t[2 * j], o = t[2 * j + 1];
+          t[2 * j] = e * cs[j] - o * sn[j];
+          t[2 * j + 1] = e * sn[j] + o * cs[j];
+        }
       }
       store_bf16x8(C + (int64_t)row * p.ldc + c0, t);
     }
@@ -243,7 +276,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 4);
+      mbar_init(&tempty[a], kEpiWarps);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -346,8 +379,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // ---------------- epilogue warps 2..5
+    // ---------------- epilogue warps 2..9: warp w reads TMEM lanes of quadrant
+    // w % 4 and one half of the tile columns
     const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int r_in_tile = quad * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -372,14 +407,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       EpilogueRowState<EPI> st;
       const uint32_t trow = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
         float v[32];
         tmem_ld32(trow + c * 32, v);
         epilogue_chunk<EPI>(p, row, n0 + c * 32, v, st, target, lse, cot);
       }
       if constexpr (EPI == EPI_LCE_FWD_) {
         if (row < p.M)
-          p.partial[(int64_t)row * p.tiles_n + tc.tn] = make_float2(st.run_max, st.run_sum);
+          p.partial[((int64_t)row * p.tiles_n + tc.tn) * 2 + half] = make_float2(st.run_max, st.run_sum);
       }
       tc_fence_before();
       __syncwarp();
@@ -516,6 +551,9 @@ int gemm_launch(const void* a, int a_mn, int64_t lda, const void* b, int b_mn, i
     case EPI_BF16_: return dispatch_layout<EPI_BF16_>(a_mn, b_mn, ta, tb, p, stream);
     case EPI_F32_: return dispatch_layout<EPI_F32_>(a_mn, b_mn, ta, tb, p, stream);
     case EPI_F32_ATOMIC_: return dispatch_layout<EPI_F32_ATOMIC_>(a_mn, b_mn, ta, tb, p, stream);
+    case EPI_BIAS_ROPE_:
+      if (a_mn || !b_mn) return GPTB200_EUNSUPPORTED;
+      return launch_variant<kBN, kStages, EPI_BIAS_ROPE_, 0, 1>(ta, tb, p, stream);
     case EPI_BIAS_GELU_:
       if (a_mn || !b_mn) return GPTB200_EUNSUPPORTED;
       return launch_variant<kBN, kStages, EPI_BIAS_GELU_, 0, 1>(ta, tb, p, stream);
@@ -571,6 +609,16 @@ extern "C" int gptb200_gemm(const void* a, int a_mn_major, int64_t lda, const vo
     case GPTB200_EPI_DGELU:
       if (!e->aux || e->ld_aux < n || (e->ld_aux % 8)) return GPTB200_EINVAL;
       kind = EPI_DGELU_;
+      break;
+    case GPTB200_EPI_BIAS_ROPE:
+      if (!e->bias || !e->rope_cos || !e->rope_sin || e->rope_seq <= 0 || e->rope_cols < 0 ||
+          (e->rope_cols % 64) || e->rope_cols > n)
+        return GPTB200_EINVAL;
+      kind = EPI_BIAS_ROPE_;
+      p.rope_cos = reinterpret_cast<const bf16*>(e->rope_cos);
+      p.rope_sin = reinterpret_cast<const bf16*>(e->rope_sin);
+      p.rope_seq = (int)e->rope_seq;
+      p.rope_cols = (int)e->rope_cols;
       break;
     case GPTB200_EPI_F32: kind = EPI_F32_; break;
     case GPTB200_EPI_F32_ATOMIC: kind = EPI_F32_ATOMIC_; break;

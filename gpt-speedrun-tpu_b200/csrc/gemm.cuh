@@ -13,6 +13,7 @@ enum {
   EPI_DGELU_ = 2,
   EPI_F32_ = 3,
   EPI_F32_ATOMIC_ = 4,
+  EPI_BIAS_ROPE_ = 5,
   EPI_LCE_FWD_ = 10,  // per (row, N-tile) partial (max, sum exp) + target logit
   EPI_LCE_BWD_ = 11,  // bf16 (softmax - onehot) * cotangent
 };
@@ -31,6 +32,11 @@ struct GemmParams {
   int64_t ld_resid;
   __nv_bfloat16* aux;
   int64_t ld_aux;
+  // RoPE epilogue
+  const __nv_bfloat16* rope_cos;
+  const __nv_bfloat16* rope_sin;
+  int rope_seq;
+  int rope_cols;
   // cross-entropy epilogues
   const int32_t* targets;
   const float* lse;

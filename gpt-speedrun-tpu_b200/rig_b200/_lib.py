@@ -31,6 +31,10 @@ class Epilogue(ctypes.Structure):
         ("ld_residual", c_i64),
         ("aux", c_vp),
         ("ld_aux", c_i64),
+        ("rope_cos", c_vp),
+        ("rope_sin", c_vp),
+        ("rope_seq", c_i64),
+        ("rope_cols", c_i64),
     ]
 
 
@@ -68,6 +72,7 @@ EPI_BIAS_GELU = 1
 EPI_DGELU = 2
 EPI_F32 = 3
 EPI_F32_ATOMIC = 4
+EPI_BIAS_ROPE = 5
 
 # name -> (restype, argtypes). Mirrors include/gptb200.h one to one.
 SIGNATURES: dict[str, tuple[object, list[object]]] = {
@@ -86,10 +91,12 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "gptb200_embedding_fwd": (c_int, [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp]),
     "gptb200_embedding_bwd": (c_int, [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp]),
     "gptb200_rope_tables": (c_int, [c_vp, c_vp, c_i64, c_i64, c_vp]),
+    "gptb200_rope_apply": (
+        c_int, [c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_int, c_vp]),
     "gptb200_attention_fwd": (
         c_int,
         [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_i64, c_vp,
-         c_i64, c_i64, c_i64, c_i64, c_f32, c_vp, c_vp, c_vp],
+         c_i64, c_i64, c_i64, c_i64, c_f32, c_vp],
     ),
     "gptb200_attention_bwd_workspace_size": (c_size, [c_i64, c_i64, c_i64]),
     "gptb200_attention_bwd": (

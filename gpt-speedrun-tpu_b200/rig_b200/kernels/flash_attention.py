@@ -54,10 +54,14 @@ class _Attention(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, scale, rope):
         q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+        if rope is not None:  # rotate copies of q and k (BHSD viewed as BTHD)
+            q, k = q.clone(), k.clone()
+            ops.rope_apply(q.transpose(1, 2), rope)
+            ops.rope_apply(k.transpose(1, 2), rope)
         b, h, t, _ = q.shape
         o = torch.empty_like(q)
         lse = torch.empty(b, h, t, dtype=torch.float32, device=q.device)
-        ops.attention_fwd(q, k, v, o, lse, scale=scale, rope=rope)
+        ops.attention_fwd(q, k, v, o, lse, scale=scale)
         ctx.save_for_backward(q, k, v, o, lse)
         ctx.scale, ctx.rope = scale, rope
         return o

@@ -323,10 +323,12 @@ class GPTTrainer:
         ops.embedding_fwd(self.tokens.view(-1), self.tok_emb, self.x[0])
         for l, blk in enumerate(self.blocks):
             ops.rms_norm_fwd(self.x[l], blk.ln1_scale, self.ln1[l], self.rstd1[l])
-            ops.matmul(self.ln1[l], blk.qkv_w, bias=blk.qkv_b, out=self.qkv[l])
+            # QKV projection with bias and RoPE on the q/k columns in the epilogue
+            ops.matmul(self.ln1[l], blk.qkv_w, bias=blk.qkv_b, out=self.qkv[l],
+                       kind=_lib.EPI_BIAS_ROPE, rope=self.rope, rope_cols=2 * d)
             q, k, v = self._qkv_views(self.qkv[l])
             ops.attention_fwd(q, k, v, self._bthd(self.att[l]), self.lse[l], scale=c.softmax_scale,
-                              layout="bthd", rope=self.rope)
+                              layout="bthd")
             ops.matmul(self.att[l], blk.attn_w, bias=blk.attn_b, alpha=a, residual=self.x[l],
                        out=self.xm[l])
             ops.rms_norm_fwd(self.xm[l], blk.ln2_scale, self.ln2[l], self.rstd2[l])

@@ -58,6 +58,8 @@ def gemm(
     residual: torch.Tensor | None = None,
     aux: torch.Tensor | None = None,
     accumulate: bool = False,
+    rope: tuple[torch.Tensor, torch.Tensor] | None = None,
+    rope_cols: int = 0,
 ) -> torch.Tensor:
     """out[m, n] = epilogue(sum_k A[m, k] B[n, k]); see include/gptb200.h."""
 
@@ -74,6 +76,10 @@ def gemm(
         ld_residual=0 if residual is None else _row_major(residual, "residual"),
         aux=_ptr(aux),
         ld_aux=0 if aux is None else _row_major(aux, "aux"),
+        rope_cos=None if rope is None else rope[0].data_ptr(),
+        rope_sin=None if rope is None else rope[1].data_ptr(),
+        rope_seq=0 if rope is None else rope[0].shape[0],
+        rope_cols=int(rope_cols),
     )
     if gemm_timer is not None:
         start = torch.cuda.Event(enable_timing=True)
@@ -103,7 +109,7 @@ def launch_count() -> int:
 
 
 def matmul(x: torch.Tensor, w: torch.Tensor, *, bias=None, out=None, kind=_lib.EPI_BF16,
-           alpha=1.0, residual=None, aux=None) -> torch.Tensor:
+           alpha=1.0, residual=None, aux=None, rope=None, rope_cols=0) -> torch.Tensor:
     """y[M, N] = x[M, K] @ w[K, N] (w in the reference's [in, out] layout)."""
 
     m, k = x.shape
@@ -111,7 +117,19 @@ def matmul(x: torch.Tensor, w: torch.Tensor, *, bias=None, out=None, kind=_lib.E
     if out is None:
         out = torch.empty(m, n, device=x.device, dtype=BF16)
     return gemm(x, w, out, b_mn_major=True, m=m, n=n, k=k, kind=kind, alpha=alpha, bias=bias,
-                residual=residual, aux=aux)
+                residual=residual, aux=aux, rope=rope, rope_cols=rope_cols)
+
+
+def rope_apply(x: torch.Tensor, rope, *, inverse: bool = False) -> torch.Tensor:
+    """In-place interleaved RoPE on a BTHD view (inverse: the transpose rotation)."""
+
+    _cuda(x)
+    if x.dim() != 4 or x.stride(3) != 1:
+        raise ValueError("rope_apply expects a [B, T, H, D] view with a contiguous head dim")
+    b, t, h, d = x.shape
+    call("gptb200_rope_apply", x.data_ptr(), x.stride(0), x.stride(1), x.stride(2), b, t, h, d,
+         rope[0].data_ptr(), rope[1].data_ptr(), int(inverse), _stream())
+    return x
 
 
 # ----------------------------------------------------------------- RMSNorm
@@ -166,8 +184,9 @@ def _strides4(t: torch.Tensor, layout: str) -> tuple[int, int, int]:
     return t.stride(0), t.stride(2), t.stride(1)  # bthd
 
 
-def attention_fwd(q, k, v, o, lse, *, scale: float, layout: str = "bhsd", rope=None):
-    """Causal attention; q/k/v/o are rank-4 views in `layout` ('bhsd' or 'bthd')."""
+def attention_fwd(q, k, v, o, lse, *, scale: float, layout: str = "bhsd"):
+    """Causal attention; q/k/v/o are rank-4 views in `layout` ('bhsd' or 'bthd').
+    q and k are used as given (apply RoPE before, e.g. with `rope_apply`)."""
 
     _cuda(q, k, v, o, lse)
     sb, sh, st = _strides4(q, layout)
@@ -178,10 +197,8 @@ def attention_fwd(q, k, v, o, lse, *, scale: float, layout: str = "bhsd", rope=N
         b, h, t, dh = q.shape
     else:
         b, t, h, dh = q.shape
-    cos, sin = rope if rope is not None else (None, None)
     call("gptb200_attention_fwd", q.data_ptr(), k.data_ptr(), v.data_ptr(), sb, sh, st,
-         o.data_ptr(), osb, osh, ost, lse.data_ptr(), b, h, t, dh, float(scale), _ptr(cos),
-         _ptr(sin), _stream())
+         o.data_ptr(), osb, osh, ost, lse.data_ptr(), b, h, t, dh, float(scale), _stream())
     return o, lse
 
 

@@ -64,6 +64,9 @@ uint64_t gptb200_launch_count(void);
 #define GPTB200_EPI_DGELU 2      /* C bf16 = bf16(alpha*acc) * gelu_tanh'(aux) */
 #define GPTB200_EPI_F32 3        /* C fp32 = alpha*acc (accumulate=1: C += alpha*acc) */
 #define GPTB200_EPI_F32_ATOMIC 4 /* C fp32 += alpha*acc with atomics; K may be split across CTAs */
+#define GPTB200_EPI_BIAS_ROPE 5  /* C bf16 = bf16(acc)+bias, then columns < rope_cols rotated by
+                                    RoPE at position (row % rope_seq), pairs (2i, 2i+1) within
+                                    each 64-wide head (the QKV projection + apply_rotary) */
 
 typedef struct gptb200_epilogue {
   int kind;              /* GPTB200_EPI_* */
@@ -74,6 +77,10 @@ typedef struct gptb200_epilogue {
   int64_t ld_residual;
   void* aux;             /* bf16 [M, ld_aux]: written by BIAS_GELU, read by DGELU */
   int64_t ld_aux;
+  const void* rope_cos;  /* EPI_BIAS_ROPE: bf16 [rope_seq, 32] tables (gptb200_rope_tables) */
+  const void* rope_sin;
+  int64_t rope_seq;      /* rows are token positions row % rope_seq */
+  int64_t rope_cols;     /* columns [0, rope_cols) are rotated (q and k: 2 * d_model) */
 } gptb200_epilogue;
 
 int gptb200_gemm(const void* a, int a_mn_major, int64_t lda, const void* b, int b_mn_major,
@@ -115,28 +122,38 @@ int gptb200_embedding_bwd(const int32_t* tokens, const void* dout, float* dtable
 int gptb200_rope_tables(void* cos_out, void* sin_out, int64_t seq, int64_t head_dim,
                         void* stream);
 
+/* Applies (inverse = 0) or undoes (inverse = 1, the transpose rotation, i.e.
+ * the backward of apply_rotary) the interleaved RoPE in place on a
+ * [batch, seq, heads, head_dim] bf16 view with element strides (stride_b,
+ * stride_t, stride_h) and a contiguous head dimension. Replaces rig/nn.py:36-52
+ * (`apply_rotary`) when q/k are not produced by a GEMM with EPI_BIAS_ROPE. */
+int gptb200_rope_apply(void* x, int64_t stride_b, int64_t stride_t, int64_t stride_h,
+                       int64_t batch, int64_t seq, int64_t heads, int64_t head_dim,
+                       const void* rope_cos, const void* rope_sin, int inverse, void* stream);
+
 /* ------------------------------------------------------------------ attention
- * Causal softmax attention, fp32 statistics, bf16 P before P·V, with optional
- * interleaved RoPE applied to q and k as they are loaded (rope_cos/rope_sin
- * from gptb200_rope_tables, or NULL for none).
+ * Causal softmax attention on tcgen05 tensor cores, fp32 statistics, bf16 P
+ * before P·V. q and k are taken as given (already rotated: in the training
+ * step RoPE runs in the QKV projection epilogue, GPTB200_EPI_BIAS_ROPE).
  * Tensors are addressed as base + b*stride_b + h*stride_h + t*stride_t + e
  * (element strides); q, k, v share (stride_b, stride_h, stride_t), o and do
  * share (o_stride_*). lse: fp32 [batch, heads, seq] (natural-log units of the
- * scaled scores). head_dim must be 64.
+ * scaled scores). head_dim must be 64; strides multiples of 8 elements.
  * Replaces rig/kernels/tpu_flash_attention.py:236-348 (forward kernel) behind
  * make_causal_attention (:962-1164); semantics of reference_causal_attention
- * (:171-207) and, with rope, of rig/nn.py:36-52 applied first.
+ * (:171-207).
  */
 int gptb200_attention_fwd(const void* q, const void* k, const void* v, int64_t stride_b,
                           int64_t stride_h, int64_t stride_t, void* o, int64_t o_stride_b,
                           int64_t o_stride_h, int64_t o_stride_t, float* lse, int64_t batch,
                           int64_t heads, int64_t seq, int64_t head_dim, float softmax_scale,
-                          const void* rope_cos, const void* rope_sin, void* stream);
+                          void* stream);
 
 size_t gptb200_attention_bwd_workspace_size(int64_t batch, int64_t heads, int64_t seq);
 
-/* Backward: dq, dk, dv are written (not accumulated) with the q/k/v strides;
- * with rope, dq and dk are gradients with respect to the pre-rotation inputs.
+/* Backward: dq, dk, dv are written (not accumulated) with the q/k/v strides.
+ * With rope tables (the ones q and k were rotated with), dq and dk are rotated
+ * back, i.e. they are gradients with respect to the unrotated q and k.
  * Replaces rig/kernels/tpu_flash_attention.py:479-575 (dQ) and :578-701 (dK/dV). */
 int gptb200_attention_bwd(const void* q, const void* k, const void* v, int64_t stride_b,
                           int64_t stride_h, int64_t stride_t, const void* o, const void* dout,

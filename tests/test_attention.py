@@ -29,9 +29,12 @@ def _run(cuda, b, h, t, rope, seed=0, scale=1 / 64):
     (o_ref.float() * do.float()).sum().backward()
     tables = ops.rope_tables(t, 64, cuda) if rope else None
     qd, kd, vd, dod = (x.to(cuda) for x in (q, k, v, do))
+    if rope:  # q/k are rotated before the kernel; its backward rotates dq/dk back
+        ops.rope_apply(qd.transpose(1, 2), tables)
+        ops.rope_apply(kd.transpose(1, 2), tables)
     o = torch.empty_like(qd)
     lse = torch.empty(b, h, t, device=cuda)
-    ops.attention_fwd(qd, kd, vd, o, lse, scale=scale, rope=tables)
+    ops.attention_fwd(qd, kd, vd, o, lse, scale=scale)
     dq, dk, dv = torch.empty_like(qd), torch.empty_like(kd), torch.empty_like(vd)
     ops.attention_bwd(qd, kd, vd, o, dod, lse, dq, dk, dv, scale=scale, rope=tables)
     torch.cuda.synchronize()
@@ -40,7 +43,8 @@ def _run(cuda, b, h, t, rope, seed=0, scale=1 / 64):
 
 
 @pytest.mark.parametrize("rope", [False, True])
-@pytest.mark.parametrize("b,h,t", [(2, 3, 256), (1, 2, 1024), (1, 1, 200), (2, 1, 64)])
+@pytest.mark.parametrize("b,h,t", [(2, 3, 256), (1, 2, 1024), (1, 1, 200), (2, 1, 64),
+                                   (1, 1, 128), (1, 2, 384), (1, 1, 1000)])
 def test_fwd_bwd_vs_restatement(cuda, b, h, t, rope):
     got, want = _run(cuda, b, h, t, rope)
     names = ("o", "dq", "dk", "dv")
@@ -62,11 +66,40 @@ def test_bthd_strided_layout(cuda):
     q, k, v = qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2]
     o = torch.empty(b, t, h, 64, device=cuda, dtype=torch.bfloat16)
     lse = torch.empty(b, h, t, device=cuda)
-    tables = ops.rope_tables(t, 64, cuda)
-    ops.attention_fwd(q, k, v, o, lse, scale=1 / 64, layout="bthd", rope=tables)
+    ops.attention_fwd(q, k, v, o, lse, scale=1 / 64, layout="bthd")
     qc, kc, vc = (x.transpose(1, 2).contiguous() for x in (q, k, v))
     o2 = torch.empty_like(qc)
     lse2 = torch.empty_like(lse)
-    ops.attention_fwd(qc, kc, vc, o2, lse2, scale=1 / 64, rope=tables)
+    ops.attention_fwd(qc, kc, vc, o2, lse2, scale=1 / 64)
     assert torch.equal(o.transpose(1, 2), o2)
     assert torch.equal(lse, lse2)
+
+
+def test_rope_apply_matches_restatement(cuda):
+    x = torch.randn(2, 300, 3, 64).bfloat16()
+    tables = ops.rope_tables(300, 64, cuda)
+    xd = x.to(cuda)
+    ops.rope_apply(xd, tables)
+    want = ref.apply_rotary(x)
+    assert (xd.cpu().float() - want.float()).abs().max().item() <= 2 ** -7 * want.abs().max().item()
+    ops.rope_apply(xd, tables, inverse=True)  # the transpose rotation undoes it (to rounding)
+    assert _rel(xd.cpu(), x) < 1e-2
+
+
+def test_qkv_rope_epilogue(cuda):
+    """The QKV GEMM epilogue applies bias + RoPE to the q/k columns only."""
+
+    from rig_b200 import _lib
+    n_tok, t, d = 512, 256, 128
+    x = torch.randn(n_tok, d, device=cuda).bfloat16()
+    w = (0.1 * torch.randn(d, 3 * d, device=cuda)).bfloat16()
+    bias = (0.1 * torch.randn(3 * d, device=cuda)).bfloat16()
+    tables = ops.rope_tables(t, 64, cuda)
+    out = torch.empty(n_tok, 3 * d, device=cuda, dtype=torch.bfloat16)
+    ops.matmul(x, w, bias=bias, out=out, kind=_lib.EPI_BIAS_ROPE, rope=tables, rope_cols=2 * d)
+    plain = ops.matmul(x, w, bias=bias)
+    pl = plain.view(n_tok // t, t, 3, d // 64, 64).clone()
+    ops.rope_apply(pl[:, :, 0], tables)
+    ops.rope_apply(pl[:, :, 1], tables)
+    o = out.view_as(pl).float()
+    assert ((o - pl.float()).abs() <= 2 ** -7 * pl.float().abs() + 1e-6).all()
