@@ -6,9 +6,9 @@
 //           and rows past the sequence end arrive as zeros);
 //   warp 1  one thread issues tcgen05.mma: S = Q·Kᵀ (128x128, fp32 in TMEM),
 //           then O += P·V (128x64, fp32 in TMEM, V as an MN-major operand);
-//   warps 2-5 softmax: thread r owns query row r (TMEM lane r). It copies its
-//           S row to registers (freeing TMEM for the next S while it computes),
-//           applies scale·log2(e) and the causal mask, and keeps a running max
+//   warps 2-5 softmax: thread r owns query row r (TMEM lane r). Two passes
+//           over its S row, 32 TMEM columns at a time (max, then exp + store),
+//           apply scale·log2(e) and the causal mask, and keep a running max
 //           that is only raised when the row max grows by more than 2^8, in
 //           which case O is rescaled in TMEM (tcgen05.ld/st) — otherwise the
 //           stale max is exact because O and the row sum use the same one.
@@ -36,8 +36,6 @@ namespace gptb200 {
 static __device__ int g_attn_error;
 
 constexpr int HD = 64;
-constexpr int TILE = 128;          // queries per forward CTA / keys per backward CTA
-constexpr int TILE_BYTES = TILE * 128;  // 128 rows x 64 bf16 (128 B)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr int kThreads = 192;
@@ -79,16 +77,22 @@ __device__ __forceinline__ void rope_back(float* v, const bf16* rcos, const bf16
 }
 
 // ------------------------------------------------------------------ forward
+constexpr int FQ = 128;                 // queries per forward CTA (TMEM lanes)
+constexpr int FK = 64;                  // keys per K/V tile
+constexpr int Q_BYTES = FQ * 128;       // 128 rows x 64 bf16
+constexpr int KV_BYTES = FK * 128;      // 64 rows x 64 bf16
+constexpr int P_BYTES = FQ * FK * 2;    // 128 rows x 64 keys bf16 (one 128-byte-wide block)
+
 struct FwdSmem {
   static constexpr int Q = 0;
-  static constexpr int K = Q + TILE_BYTES;        // 2 stages
-  static constexpr int V = K + 2 * TILE_BYTES;    // 2 stages
-  static constexpr int P = V + 2 * TILE_BYTES;    // 2 blocks of 64 keys
-  static constexpr int BAR = P + 2 * TILE_BYTES;
+  static constexpr int K = Q + Q_BYTES;       // 2 stages
+  static constexpr int V = K + 2 * KV_BYTES;  // 2 stages
+  static constexpr int P = V + 2 * KV_BYTES;
+  static constexpr int BAR = P + P_BYTES;
   static constexpr int TOTAL = BAR + 256 + 1024;
 };
 
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kThreads, 3)
     attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -106,12 +110,12 @@ __global__ void __launch_bounds__(kThreads, 2)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nqt = (p.T + TILE - 1) / TILE;
+  const int nqt = (p.T + FQ - 1) / FQ;
   const int qt = nqt - 1 - (int)blockIdx.x;  // heaviest tiles first
   const int bh = blockIdx.y;
   const int b = bh / p.H, h = bh - b * p.H;
-  const int q0 = qt * TILE;
-  const int nkv = qt + 1;
+  const int q0 = qt * FQ;
+  const int nkv = min((q0 + FQ) / FK, (p.T + FK - 1) / FK);
   int* err = &g_attn_error;
 
   if (threadIdx.x == 0) {
@@ -127,29 +131,29 @@ __global__ void __launch_bounds__(kThreads, 2)
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 1) tmem_alloc(tmem_slot, 256);
+  if (warp == 1) tmem_alloc(tmem_slot, 128);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem, tO = tmem + 128;
+  const uint32_t tS = tmem, tO = tmem + 64;
 
   if (warp == 0) {
     if (lane == 0) {
-      mbar_arrive_expect_tx(q_full, TILE_BYTES);
+      mbar_arrive_expect_tx(q_full, Q_BYTES);
       tma_load_4d(sm + FwdSmem::Q, &tmQ, q_full, 0, q0, h, b);
       for (int j = 0; j < nkv; ++j) {
         const int s = j & 1;
         if (!mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1, abort_flag, err)) break;
-        mbar_arrive_expect_tx(&kv_full[s], 2 * TILE_BYTES);
-        tma_load_4d(sm + FwdSmem::K + s * TILE_BYTES, &tmK, &kv_full[s], 0, j * TILE, h, b);
-        tma_load_4d(sm + FwdSmem::V + s * TILE_BYTES, &tmV, &kv_full[s], 0, j * TILE, h, b);
+        mbar_arrive_expect_tx(&kv_full[s], 2 * KV_BYTES);
+        tma_load_4d(sm + FwdSmem::K + s * KV_BYTES, &tmK, &kv_full[s], 0, j * FK, h, b);
+        tma_load_4d(sm + FwdSmem::V + s * KV_BYTES, &tmV, &kv_full[s], 0, j * FK, h, b);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idS = umma_idesc_bf16(128, 128, 0, 0);
-      constexpr uint32_t idO = umma_idesc_bf16(128, 64, 0, 1);
+      constexpr uint32_t idS = umma_idesc_bf16(128, FK, 0, 0);
+      constexpr uint32_t idO = umma_idesc_bf16(128, HD, 0, 1);
       const uint32_t sQ = smem_u32(sm + FwdSmem::Q);
       const uint32_t sP = smem_u32(sm + FwdSmem::P);
       bool ok = mbar_wait(q_full, 0, abort_flag, err);
@@ -158,8 +162,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (!mbar_wait(&kv_full[s], (j >> 1) & 1, abort_flag, err)) break;
         if (j > 0 && !mbar_wait(s_free, (j - 1) & 1, abort_flag, err)) break;
         tc_fence_after();
-        const uint32_t sK = smem_u32(sm + FwdSmem::K + s * TILE_BYTES);
-        const uint32_t sV = smem_u32(sm + FwdSmem::V + s * TILE_BYTES);
+        const uint32_t sK = smem_u32(sm + FwdSmem::K + s * KV_BYTES);
+        const uint32_t sV = smem_u32(sm + FwdSmem::V + s * KV_BYTES);
 #pragma unroll
         for (int k = 0; k < HD / 16; ++k)
           umma_bf16(tS, umma_smem_desc(sQ + k * 32, 16, 1024), umma_smem_desc(sK + k * 32, 16, 1024),
@@ -168,9 +172,9 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (!mbar_wait(p_full, j & 1, abort_flag, err)) break;
         tc_fence_after();
 #pragma unroll
-        for (int k = 0; k < TILE / 16; ++k)
-          umma_bf16(tO, umma_smem_desc(sP + (k >> 2) * TILE_BYTES + (k & 3) * 32, 16, 1024),
-                    umma_smem_desc(sV + k * 2048, TILE_BYTES, 1024), idO, (j > 0 || k > 0));
+        for (int k = 0; k < FK / 16; ++k)
+          umma_bf16(tO, umma_smem_desc(sP + k * 32, 16, 1024),
+                    umma_smem_desc(sV + k * 2048, KV_BYTES, 1024), idO, (j > 0 || k > 0));
         umma_commit(pv_done);
         umma_commit(&kv_empty[s]);
       }
@@ -191,20 +195,20 @@ __global__ void __launch_bounds__(kThreads, 2)
         break;
       }
       tc_fence_after();
-      float s[TILE];
-#pragma unroll
-      for (int cc = 0; cc < TILE / 32; ++cc) tmem_ld32(tS + lane_off + cc * 32, s + cc * 32);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(s_free);
-      const bool diag = (j == qt);
+      const int k0 = j * FK;
+      const bool diag = k0 + FK - 1 > q0;  // tile crosses the causal diagonal
+      const int lim = qrow - k0;           // visible keys: column index <= lim
+      // Pass 1: row max of the scaled, masked scores, straight from TMEM.
       float mx = -INFINITY;
+#pragma unroll 1
+      for (int cc = 0; cc < FK / 32; ++cc) {
+        float v[32];
+        tmem_ld32(tS + lane_off + cc * 32, v);
 #pragma unroll
-      for (int i = 0; i < TILE; ++i) {
-        float v = s[i] * c;
-        if (diag && i > r) v = -INFINITY;
-        s[i] = v;
-        mx = fmaxf(mx, v);
+        for (int i = 0; i < 32; ++i) {
+          const float x = (diag && cc * 32 + i > lim) ? -INFINITY : v[i] * c;
+          mx = fmaxf(mx, x);
+        }
       }
       bool waited_pv = false;
       if (mx > m_used + 8.0f) {
@@ -229,13 +233,6 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         m_used = m_new;
       }
-      float sum = 0.f;
-#pragma unroll
-      for (int i = 0; i < TILE; ++i) {
-        s[i] = ex2(s[i] - m_used);
-        sum += s[i];
-      }
-      l += sum;
       // P_{j-1} must have been consumed by its P·V MMA before P_j overwrites it.
       if (j > 0 && !waited_pv) {
         if (!mbar_wait(pv_done, (j - 1) & 1, abort_flag, err)) {
@@ -243,23 +240,37 @@ __global__ void __launch_bounds__(kThreads, 2)
           break;
         }
       }
+      // Pass 2: P = exp2(s*c - m) as bf16 into the swizzled K-major P tile.
+      float sum = 0.f;
+#pragma unroll 1
+      for (int cc = 0; cc < FK / 32; ++cc) {
+        float v[32];
+        tmem_ld32(tS + lane_off + cc * 32, v);
 #pragma unroll
-      for (int blk = 0; blk < 2; ++blk) {
+        for (int i = 0; i < 32; ++i) {
+          float pv = ex2(fmaf(v[i], c, -m_used));
+          if (diag && cc * 32 + i > lim) pv = 0.f;
+          v[i] = pv;
+          sum += pv;
+        }
 #pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {
-          const float* v = s + blk * 64 + ch * 8;
+        for (int g = 0; g < 4; ++g) {
           uint4 q;
-          q.x = pack_bf16x2(v[0], v[1]);
-          q.y = pack_bf16x2(v[2], v[3]);
-          q.z = pack_bf16x2(v[4], v[5]);
-          q.w = pack_bf16x2(v[6], v[7]);
-          *reinterpret_cast<uint4*>(sP + blk * TILE_BYTES + swz128(r, ch)) = q;
+          q.x = pack_bf16x2(v[8 * g], v[8 * g + 1]);
+          q.y = pack_bf16x2(v[8 * g + 2], v[8 * g + 3]);
+          q.z = pack_bf16x2(v[8 * g + 4], v[8 * g + 5]);
+          q.w = pack_bf16x2(v[8 * g + 6], v[8 * g + 7]);
+          *reinterpret_cast<uint4*>(sP + swz128(r, cc * 4 + g)) = q;
         }
       }
+      l += sum;
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
+      if (lane == 0) {
+        mbar_arrive(s_free);
+        mbar_arrive(p_full);
+      }
     }
     if (ok && mbar_wait(pv_done, (nkv - 1) & 1, abort_flag, err)) {
       tc_fence_after();
@@ -288,25 +299,30 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, 128);
   }
 }
 
 // ------------------------------------------------------------------ backward
+constexpr int BT = 128;                 // keys per CTA = queries per inner tile
+constexpr int BT_BYTES = BT * 128;      // 128 rows x 64 bf16
+constexpr int kBwdSoftWarps = 8;        // two per TMEM lane quadrant, 64 columns each
+constexpr int kBwdThreads = 64 + 32 * kBwdSoftWarps;
+
 struct BwdSmem {
   static constexpr int K = 0;
-  static constexpr int V = K + TILE_BYTES;
-  static constexpr int Q = V + TILE_BYTES;       // 2 stages
-  static constexpr int DO = Q + 2 * TILE_BYTES;  // 2 stages
-  static constexpr int PT = DO + 2 * TILE_BYTES; // 2 blocks of 64 queries
-  static constexpr int DST = PT + 2 * TILE_BYTES;
-  static constexpr int LSE = DST + 2 * TILE_BYTES;  // 128 floats
-  static constexpr int DEL = LSE + 512;
-  static constexpr int BAR = DEL + 512;
+  static constexpr int V = K + BT_BYTES;
+  static constexpr int Q = V + BT_BYTES;         // 2 stages
+  static constexpr int DO = Q + 2 * BT_BYTES;    // 2 stages
+  static constexpr int PT = DO + 2 * BT_BYTES;   // 2 blocks of 64 queries
+  static constexpr int DST = PT + 2 * BT_BYTES;
+  static constexpr int LSE = DST + 2 * BT_BYTES; // 2 slots x 128 floats
+  static constexpr int DEL = LSE + 1024;         // 2 slots x 128 floats
+  static constexpr int BAR = DEL + 1024;
   static constexpr int TOTAL = BAR + 256 + 1024;
 };
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                 const AttnParams p) {
@@ -318,23 +334,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* q_full = bars + 1;   // [2]
   uint64_t* q_empty = bars + 3;  // [2]
   uint64_t* s_full = bars + 5;
-  uint64_t* s_free = bars + 6;
-  uint64_t* p_full = bars + 7;
-  uint64_t* dq_full = bars + 8;
-  uint64_t* dq_free = bars + 9;
-  uint64_t* ps_free = bars + 10;
-  uint64_t* fin = bars + 11;
+  uint64_t* p_full = bars + 6;
+  uint64_t* dq_full = bars + 7;
+  uint64_t* dq_free = bars + 8;
+  uint64_t* ps_free = bars + 9;
+  uint64_t* fin = bars + 10;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* sLse = reinterpret_cast<float*>(sm + BwdSmem::LSE);
   float* sDel = reinterpret_cast<float*>(sm + BwdSmem::DEL);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nt = (p.T + TILE - 1) / TILE;
+  const int nt = (p.T + BT - 1) / BT;
   const int kt = (int)blockIdx.x;
   const int bh = blockIdx.y;
   const int b = bh / p.H, h = bh - b * p.H;
-  const int k0 = kt * TILE;
+  const int k0 = kt * BT;
   const int nq = nt - kt;  // query tiles kt .. nt-1
   int* err = &g_attn_error;
 
@@ -345,10 +360,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&q_empty[s], 1);
     }
     mbar_init(s_full, 1);
-    mbar_init(s_free, 4);
-    mbar_init(p_full, 4);
+    mbar_init(p_full, kBwdSoftWarps);
     mbar_init(dq_full, 1);
-    mbar_init(dq_free, 4);
+    mbar_init(dq_free, kBwdSoftWarps);
     mbar_init(ps_free, 1);
     mbar_init(fin, 1);
     *abort_flag = 0;
@@ -364,16 +378,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      mbar_arrive_expect_tx(kv_full, 2 * TILE_BYTES);
+      mbar_arrive_expect_tx(kv_full, 2 * BT_BYTES);
       tma_load_4d(sm + BwdSmem::K, &tmK, kv_full, 0, k0, h, b);
       tma_load_4d(sm + BwdSmem::V, &tmV, kv_full, 0, k0, h, b);
       for (int it = 0; it < nq; ++it) {
         const int s = it & 1;
         if (!mbar_wait(&q_empty[s], ((it >> 1) & 1) ^ 1, abort_flag, err)) break;
-        mbar_arrive_expect_tx(&q_full[s], 2 * TILE_BYTES);
-        const int qq = (kt + it) * TILE;
-        tma_load_4d(sm + BwdSmem::Q + s * TILE_BYTES, &tmQ, &q_full[s], 0, qq, h, b);
-        tma_load_4d(sm + BwdSmem::DO + s * TILE_BYTES, &tmDO, &q_full[s], 0, qq, h, b);
+        mbar_arrive_expect_tx(&q_full[s], 2 * BT_BYTES);
+        const int qq = (kt + it) * BT;
+        tma_load_4d(sm + BwdSmem::Q + s * BT_BYTES, &tmQ, &q_full[s], 0, qq, h, b);
+        tma_load_4d(sm + BwdSmem::DO + s * BT_BYTES, &tmDO, &q_full[s], 0, qq, h, b);
       }
     }
   } else if (warp == 1) {
@@ -383,14 +397,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idMN = umma_idesc_bf16(128, 64, 1, 1);  // A MN-major, B MN-major
       const uint32_t sK = smem_u32(sm + BwdSmem::K), sV = smem_u32(sm + BwdSmem::V);
       const uint32_t sPt = smem_u32(sm + BwdSmem::PT), sdSt = smem_u32(sm + BwdSmem::DST);
-      bool ok = mbar_wait(kv_full, 0, abort_flag, err);
-      for (int it = 0; ok && it < nq; ++it) {
+      // S^T = K Q^T and dP^T = V dO^T for query tile `it` into TMEM.
+      auto issue_s = [&](int it) {
         const int s = it & 1;
-        const uint32_t sQ = smem_u32(sm + BwdSmem::Q + s * TILE_BYTES);
-        const uint32_t sDO = smem_u32(sm + BwdSmem::DO + s * TILE_BYTES);
-        if (!mbar_wait(&q_full[s], (it >> 1) & 1, abort_flag, err)) break;
-        if (it > 0 && !mbar_wait(s_free, (it - 1) & 1, abort_flag, err)) break;
-        tc_fence_after();
+        const uint32_t sQ = smem_u32(sm + BwdSmem::Q + s * BT_BYTES);
+        const uint32_t sDO = smem_u32(sm + BwdSmem::DO + s * BT_BYTES);
 #pragma unroll
         for (int k = 0; k < HD / 16; ++k) {
           umma_bf16(tS, umma_smem_desc(sK + k * 32, 16, 1024), umma_smem_desc(sQ + k * 32, 16, 1024),
@@ -399,24 +410,42 @@ __global__ void __launch_bounds__(kThreads, 1)
                     umma_smem_desc(sDO + k * 32, 16, 1024), idS, k > 0);
         }
         umma_commit(s_full);
+      };
+      bool ok = mbar_wait(kv_full, 0, abort_flag, err) && mbar_wait(&q_full[0], 0, abort_flag, err);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0);
+      }
+      for (int it = 0; ok && it < nq; ++it) {
+        const int s = it & 1;
+        const uint32_t sQ = smem_u32(sm + BwdSmem::Q + s * BT_BYTES);
+        const uint32_t sDO = smem_u32(sm + BwdSmem::DO + s * BT_BYTES);
         if (!mbar_wait(p_full, it & 1, abort_flag, err)) break;
+        tc_fence_after();
+        // Scores of the next query tile first, so the softmax warps can start
+        // on them while dQ/dV/dK of this tile run.
+        if (it + 1 < nq) {
+          if (!mbar_wait(&q_full[(it + 1) & 1], ((it + 1) >> 1) & 1, abort_flag, err)) break;
+          tc_fence_after();
+          issue_s(it + 1);
+        }
         if (it > 0 && !mbar_wait(dq_free, (it - 1) & 1, abort_flag, err)) break;
         tc_fence_after();
-        // dQ = dS · K: A = dSᵀ tile read MN-major (M = queries in two 64-wide
+        // dQ = dS · K: A = dSᵀ read MN-major (M = queries in two 64-wide
         // blocks 16 KB apart), B = K tile MN-major (N = head dim).
 #pragma unroll
-        for (int k = 0; k < TILE / 16; ++k)
-          umma_bf16(tDQ, umma_smem_desc(sdSt + k * 2048, TILE_BYTES, 1024),
-                    umma_smem_desc(sK + k * 2048, TILE_BYTES, 1024), idMN, k > 0);
+        for (int k = 0; k < BT / 16; ++k)
+          umma_bf16(tDQ, umma_smem_desc(sdSt + k * 2048, BT_BYTES, 1024),
+                    umma_smem_desc(sK + k * 2048, BT_BYTES, 1024), idMN, k > 0);
         umma_commit(dq_full);
         // dV += Pᵀ · dO ; dK += dSᵀ · Q  (A K-major over queries, B MN-major)
 #pragma unroll
-        for (int k = 0; k < TILE / 16; ++k) {
-          const uint32_t aoff = (k >> 2) * TILE_BYTES + (k & 3) * 32;
+        for (int k = 0; k < BT / 16; ++k) {
+          const uint32_t aoff = (k >> 2) * BT_BYTES + (k & 3) * 32;
           umma_bf16(tDV, umma_smem_desc(sPt + aoff, 16, 1024),
-                    umma_smem_desc(sDO + k * 2048, TILE_BYTES, 1024), idKN, (it > 0 || k > 0));
+                    umma_smem_desc(sDO + k * 2048, BT_BYTES, 1024), idKN, (it > 0 || k > 0));
           umma_bf16(tDK, umma_smem_desc(sdSt + aoff, 16, 1024),
-                    umma_smem_desc(sQ + k * 2048, TILE_BYTES, 1024), idKN, (it > 0 || k > 0));
+                    umma_smem_desc(sQ + k * 2048, BT_BYTES, 1024), idKN, (it > 0 || k > 0));
         }
         umma_commit(ps_free);
         umma_commit(&q_empty[s]);
@@ -424,126 +453,142 @@ __global__ void __launch_bounds__(kThreads, 1)
       umma_commit(fin);
     }
   } else {
+    // 8 softmax warps: warp w reads TMEM lanes of quadrant w % 4 (key rows)
+    // and the query columns [64*half, 64*half + 64).
     const int quad = warp & 3;
-    const int r = quad * 32 + lane;  // key row of this CTA (and query row for dQ)
+    const int half = (warp - 2) >> 2;
+    const int r = quad * 32 + lane;
     const int key = k0 + r;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const float c = p.scale * kLog2e;
-    const int tid = threadIdx.x - 64;
-    uint8_t* sPt = sm + BwdSmem::PT;
-    uint8_t* sdSt = sm + BwdSmem::DST;
+    const int tid = threadIdx.x - 64;  // 0..255
+    uint8_t* sPt = sm + BwdSmem::PT + half * BT_BYTES;
+    uint8_t* sdSt = sm + BwdSmem::DST + half * BT_BYTES;
     const float* Lg = p.lse + (int64_t)bh * p.T;
     const float* Dg = p.delta + (int64_t)bh * p.T;
+    // statistics of query tile `it` -> slot it % 2 (threads 0-127: lse, 128-255: delta)
+    auto fetch = [&](int it) -> float {
+      const int t = (kt + it) * BT + (tid & 127);
+      if (tid < 128) return (t < p.T) ? Lg[t] * kLog2e : INFINITY;  // rows past T: P = 0
+      return (t < p.T) ? Dg[t] : 0.f;
+    };
+    auto stash = [&](int it, float v) {
+      float* dst = (tid < 128 ? sLse : sDel) + (it & 1) * 128 + (tid & 127);
+      *dst = v;
+    };
+    stash(0, fetch(0));
+    float pending = (nq > 1) ? fetch(1) : 0.f;
     bool ok = true;
     for (int it = 0; it < nq && ok; ++it) {
-      const int qq0 = (kt + it) * TILE;
-      named_bar_sync(1, 128);  // previous iteration's readers of sLse/sDel are done
-      {
-        const int t = qq0 + tid;
-        sLse[tid] = (t < p.T) ? Lg[t] * kLog2e : INFINITY;  // rows past T: P = 0
-        sDel[tid] = (t < p.T) ? Dg[t] : 0.f;
-      }
-      named_bar_sync(1, 128);
+      named_bar_sync(1, 32 * kBwdSoftWarps);  // slot it % 2 is complete and visible
       if (!mbar_wait(s_full, it & 1, abort_flag, err)) {
         ok = false;
         break;
       }
-      if (it > 0 && !mbar_wait(ps_free, (it - 1) & 1, abort_flag, err)) {
-        ok = false;
-        break;
-      }
       tc_fence_after();
+      const float* lq = sLse + (it & 1) * 128 + half * 64;
+      const float* dl = sDel + (it & 1) * 128 + half * 64;
+      const int qq0 = (kt + it) * BT;
       const bool diag = (it == 0);
-#pragma unroll 1
-      for (int cc = 0; cc < TILE / 32; ++cc) {
-        float sv[32], dp[32];
-        tmem_ld32(tS + lane_off + cc * 32, sv);
-        tmem_ld32(tDP + lane_off + cc * 32, dp);
+      // Pᵀ and dSᵀ for this warp's 64 query columns, packed to bf16 in registers.
+      uint32_t pk[32], dk[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int qc = cc * 32 + i;
-          float pv = ex2(sv[i] * c - sLse[qc]);
-          if (diag && r > qc) pv = 0.f;
-          sv[i] = pv;
-          dp[i] = pv * (dp[i] - sDel[qc]);
-        }
-        const int blk = cc >> 1;
+      for (int cc = 0; cc < 4; ++cc) {
+        float sv[16], dp[16];
+        tmem_ld16(tS + lane_off + half * 64 + cc * 16, sv);
+        tmem_ld16(tDP + lane_off + half * 64 + cc * 16, dp);
 #pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          const int ch = (cc & 1) * 4 + g;
-          uint4 qa, qb;
-          qa.x = pack_bf16x2(sv[8 * g], sv[8 * g + 1]);
-          qa.y = pack_bf16x2(sv[8 * g + 2], sv[8 * g + 3]);
-          qa.z = pack_bf16x2(sv[8 * g + 4], sv[8 * g + 5]);
-          qa.w = pack_bf16x2(sv[8 * g + 6], sv[8 * g + 7]);
-          qb.x = pack_bf16x2(dp[8 * g], dp[8 * g + 1]);
-          qb.y = pack_bf16x2(dp[8 * g + 2], dp[8 * g + 3]);
-          qb.z = pack_bf16x2(dp[8 * g + 4], dp[8 * g + 5]);
-          qb.w = pack_bf16x2(dp[8 * g + 6], dp[8 * g + 7]);
-          *reinterpret_cast<uint4*>(sPt + blk * TILE_BYTES + swz128(r, ch)) = qa;
-          *reinterpret_cast<uint4*>(sdSt + blk * TILE_BYTES + swz128(r, ch)) = qb;
+        for (int i = 0; i < 16; i += 2) {
+          const int qc = cc * 16 + i;
+          float p0 = ex2(fmaf(sv[i], c, -lq[qc]));
+          float p1 = ex2(fmaf(sv[i + 1], c, -lq[qc + 1]));
+          if (diag && r > half * 64 + qc) p0 = 0.f;
+          if (diag && r > half * 64 + qc + 1) p1 = 0.f;
+          pk[cc * 8 + i / 2] = pack_bf16x2(p0, p1);
+          dk[cc * 8 + i / 2] = pack_bf16x2(p0 * (dp[i] - dl[qc]), p1 * (dp[i + 1] - dl[qc + 1]));
         }
+      }
+      // prefetched statistics of the tile after next go into the freed slot
+      if (it + 1 < nq) stash(it + 1, pending);
+      if (it + 2 < nq) pending = fetch(it + 2);
+      // dQ of the previous tile: lane r of TMEM holds query (qq0 - BT) + r.
+      if (it > 0) {
+        if (!mbar_wait(dq_full, (it - 1) & 1, abort_flag, err)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        float v[32];
+        tmem_ld32(tDQ + lane_off + half * 32, v);
+        const int qrow = qq0 - BT + r;
+        if (qrow < p.T) {
+          float* dst = p.dq_acc + ((int64_t)bh * p.T + qrow) * HD + half * 32;
+#pragma unroll
+          for (int g = 0; g < 8; ++g)
+            atomicAdd(reinterpret_cast<float4*>(dst + 4 * g),
+                      make_float4(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]));
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(dq_free);
+        if (!mbar_wait(ps_free, (it - 1) & 1, abort_flag, err)) {
+          ok = false;
+          break;
+        }
+      }
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) {
+        *reinterpret_cast<uint4*>(sPt + swz128(r, ch)) =
+            make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
+        *reinterpret_cast<uint4*>(sdSt + swz128(r, ch)) =
+            make_uint4(dk[4 * ch], dk[4 * ch + 1], dk[4 * ch + 2], dk[4 * ch + 3]);
       }
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(s_free);
-        mbar_arrive(p_full);
-      }
-      // dQ rows of this query tile: lane r of TMEM holds query qq0 + r.
-      if (!mbar_wait(dq_full, it & 1, abort_flag, err)) {
-        ok = false;
-        break;
-      }
+      if (lane == 0) mbar_arrive(p_full);
+    }
+    // dQ of the last tile, then dK and dV.
+    if (ok && mbar_wait(dq_full, (nq - 1) & 1, abort_flag, err)) {
       tc_fence_after();
-      const int qrow = qq0 + r;
-      float* dst = p.dq_acc + ((int64_t)bh * p.T + qrow) * HD;
+      float v[32];
+      tmem_ld32(tDQ + lane_off + half * 32, v);
+      const int qrow = (kt + nq - 1) * BT + r;
+      if (qrow < p.T) {
+        float* dst = p.dq_acc + ((int64_t)bh * p.T + qrow) * HD + half * 32;
 #pragma unroll
-      for (int cc = 0; cc < HD / 32; ++cc) {
-        float v[32];
-        tmem_ld32(tDQ + lane_off + cc * 32, v);
-        if (qrow < p.T) {
-#pragma unroll
-          for (int g = 0; g < 8; ++g)
-            atomicAdd(reinterpret_cast<float4*>(dst + cc * 32 + 4 * g),
-                      make_float4(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]));
-        }
+        for (int g = 0; g < 8; ++g)
+          atomicAdd(reinterpret_cast<float4*>(dst + 4 * g),
+                    make_float4(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]));
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(dq_free);
     }
     if (ok && mbar_wait(fin, 0, abort_flag, err)) {
       tc_fence_after();
-      bf16* dkrow = p.dk + b * p.sb + h * p.sh + (int64_t)key * p.st;
-      bf16* dvrow = p.dv + b * p.sb + h * p.sh + (int64_t)key * p.st;
+      float kk[32], vv[32];
+      // warp-collective TMEM loads stay outside the per-row guard
+      tmem_ld32(tDK + lane_off + half * 32, kk);
+      tmem_ld32(tDV + lane_off + half * 32, vv);
+      if (key < p.T) {
+        bf16* dkrow = p.dk + b * p.sb + h * p.sh + (int64_t)key * p.st + half * 32;
+        bf16* dvrow = p.dv + b * p.sb + h * p.sh + (int64_t)key * p.st + half * 32;
 #pragma unroll
-      for (int cc = 0; cc < HD / 32; ++cc) {
-        float kk[32], vv[32];
-        // warp-collective TMEM loads stay outside the per-row guard
-        tmem_ld32(tDK + lane_off + cc * 32, kk);
-        tmem_ld32(tDV + lane_off + cc * 32, vv);
-        if (key < p.T) {
+        for (int g = 0; g < 4; ++g) {
+          float* kv = kk + 8 * g;
 #pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            float* kv = kk + 8 * g;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) kv[i] *= p.scale;
-            if (p.rcos) rope_back(kv, p.rcos, p.rsin, key, cc * 4 + g);
-            uint4 qk, qv;
-            qk.x = pack_bf16x2(kv[0], kv[1]);
-            qk.y = pack_bf16x2(kv[2], kv[3]);
-            qk.z = pack_bf16x2(kv[4], kv[5]);
-            qk.w = pack_bf16x2(kv[6], kv[7]);
-            const float* w = vv + 8 * g;
-            qv.x = pack_bf16x2(w[0], w[1]);
-            qv.y = pack_bf16x2(w[2], w[3]);
-            qv.z = pack_bf16x2(w[4], w[5]);
-            qv.w = pack_bf16x2(w[6], w[7]);
-            *reinterpret_cast<uint4*>(dkrow + cc * 32 + 8 * g) = qk;
-            *reinterpret_cast<uint4*>(dvrow + cc * 32 + 8 * g) = qv;
-          }
+          for (int i = 0; i < 8; ++i) kv[i] *= p.scale;
+          if (p.rcos) rope_back(kv, p.rcos, p.rsin, key, half * 4 + g);
+          uint4 qk, qv;
+          qk.x = pack_bf16x2(kv[0], kv[1]);
+          qk.y = pack_bf16x2(kv[2], kv[3]);
+          qk.z = pack_bf16x2(kv[4], kv[5]);
+          qk.w = pack_bf16x2(kv[6], kv[7]);
+          const float* w = vv + 8 * g;
+          qv.x = pack_bf16x2(w[0], w[1]);
+          qv.y = pack_bf16x2(w[2], w[3]);
+          qv.z = pack_bf16x2(w[4], w[5]);
+          qv.w = pack_bf16x2(w[6], w[7]);
+          *reinterpret_cast<uint4*>(dkrow + 8 * g) = qk;
+          *reinterpret_cast<uint4*>(dvrow + 8 * g) = qv;
         }
       }
     }
@@ -632,14 +677,14 @@ static EncodeTiledFn encode_fn() {
 }
 
 // 4-D map over a [b, t, h, e] tensor with element strides (sb, st, sh), box
-// 64 (e) x 128 (t), 128-byte swizzle.
+// 64 (e) x box_rows (t), 128-byte swizzle.
 static bool make_map4(CUtensorMap* m, const void* base, int B, int H, int T, int64_t sb,
-                      int64_t sh, int64_t st) {
+                      int64_t sh, int64_t st, int box_rows) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return false;
   cuuint64_t dims[4] = {HD, (cuuint64_t)T, (cuuint64_t)H, (cuuint64_t)B};
   cuuint64_t strides[3] = {(cuuint64_t)st * 2, (cuuint64_t)sh * 2, (cuuint64_t)sb * 2};
-  cuuint32_t box[4] = {HD, TILE, 1, 1};
+  cuuint32_t box[4] = {HD, (cuuint32_t)box_rows, 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box,
              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -675,9 +720,9 @@ extern "C" int gptb200_attention_fwd(const void* q, const void* k, const void* v
   if (!o || !lse || !(softmax_scale > 0.f)) return GPTB200_EINVAL;
   if (reinterpret_cast<uintptr_t>(o) & 15) return GPTB200_ESHAPE;
   CUtensorMap mq, mk, mv;
-  if (!make_map4(&mq, q, (int)batch, (int)heads, (int)seq, stride_b, stride_h, stride_t) ||
-      !make_map4(&mk, k, (int)batch, (int)heads, (int)seq, stride_b, stride_h, stride_t) ||
-      !make_map4(&mv, v, (int)batch, (int)heads, (int)seq, stride_b, stride_h, stride_t))
+  if (!make_map4(&mq, q, (int)batch, (int)heads, (int)seq, stride_b, stride_h, stride_t, FQ) ||
+      !make_map4(&mk, k, (int)batch, (int)heads, (int)seq, stride_b, stride_h, stride_t, FK) ||
+      !make_map4(&mv, v, (int)batch, (int)heads, (int)seq, stride_b, stride_h, stride_t, FK))
     return GPTB200_ESHAPE;
   AttnParams p = {};
   p.B = (int)batch;
@@ -698,7 +743,7 @@ extern "C" int gptb200_attention_fwd(const void* q, const void* k, const void* v
     if (e != cudaSuccess) return -static_cast<int>(e);
     if (dev < 64) cfg[dev] = true;
   }
-  dim3 grid((unsigned)((seq + TILE - 1) / TILE), (unsigned)(batch * heads));
+  dim3 grid((unsigned)((seq + FQ - 1) / FQ), (unsigned)(batch * heads));
   attn_fwd_tc<<<grid, kThreads, FwdSmem::TOTAL, reinterpret_cast<cudaStream_t>(stream)>>>(mq, mk,
                                                                                           mv, p);
   GPTB200_CHECK_LAUNCH();
@@ -731,10 +776,10 @@ extern "C" int gptb200_attention_bwd(const void* q, const void* k, const void* v
   auto st = reinterpret_cast<cudaStream_t>(stream);
   const int B = (int)batch, H = (int)heads, T = (int)seq;
   CUtensorMap mq, mk, mv, mdo;
-  if (!make_map4(&mq, q, B, H, T, stride_b, stride_h, stride_t) ||
-      !make_map4(&mk, k, B, H, T, stride_b, stride_h, stride_t) ||
-      !make_map4(&mv, v, B, H, T, stride_b, stride_h, stride_t) ||
-      !make_map4(&mdo, dout, B, H, T, o_stride_b, o_stride_h, o_stride_t))
+  if (!make_map4(&mq, q, B, H, T, stride_b, stride_h, stride_t, BT) ||
+      !make_map4(&mk, k, B, H, T, stride_b, stride_h, stride_t, BT) ||
+      !make_map4(&mv, v, B, H, T, stride_b, stride_h, stride_t, BT) ||
+      !make_map4(&mdo, dout, B, H, T, o_stride_b, o_stride_h, o_stride_t, BT))
     return GPTB200_ESHAPE;
   const int64_t rows = batch * heads * seq;
   float* delta = reinterpret_cast<float*>(workspace);
@@ -768,8 +813,8 @@ extern "C" int gptb200_attention_bwd(const void* q, const void* k, const void* v
     if (e != cudaSuccess) return -static_cast<int>(e);
     if (dev < 64) cfg[dev] = true;
   }
-  dim3 grid((unsigned)((seq + TILE - 1) / TILE), (unsigned)(batch * heads));
-  attn_bwd_tc<<<grid, kThreads, BwdSmem::TOTAL, st>>>(mq, mk, mv, mdo, p);
+  dim3 grid((unsigned)((seq + BT - 1) / BT), (unsigned)(batch * heads));
+  attn_bwd_tc<<<grid, kBwdThreads, BwdSmem::TOTAL, st>>>(mq, mk, mv, mdo, p);
   GPTB200_CHECK_LAUNCH();
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
