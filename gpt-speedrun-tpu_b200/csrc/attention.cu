@@ -312,14 +312,14 @@ constexpr int kBwdThreads = 64 + 32 * kBwdSoftWarps;
 struct BwdSmem {
   static constexpr int K = 0;
   static constexpr int V = K + BT_BYTES;
-  static constexpr int Q = V + BT_BYTES;         // 2 stages
-  static constexpr int DO = Q + 2 * BT_BYTES;    // 2 stages
-  static constexpr int PT = DO + 2 * BT_BYTES;   // 2 blocks of 64 queries
-  static constexpr int DST = PT + 2 * BT_BYTES;
-  static constexpr int LSE = DST + 2 * BT_BYTES; // 2 slots x 128 floats
-  static constexpr int DEL = LSE + 1024;         // 2 slots x 128 floats
-  static constexpr int BAR = DEL + 1024;
-  static constexpr int TOTAL = BAR + 256 + 1024;
+  static constexpr int Q = V + BT_BYTES;          // 2 stages
+  static constexpr int DO = Q + 2 * BT_BYTES;     // 2 stages
+  static constexpr int PT = DO + 2 * BT_BYTES;    // 2 buffers x 2 blocks of 64 queries
+  static constexpr int DST = PT + 4 * BT_BYTES;   // 2 buffers x 2 blocks
+  static constexpr int LSE = DST + 4 * BT_BYTES;  // 128 floats
+  static constexpr int DEL = LSE + 512;           // 128 floats
+  static constexpr int BAR = DEL + 512;
+  static constexpr int TOTAL = BAR + 256 + 1023;
 };
 
 __global__ void __launch_bounds__(kBwdThreads, 1)
@@ -337,8 +337,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint64_t* p_full = bars + 6;
   uint64_t* dq_full = bars + 7;
   uint64_t* dq_free = bars + 8;
-  uint64_t* ps_free = bars + 9;
-  uint64_t* fin = bars + 10;
+  uint64_t* ps_free = bars + 9;  // [2]: P/dS buffer b consumed by its dV/dK MMAs
+  uint64_t* fin = bars + 11;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* sLse = reinterpret_cast<float*>(sm + BwdSmem::LSE);
@@ -358,12 +358,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     for (int s = 0; s < 2; ++s) {
       mbar_init(&q_full[s], 1);
       mbar_init(&q_empty[s], 1);
+      mbar_init(&ps_free[s], 1);
     }
     mbar_init(s_full, 1);
     mbar_init(p_full, kBwdSoftWarps);
     mbar_init(dq_full, 1);
     mbar_init(dq_free, kBwdSoftWarps);
-    mbar_init(ps_free, 1);
     mbar_init(fin, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -396,7 +396,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       constexpr uint32_t idKN = umma_idesc_bf16(128, 64, 0, 1);  // A K-major, B MN-major
       constexpr uint32_t idMN = umma_idesc_bf16(128, 64, 1, 1);  // A MN-major, B MN-major
       const uint32_t sK = smem_u32(sm + BwdSmem::K), sV = smem_u32(sm + BwdSmem::V);
-      const uint32_t sPt = smem_u32(sm + BwdSmem::PT), sdSt = smem_u32(sm + BwdSmem::DST);
       // S^T = K Q^T and dP^T = V dO^T for query tile `it` into TMEM.
       auto issue_s = [&](int it) {
         const int s = it & 1;
@@ -420,6 +419,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const int s = it & 1;
         const uint32_t sQ = smem_u32(sm + BwdSmem::Q + s * BT_BYTES);
         const uint32_t sDO = smem_u32(sm + BwdSmem::DO + s * BT_BYTES);
+        const uint32_t sPt = smem_u32(sm + BwdSmem::PT + s * 2 * BT_BYTES);
+        const uint32_t sdSt = smem_u32(sm + BwdSmem::DST + s * 2 * BT_BYTES);
         if (!mbar_wait(p_full, it & 1, abort_flag, err)) break;
         tc_fence_after();
         // Scores of the next query tile first, so the softmax warps can start
@@ -447,7 +448,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           umma_bf16(tDK, umma_smem_desc(sdSt + aoff, 16, 1024),
                     umma_smem_desc(sQ + k * 2048, BT_BYTES, 1024), idKN, (it > 0 || k > 0));
         }
-        umma_commit(ps_free);
+        umma_commit(&ps_free[s]);
         umma_commit(&q_empty[s]);
       }
       umma_commit(fin);
@@ -462,98 +463,22 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const float c = p.scale * kLog2e;
     const int tid = threadIdx.x - 64;  // 0..255
-    uint8_t* sPt = sm + BwdSmem::PT + half * BT_BYTES;
-    uint8_t* sdSt = sm + BwdSmem::DST + half * BT_BYTES;
     const float* Lg = p.lse + (int64_t)bh * p.T;
     const float* Dg = p.delta + (int64_t)bh * p.T;
-    // statistics of query tile `it` -> slot it % 2 (threads 0-127: lse, 128-255: delta)
+    // statistics of query tile `it` (threads 0-127: lse, 128-255: delta)
     auto fetch = [&](int it) -> float {
       const int t = (kt + it) * BT + (tid & 127);
       if (tid < 128) return (t < p.T) ? Lg[t] * kLog2e : INFINITY;  // rows past T: P = 0
       return (t < p.T) ? Dg[t] : 0.f;
     };
-    auto stash = [&](int it, float v) {
-      float* dst = (tid < 128 ? sLse : sDel) + (it & 1) * 128 + (tid & 127);
-      *dst = v;
-    };
-    stash(0, fetch(0));
-    float pending = (nq > 1) ? fetch(1) : 0.f;
+    float pending = fetch(0);
     bool ok = true;
-    for (int it = 0; it < nq && ok; ++it) {
-      named_bar_sync(1, 32 * kBwdSoftWarps);  // slot it % 2 is complete and visible
-      if (!mbar_wait(s_full, it & 1, abort_flag, err)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const float* lq = sLse + (it & 1) * 128 + half * 64;
-      const float* dl = sDel + (it & 1) * 128 + half * 64;
-      const int qq0 = (kt + it) * BT;
-      const bool diag = (it == 0);
-      // Pᵀ and dSᵀ for this warp's 64 query columns, packed to bf16 in registers.
-      uint32_t pk[32], dk[32];
-#pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        float sv[16], dp[16];
-        tmem_ld16(tS + lane_off + half * 64 + cc * 16, sv);
-        tmem_ld16(tDP + lane_off + half * 64 + cc * 16, dp);
-#pragma unroll
-        for (int i = 0; i < 16; i += 2) {
-          const int qc = cc * 16 + i;
-          float p0 = ex2(fmaf(sv[i], c, -lq[qc]));
-          float p1 = ex2(fmaf(sv[i + 1], c, -lq[qc + 1]));
-          if (diag && r > half * 64 + qc) p0 = 0.f;
-          if (diag && r > half * 64 + qc + 1) p1 = 0.f;
-          pk[cc * 8 + i / 2] = pack_bf16x2(p0, p1);
-          dk[cc * 8 + i / 2] = pack_bf16x2(p0 * (dp[i] - dl[qc]), p1 * (dp[i + 1] - dl[qc + 1]));
-        }
-      }
-      // prefetched statistics of the tile after next go into the freed slot
-      if (it + 1 < nq) stash(it + 1, pending);
-      if (it + 2 < nq) pending = fetch(it + 2);
-      // dQ of the previous tile: lane r of TMEM holds query (qq0 - BT) + r.
-      if (it > 0) {
-        if (!mbar_wait(dq_full, (it - 1) & 1, abort_flag, err)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        float v[32];
-        tmem_ld32(tDQ + lane_off + half * 32, v);
-        const int qrow = qq0 - BT + r;
-        if (qrow < p.T) {
-          float* dst = p.dq_acc + ((int64_t)bh * p.T + qrow) * HD + half * 32;
-#pragma unroll
-          for (int g = 0; g < 8; ++g)
-            atomicAdd(reinterpret_cast<float4*>(dst + 4 * g),
-                      make_float4(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]));
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(dq_free);
-        if (!mbar_wait(ps_free, (it - 1) & 1, abort_flag, err)) {
-          ok = false;
-          break;
-        }
-      }
-#pragma unroll
-      for (int ch = 0; ch < 8; ++ch) {
-        *reinterpret_cast<uint4*>(sPt + swz128(r, ch)) =
-            make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
-        *reinterpret_cast<uint4*>(sdSt + swz128(r, ch)) =
-            make_uint4(dk[4 * ch], dk[4 * ch + 1], dk[4 * ch + 2], dk[4 * ch + 3]);
-      }
-      fence_proxy_async_smem();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
-    }
-    // dQ of the last tile, then dK and dV.
-    if (ok && mbar_wait(dq_full, (nq - 1) & 1, abort_flag, err)) {
-      tc_fence_after();
+    // dQ rows of query tile `it` (TMEM lane r = query (kt+it)*BT + r) into the
+    // fp32 accumulator.
+    auto flush_dq = [&](int it) {
       float v[32];
       tmem_ld32(tDQ + lane_off + half * 32, v);
-      const int qrow = (kt + nq - 1) * BT + r;
+      const int qrow = (kt + it) * BT + r;
       if (qrow < p.T) {
         float* dst = p.dq_acc + ((int64_t)bh * p.T + qrow) * HD + half * 32;
 #pragma unroll
@@ -561,6 +486,72 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           atomicAdd(reinterpret_cast<float4*>(dst + 4 * g),
                     make_float4(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]));
       }
+    };
+    for (int it = 0; it < nq && ok; ++it) {
+      named_bar_sync(1, 32 * kBwdSoftWarps);  // all reads of the previous tile's stats done
+      (tid < 128 ? sLse : sDel)[tid & 127] = pending;
+      named_bar_sync(1, 32 * kBwdSoftWarps);
+      if (it + 1 < nq) pending = fetch(it + 1);
+      const int s = it & 1;
+      uint8_t* sPt = sm + BwdSmem::PT + s * 2 * BT_BYTES + half * BT_BYTES;
+      uint8_t* sdSt = sm + BwdSmem::DST + s * 2 * BT_BYTES + half * BT_BYTES;
+      if (!mbar_wait(s_full, it & 1, abort_flag, err)) {
+        ok = false;
+        break;
+      }
+      // the P/dS buffer of this tile was last read by the MMAs of tile it-2
+      if (it >= 2 && !mbar_wait(&ps_free[s], ((it >> 1) + 1) & 1, abort_flag, err)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const float* lq = sLse + half * 64;
+      const float* dl = sDel + half * 64;
+      const bool diag = (it == 0);
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        float sv[16], dp[16];
+        tmem_ld16(tS + lane_off + half * 64 + cc * 16, sv);
+        tmem_ld16(tDP + lane_off + half * 64 + cc * 16, dp);
+        uint32_t pk[8], dk[8];
+#pragma unroll
+        for (int i = 0; i < 16; i += 2) {
+          const int qc = cc * 16 + i;
+          float p0 = ex2(fmaf(sv[i], c, -lq[qc]));
+          float p1 = ex2(fmaf(sv[i + 1], c, -lq[qc + 1]));
+          if (diag && r > half * 64 + qc) p0 = 0.f;
+          if (diag && r > half * 64 + qc + 1) p1 = 0.f;
+          pk[i / 2] = pack_bf16x2(p0, p1);
+          dk[i / 2] = pack_bf16x2(p0 * (dp[i] - dl[qc]), p1 * (dp[i + 1] - dl[qc + 1]));
+        }
+        *reinterpret_cast<uint4*>(sPt + swz128(r, 2 * cc)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        *reinterpret_cast<uint4*>(sPt + swz128(r, 2 * cc + 1)) =
+            make_uint4(pk[4], pk[5], pk[6], pk[7]);
+        *reinterpret_cast<uint4*>(sdSt + swz128(r, 2 * cc)) = make_uint4(dk[0], dk[1], dk[2], dk[3]);
+        *reinterpret_cast<uint4*>(sdSt + swz128(r, 2 * cc + 1)) =
+            make_uint4(dk[4], dk[5], dk[6], dk[7]);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+      // dQ of the previous tile (its MMA ran behind this tile's scores).
+      if (it > 0) {
+        if (!mbar_wait(dq_full, (it - 1) & 1, abort_flag, err)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        flush_dq(it - 1);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(dq_free);
+      }
+    }
+    // dQ of the last tile, then dK and dV.
+    if (ok && mbar_wait(dq_full, (nq - 1) & 1, abort_flag, err)) {
+      tc_fence_after();
+      flush_dq(nq - 1);
     }
     if (ok && mbar_wait(fin, 0, abort_flag, err)) {
       tc_fence_after();
@@ -601,24 +592,40 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   }
 }
 
-// delta[bh, t] = sum_e dO * O, and zero the dQ accumulator row. One warp per row.
+// delta[bh, t] = sum_e dO * O, and zero the dQ accumulator row. Eight lanes
+// per row (16-byte loads), four rows per warp.
 __global__ void attn_delta_kernel(const bf16* __restrict__ o, const bf16* __restrict__ dout,
                                   int64_t osb, int64_t osh, int64_t ost, int B, int H, int T,
                                   float* __restrict__ delta, float* __restrict__ dq_acc) {
   const int64_t rows = (int64_t)B * H * T;
-  const int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (r >= rows) return;
-  const int64_t bh = r / T;
-  const int t = (int)(r - bh * T);
+  const int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 3;
+  const int seg = threadIdx.x & 7;
+  const bool valid = r < rows;  // no early return: the 8-lane shuffles below span the warp
+  const int64_t rr = valid ? r : 0;
+  const int64_t bh = rr / T;
+  const int t = (int)(rr - bh * T);
   const int b = (int)(bh / H), h = (int)(bh - (int64_t)b * H);
-  const int64_t off = b * osb + h * osh + (int64_t)t * ost + lane * 2;
-  float o0, o1, g0, g1;
-  unpack_bf16x2(*reinterpret_cast<const uint32_t*>(o + off), o0, o1);
-  unpack_bf16x2(*reinterpret_cast<const uint32_t*>(dout + off), g0, g1);
-  float s = warp_sum(o0 * g0 + o1 * g1);
-  if (lane == 0) delta[r] = s;
-  reinterpret_cast<float2*>(dq_acc + r * HD)[lane] = make_float2(0.f, 0.f);
+  const int64_t off = b * osb + h * osh + (int64_t)t * ost + seg * 8;
+  const uint4 qo = *reinterpret_cast<const uint4*>(o + off);
+  const uint4 qg = *reinterpret_cast<const uint4*>(dout + off);
+  const uint32_t* wo = &qo.x;
+  const uint32_t* wg = &qg.x;
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float o0, o1, g0, g1;
+    unpack_bf16x2(wo[j], o0, o1);
+    unpack_bf16x2(wg[j], g0, g1);
+    s += o0 * g0 + o1 * g1;
+  }
+  s += __shfl_xor_sync(0xffffffffu, s, 1);
+  s += __shfl_xor_sync(0xffffffffu, s, 2);
+  s += __shfl_xor_sync(0xffffffffu, s, 4);
+  if (!valid) return;
+  if (seg == 0) delta[r] = s;
+  float4* z = reinterpret_cast<float4*>(dq_acc + r * HD + seg * 8);
+  z[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+  z[1] = make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
 // dq = bf16(scale * dq_acc), rotated back by RoPE when tables are given.
@@ -785,7 +792,7 @@ extern "C" int gptb200_attention_bwd(const void* q, const void* k, const void* v
   float* delta = reinterpret_cast<float*>(workspace);
   float* dq_acc = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) +
                                            (rows * 4 + 255) / 256 * 256);
-  attn_delta_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(
+  attn_delta_kernel<<<(unsigned)((rows * 8 + 255) / 256), 256, 0, st>>>(
       reinterpret_cast<const bf16*>(o), reinterpret_cast<const bf16*>(dout), o_stride_b,
       o_stride_h, o_stride_t, B, H, T, delta, dq_acc);
   GPTB200_CHECK_LAUNCH();

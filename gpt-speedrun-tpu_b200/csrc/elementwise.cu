@@ -161,8 +161,8 @@ template <int CH>
 static int rms_bwd_launch(const bf16* x, const bf16* s, const float* rstd, const bf16* dy,
                           const bf16* dxi, bf16* dxo, float* dscale, int64_t rows, int d,
                           cudaStream_t st) {
-  const int threads = 256;
-  int64_t blocks = std::min<int64_t>((rows + 7) / 8, (int64_t)sms() * 2);
+  const int threads = 128;
+  int64_t blocks = std::min<int64_t>((rows + 3) / 4, (int64_t)sms() * 8);
   size_t smem = (size_t)(threads / 32) * d * sizeof(float);
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(rms_bwd_kernel<CH>,

@@ -3,21 +3,25 @@
 //   C[M,N] = epilogue( sum_k A[m,k] B[n,k] )   bf16 operands, fp32 accumulation in TMEM
 //
 // One CTA per SM loops over output tiles (128 x BN) and, for weight gradients,
-// over K splits. Roles inside the CTA (192 threads):
+// over K splits. Roles inside the CTA (576 threads):
 //   warp 0  lane 0 : TMA producer. Each pipeline stage holds a 128x64 A tile and
 //                    a BNx64 B tile in 128-byte-swizzled shared memory. K-major
 //                    operands are one box; MN-major operands are 64-wide boxes.
 //   warp 1  lane 0 : MMA issuer. 4 tcgen05.mma (K=16 each) per stage into one of
 //                    two TMEM accumulators (2 x BN fp32 columns), so the
 //                    epilogue of tile i overlaps the main loop of tile i+1.
-//   warps 2-5      : epilogue. Each warp owns the 32 TMEM lanes (= tile rows) of
-//                    its quadrant (warp % 4), reads 32 columns at a time with
-//                    tcgen05.ld and applies the fused epilogue (bias, residual,
-//                    GELU, dGELU, fp32 store or atomic add, and the two
-//                    cross-entropy epilogues used by lce.cu).
+//   warps 2-17     : epilogue. Each warp owns the 32 TMEM lanes (= tile rows) of
+//                    its quadrant (warp % 4) and a quarter of the tile's columns,
+//                    pulls them out of TMEM with tcgen05.ld (releasing the
+//                    accumulator right away) and applies the fused epilogue
+//                    (bias, branch multiplier, residual, RoPE, GELU, dGELU, fp32
+//                    store or atomic add, and the two cross-entropy epilogues
+//                    used by lce.cu).
 // Every wait is bounded (common.cuh); a wait that runs out raises the CTA's
 // abort flag so all roles leave their loops, TMEM is freed and the error is
 // visible through gptb200_device_error().
+#include <string.h>
+
 #include <algorithm>
 #include <mutex>
 #include <vector>
@@ -31,7 +35,7 @@ static __device__ int g_gemm_error;
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int kEpiWarps = 8;                   // two per TMEM lane quadrant
+constexpr int kEpiWarps = 16;                  // four per TMEM lane quadrant
 constexpr int kThreads = 64 + 32 * kEpiWarps;  // TMA warp + MMA warp + epilogue
 
 template <int BN, int STAGES>
@@ -39,8 +43,20 @@ struct GemmSmem {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int BAR_OFFSET = STAGES * STAGE_BYTES;
-  static constexpr int TOTAL = BAR_OFFSET + 256 + 1024;  // barriers + alignment slack
+  // Per epilogue warp a 2 KB staging tile (32 rows x 32 bf16, 64-byte swizzle)
+  // for the TMA stores of bf16 outputs; the LCE forward reuses it for its
+  // 4 x 128 float2 row partials.
+  static constexpr int STAGE_OFFSET = STAGES * STAGE_BYTES;
+  static constexpr int STAGE_TILE = 2048;
+  static constexpr int RED_OFFSET = STAGE_OFFSET;
+  static constexpr int BAR_OFFSET = STAGE_OFFSET + 16 * STAGE_TILE;
+  static constexpr int TOTAL = BAR_OFFSET + 256 + 1023;  // + alignment slack
+};
+
+// Tensor maps of the bf16 outputs (C and the GELU pre-activation), box 32 x 32.
+struct EpiMaps {
+  CUtensorMap c;
+  CUtensorMap aux;
 };
 
 struct TileCoord {
@@ -82,100 +98,99 @@ __device__ __forceinline__ void load_bf16x8(const bf16* src, float* v) {
   unpack_bf16x2(q.w, v[6], v[7]);
 }
 
-// Applies the epilogue to 32 accumulator columns [col, col+32) of one row.
+template <int EPI>
+constexpr bool kStagedEpi = EPI == EPI_BF16_ || EPI == EPI_BIAS_ROPE_ || EPI == EPI_BIAS_GELU_ ||
+                            EPI == EPI_DGELU_ || EPI == EPI_LCE_BWD_;
+
+// Values of 8 consecutive output columns [c0, c0+8) of one row for the
+// bf16-output epilogues (`which` = 0: C, 1: the GELU pre-activation). Rows
+// and columns outside the matrix produce zeros without touching memory (the
+// TMA store clips them).
+template <int EPI>
+__device__ __forceinline__ void epi_value8(const GemmParams& p, int row, int c0, const float* a,
+                                           float* o, int which, int target, float lse,
+                                           float cot) {
+  if (row >= p.M || c0 >= p.N) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = 0.f;
+    return;
+  }
+  if constexpr (EPI == EPI_BF16_) {
+    float b[8], r[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = bf16r(a[j]);
+    if (p.bias) {
+      load_bf16x8(p.bias + c0, b);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = bf16r(o[j] + b[j]);
+    }
+    if (p.alpha != 1.0f) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = bf16r(p.alpha * o[j]);
+    }
+    if (p.resid) {
+      load_bf16x8(p.resid + (int64_t)row * p.ld_resid + c0, r);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = r[j] + o[j];
+    }
+  } else if constexpr (EPI == EPI_BIAS_ROPE_) {
+    // bias, then the interleaved RoPE rotation of q/k columns at this row's
+    // position (rig/nn.py:36-52), one bf16 rounding per value as in the reference.
+    float b[8];
+    load_bf16x8(p.bias + c0, b);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = bf16r(bf16r(a[j]) + b[j]);
+    if (c0 < p.rope_cols) {
+      const int pos = row % p.rope_seq;
+      const int pair0 = (c0 & 63) >> 1;
+      uint2 cq = *reinterpret_cast<const uint2*>(p.rope_cos + (int64_t)pos * 32 + pair0);
+      uint2 sq = *reinterpret_cast<const uint2*>(p.rope_sin + (int64_t)pos * 32 + pair0);
+      float cs[4], sn[4];
+      unpack_bf16x2(cq.x, cs[0], cs[1]);
+      unpack_bf16x2(cq.y, cs[2], cs[3]);
+      unpack_bf16x2(sq.x, sn[0], sn[1]);
+      unpack_bf16x2(sq.y, sn[2], sn[3]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float e = o[2 * j], d = o[2 * j + 1];
+        o[2 * j] = e * cs[j] - d * sn[j];
+        o[2 * j + 1] = e * sn[j] + d * cs[j];
+      }
+    }
+  } else if constexpr (EPI == EPI_BIAS_GELU_) {
+    float b[8];
+    load_bf16x8(p.bias + c0, b);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float u = bf16r(bf16r(a[j]) + b[j]);
+      o[j] = which ? u : gelu_tanh(u);
+    }
+  } else if constexpr (EPI == EPI_DGELU_) {
+    float u[8];
+    load_bf16x8(p.aux + (int64_t)row * p.ld_aux + c0, u);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = bf16r(p.alpha * a[j]) * gelu_tanh_grad(u[j]);
+  } else if constexpr (EPI == EPI_LCE_BWD_) {
+    // G = (softmax - onehot(target)) * cotangent
+    const float kLog2e = 1.4426950408889634f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int c = c0 + j;
+      const float pr = (c < p.v_sem) ? exp2f((a[j] - lse) * kLog2e) : 0.f;
+      o[j] = (pr - (c == target ? 1.f : 0.f)) * cot;
+    }
+  }
+}
+
+// Applies the fp32 / cross-entropy-forward epilogues to 32 accumulator
+// columns [col, col+32) of one row (bf16 outputs go through epi_value8).
 template <int EPI>
 __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int row, int col, float* v,
                                                EpilogueRowState<EPI>& st, int target,
                                                float lse, float cot) {
   const bool row_ok = row < p.M;
-  if constexpr (EPI == EPI_BF16_) {
-    if (!row_ok) return;
-    bf16* C = reinterpret_cast<bf16*>(p.C);
-#pragma unroll
-    for (int g = 0; g < 4; ++g) {
-      int c0 = col + 8 * g;
-      if (c0 >= p.N) break;
-      float t[8], b[8], r[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) t[j] = bf16r(v[8 * g + j]);
-      if (p.bias) {
-        load_bf16x8(p.bias + c0, b);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) t[j] = bf16r(t[j] + b[j]);
-      }
-      if (p.alpha != 1.0f) {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) t[j] = bf16r(p.alpha * t[j]);
-      }
-      if (p.resid) {
-        load_bf16x8(p.resid + (int64_t)row * p.ld_resid + c0, r);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) t[j] = r[j] + t[j];
-      }
-      store_bf16x8(C + (int64_t)row * p.ldc + c0, t);
-    }
-  } else if constexpr (EPI == EPI_BIAS_ROPE_) {
-    // bias, then the interleaved RoPE rotation of q/k columns at this row's
-    // position (rig/nn.py:36-52), one bf16 rounding per value as in the reference.
-    if (!row_ok) return;
-    bf16* C = reinterpret_cast<bf16*>(p.C);
-    const int pos = row % p.rope_seq;
-#pragma unroll
-    for (int g = 0; g < 4; ++g) {
-      int c0 = col + 8 * g;
-      if (c0 >= p.N) break;
-      float t[8], b[8];
-      load_bf16x8(p.bias + c0, b);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) t[j] = bf16r(bf16r(v[8 * g + j]) + b[j]);
-      if (c0 < p.rope_cols) {
-        const int pair0 = (c0 & 63) >> 1;
-        uint2 cq = *reinterpret_cast<const uint2*>(p.rope_cos + (int64_t)pos * 32 + pair0);
-        uint2 sq = *reinterpret_cast<const uint2*>(p.rope_sin + (int64_t)pos * 32 + pair0);
-        float cs[4], sn[4];
-        unpack_bf16x2(cq.x, cs[0], cs[1]);
-        unpack_bf16x2(cq.y, cs[2], cs[3]);
-        unpack_bf16x2(sq.x, sn[0], sn[1]);
-        unpack_bf16x2(sq.y, sn[2], sn[3]);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float e = t[2 * j], o = t[2 * j + 1];
-          t[2 * j] = e * cs[j] - o * sn[j];
-          t[2 * j + 1] = e * sn[j] + o * cs[j];
-        }
-      }
-      store_bf16x8(C + (int64_t)row * p.ldc + c0, t);
-    }
-  } else if constexpr (EPI == EPI_BIAS_GELU_) {
-    if (!row_ok) return;
-    bf16* C = reinterpret_cast<bf16*>(p.C);
-#pragma unroll
-    for (int g = 0; g < 4; ++g) {
-      int c0 = col + 8 * g;
-      if (c0 >= p.N) break;
-      float u[8], b[8], o[8];
-      load_bf16x8(p.bias + c0, b);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        u[j] = bf16r(bf16r(v[8 * g + j]) + b[j]);
-        o[j] = gelu_tanh(u[j]);
-      }
-      store_bf16x8(p.aux + (int64_t)row * p.ld_aux + c0, u);
-      store_bf16x8(C + (int64_t)row * p.ldc + c0, o);
-    }
-  } else if constexpr (EPI == EPI_DGELU_) {
-    if (!row_ok) return;
-    bf16* C = reinterpret_cast<bf16*>(p.C);
-#pragma unroll
-    for (int g = 0; g < 4; ++g) {
-      int c0 = col + 8 * g;
-      if (c0 >= p.N) break;
-      float u[8], o[8];
-      load_bf16x8(p.aux + (int64_t)row * p.ld_aux + c0, u);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) o[j] = bf16r(p.alpha * v[8 * g + j]) * gelu_tanh_grad(u[j]);
-      store_bf16x8(C + (int64_t)row * p.ldc + c0, o);
-    }
+  if constexpr (kStagedEpi<EPI>) {
+    return;
   } else if constexpr (EPI == EPI_F32_) {
     if (!row_ok) return;
     float* C = reinterpret_cast<float*>(p.C);
@@ -229,24 +244,6 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int row, int
     for (int j = 0; j < 32; ++j) s += exp2f((v[j] - nm) * kLog2e);
     st.run_sum = st.run_sum * exp2f((st.run_max - nm) * kLog2e) + s;
     st.run_max = nm;
-  } else if constexpr (EPI == EPI_LCE_BWD_) {
-    // G = (softmax - onehot(target)) * cotangent, rounded to bf16.
-    if (!row_ok) return;
-    bf16* C = reinterpret_cast<bf16*>(p.C);
-    const float kLog2e = 1.4426950408889634f;
-#pragma unroll
-    for (int g = 0; g < 4; ++g) {
-      int c0 = col + 8 * g;
-      if (c0 >= p.N) break;
-      float o[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        int c = c0 + j;
-        float pr = (c < p.v_sem) ? exp2f((v[8 * g + j] - lse) * kLog2e) : 0.f;
-        o[j] = (pr - (c == target ? 1.f : 0.f)) * cot;
-      }
-      store_bf16x8(C + (int64_t)row * p.ldc + c0, o);
-    }
   }
 }
 
@@ -254,7 +251,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int row, int
 template <int BN, int STAGES, int EPI, int A_MN, int B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const GemmParams p) {
+                   const __grid_constant__ EpiMaps maps, const GemmParams p) {
   using L = GemmSmem<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -379,17 +376,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // ---------------- epilogue warps 2..9: warp w reads TMEM lanes of quadrant
-    // w % 4 and one half of the tile columns
+    // ---------------- epilogue warps 2..17: warp w reads the TMEM lanes of
+    // quadrant w % 4 and one quarter (BN / 4 columns) of the tile. Both 32-column
+    // loads are issued before one wait, and the accumulator is handed back to
+    // the MMA warp as soon as it is in registers.
+    constexpr int COLS = BN / 4;
     const int quad = warp & 3;
-    const int half = (warp - 2) >> 2;
+    const int part = (warp - 2) >> 2;
     const int r_in_tile = quad * 32 + lane;
+    float2* red = reinterpret_cast<float2*>(smem + L::RED_OFFSET);  // [4][128] LCE partials
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int u = blockIdx.x; u < p.num_units; u += gridDim.x) {
       TileCoord tc = decode_unit(p, u);
       const int row = tc.tm * BM + r_in_tile;
-      const int n0 = tc.tn * BN;
+      const int n0 = tc.tn * BN + part * COLS;
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, err)) break;
       tc_fence_after();
       int target = -1;
@@ -404,21 +405,76 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      EpilogueRowState<EPI> st;
-      const uint32_t trow = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN;
-#pragma unroll 1
-      for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
-        float v[32];
-        tmem_ld32(trow + c * 32, v);
-        epilogue_chunk<EPI>(p, row, n0 + c * 32, v, st, target, lse, cot);
-      }
-      if constexpr (EPI == EPI_LCE_FWD_) {
-        if (row < p.M)
-          p.partial[((int64_t)row * p.tiles_n + tc.tn) * 2 + half] = make_float2(st.run_max, st.run_sum);
-      }
+      uint32_t raw[COLS];
+      const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + part * COLS;
+#pragma unroll
+      for (int c = 0; c < COLS / 32; ++c) tmem_ld32_nw(taddr + c * 32, raw + c * 32);
+      tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
+      EpilogueRowState<EPI> st;
+      if constexpr (kStagedEpi<EPI>) {
+        // bf16 outputs: 32x32 sub-tiles through the warp's swizzled staging
+        // tile, written by TMA stores (full 128-byte lines, clipped to M x N).
+        uint8_t* stage = smem + L::STAGE_OFFSET + (warp - 2) * L::STAGE_TILE;
+        constexpr int NOUT = (EPI == EPI_BIAS_GELU_) ? 2 : 1;
+#pragma unroll
+        for (int o = 0; o < NOUT; ++o) {
+#pragma unroll
+          for (int c = 0; c < COLS / 32; ++c) {
+            if (lane == 0) bulk_wait_read();
+            __syncwarp();
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+              float a8[8], v8[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) a8[j] = __uint_as_float(raw[c * 32 + g * 8 + j]);
+              epi_value8<EPI>(p, row, n0 + c * 32 + g * 8, a8, v8, o, target, lse, cot);
+              uint4 q;
+              q.x = pack_bf16x2(v8[0], v8[1]);
+              q.y = pack_bf16x2(v8[2], v8[3]);
+              q.z = pack_bf16x2(v8[4], v8[5]);
+              q.w = pack_bf16x2(v8[6], v8[7]);
+              *reinterpret_cast<uint4*>(stage + lane * 64 + ((g ^ ((lane >> 1) & 3)) << 4)) = q;
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(o == 0 ? &maps.c : &maps.aux, stage, n0 + c * 32,
+                           tc.tm * BM + quad * 32);
+              bulk_commit();
+            }
+          }
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < COLS / 32; ++c) {
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(raw[c * 32 + i]);
+          epilogue_chunk<EPI>(p, row, n0 + c * 32, v, st, target, lse, cot);
+        }
+      }
+      if constexpr (EPI == EPI_LCE_FWD_) {
+        // combine the four column quarters of each row, one partial per tile
+        red[part * BM + r_in_tile] = make_float2(st.run_max, st.run_sum);
+        named_bar_sync(1, 32 * kEpiWarps);
+        if (part == 0 && row < p.M) {
+          const float kLog2e = 1.4426950408889634f;
+          float m = -INFINITY, sum = 0.f;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float2 e = red[q * BM + r_in_tile];
+            if (e.x == -INFINITY) continue;
+            const float nm = fmaxf(m, e.x);
+            sum = sum * exp2f((m - nm) * kLog2e) + e.y * exp2f((e.x - nm) * kLog2e);
+            m = nm;
+          }
+          p.partial[(int64_t)row * p.tiles_n + tc.tn] = make_float2(m, sum);
+        }
+        named_bar_sync(1, 32 * kEpiWarps);
+      }
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1;
@@ -426,6 +482,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
+  if constexpr (kStagedEpi<EPI>) {
+    if (warp >= 2 && lane == 0) bulk_wait_all();
+  }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -470,6 +529,21 @@ static bool make_map(CUtensorMap* map, const void* base, int64_t inner, int64_t 
   return r == CUDA_SUCCESS;
 }
 
+// Store map of a bf16 [outer, inner] output (row stride ld): box 32 x 32 with
+// 64-byte swizzle, matching the epilogue staging tiles.
+static bool make_store_map(CUtensorMap* map, const void* base, int64_t inner, int64_t outer,
+                           int64_t ld) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+             CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 static int sm_count() {
   int dev = 0;
   cudaGetDevice(&dev);
@@ -482,8 +556,8 @@ static int sm_count() {
 }
 
 template <int BN, int STAGES, int EPI, int A_MN, int B_MN>
-static int launch_variant(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
-                          cudaStream_t stream) {
+static int launch_variant(const CUtensorMap& ta, const CUtensorMap& tb, const EpiMaps& em,
+                          const GemmParams& p, cudaStream_t stream) {
   using L = GemmSmem<BN, STAGES>;
   auto kern = gemm_tc_kernel<BN, STAGES, EPI, A_MN, B_MN>;
   static bool configured[64] = {false};
@@ -495,7 +569,7 @@ static int launch_variant(const CUtensorMap& ta, const CUtensorMap& tb, const Ge
     if (dev < 64) configured[dev] = true;
   }
   int grid = std::min<int64_t>(p.num_units, sm_count());
-  kern<<<grid, kThreads, L::TOTAL, stream>>>(ta, tb, p);
+  kern<<<grid, kThreads, L::TOTAL, stream>>>(ta, tb, em, p);
   GPTB200_CHECK_LAUNCH();
   return GPTB200_OK;
 }
@@ -505,11 +579,11 @@ constexpr int kStages = 4;
 
 template <int EPI>
 static int dispatch_layout(int a_mn, int b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
-                           const GemmParams& p, cudaStream_t s) {
-  if (a_mn == 0 && b_mn == 0) return launch_variant<kBN, kStages, EPI, 0, 0>(ta, tb, p, s);
-  if (a_mn == 0 && b_mn == 1) return launch_variant<kBN, kStages, EPI, 0, 1>(ta, tb, p, s);
-  if (a_mn == 1 && b_mn == 0) return launch_variant<kBN, kStages, EPI, 1, 0>(ta, tb, p, s);
-  return launch_variant<kBN, kStages, EPI, 1, 1>(ta, tb, p, s);
+                           const EpiMaps& em, const GemmParams& p, cudaStream_t s) {
+  if (a_mn == 0 && b_mn == 0) return launch_variant<kBN, kStages, EPI, 0, 0>(ta, tb, em, p, s);
+  if (a_mn == 0 && b_mn == 1) return launch_variant<kBN, kStages, EPI, 0, 1>(ta, tb, em, p, s);
+  if (a_mn == 1 && b_mn == 0) return launch_variant<kBN, kStages, EPI, 1, 0>(ta, tb, em, p, s);
+  return launch_variant<kBN, kStages, EPI, 1, 1>(ta, tb, em, p, s);
 }
 
 int gemm_launch(const void* a, int a_mn, int64_t lda, const void* b, int b_mn, int64_t ldb,
@@ -529,6 +603,14 @@ int gemm_launch(const void* a, int a_mn, int64_t lda, const void* b, int b_mn, i
   bool ok = a_mn ? make_map(&ta, a, M, K, lda, BK) : make_map(&ta, a, K, M, lda, BM);
   ok = ok && (b_mn ? make_map(&tb, b, N, K, ldb, BK) : make_map(&tb, b, K, N, ldb, kBN));
   if (!ok) return GPTB200_ESHAPE;
+  EpiMaps em;
+  memset(&em, 0, sizeof(em));
+  if (epi == EPI_BF16_ || epi == EPI_BIAS_ROPE_ || epi == EPI_BIAS_GELU_ || epi == EPI_DGELU_ ||
+      epi == EPI_LCE_BWD_) {
+    if (!make_store_map(&em.c, p.C, N, M, p.ldc)) return GPTB200_ESHAPE;
+    if (epi == EPI_BIAS_GELU_ && !make_store_map(&em.aux, p.aux, N, M, p.ld_aux))
+      return GPTB200_ESHAPE;
+  }
 
   p.M = (int)M;
   p.N = (int)N;
@@ -548,24 +630,24 @@ int gemm_launch(const void* a, int a_mn, int64_t lda, const void* b, int b_mn, i
   p.num_units = p.tiles_m * p.tiles_n * p.splits;
 
   switch (epi) {
-    case EPI_BF16_: return dispatch_layout<EPI_BF16_>(a_mn, b_mn, ta, tb, p, stream);
-    case EPI_F32_: return dispatch_layout<EPI_F32_>(a_mn, b_mn, ta, tb, p, stream);
-    case EPI_F32_ATOMIC_: return dispatch_layout<EPI_F32_ATOMIC_>(a_mn, b_mn, ta, tb, p, stream);
+    case EPI_BF16_: return dispatch_layout<EPI_BF16_>(a_mn, b_mn, ta, tb, em, p, stream);
+    case EPI_F32_: return dispatch_layout<EPI_F32_>(a_mn, b_mn, ta, tb, em, p, stream);
+    case EPI_F32_ATOMIC_: return dispatch_layout<EPI_F32_ATOMIC_>(a_mn, b_mn, ta, tb, em, p, stream);
     case EPI_BIAS_ROPE_:
       if (a_mn || !b_mn) return GPTB200_EUNSUPPORTED;
-      return launch_variant<kBN, kStages, EPI_BIAS_ROPE_, 0, 1>(ta, tb, p, stream);
+      return launch_variant<kBN, kStages, EPI_BIAS_ROPE_, 0, 1>(ta, tb, em, p, stream);
     case EPI_BIAS_GELU_:
       if (a_mn || !b_mn) return GPTB200_EUNSUPPORTED;
-      return launch_variant<kBN, kStages, EPI_BIAS_GELU_, 0, 1>(ta, tb, p, stream);
+      return launch_variant<kBN, kStages, EPI_BIAS_GELU_, 0, 1>(ta, tb, em, p, stream);
     case EPI_DGELU_:
       if (a_mn || b_mn) return GPTB200_EUNSUPPORTED;
-      return launch_variant<kBN, kStages, EPI_DGELU_, 0, 0>(ta, tb, p, stream);
+      return launch_variant<kBN, kStages, EPI_DGELU_, 0, 0>(ta, tb, em, p, stream);
     case EPI_LCE_FWD_:
       if (a_mn || b_mn) return GPTB200_EUNSUPPORTED;
-      return launch_variant<kBN, kStages, EPI_LCE_FWD_, 0, 0>(ta, tb, p, stream);
+      return launch_variant<kBN, kStages, EPI_LCE_FWD_, 0, 0>(ta, tb, em, p, stream);
     case EPI_LCE_BWD_:
       if (a_mn || b_mn) return GPTB200_EUNSUPPORTED;
-      return launch_variant<kBN, kStages, EPI_LCE_BWD_, 0, 0>(ta, tb, p, stream);
+      return launch_variant<kBN, kStages, EPI_LCE_BWD_, 0, 0>(ta, tb, em, p, stream);
     default: return GPTB200_EUNSUPPORTED;
   }
 }

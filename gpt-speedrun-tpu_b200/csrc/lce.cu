@@ -21,10 +21,9 @@ namespace gptb200 {
 
 static int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
 
-// Partial (max, sum-exp) pairs per row: the GEMM epilogue emits one per half
-// of each 256-wide vocabulary tile (two epilogue warps share a tile's rows).
+// Partial (max, sum-exp) pairs per row: one per 256-wide vocabulary tile.
 static int64_t lce_tiles_n(int64_t v_storage) {
-  return 2 * ((round_up(v_storage, 8) + gemm_tile_n() - 1) / gemm_tile_n());
+  return (round_up(v_storage, 8) + gemm_tile_n() - 1) / gemm_tile_n();
 }
 
 // Rows per backward chunk: bounds the G scratch to chunk * vocab bf16.
