@@ -35,6 +35,20 @@ namespace gptb200 {
 
 static __device__ int g_attn_error;
 
+#ifdef GPTB200_TRACE
+// Per-phase clock stamps of CTA (0, 0), for performance diagnostics builds.
+__device__ long long g_attn_trace[4096];
+#define ATTN_TRACE(slot)                                                  \
+  do {                                                                    \
+    if (blockIdx.x == 0 && blockIdx.y == 0 && (slot) < 4096)              \
+      g_attn_trace[(slot)] = clock64();                                   \
+  } while (0)
+#else
+#define ATTN_TRACE(slot) \
+  do {                   \
+  } while (0)
+#endif
+
 constexpr int HD = 64;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
@@ -314,18 +328,16 @@ struct BwdSmem {
   static constexpr int V = K + BT_BYTES;
   static constexpr int Q = V + BT_BYTES;          // 2 stages
   static constexpr int DO = Q + 2 * BT_BYTES;     // 2 stages
-  static constexpr int PT = DO + 2 * BT_BYTES;    // 2 buffers x 2 blocks of 64 queries
-  static constexpr int DST = PT + 4 * BT_BYTES;   // 2 buffers x 2 blocks
-  static constexpr int LSE = DST + 4 * BT_BYTES;  // 128 floats
-  static constexpr int DEL = LSE + 512;           // 128 floats
-  static constexpr int BAR = DEL + 512;
+  static constexpr int DST = DO + 2 * BT_BYTES;   // 2 buffers x 2 blocks of 64 queries
+  static constexpr int DQS = DST + 4 * BT_BYTES;  // dQ staging: 8 warps x (32 x 32 fp32)
+  static constexpr int BAR = DQS + 8 * 4096;
   static constexpr int TOTAL = BAR + 256 + 1023;
 };
 
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
-                const AttnParams p) {
+                const __grid_constant__ CUtensorMap tmDQ, const AttnParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                            ~static_cast<uintptr_t>(1023));
@@ -335,14 +347,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint64_t* q_empty = bars + 3;  // [2]
   uint64_t* s_full = bars + 5;
   uint64_t* p_full = bars + 6;
-  uint64_t* dq_full = bars + 7;
-  uint64_t* dq_free = bars + 8;
-  uint64_t* ps_free = bars + 9;  // [2]: P/dS buffer b consumed by its dV/dK MMAs
-  uint64_t* fin = bars + 11;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* pv_done = bars + 7;  // dV MMA of the tile has read P^T from TMEM
+  uint64_t* dq_full = bars + 8;
+  uint64_t* dq_free = bars + 9;
+  uint64_t* ds_free = bars + 10;  // [2]: dS^T buffer read by its dQ and dK MMAs
+  uint64_t* fin = bars + 12;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* sLse = reinterpret_cast<float*>(sm + BwdSmem::LSE);
-  float* sDel = reinterpret_cast<float*>(sm + BwdSmem::DEL);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nt = (p.T + BT - 1) / BT;
@@ -358,10 +369,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     for (int s = 0; s < 2; ++s) {
       mbar_init(&q_full[s], 1);
       mbar_init(&q_empty[s], 1);
-      mbar_init(&ps_free[s], 1);
+      mbar_init(&ds_free[s], 1);
     }
     mbar_init(s_full, 1);
     mbar_init(p_full, kBwdSoftWarps);
+    mbar_init(pv_done, 1);
     mbar_init(dq_full, 1);
     mbar_init(dq_free, kBwdSoftWarps);
     mbar_init(fin, 1);
@@ -372,9 +384,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // TMEM columns: S^T | dP^T | dV | dK | dQ | P^T (bf16 pairs)
   const uint32_t tmem = *tmem_slot;
   const uint32_t tS = tmem, tDP = tmem + 128, tDV = tmem + 256, tDK = tmem + 320,
-                 tDQ = tmem + 384;
+                 tDQ = tmem + 384, tP = tmem + 448;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -419,37 +432,43 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const int s = it & 1;
         const uint32_t sQ = smem_u32(sm + BwdSmem::Q + s * BT_BYTES);
         const uint32_t sDO = smem_u32(sm + BwdSmem::DO + s * BT_BYTES);
-        const uint32_t sPt = smem_u32(sm + BwdSmem::PT + s * 2 * BT_BYTES);
         const uint32_t sdSt = smem_u32(sm + BwdSmem::DST + s * 2 * BT_BYTES);
+        ATTN_TRACE(64 * it + 0);
         if (!mbar_wait(p_full, it & 1, abort_flag, err)) break;
+        ATTN_TRACE(64 * it + 1);
         tc_fence_after();
-        // Scores of the next query tile first, so the softmax warps can start
-        // on them while dQ/dV/dK of this tile run.
+        // dV += P^T · dO with P^T read straight from TMEM (K = queries).
+#pragma unroll
+        for (int k = 0; k < BT / 16; ++k)
+          umma_bf16_ts(tDV, tP + k * 8, umma_smem_desc(sDO + k * 2048, BT_BYTES, 1024), idKN,
+                       (it > 0 || k > 0));
+        umma_commit(pv_done);
+        // Scores of the next query tile, so the softmax warps can start on
+        // them while dQ and dK of this tile run.
         if (it + 1 < nq) {
           if (!mbar_wait(&q_full[(it + 1) & 1], ((it + 1) >> 1) & 1, abort_flag, err)) break;
           tc_fence_after();
           issue_s(it + 1);
         }
+        ATTN_TRACE(64 * it + 2);
         if (it > 0 && !mbar_wait(dq_free, (it - 1) & 1, abort_flag, err)) break;
+        ATTN_TRACE(64 * it + 3);
         tc_fence_after();
-        // dQ = dS · K: A = dSᵀ read MN-major (M = queries in two 64-wide
+        // dQ = dS · K: A = dS^T read MN-major (M = queries in two 64-wide
         // blocks 16 KB apart), B = K tile MN-major (N = head dim).
 #pragma unroll
         for (int k = 0; k < BT / 16; ++k)
           umma_bf16(tDQ, umma_smem_desc(sdSt + k * 2048, BT_BYTES, 1024),
                     umma_smem_desc(sK + k * 2048, BT_BYTES, 1024), idMN, k > 0);
         umma_commit(dq_full);
-        // dV += Pᵀ · dO ; dK += dSᵀ · Q  (A K-major over queries, B MN-major)
+        // dK += dS^T · Q  (A K-major over queries, B MN-major)
 #pragma unroll
-        for (int k = 0; k < BT / 16; ++k) {
-          const uint32_t aoff = (k >> 2) * BT_BYTES + (k & 3) * 32;
-          umma_bf16(tDV, umma_smem_desc(sPt + aoff, 16, 1024),
-                    umma_smem_desc(sDO + k * 2048, BT_BYTES, 1024), idKN, (it > 0 || k > 0));
-          umma_bf16(tDK, umma_smem_desc(sdSt + aoff, 16, 1024),
+        for (int k = 0; k < BT / 16; ++k)
+          umma_bf16(tDK, umma_smem_desc(sdSt + (k >> 2) * BT_BYTES + (k & 3) * 32, 16, 1024),
                     umma_smem_desc(sQ + k * 2048, BT_BYTES, 1024), idKN, (it > 0 || k > 0));
-        }
-        umma_commit(&ps_free[s]);
+        umma_commit(&ds_free[s]);
         umma_commit(&q_empty[s]);
+        ATTN_TRACE(64 * it + 4);
       }
       umma_commit(fin);
     }
@@ -462,51 +481,60 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const int key = k0 + r;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const float c = p.scale * kLog2e;
-    const int tid = threadIdx.x - 64;  // 0..255
     const float* Lg = p.lse + (int64_t)bh * p.T;
     const float* Dg = p.delta + (int64_t)bh * p.T;
-    // statistics of query tile `it` (threads 0-127: lse, 128-255: delta)
-    auto fetch = [&](int it) -> float {
-      const int t = (kt + it) * BT + (tid & 127);
-      if (tid < 128) return (t < p.T) ? Lg[t] * kLog2e : INFINITY;  // rows past T: P = 0
-      return (t < p.T) ? Dg[t] : 0.f;
+    uint8_t* stage = sm + BwdSmem::DQS + (warp - 2) * 4096;
+    // Statistics of this warp's 64 query columns of tile `it`: lane j holds
+    // columns j and 32 + j (broadcast with shuffles in the inner loop).
+    float ls[2], dl[2], nls[2], ndl[2];
+    auto fetch = [&](int it, float* l2, float* d2) {
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int t = (kt + it) * BT + half * 64 + u * 32 + lane;
+        l2[u] = (t < p.T) ? Lg[t] * kLog2e : INFINITY;  // rows past T: P = 0
+        d2[u] = (t < p.T) ? Dg[t] : 0.f;
+      }
     };
-    float pending = fetch(0);
+    fetch(0, ls, dl);
     bool ok = true;
-    // dQ rows of query tile `it` (TMEM lane r = query (kt+it)*BT + r) into the
-    // fp32 accumulator.
+    // dQ rows of query tile `it` (TMEM lane r = query (kt+it)*BT + r): one
+    // 32x32 fp32 sub-tile per warp, reduced into dq_acc by a TMA reduce-add.
     auto flush_dq = [&](int it) {
       float v[32];
       tmem_ld32(tDQ + lane_off + half * 32, v);
-      const int qrow = (kt + it) * BT + r;
-      if (qrow < p.T) {
-        float* dst = p.dq_acc + ((int64_t)bh * p.T + qrow) * HD + half * 32;
+      if (lane == 0) bulk_wait_read();  // the previous reduce has read the staging tile
+      __syncwarp();
 #pragma unroll
-        for (int g = 0; g < 8; ++g)
-          atomicAdd(reinterpret_cast<float4*>(dst + 4 * g),
-                    make_float4(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]));
+      for (int ch = 0; ch < 8; ++ch)
+        *reinterpret_cast<float4*>(stage + lane * 128 + ((ch ^ (lane & 7)) << 4)) =
+            make_float4(v[4 * ch], v[4 * ch + 1], v[4 * ch + 2], v[4 * ch + 3]);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_reduce_add_3d(&tmDQ, stage, half * 32, (kt + it) * BT + quad * 32, bh);
+        bulk_commit();
       }
     };
     for (int it = 0; it < nq && ok; ++it) {
-      named_bar_sync(1, 32 * kBwdSoftWarps);  // all reads of the previous tile's stats done
-      (tid < 128 ? sLse : sDel)[tid & 127] = pending;
-      named_bar_sync(1, 32 * kBwdSoftWarps);
-      if (it + 1 < nq) pending = fetch(it + 1);
-      const int s = it & 1;
-      uint8_t* sPt = sm + BwdSmem::PT + s * 2 * BT_BYTES + half * BT_BYTES;
-      uint8_t* sdSt = sm + BwdSmem::DST + s * 2 * BT_BYTES + half * BT_BYTES;
+      if (it + 1 < nq) fetch(it + 1, nls, ndl);
+      if (threadIdx.x == 64) ATTN_TRACE(64 * it + 11);
       if (!mbar_wait(s_full, it & 1, abort_flag, err)) {
         ok = false;
         break;
       }
-      // the P/dS buffer of this tile was last read by the MMAs of tile it-2
-      if (it >= 2 && !mbar_wait(&ps_free[s], ((it >> 1) + 1) & 1, abort_flag, err)) {
+      if (threadIdx.x == 64) ATTN_TRACE(64 * it + 12);
+      // P^T of the previous tile has been consumed by its dV MMA; the dS^T
+      // buffer of this tile was last read by the MMAs of tile it-2.
+      if (it > 0 && !mbar_wait(pv_done, (it - 1) & 1, abort_flag, err)) {
+        ok = false;
+        break;
+      }
+      if (it >= 2 && !mbar_wait(&ds_free[it & 1], ((it >> 1) + 1) & 1, abort_flag, err)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const float* lq = sLse + half * 64;
-      const float* dl = sDel + half * 64;
+      uint8_t* sdSt = sm + BwdSmem::DST + (it & 1) * 2 * BT_BYTES + half * BT_BYTES;
       const bool diag = (it == 0);
 #pragma unroll
       for (int cc = 0; cc < 4; ++cc) {
@@ -516,36 +544,47 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         uint32_t pk[8], dk[8];
 #pragma unroll
         for (int i = 0; i < 16; i += 2) {
-          const int qc = cc * 16 + i;
-          float p0 = ex2(fmaf(sv[i], c, -lq[qc]));
-          float p1 = ex2(fmaf(sv[i + 1], c, -lq[qc + 1]));
+          const int qc = cc * 16 + i;  // column within this warp's 64
+          const float l0 = __shfl_sync(0xffffffffu, ls[qc >> 5], qc & 31);
+          const float l1 = __shfl_sync(0xffffffffu, ls[(qc + 1) >> 5], (qc + 1) & 31);
+          const float d0 = __shfl_sync(0xffffffffu, dl[qc >> 5], qc & 31);
+          const float d1 = __shfl_sync(0xffffffffu, dl[(qc + 1) >> 5], (qc + 1) & 31);
+          float p0 = ex2(fmaf(sv[i], c, -l0));
+          float p1 = ex2(fmaf(sv[i + 1], c, -l1));
           if (diag && r > half * 64 + qc) p0 = 0.f;
           if (diag && r > half * 64 + qc + 1) p1 = 0.f;
           pk[i / 2] = pack_bf16x2(p0, p1);
-          dk[i / 2] = pack_bf16x2(p0 * (dp[i] - dl[qc]), p1 * (dp[i + 1] - dl[qc + 1]));
+          dk[i / 2] = pack_bf16x2(p0 * (dp[i] - d0), p1 * (dp[i + 1] - d1));
         }
-        *reinterpret_cast<uint4*>(sPt + swz128(r, 2 * cc)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-        *reinterpret_cast<uint4*>(sPt + swz128(r, 2 * cc + 1)) =
-            make_uint4(pk[4], pk[5], pk[6], pk[7]);
+        tmem_st8_nw(tP + lane_off + half * 32 + cc * 8, pk);
         *reinterpret_cast<uint4*>(sdSt + swz128(r, 2 * cc)) = make_uint4(dk[0], dk[1], dk[2], dk[3]);
         *reinterpret_cast<uint4*>(sdSt + swz128(r, 2 * cc + 1)) =
             make_uint4(dk[4], dk[5], dk[6], dk[7]);
       }
+      tmem_wait_st();
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
+      if (threadIdx.x == 64) ATTN_TRACE(64 * it + 13);
       // dQ of the previous tile (its MMA ran behind this tile's scores).
       if (it > 0) {
         if (!mbar_wait(dq_full, (it - 1) & 1, abort_flag, err)) {
           ok = false;
           break;
         }
+        if (threadIdx.x == 64) ATTN_TRACE(64 * it + 14);
         tc_fence_after();
         flush_dq(it - 1);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(dq_free);
+        if (threadIdx.x == 64) ATTN_TRACE(64 * it + 15);
+      }
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        ls[u] = nls[u];
+        dl[u] = ndl[u];
       }
     }
     // dQ of the last tile, then dK and dV.
@@ -553,6 +592,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tc_fence_after();
       flush_dq(nq - 1);
     }
+    if (lane == 0) bulk_wait_all();
     if (ok && mbar_wait(fin, 0, abort_flag, err)) {
       tc_fence_after();
       float kk[32], vv[32];
@@ -654,6 +694,12 @@ __global__ void attn_dq_store_kernel(const float* __restrict__ dq_acc, bf16* __r
   }
 }
 
+#ifdef GPTB200_TRACE
+extern "C" int gptb200_attention_trace(long long* out, int n) {
+  return (int)cudaMemcpyFromSymbol(out, g_attn_trace, sizeof(long long) * (n < 4096 ? n : 4096));
+}
+#endif
+
 int attention_read_error(int clear) {
   int hv = 0;
   cudaMemcpyFromSymbol(&hv, g_attn_error, sizeof(int));
@@ -701,6 +747,20 @@ static bool make_map4(CUtensorMap* m, const void* base, int B, int H, int T, int
 }  // namespace gptb200
 
 using namespace gptb200;
+
+// 3-D fp32 map over dq_acc [B*H, T, 64], box 32 x 32 x 1, 128-byte swizzle
+// (the bwd kernel's TMA reduce-add target).
+static bool make_dq_map(CUtensorMap* m, float* base, int BH, int T) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[3] = {HD, (cuuint64_t)T, (cuuint64_t)BH};
+  cuuint64_t strides[2] = {(cuuint64_t)HD * 4, (cuuint64_t)T * HD * 4};
+  cuuint32_t box[3] = {32, 32, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base, dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
 
 static int check_attn(const void* q, const void* k, const void* v, int64_t sb, int64_t sh,
                       int64_t st, int64_t osb, int64_t osh, int64_t ost, int64_t batch,
@@ -821,7 +881,9 @@ extern "C" int gptb200_attention_bwd(const void* q, const void* k, const void* v
     if (dev < 64) cfg[dev] = true;
   }
   dim3 grid((unsigned)((seq + BT - 1) / BT), (unsigned)(batch * heads));
-  attn_bwd_tc<<<grid, kBwdThreads, BwdSmem::TOTAL, st>>>(mq, mk, mv, mdo, p);
+  CUtensorMap mdq;
+  if (!make_dq_map(&mdq, dq_acc, B * H, T)) return GPTB200_ESHAPE;
+  attn_bwd_tc<<<grid, kBwdThreads, BwdSmem::TOTAL, st>>>(mq, mk, mv, mdo, mdq, p);
   GPTB200_CHECK_LAUNCH();
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
