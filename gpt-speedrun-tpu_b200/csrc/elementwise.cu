@@ -76,8 +76,12 @@ __global__ void __launch_bounds__(256) rms_fwd_kernel(const bf16* __restrict__ x
 
 // Backward: dn = dy*scale; xhat = x*rstd;
 // dx = rstd * (dn - xhat * mean(dn * xhat)); dscale += dy * bf16(xhat).
+// x and dy stay packed (bf16) in registers between the two passes, which keeps
+// the register count low enough for full occupancy (the kernel is latency-bound
+// on its three input streams); each warp accumulates its dscale partial in its
+// own shared-memory row instead of registers.
 template <int CH>
-__global__ void __launch_bounds__(256) rms_bwd_kernel(
+__global__ void __launch_bounds__(128, 6) rms_bwd_kernel(
     const bf16* __restrict__ x, const bf16* __restrict__ scale, const float* __restrict__ rstd_in,
     const bf16* __restrict__ dy, const bf16* dx_in, bf16* dx_out, float* __restrict__ dscale,
     int64_t rows, int d) {
@@ -87,59 +91,82 @@ __global__ void __launch_bounds__(256) rms_bwd_kernel(
   const int wpb = blockDim.x >> 5;
   const int64_t warps = (int64_t)gridDim.x * wpb;
   const int nch = d >> 3;
-  float ds[CH][8];
+  float* myred = red + wib * d;
+  for (int i = lane; i < d; i += 32) myred[i] = 0.f;
+  __syncwarp();
+  uint4 sc[CH];
 #pragma unroll
-  for (int c = 0; c < CH; ++c)
-#pragma unroll
-    for (int j = 0; j < 8; ++j) ds[c][j] = 0.f;
+  for (int c = 0; c < CH; ++c) {
+    const int ch = lane + 32 * c;
+    sc[c] = (ch < nch) ? *reinterpret_cast<const uint4*>(scale + ch * 8) : make_uint4(0, 0, 0, 0);
+  }
 
   for (int64_t r = (int64_t)blockIdx.x * wpb + wib; r < rows; r += warps) {
     const float rstd = rstd_in[r];
-    float xh[CH][8], dn[CH][8];
+    uint4 xq[CH], gq[CH], pq[CH];
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      const int ch = lane + 32 * c;
+      if (ch < nch) {
+        xq[c] = *reinterpret_cast<const uint4*>(x + r * d + ch * 8);
+        gq[c] = *reinterpret_cast<const uint4*>(dy + r * d + ch * 8);
+        pq[c] = dx_in ? *reinterpret_cast<const uint4*>(dx_in + r * d + ch * 8)
+                      : make_uint4(0, 0, 0, 0);
+      }
+    }
     float dot = 0.f;
 #pragma unroll
     for (int c = 0; c < CH; ++c) {
-      int ch = lane + 32 * c;
+      const int ch = lane + 32 * c;
       if (ch < nch) {
-        float xv[8], g[8], s[8];
-        ld8(x + r * d + ch * 8, xv);
-        ld8(dy + r * d + ch * 8, g);
-        ld8(scale + ch * 8, s);
+        const uint32_t* xw = &xq[c].x;
+        const uint32_t* gw = &gq[c].x;
+        const uint32_t* sw = &sc[c].x;
+        float4* acc = reinterpret_cast<float4*>(myred + ch * 8);
+        const float4 a0 = acc[0], a1 = acc[1];
+        float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          xh[c][j] = xv[j] * rstd;
-          dn[c][j] = g[j] * s[j];
-          ds[c][j] += g[j] * bf16r(xh[c][j]);
-          dot += dn[c][j] * xh[c][j];
+        for (int j = 0; j < 4; ++j) {
+          float x0, x1, g0, g1, s0, s1;
+          unpack_bf16x2(xw[j], x0, x1);
+          unpack_bf16x2(gw[j], g0, g1);
+          unpack_bf16x2(sw[j], s0, s1);
+          const float h0 = x0 * rstd, h1 = x1 * rstd;
+          av[2 * j] += g0 * bf16r(h0);
+          av[2 * j + 1] += g1 * bf16r(h1);
+          dot += g0 * s0 * h0 + g1 * s1 * h1;
         }
+        acc[0] = make_float4(av[0], av[1], av[2], av[3]);
+        acc[1] = make_float4(av[4], av[5], av[6], av[7]);
       }
     }
     dot = warp_sum(dot) / (float)d;
 #pragma unroll
     for (int c = 0; c < CH; ++c) {
-      int ch = lane + 32 * c;
+      const int ch = lane + 32 * c;
       if (ch < nch) {
-        float o[8], prev[8];
-        if (dx_in) {
-          ld8(dx_in + r * d + ch * 8, prev);
-        } else {
+        const uint32_t* xw = &xq[c].x;
+        const uint32_t* gw = &gq[c].x;
+        const uint32_t* sw = &sc[c].x;
+        const uint32_t* pw = &pq[c].x;
+        uint4 o;
+        uint32_t* ow = &o.x;
 #pragma unroll
-          for (int j = 0; j < 8; ++j) prev[j] = 0.f;
+        for (int j = 0; j < 4; ++j) {
+          float x0, x1, g0, g1, s0, s1, p0, p1;
+          unpack_bf16x2(xw[j], x0, x1);
+          unpack_bf16x2(gw[j], g0, g1);
+          unpack_bf16x2(sw[j], s0, s1);
+          unpack_bf16x2(pw[j], p0, p1);
+          const float v0 = p0 + bf16r(rstd * (g0 * s0 - x0 * rstd * dot));
+          const float v1 = p1 + bf16r(rstd * (g1 * s1 - x1 * rstd * dot));
+          ow[j] = pack_bf16x2(v0, v1);
         }
-#pragma unroll
-        for (int j = 0; j < 8; ++j) o[j] = prev[j] + bf16r(rstd * (dn[c][j] - xh[c][j] * dot));
-        st8(dx_out + r * d + ch * 8, o);
+        *reinterpret_cast<uint4*>(dx_out + r * d + ch * 8) = o;
       }
     }
   }
   // Reduce the per-warp dscale partials inside the block, then one atomic per column.
-#pragma unroll
-  for (int c = 0; c < CH; ++c) {
-    int ch = lane + 32 * c;
-    if (ch < nch)
-#pragma unroll
-      for (int j = 0; j < 8; ++j) red[wib * d + ch * 8 + j] = ds[c][j];
-  }
   __syncthreads();
   for (int col = threadIdx.x; col < d; col += blockDim.x) {
     float s = 0.f;
