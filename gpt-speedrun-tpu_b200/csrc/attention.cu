@@ -225,8 +225,11 @@ __global__ void __launch_bounds__(kThreads, 3)
         }
       }
       bool waited_pv = false;
-      if (mx > m_used + 8.0f) {
-        const float m_new = mx;
+      // The rescale decision is made per warp: the TMEM loads/stores inside
+      // are warp-collective and must not run in a divergent branch. Rows whose
+      // max did not move rescale by exactly 1.
+      if (__any_sync(0xffffffffu, mx > m_used + 8.0f)) {
+        const float m_new = fmaxf(m_used, mx);
         if (j > 0) {
           const float alpha = ex2(m_used - m_new);
           l *= alpha;

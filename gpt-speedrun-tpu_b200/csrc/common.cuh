@@ -26,8 +26,9 @@ enum {
 
 // Upper bound of try_wait polls before a wait gives up. Each poll can suspend
 // for a hardware-chosen interval, so this is far above any legitimate wait
-// (a stage of a GEMM waits microseconds) yet ends in well under a minute.
-#define GPTB200_WAIT_LIMIT (1u << 24)
+// (the longest waits here are one split-K unit, ~100 us) yet a wait that can
+// never complete ends in seconds.
+#define GPTB200_WAIT_LIMIT (1u << 20)
 
 GPTB200_DEV uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -298,6 +299,18 @@ GPTB200_DEV uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// bf16x2 arithmetic with one rounding per result (add.rn / mul.rn .bf16x2).
+GPTB200_DEV uint32_t hadd2_bf16(uint32_t a, uint32_t b) {
+  __nv_bfloat162 r = __hadd2(*reinterpret_cast<__nv_bfloat162*>(&a),
+                             *reinterpret_cast<__nv_bfloat162*>(&b));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+GPTB200_DEV uint32_t hmul2_bf16(uint32_t a, uint32_t b) {
+  __nv_bfloat162 r = __hmul2(*reinterpret_cast<__nv_bfloat162*>(&a),
+                             *reinterpret_cast<__nv_bfloat162*>(&b));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+
 GPTB200_DEV void unpack_bf16x2(uint32_t u, float& lo, float& hi) {
   __nv_bfloat162 h = *reinterpret_cast<__nv_bfloat162*>(&u);
   float2 f = __bfloat1622float2(h);
@@ -318,6 +331,17 @@ GPTB200_DEV float gelu_tanh(float x) {
   float t = tanh_fast(k0 * (x + k1 * x * x * x));
   return 0.5f * x * (1.0f + t);
 }
+// gelu_tanh(x) and its derivative, sharing one tanh.
+GPTB200_DEV void gelu_tanh_fwd_grad(float x, float& g, float& gp) {
+  const float k0 = 0.7978845608028654f;
+  const float k1 = 0.044715f;
+  const float x2 = x * x;
+  const float t = tanh_fast(k0 * x * fmaf(k1, x2, 1.0f));
+  const float hx = 0.5f * x;
+  g = fmaf(hx, t, hx);
+  gp = fmaf(0.5f, t, 0.5f) + hx * (1.0f - t * t) * (k0 * fmaf(3.0f * k1, x2, 1.0f));
+}
+
 // d/dx of gelu_tanh.
 GPTB200_DEV float gelu_tanh_grad(float x) {
   const float k0 = 0.7978845608028654f;

@@ -102,49 +102,56 @@ template <int EPI>
 constexpr bool kStagedEpi = EPI == EPI_BF16_ || EPI == EPI_BIAS_ROPE_ || EPI == EPI_BIAS_GELU_ ||
                             EPI == EPI_DGELU_ || EPI == EPI_LCE_BWD_;
 
-// Values of 8 consecutive output columns [c0, c0+8) of one row for the
-// bf16-output epilogues (`which` = 0: C, 1: the GELU pre-activation). Rows
-// and columns outside the matrix produce zeros without touching memory (the
-// TMA store clips them).
+// Packed bf16 outputs for 8 consecutive columns [c0, c0+8) of one row of the
+// bf16-output epilogues: o0 = C, o1 = the GELU derivative (EPI_BIAS_GELU only).
+// Each operation rounds where the reference's bf16 op does: bf16(acc), then
+// bias / branch-multiplier / residual as bf16x2 ops with one rounding each.
+// Rows and columns outside the matrix produce zeros without touching memory
+// (the TMA store clips them).
 template <int EPI>
-__device__ __forceinline__ void epi_value8(const GemmParams& p, int row, int c0, const float* a,
-                                           float* o, int which, int target, float lse,
-                                           float cot) {
+__device__ __forceinline__ void epi_pack8(const GemmParams& p, int row, int c0, const float* a,
+                                          uint32_t* o0, uint32_t* o1, int target, float lse,
+                                          float cot) {
   if (row >= p.M || c0 >= p.N) {
 #pragma unroll
-    for (int j = 0; j < 8; ++j) o[j] = 0.f;
+    for (int j = 0; j < 4; ++j) o0[j] = o1[j] = 0u;
     return;
   }
+  uint32_t t[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) t[j] = pack_bf16x2(a[2 * j], a[2 * j + 1]);
   if constexpr (EPI == EPI_BF16_) {
-    float b[8], r[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) o[j] = bf16r(a[j]);
     if (p.bias) {
-      load_bf16x8(p.bias + c0, b);
+      const uint4 bq = *reinterpret_cast<const uint4*>(p.bias + c0);
+      const uint32_t* bw = &bq.x;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) o[j] = bf16r(o[j] + b[j]);
+      for (int j = 0; j < 4; ++j) t[j] = hadd2_bf16(t[j], bw[j]);
     }
     if (p.alpha != 1.0f) {
+      const uint32_t al = pack_bf16x2(p.alpha, p.alpha);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) o[j] = bf16r(p.alpha * o[j]);
+      for (int j = 0; j < 4; ++j) t[j] = hmul2_bf16(t[j], al);
     }
     if (p.resid) {
-      load_bf16x8(p.resid + (int64_t)row * p.ld_resid + c0, r);
+      const uint4 rq = *reinterpret_cast<const uint4*>(p.resid + (int64_t)row * p.ld_resid + c0);
+      const uint32_t* rw = &rq.x;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) o[j] = r[j] + o[j];
+      for (int j = 0; j < 4; ++j) t[j] = hadd2_bf16(rw[j], t[j]);
     }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) o0[j] = t[j];
   } else if constexpr (EPI == EPI_BIAS_ROPE_) {
     // bias, then the interleaved RoPE rotation of q/k columns at this row's
     // position (rig/nn.py:36-52), one bf16 rounding per value as in the reference.
-    float b[8];
-    load_bf16x8(p.bias + c0, b);
+    const uint4 bq = *reinterpret_cast<const uint4*>(p.bias + c0);
+    const uint32_t* bw = &bq.x;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) o[j] = bf16r(bf16r(a[j]) + b[j]);
+    for (int j = 0; j < 4; ++j) t[j] = hadd2_bf16(t[j], bw[j]);
     if (c0 < p.rope_cols) {
       const int pos = row % p.rope_seq;
       const int pair0 = (c0 & 63) >> 1;
-      uint2 cq = *reinterpret_cast<const uint2*>(p.rope_cos + (int64_t)pos * 32 + pair0);
-      uint2 sq = *reinterpret_cast<const uint2*>(p.rope_sin + (int64_t)pos * 32 + pair0);
+      const uint2 cq = *reinterpret_cast<const uint2*>(p.rope_cos + (int64_t)pos * 32 + pair0);
+      const uint2 sq = *reinterpret_cast<const uint2*>(p.rope_sin + (int64_t)pos * 32 + pair0);
       float cs[4], sn[4];
       unpack_bf16x2(cq.x, cs[0], cs[1]);
       unpack_bf16x2(cq.y, cs[2], cs[3]);
@@ -152,33 +159,44 @@ __device__ __forceinline__ void epi_value8(const GemmParams& p, int row, int c0,
       unpack_bf16x2(sq.y, sn[2], sn[3]);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const float e = o[2 * j], d = o[2 * j + 1];
-        o[2 * j] = e * cs[j] - d * sn[j];
-        o[2 * j + 1] = e * sn[j] + d * cs[j];
+        float e, d;
+        unpack_bf16x2(t[j], e, d);
+        t[j] = pack_bf16x2(e * cs[j] - d * sn[j], e * sn[j] + d * cs[j]);
       }
     }
-  } else if constexpr (EPI == EPI_BIAS_GELU_) {
-    float b[8];
-    load_bf16x8(p.bias + c0, b);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float u = bf16r(bf16r(a[j]) + b[j]);
-      o[j] = which ? u : gelu_tanh(u);
+    for (int j = 0; j < 4; ++j) o0[j] = t[j];
+  } else if constexpr (EPI == EPI_BIAS_GELU_) {
+    const uint4 bq = *reinterpret_cast<const uint4*>(p.bias + c0);
+    const uint32_t* bw = &bq.x;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float u0, u1, g0, g1, d0, d1;
+      unpack_bf16x2(hadd2_bf16(t[j], bw[j]), u0, u1);
+      gelu_tanh_fwd_grad(u0, g0, d0);
+      gelu_tanh_fwd_grad(u1, g1, d1);
+      o0[j] = pack_bf16x2(g0, g1);
+      o1[j] = pack_bf16x2(d0, d1);
     }
   } else if constexpr (EPI == EPI_DGELU_) {
-    float u[8];
-    load_bf16x8(p.aux + (int64_t)row * p.ld_aux + c0, u);
+    // du = bf16(alpha * acc) * gelu'(u), the derivative saved by the forward epilogue
+    const uint4 gq = *reinterpret_cast<const uint4*>(p.aux + (int64_t)row * p.ld_aux + c0);
+    const uint32_t* gw = &gq.x;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) o[j] = bf16r(p.alpha * a[j]) * gelu_tanh_grad(u[j]);
+    for (int j = 0; j < 4; ++j)
+      o0[j] = hmul2_bf16(pack_bf16x2(p.alpha * a[2 * j], p.alpha * a[2 * j + 1]), gw[j]);
   } else if constexpr (EPI == EPI_LCE_BWD_) {
     // G = (softmax - onehot(target)) * cotangent
     const float kLog2e = 1.4426950408889634f;
+    float g[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int c = c0 + j;
-      const float pr = (c < p.v_sem) ? exp2f((a[j] - lse) * kLog2e) : 0.f;
-      o[j] = (pr - (c == target ? 1.f : 0.f)) * cot;
+      const float pr = (c < p.v_sem) ? ex2((a[j] - lse) * kLog2e) : 0.f;
+      g[j] = (pr - (c == target ? 1.f : 0.f)) * cot;
     }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) o0[j] = pack_bf16x2(g[2 * j], g[2 * j + 1]);
   }
 }
 
@@ -420,29 +438,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint8_t* stage = smem + L::STAGE_OFFSET + (warp - 2) * L::STAGE_TILE;
         constexpr int NOUT = (EPI == EPI_BIAS_GELU_) ? 2 : 1;
 #pragma unroll
-        for (int o = 0; o < NOUT; ++o) {
+        for (int c = 0; c < COLS / 32; ++c) {
+          uint32_t out0[16], out1[16];
 #pragma unroll
-          for (int c = 0; c < COLS / 32; ++c) {
+          for (int g = 0; g < 4; ++g) {
+            float a8[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) a8[j] = __uint_as_float(raw[c * 32 + g * 8 + j]);
+            epi_pack8<EPI>(p, row, n0 + c * 32 + g * 8, a8, out0 + 4 * g, out1 + 4 * g, target,
+                           lse, cot);
+          }
+#pragma unroll
+          for (int o = 0; o < NOUT; ++o) {
+            const uint32_t* w = o ? out1 : out0;
             if (lane == 0) bulk_wait_read();
             __syncwarp();
 #pragma unroll
-            for (int g = 0; g < 4; ++g) {
-              float a8[8], v8[8];
-#pragma unroll
-              for (int j = 0; j < 8; ++j) a8[j] = __uint_as_float(raw[c * 32 + g * 8 + j]);
-              epi_value8<EPI>(p, row, n0 + c * 32 + g * 8, a8, v8, o, target, lse, cot);
-              uint4 q;
-              q.x = pack_bf16x2(v8[0], v8[1]);
-              q.y = pack_bf16x2(v8[2], v8[3]);
-              q.z = pack_bf16x2(v8[4], v8[5]);
-              q.w = pack_bf16x2(v8[6], v8[7]);
-              *reinterpret_cast<uint4*>(stage + lane * 64 + ((g ^ ((lane >> 1) & 3)) << 4)) = q;
-            }
+            for (int g = 0; g < 4; ++g)
+              *reinterpret_cast<uint4*>(stage + lane * 64 + ((g ^ ((lane >> 1) & 3)) << 4)) =
+                  make_uint4(w[4 * g], w[4 * g + 1], w[4 * g + 2], w[4 * g + 3]);
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
-              tma_store_2d(o == 0 ? &maps.c : &maps.aux, stage, n0 + c * 32,
-                           tc.tm * BM + quad * 32);
+              tma_store_2d(o ? &maps.aux : &maps.c, stage, n0 + c * 32, tc.tm * BM + quad * 32);
               bulk_commit();
             }
           }

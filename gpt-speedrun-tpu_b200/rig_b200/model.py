@@ -15,10 +15,10 @@ loss :1194-1216, update :1362-1457). It owns:
   on the hot path: each launch is a libgptb200 kernel on the current stream.
 
 Forward, per block (activations bf16, rows = local tokens):
-  rms_norm -> GEMM(+bias) -> qkv -> attention (RoPE on load) -> GEMM(+bias,
-  x branch multiplier, + residual) -> rms_norm -> GEMM(+bias, GELU) ->
-  GEMM(+bias, x multiplier, + residual); then the final rms_norm and the fused
-  linear cross-entropy (no logits in HBM).
+  rms_norm -> GEMM(+bias, RoPE on the q/k columns) -> qkv -> attention ->
+  GEMM(+bias, x branch multiplier, + residual) -> rms_norm -> GEMM(+bias, GELU,
+  saving gelu'(u)) -> GEMM(+bias, x multiplier, + residual); then the final
+  rms_norm and the fused linear cross-entropy (no logits in HBM).
 Backward mirrors it with dgrad GEMMs (dGELU fused), weight-gradient GEMMs that
 accumulate into the fp32 gradient buffer with split-K atomics, bias-gradient
 column sums, RMSNorm backward fused with the residual-gradient add, and the
@@ -258,7 +258,7 @@ class GPTTrainer:
         self.xm = [torch.empty(N, d, **bf) for _ in range(L)]
         self.ln2 = [torch.empty(N, d, **bf) for _ in range(L)]
         self.rstd2 = [torch.empty(N, **f32) for _ in range(L)]
-        self.u = [torch.empty(N, h, **bf) for _ in range(L)]
+        self.gelu_grad = [torch.empty(N, h, **bf) for _ in range(L)]  # gelu'(u), saved by the forward
         self.g = [torch.empty(N, h, **bf) for _ in range(L)]
         self.lnf = torch.empty(N, d, **bf)
         self.rstdf = torch.empty(N, **f32)
@@ -333,7 +333,7 @@ class GPTTrainer:
                        out=self.xm[l])
             ops.rms_norm_fwd(self.xm[l], blk.ln2_scale, self.ln2[l], self.rstd2[l])
             ops.matmul(self.ln2[l], blk.mlp_up_w, bias=blk.mlp_up_b, kind=_lib.EPI_BIAS_GELU,
-                       aux=self.u[l], out=self.g[l])
+                       aux=self.gelu_grad[l], out=self.g[l])
             ops.matmul(self.g[l], blk.mlp_down_w, bias=blk.mlp_down_b, alpha=a,
                        residual=self.xm[l], out=self.x[l + 1])
         ops.rms_norm_fwd(self.x[c.layers], self.final_scale, self.lnf, self.rstdf)
@@ -365,7 +365,7 @@ class GPTTrainer:
         for l in reversed(range(c.layers)):
             blk = self.blocks[l]
             # MLP: x[l+1] = xm + a * (gelu(ln2 Wu + bu) Wd + bd)
-            self._dgrad(dx, blk.mlp_down_w, self.du, kind=_lib.EPI_DGELU, alpha=a, aux=self.u[l])
+            self._dgrad(dx, blk.mlp_down_w, self.du, kind=_lib.EPI_DGELU, alpha=a, aux=self.gelu_grad[l])
             self._wgrad(self.g[l], dx, blk.g_mlp_down_w, a)
             ops.colsum(dx, blk.g_mlp_down_b, a)
             self._wgrad(self.ln2[l], self.du, blk.g_mlp_up_w, 1.0)

@@ -60,8 +60,9 @@ uint64_t gptb200_launch_count(void);
  * N must be multiples of 8 elements; pointers 16-byte aligned.
  */
 #define GPTB200_EPI_BF16 0       /* C bf16 = resid + alpha*(bf16(acc) + bias), each step rounded to bf16 */
-#define GPTB200_EPI_BIAS_GELU 1  /* aux bf16 = bf16(acc)+bias; C bf16 = gelu_tanh(aux) */
-#define GPTB200_EPI_DGELU 2      /* C bf16 = bf16(alpha*acc) * gelu_tanh'(aux) */
+#define GPTB200_EPI_BIAS_GELU 1  /* u = bf16(bf16(acc)+bias); C bf16 = gelu_tanh(u);
+                                    aux bf16 = gelu_tanh'(u) (saved for the backward) */
+#define GPTB200_EPI_DGELU 2      /* C bf16 = bf16(alpha*acc) * aux, aux from EPI_BIAS_GELU */
 #define GPTB200_EPI_F32 3        /* C fp32 = alpha*acc (accumulate=1: C += alpha*acc) */
 #define GPTB200_EPI_F32_ATOMIC 4 /* C fp32 += alpha*acc with atomics; K may be split across CTAs */
 #define GPTB200_EPI_BIAS_ROPE 5  /* C bf16 = bf16(acc)+bias, then columns < rope_cols rotated by

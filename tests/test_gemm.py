@@ -50,26 +50,27 @@ def test_bias_alpha_residual(cuda):
 
 
 def test_gelu_and_dgelu(cuda):
+    """Forward: C = gelu(u), aux = gelu'(u) with u = bf16(bf16(acc) + bias).
+    Backward: C = bf16(alpha * acc) * aux."""
+
     m, n, k = 512, 1024, 256
     a, b, _, b_st = _operands(m, n, k, 0, 1, cuda, 2)
     bias = (0.1 * torch.randn(n, device=cuda)).bfloat16()
-    u = torch.empty(m, n, device=cuda, dtype=torch.bfloat16)
-    g = torch.empty_like(u)
-    ops.gemm(a, b_st, g, b_mn_major=True, m=m, n=n, k=k, kind=_lib.EPI_BIAS_GELU, bias=bias, aux=u)
-    u_ref = ((a.float() @ b.float().t()).bfloat16().float() + bias.float()).bfloat16().float()
-    assert _rel(u, u_ref) < 4e-3
-    g_ref = torch.nn.functional.gelu(u.float(), approximate="tanh")
-    assert _rel(g, g_ref) < 4e-3
-    # dgelu: C = bf16(alpha * dy @ w^T) * gelu'(u)
+    gp = torch.empty(m, n, device=cuda, dtype=torch.bfloat16)
+    g = torch.empty_like(gp)
+    ops.gemm(a, b_st, g, b_mn_major=True, m=m, n=n, k=k, kind=_lib.EPI_BIAS_GELU, bias=bias, aux=gp)
+    u = ((a.float() @ b.float().t()).bfloat16().float() + bias.float()).bfloat16().float()
+    x = u.clone().requires_grad_(True)
+    g_ref = torch.nn.functional.gelu(x, approximate="tanh")
+    g_ref.sum().backward()
+    assert _rel(g, g_ref.detach()) < 4e-3
+    assert _rel(gp, x.grad) < 4e-3
     dy = torch.randn(m, 256, device=cuda).bfloat16()
     w = torch.randn(n, 256, device=cuda).bfloat16()  # [N, K] K-major
     du = torch.empty(m, n, device=cuda, dtype=torch.bfloat16)
-    ops.gemm(dy, w, du, m=m, n=n, k=256, kind=_lib.EPI_DGELU, alpha=0.5, aux=u)
-    x = u.float().requires_grad_(True)
-    gl = torch.nn.functional.gelu(x, approximate="tanh")
+    ops.gemm(dy, w, du, m=m, n=n, k=256, kind=_lib.EPI_DGELU, alpha=0.5, aux=gp)
     up = (0.5 * (dy.float() @ w.float().t())).bfloat16().float()
-    (gl * up).sum().backward()
-    assert _rel(du, x.grad) < 5e-3
+    assert _rel(du, up * gp.float()) < 5e-3
 
 
 @pytest.mark.parametrize("k", [64, 4096, 20000])
