@@ -24,6 +24,7 @@ extern "C" const char* gptb200_status_string(int status) {
     case GPTB200_EUNSUPPORTED: return "unsupported option combination";
     case GPTB200_EDEVICE: return "a kernel reported a device-side error";
     case GPTB200_ERANGE: return "token id outside the vocabulary";
+    case GPTB200_ETOOLARGE: return "size exceeds the fixed scratch of this allocation-free entry point";
     default:
       if (status < 0) return cudaGetErrorString(static_cast<cudaError_t>(-status));
       return "unknown status";

@@ -13,6 +13,7 @@
 // 115-302 (invalid targets: +inf loss and no gradient; rows >= the semantic
 // vocabulary get no probability mass and no gradient).
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 #include "gemm.cuh"
@@ -121,6 +122,64 @@ extern "C" int gptb200_lce_fwd(const void* hidden, const void* embedding, const 
     GPTB200_CHECK_LAUNCH();
   }
   return 0;
+}
+
+// ------------------------------------------------------------------ allocation-free forward
+// Scratch of gptb200_lce_fwd_noalloc: the per-(row, vocabulary tile) partials
+// and the target logits, in a fixed device array instead of a caller
+// workspace. Every GPU that loads this library holds these 8 MiB until the
+// process exits.
+constexpr int64_t kNoAllocPartials = int64_t(1) << 20;   // float2 entries: rows x vocab tiles
+constexpr int64_t kNoAllocRows = 16384;                  // target logits
+constexpr int64_t kNoAllocBytes = kNoAllocPartials * 8 + kNoAllocRows * 4;
+static __device__ __align__(256) unsigned char g_lce_noalloc_scratch[kNoAllocBytes];
+
+// Device address of the scratch array for the current device. In host code
+// the array's name is only a host-side stand-in, so the address is looked up
+// once per device (with that device current) and cached.
+static void* noalloc_scratch_address(int* status) {
+  static std::mutex mu;
+  static void* addr[64] = {nullptr};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    *status = -static_cast<int>(e);
+    return nullptr;
+  }
+  if (dev < 0 || dev >= 64) {
+    *status = GPTB200_EUNSUPPORTED;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_lce_noalloc_scratch);
+    if (e != cudaSuccess || !p) {
+      *status = e != cudaSuccess ? -static_cast<int>(e) : GPTB200_EDEVICE;
+      return nullptr;
+    }
+    addr[dev] = p;
+  }
+  *status = GPTB200_OK;
+  return addr[dev];
+}
+
+extern "C" int gptb200_lce_fwd_noalloc(const void* hidden, const void* embedding,
+                                       const int32_t* targets, int64_t n, int64_t d,
+                                       int64_t v_storage, int64_t v_semantic, float* losses,
+                                       float* lse, float* mean_loss, void* stream) {
+  if (n <= 0 || v_storage <= 0) return GPTB200_EINVAL;
+  const int64_t tiles = lce_tiles_n(v_storage);
+  if (n > kNoAllocRows || n * tiles > kNoAllocPartials) return GPTB200_ETOOLARGE;
+  int status = GPTB200_OK;
+  void* scratch = noalloc_scratch_address(&status);
+  if (!scratch) return status;
+  // Same layout as the workspace of gptb200_lce_fwd: partials, then (256-byte
+  // aligned) the target logits. Both are fully rewritten by every call before
+  // they are read, so nothing needs clearing between calls.
+  static_assert(kNoAllocPartials * 8 % 256 == 0, "target logits must stay 256-byte aligned");
+  return gptb200_lce_fwd(hidden, embedding, targets, n, d, v_storage, v_semantic, losses, lse,
+                         mean_loss, scratch, stream);
 }
 
 extern "C" size_t gptb200_lce_bwd_workspace_size(int64_t n, int64_t v_storage) {

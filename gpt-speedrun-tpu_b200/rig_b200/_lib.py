@@ -109,6 +109,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         c_int,
         [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp],
     ),
+    "gptb200_lce_fwd_noalloc": (
+        c_int, [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp]),
     "gptb200_lce_bwd_workspace_size": (c_size, [c_i64, c_i64]),
     "gptb200_lce_bwd": (
         c_int,

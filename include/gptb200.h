@@ -32,6 +32,7 @@ extern "C" {
 #define GPTB200_EUNSUPPORTED 3 /* unsupported combination of options */
 #define GPTB200_EDEVICE 4      /* a kernel reported a device-side error (bounded wait ran out) */
 #define GPTB200_ERANGE 5       /* token id outside the vocabulary */
+#define GPTB200_ETOOLARGE 6    /* size exceeds the fixed scratch of an allocation-free entry point */
 
 /* Library identification; no reference counterpart. */
 const char* gptb200_version(void);
@@ -177,6 +178,23 @@ size_t gptb200_lce_fwd_workspace_size(int64_t n, int64_t v_storage);
 int gptb200_lce_fwd(const void* hidden, const void* embedding, const int32_t* targets, int64_t n,
                     int64_t d, int64_t v_storage, int64_t v_semantic, float* losses, float* lse,
                     float* mean_loss, void* workspace, void* stream);
+
+/* Allocation-free variant of gptb200_lce_fwd, for callers that cannot allocate
+ * device memory or own a workspace: for example an XLA custom-call handler,
+ * whose device memory is owned by XLA's allocator, or code recording a CUDA
+ * graph, where cudaMalloc is not allowed. Same arguments and results as
+ * gptb200_lce_fwd without `workspace`: the scratch lives in a fixed 8 MiB
+ * device array inside this library, held by every GPU that loads it until the
+ * process exits. Limits: n <= 16384 rows and n * ceil(v_storage / 256) <=
+ * 1,048,576 (about 5,300 rows at vocabulary 50,304); larger sizes return
+ * GPTB200_ETOOLARGE before anything is launched. The first call on a device
+ * looks up the array's device address (a one-time set-up), so make it before
+ * any stream capture. All calls share the one array: calls that overlap on the
+ * GPU (different streams, or devices sharing nothing but this process) race.
+ * No counterpart in the reference. */
+int gptb200_lce_fwd_noalloc(const void* hidden, const void* embedding, const int32_t* targets,
+                            int64_t n, int64_t d, int64_t v_storage, int64_t v_semantic,
+                            float* losses, float* lse, float* mean_loss, void* stream);
 
 /* Backward with per-token cotangent dlosses (fp32 [n]; for the mean this is
  * 1/n everywhere). dhidden bf16 [n, d] is written; dembedding fp32
