@@ -84,15 +84,16 @@ template <int CH>
 __global__ void __launch_bounds__(128, 6) rms_bwd_kernel(
     const bf16* __restrict__ x, const bf16* __restrict__ scale, const float* __restrict__ rstd_in,
     const bf16* __restrict__ dy, const bf16* dx_in, bf16* dx_out, float* __restrict__ dscale,
-    int64_t rows, int d) {
-  extern __shared__ float red[];  // [warps_per_block][d]
+    float* __restrict__ dcol, float col_alpha, int64_t rows, int d) {
+  extern __shared__ float red[];  // [2][warps_per_block][d]: dscale, then column sums of dx_out
   const int lane = threadIdx.x & 31;
   const int wib = threadIdx.x >> 5;
   const int wpb = blockDim.x >> 5;
   const int64_t warps = (int64_t)gridDim.x * wpb;
   const int nch = d >> 3;
   float* myred = red + wib * d;
-  for (int i = lane; i < d; i += 32) myred[i] = 0.f;
+  float* mycol = red + (wpb + wib) * d;
+  for (int i = lane; i < d; i += 32) myred[i] = mycol[i] = 0.f;
   __syncwarp();
   uint4 sc[CH];
 #pragma unroll
@@ -163,15 +164,30 @@ __global__ void __launch_bounds__(128, 6) rms_bwd_kernel(
           ow[j] = pack_bf16x2(v0, v1);
         }
         *reinterpret_cast<uint4*>(dx_out + r * d + ch * 8) = o;
+        if (dcol) {  // column sums of the stored (bf16) gradient, for a bias gradient
+          float4* cs = reinterpret_cast<float4*>(mycol + ch * 8);
+          float4 c0 = cs[0], c1 = cs[1];
+          float f[8];
+          unpack_bf16x2(ow[0], f[0], f[1]);
+          unpack_bf16x2(ow[1], f[2], f[3]);
+          unpack_bf16x2(ow[2], f[4], f[5]);
+          unpack_bf16x2(ow[3], f[6], f[7]);
+          cs[0] = make_float4(c0.x + f[0], c0.y + f[1], c0.z + f[2], c0.w + f[3]);
+          cs[1] = make_float4(c1.x + f[4], c1.y + f[5], c1.z + f[6], c1.w + f[7]);
+        }
       }
     }
   }
   // Reduce the per-warp dscale partials inside the block, then one atomic per column.
   __syncthreads();
   for (int col = threadIdx.x; col < d; col += blockDim.x) {
-    float s = 0.f;
-    for (int w = 0; w < wpb; ++w) s += red[w * d + col];
+    float s = 0.f, c = 0.f;
+    for (int w = 0; w < wpb; ++w) {
+      s += red[w * d + col];
+      c += red[(wpb + w) * d + col];
+    }
     atomicAdd(dscale + col, s);
+    if (dcol) atomicAdd(dcol + col, col_alpha * c);
   }
 }
 
@@ -186,17 +202,18 @@ static int rms_fwd_launch(const bf16* x, const bf16* s, bf16* y, float* rstd, in
 
 template <int CH>
 static int rms_bwd_launch(const bf16* x, const bf16* s, const float* rstd, const bf16* dy,
-                          const bf16* dxi, bf16* dxo, float* dscale, int64_t rows, int d,
-                          cudaStream_t st) {
+                          const bf16* dxi, bf16* dxo, float* dscale, float* dcol, float col_alpha,
+                          int64_t rows, int d, cudaStream_t st) {
   const int threads = 128;
   int64_t blocks = std::min<int64_t>((rows + 3) / 4, (int64_t)sms() * 8);
-  size_t smem = (size_t)(threads / 32) * d * sizeof(float);
+  size_t smem = 2 * (size_t)(threads / 32) * d * sizeof(float);
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(rms_bwd_kernel<CH>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return -static_cast<int>(e);
   }
-  rms_bwd_kernel<CH><<<(int)blocks, threads, smem, st>>>(x, s, rstd, dy, dxi, dxo, dscale, rows, d);
+  rms_bwd_kernel<CH><<<(int)blocks, threads, smem, st>>>(x, s, rstd, dy, dxi, dxo, dscale, dcol,
+                                                       col_alpha, rows, d);
   GPTB200_CHECK_LAUNCH();
   return 0;
 }
@@ -226,7 +243,8 @@ extern "C" int gptb200_rms_norm_fwd(const void* x, const void* scale, void* y, f
 
 extern "C" int gptb200_rms_norm_bwd(const void* x, const void* scale, const float* rstd,
                                     const void* dy, const void* dx_in, void* dx_out,
-                                    float* dscale, int64_t rows, int64_t d, void* stream) {
+                                    float* dscale, float* dx_colsum, float colsum_alpha,
+                                    int64_t rows, int64_t d, void* stream) {
   if (!x || !scale || !rstd || !dy || !dx_out || !dscale || rows <= 0 || d <= 0)
     return GPTB200_EINVAL;
   if (d % 8 || d > 2048 || !aligned16(x) || !aligned16(dy) || !aligned16(dx_out) ||
@@ -239,11 +257,11 @@ extern "C" int gptb200_rms_norm_bwd(const void* x, const void* scale, const floa
   auto DXI = reinterpret_cast<const bf16*>(dx_in);
   auto DXO = reinterpret_cast<bf16*>(dx_out);
   int ch = (int)((d / 8 + 31) / 32);
-  if (ch <= 1) return rms_bwd_launch<1>(X, S, rstd, DY, DXI, DXO, dscale, rows, (int)d, st);
-  if (ch <= 2) return rms_bwd_launch<2>(X, S, rstd, DY, DXI, DXO, dscale, rows, (int)d, st);
-  if (ch <= 3) return rms_bwd_launch<3>(X, S, rstd, DY, DXI, DXO, dscale, rows, (int)d, st);
-  if (ch <= 4) return rms_bwd_launch<4>(X, S, rstd, DY, DXI, DXO, dscale, rows, (int)d, st);
-  return rms_bwd_launch<8>(X, S, rstd, DY, DXI, DXO, dscale, rows, (int)d, st);
+  if (ch <= 1) return rms_bwd_launch<1>(X, S, rstd, DY, DXI, DXO, dscale, dx_colsum, colsum_alpha, rows, (int)d, st);
+  if (ch <= 2) return rms_bwd_launch<2>(X, S, rstd, DY, DXI, DXO, dscale, dx_colsum, colsum_alpha, rows, (int)d, st);
+  if (ch <= 3) return rms_bwd_launch<3>(X, S, rstd, DY, DXI, DXO, dscale, dx_colsum, colsum_alpha, rows, (int)d, st);
+  if (ch <= 4) return rms_bwd_launch<4>(X, S, rstd, DY, DXI, DXO, dscale, dx_colsum, colsum_alpha, rows, (int)d, st);
+  return rms_bwd_launch<8>(X, S, rstd, DY, DXI, DXO, dscale, dx_colsum, colsum_alpha, rows, (int)d, st);
 }
 
 // ------------------------------------------------------------------ embedding

@@ -87,7 +87,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
     "gptb200_rms_norm_fwd": (c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_vp]),
     "gptb200_rms_norm_bwd": (
-        c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_vp]),
+        c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_f32, c_i64, c_i64, c_vp]),
     "gptb200_embedding_fwd": (c_int, [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp]),
     "gptb200_embedding_bwd": (c_int, [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp]),
     "gptb200_rope_tables": (c_int, [c_vp, c_vp, c_i64, c_i64, c_vp]),

@@ -359,24 +359,24 @@ class GPTTrainer:
         self.grads.zero_()
         ops.lce_bwd(self.lnf, self.out_emb, self.targets.view(-1), self.lse_ce, self.cot,
                     c.semantic_vocab_size, self.dln, self.g_out_emb, workspace=self.lce_bwd_ws)
+        # The residual-stream gradient each RMSNorm backward produces is also the
+        # gradient of the bias of the branch below it; its column sums are fused.
         ops.rms_norm_bwd(self.x[c.layers], self.final_scale, self.rstdf, self.dln, None, self.dx,
-                         self.g_final_scale)
+                         self.g_final_scale, self.blocks[c.layers - 1].g_mlp_down_b, a)
         dx = self.dx
         for l in reversed(range(c.layers)):
             blk = self.blocks[l]
             # MLP: x[l+1] = xm + a * (gelu(ln2 Wu + bu) Wd + bd)
             self._dgrad(dx, blk.mlp_down_w, self.du, kind=_lib.EPI_DGELU, alpha=a, aux=self.gelu_grad[l])
             self._wgrad(self.g[l], dx, blk.g_mlp_down_w, a)
-            ops.colsum(dx, blk.g_mlp_down_b, a)
             self._wgrad(self.ln2[l], self.du, blk.g_mlp_up_w, 1.0)
             ops.colsum(self.du, blk.g_mlp_up_b, 1.0)
             self._dgrad(self.du, blk.mlp_up_w, self.dln)
             ops.rms_norm_bwd(self.xm[l], blk.ln2_scale, self.rstd2[l], self.dln, dx, dx,
-                             blk.g_ln2_scale)
+                             blk.g_ln2_scale, blk.g_attn_b, a)
             # attention: xm = x + a * (att Wo + bo)
             self._dgrad(dx, blk.attn_w, self.datt, alpha=a)
             self._wgrad(self.att[l], dx, blk.g_attn_w, a)
-            ops.colsum(dx, blk.g_attn_b, a)
             q, k, v = self._qkv_views(self.qkv[l])
             dq, dk, dv = self._qkv_views(self.dqkv)
             ops.attention_bwd(q, k, v, self._bthd(self.att[l]), self._bthd(self.datt), self.lse[l],
@@ -385,8 +385,9 @@ class GPTTrainer:
             self._wgrad(self.ln1[l], self.dqkv, blk.g_qkv_w, 1.0)
             ops.colsum(self.dqkv, blk.g_qkv_b, 1.0)
             self._dgrad(self.dqkv, blk.qkv_w, self.dln)
+            below = self.blocks[l - 1].g_mlp_down_b if l > 0 else None
             ops.rms_norm_bwd(self.x[l], blk.ln1_scale, self.rstd1[l], self.dln, dx, dx,
-                             blk.g_ln1_scale)
+                             blk.g_ln1_scale, below, a)
             if reduce_hook is not None:
                 reduce_hook(*self.layout.block_ranges[l])
         ops.embedding_bwd(self.tokens.view(-1), dx, self.g_tok_emb)

@@ -141,11 +141,14 @@ def rms_norm_fwd(x: torch.Tensor, scale: torch.Tensor, y: torch.Tensor, rstd: to
     return y, rstd
 
 
-def rms_norm_bwd(x, scale, rstd, dy, dx_in, dx_out, dscale):
-    _cuda(x, scale, rstd, dy, dx_in, dx_out, dscale)
+def rms_norm_bwd(x, scale, rstd, dy, dx_in, dx_out, dscale, dx_colsum=None, colsum_alpha=1.0):
+    """dx_out = dx_in + d(rms_norm)/dx . dy; dscale +=; dx_colsum += alpha * colsum(dx_out)."""
+
+    _cuda(x, scale, rstd, dy, dx_in, dx_out, dscale, dx_colsum)
     rows, d = x.shape
     call("gptb200_rms_norm_bwd", x.data_ptr(), scale.data_ptr(), rstd.data_ptr(), dy.data_ptr(),
-         _ptr(dx_in), dx_out.data_ptr(), dscale.data_ptr(), rows, d, _stream())
+         _ptr(dx_in), dx_out.data_ptr(), dscale.data_ptr(), _ptr(dx_colsum),
+         float(colsum_alpha), rows, d, _stream())
     return dx_out
 
 

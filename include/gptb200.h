@@ -100,11 +100,13 @@ int gptb200_rms_norm_fwd(const void* x, const void* scale, void* y, float* rstd,
 
 /* Backward of rms_norm. dx_out (bf16) = dx_in (bf16 residual-stream gradient,
  * may be NULL for zero, may alias dx_out) + d(rms_norm)/dx · dy.
- * dscale (fp32 [d]) is accumulated into (+=). Replaces the XLA autodiff of
- * rig/nn.py:26-33. */
+ * dscale (fp32 [d]) is accumulated into (+=). With dx_colsum != NULL the column
+ * sums of dx_out times colsum_alpha are accumulated into dx_colsum (fp32 [d]):
+ * the bias gradient of the residual branch that consumed this gradient.
+ * Replaces the XLA autodiff of rig/nn.py:26-33. */
 int gptb200_rms_norm_bwd(const void* x, const void* scale, const float* rstd, const void* dy,
-                         const void* dx_in, void* dx_out, float* dscale, int64_t rows, int64_t d,
-                         void* stream);
+                         const void* dx_in, void* dx_out, float* dscale, float* dx_colsum,
+                         float colsum_alpha, int64_t rows, int64_t d, void* stream);
 
 /* ------------------------------------------------------------------ embedding
  * out[i, :] = bf16(table[tokens[i], :]); Replaces recipes/reference/train.py:1107

@@ -44,9 +44,13 @@ def test_rms_norm_bwd(cuda, rows, d):
     ops.rms_norm_fwd(xd, sd, yy, r)
     dx = dres.to(cuda).clone()
     dscale = torch.zeros(d, device=cuda)
-    ops.rms_norm_bwd(xd, sd, r, dyd, dx, dx, dscale)
+    colsum = torch.full((d,), 0.5, device=cuda)
+    ops.rms_norm_bwd(xd, sd, r, dyd, dx, dx, dscale, colsum, 0.25)
     assert _rel(dx.cpu().float() - dres.float(), xx.grad) < 1e-2
     assert _rel(dscale.cpu(), ss.grad) < 1e-2
+    # fused bias gradient: += alpha * column sums of the stored bf16 dx_out
+    expect = 0.5 + 0.25 * dx.cpu().float().sum(0)
+    assert torch.allclose(colsum.cpu(), expect, rtol=1e-4, atol=1e-3)
 
 
 def test_embedding(cuda):
