@@ -16,15 +16,19 @@
 //           shared tile that the next P·V MMA reads.
 //   Two CTAs fit on an SM (112 KB shared memory, 256 TMEM columns each).
 // Backward (attn_bwd_tc): one CTA per (128-key tile, batch*head), looping over
-// query tiles from the diagonal down. Per query tile the MMA thread computes
-// Sᵀ = K·Qᵀ and dPᵀ = V·dOᵀ into TMEM; the softmax warps (thread = key row)
-// form Pᵀ = exp2(Sᵀ·c - lse) and dSᵀ = Pᵀ∘(dPᵀ - δ) in 32-column chunks,
-// writing both as bf16 swizzled tiles; then dQ = dS·K (dSᵀ read as an
-// MN-major A operand), dV += Pᵀ·dO and dK += dSᵀ·Q run on the tensor cores.
-// dQ is read back from TMEM and added to an fp32 accumulator with vector
-// atomics; dK, dV leave TMEM once at the end. q and k arrive already rotated
-// (RoPE runs in the QKV projection epilogue); with RoPE tables the backward
-// rotates dq and dk back so they are gradients of the unrotated inputs.
+// 64-query tiles from the diagonal down. 19 warps: TMA (K, V once; Q/dO into a
+// 4-stage ring), a scores MMA thread (S^T = K Q^T and dP^T = V dO^T into one
+// of three 128-column TMEM buffers, as far ahead as the buffers allow), a
+// gradient MMA thread (dV += P^T dO and dK += dS^T Q with P^T / dS^T read
+// straight from TMEM; dQ = dS K per pair of tiles, dS^T read MN-major from a
+// shared-memory ring), and two softmax warpgroups taking alternate tiles
+// (thread = key row: P^T = exp2(S^T c - lse), dS^T = P^T (dP^T - delta),
+// written over the S^T columns as bf16 pairs). Two issuing threads keep the
+// tensor pipe fed while either waits on a barrier. dQ leaves TMEM through a
+// TMA reduce-add into an fp32 accumulator; dK, dV leave TMEM once at the end.
+// q and k arrive already rotated (RoPE runs in the QKV projection epilogue);
+// with RoPE tables the backward rotates dq and dk back so they are gradients
+// of the unrotated inputs.
 // Every mbarrier wait is bounded (common.cuh). Semantics follow
 // rig/kernels/tpu_flash_attention.py:171-207 (fp32 statistics, bf16 P).
 #include <algorithm>
@@ -321,19 +325,24 @@ __global__ void __launch_bounds__(kThreads, 3)
 }
 
 // ------------------------------------------------------------------ backward
-constexpr int BT = 128;                 // keys per CTA = queries per inner tile
+constexpr int BT = 128;                 // keys per CTA (TMEM lanes)
+constexpr int BQ = 64;                  // queries per inner tile
 constexpr int BT_BYTES = BT * 128;      // 128 rows x 64 bf16
-constexpr int kBwdSoftWarps = 8;        // two per TMEM lane quadrant, 64 columns each
-constexpr int kBwdThreads = 64 + 32 * kBwdSoftWarps;
+constexpr int BQ_BYTES = BQ * 128;      // 64 rows x 64 bf16
+constexpr int kQStages = 4;             // Q / dO tile ring
+constexpr int kBwdWgWarps = 8;          // per softmax warpgroup: two warps per TMEM lane quadrant
+constexpr int kBwdScoreWarp = 2 + 2 * kBwdWgWarps;  // issues the S^T / dP^T MMAs
+constexpr int kBwdThreads = 32 * (kBwdScoreWarp + 1);
 
 struct BwdSmem {
   static constexpr int K = 0;
   static constexpr int V = K + BT_BYTES;
-  static constexpr int Q = V + BT_BYTES;          // 2 stages
-  static constexpr int DO = Q + 2 * BT_BYTES;     // 2 stages
-  static constexpr int DST = DO + 2 * BT_BYTES;   // 2 buffers x 2 blocks of 64 queries
-  static constexpr int DQS = DST + 4 * BT_BYTES;  // dQ staging: 8 warps x (32 x 32 fp32)
-  static constexpr int BAR = DQS + 8 * 4096;
+  static constexpr int Q = V + BT_BYTES;                // kQStages tiles
+  static constexpr int DO = Q + kQStages * BQ_BYTES;    // kQStages tiles
+  static constexpr int DST = DO + kQStages * BQ_BYTES;  // ring of 4 dS^T tiles [128 keys x 64 queries]
+  static constexpr int DQS = DST + 4 * BT_BYTES;        // dQ staging: 8 warps x (32 x 32 fp32)
+  static constexpr int STAT = DQS + 8 * 4096;           // per warp: 32 x lse*log2(e), 32 x delta
+  static constexpr int BAR = STAT + 16 * 256;
   static constexpr int TOTAL = BAR + 256 + 1023;
 };
 
@@ -346,39 +355,40 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                                            ~static_cast<uintptr_t>(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + BwdSmem::BAR);
   uint64_t* kv_full = bars + 0;
-  uint64_t* q_full = bars + 1;   // [2]
-  uint64_t* q_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;
-  uint64_t* p_full = bars + 6;
-  uint64_t* pv_done = bars + 7;  // dV MMA of the tile has read P^T from TMEM
-  uint64_t* dq_full = bars + 8;
-  uint64_t* dq_free = bars + 9;
-  uint64_t* ds_free = bars + 10;  // [2]: dS^T buffer read by its dQ and dK MMAs
-  uint64_t* fin = bars + 12;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  uint64_t* q_full = bars + 1;    // [4]
+  uint64_t* q_empty = bars + 5;   // [4]
+  uint64_t* s_full = bars + 9;    // [3]: S^T and dP^T of a tile are in TMEM buffer b
+  uint64_t* p_full = bars + 12;   // [3]: P^T, dS^T of a tile written (TMEM buffer b, smem ring)
+  uint64_t* done = bars + 15;     // [4]: every MMA issued up to the end of tile i has completed
+  uint64_t* dq_full = bars + 19;  // [2]: dQ of query pair j is in TMEM
+  uint64_t* dq_free = bars + 21;  // [2]: ... and has been read out
+  uint64_t* fin = bars + 23;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 24);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nt = (p.T + BT - 1) / BT;
   const int kt = (int)blockIdx.x;
   const int bh = blockIdx.y;
   const int b = bh / p.H, h = bh - b * p.H;
   const int k0 = kt * BT;
-  const int nq = nt - kt;  // query tiles kt .. nt-1
+  const int nq = (p.T - k0 + BQ - 1) / BQ;  // 64-query tiles from the diagonal to the end
   int* err = &g_attn_error;
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < kQStages; ++s) {
       mbar_init(&q_full[s], 1);
-      mbar_init(&q_empty[s], 1);
-      mbar_init(&ds_free[s], 1);
+      mbar_init(&q_empty[s], 2);  // the scores MMAs and the gradient MMAs of the tile
     }
-    mbar_init(s_full, 1);
-    mbar_init(p_full, kBwdSoftWarps);
-    mbar_init(pv_done, 1);
-    mbar_init(dq_full, 1);
-    mbar_init(dq_free, kBwdSoftWarps);
+    for (int s = 0; s < 3; ++s) {
+      mbar_init(&s_full[s], 1);
+      mbar_init(&p_full[s], kBwdWgWarps);
+    }
+    for (int s = 0; s < 4; ++s) mbar_init(&done[s], 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&dq_full[s], 1);
+      mbar_init(&dq_free[s], kBwdWgWarps);
+    }
     mbar_init(fin, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -387,10 +397,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  // TMEM columns: S^T | dP^T | dV | dK | dQ | P^T (bf16 pairs)
+  // TMEM columns: three tile buffers of 128 columns, then dV | dK. In buffer
+  // b, columns [0, 64) receive S^T and [64, 128) dP^T (fp32, lane = key). The
+  // softmax writes P^T and dS^T as bf16 pairs over the S^T half (warp half hf
+  // owns columns 32 hf + [0, 16) for P^T and 32 hf + [16, 32) for dS^T); the
+  // dP^T half then holds dQ when the tile closes a query pair.
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem, tDP = tmem + 128, tDV = tmem + 256, tDK = tmem + 320,
-                 tDQ = tmem + 384, tP = tmem + 448;
+  const uint32_t tDV = tmem + 384, tDK = tmem + 448;
+  auto tBuf = [&](int bb) { return tmem + 128 * bb; };
 
   if (warp == 0) {
     if (lane == 0) {
@@ -398,113 +412,126 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tma_load_4d(sm + BwdSmem::K, &tmK, kv_full, 0, k0, h, b);
       tma_load_4d(sm + BwdSmem::V, &tmV, kv_full, 0, k0, h, b);
       for (int it = 0; it < nq; ++it) {
-        const int s = it & 1;
-        if (!mbar_wait(&q_empty[s], ((it >> 1) & 1) ^ 1, abort_flag, err)) break;
-        mbar_arrive_expect_tx(&q_full[s], 2 * BT_BYTES);
-        const int qq = (kt + it) * BT;
-        tma_load_4d(sm + BwdSmem::Q + s * BT_BYTES, &tmQ, &q_full[s], 0, qq, h, b);
-        tma_load_4d(sm + BwdSmem::DO + s * BT_BYTES, &tmDO, &q_full[s], 0, qq, h, b);
+        const int s = it % kQStages;
+        if (!mbar_wait(&q_empty[s], ((it / kQStages) & 1) ^ 1, abort_flag, err)) break;
+        mbar_arrive_expect_tx(&q_full[s], 2 * BQ_BYTES);
+        const int qq = k0 + it * BQ;
+        tma_load_4d(sm + BwdSmem::Q + s * BQ_BYTES, &tmQ, &q_full[s], 0, qq, h, b);
+        tma_load_4d(sm + BwdSmem::DO + s * BQ_BYTES, &tmDO, &q_full[s], 0, qq, h, b);
       }
     }
   } else if (warp == 1) {
+    // Gradient MMAs of tile `it` once its softmax is done. This thread and
+    // the scores thread (warp 18) issue independently: a thread that stops at
+    // a barrier leaves the tensor pipe to the other one.
     if (lane == 0) {
-      constexpr uint32_t idS = umma_idesc_bf16(128, 128, 0, 0);
-      constexpr uint32_t idKN = umma_idesc_bf16(128, 64, 0, 1);  // A K-major, B MN-major
-      constexpr uint32_t idMN = umma_idesc_bf16(128, 64, 1, 1);  // A MN-major, B MN-major
-      const uint32_t sK = smem_u32(sm + BwdSmem::K), sV = smem_u32(sm + BwdSmem::V);
-      // S^T = K Q^T and dP^T = V dO^T for query tile `it` into TMEM.
-      auto issue_s = [&](int it) {
-        const int s = it & 1;
-        const uint32_t sQ = smem_u32(sm + BwdSmem::Q + s * BT_BYTES);
-        const uint32_t sDO = smem_u32(sm + BwdSmem::DO + s * BT_BYTES);
-#pragma unroll
-        for (int k = 0; k < HD / 16; ++k) {
-          umma_bf16(tS, umma_smem_desc(sK + k * 32, 16, 1024), umma_smem_desc(sQ + k * 32, 16, 1024),
-                    idS, k > 0);
-          umma_bf16(tDP, umma_smem_desc(sV + k * 32, 16, 1024),
-                    umma_smem_desc(sDO + k * 32, 16, 1024), idS, k > 0);
-        }
-        umma_commit(s_full);
-      };
-      bool ok = mbar_wait(kv_full, 0, abort_flag, err) && mbar_wait(&q_full[0], 0, abort_flag, err);
-      if (ok) {
-        tc_fence_after();
-        issue_s(0);
-      }
-      for (int it = 0; ok && it < nq; ++it) {
-        const int s = it & 1;
-        const uint32_t sQ = smem_u32(sm + BwdSmem::Q + s * BT_BYTES);
-        const uint32_t sDO = smem_u32(sm + BwdSmem::DO + s * BT_BYTES);
-        const uint32_t sdSt = smem_u32(sm + BwdSmem::DST + s * 2 * BT_BYTES);
-        ATTN_TRACE(64 * it + 0);
-        if (!mbar_wait(p_full, it & 1, abort_flag, err)) break;
-        ATTN_TRACE(64 * it + 1);
-        tc_fence_after();
-        // dV += P^T · dO with P^T read straight from TMEM (K = queries).
-#pragma unroll
-        for (int k = 0; k < BT / 16; ++k)
-          umma_bf16_ts(tDV, tP + k * 8, umma_smem_desc(sDO + k * 2048, BT_BYTES, 1024), idKN,
-                       (it > 0 || k > 0));
-        umma_commit(pv_done);
-        // Scores of the next query tile, so the softmax warps can start on
-        // them while dQ and dK of this tile run.
-        if (it + 1 < nq) {
-          if (!mbar_wait(&q_full[(it + 1) & 1], ((it + 1) >> 1) & 1, abort_flag, err)) break;
-          tc_fence_after();
-          issue_s(it + 1);
-        }
+      constexpr uint32_t idKN = umma_idesc_bf16(128, 64, 0, 1);  // dV, dK: A in TMEM, B MN-major
+      constexpr uint32_t idMN = umma_idesc_bf16(128, 64, 1, 1);  // dQ: A, B MN-major
+      const uint32_t sK = smem_u32(sm + BwdSmem::K);
+      for (int it = 0; it < nq; ++it) {
+        const int bb = it % 3, s = it % kQStages;
+        if (!mbar_wait(&p_full[bb], (it / 3) & 1, abort_flag, err)) break;
         ATTN_TRACE(64 * it + 2);
-        if (it > 0 && !mbar_wait(dq_free, (it - 1) & 1, abort_flag, err)) break;
-        ATTN_TRACE(64 * it + 3);
         tc_fence_after();
-        // dQ = dS · K: A = dS^T read MN-major (M = queries in two 64-wide
-        // blocks 16 KB apart), B = K tile MN-major (N = head dim).
+        const uint32_t sQ = smem_u32(sm + BwdSmem::Q + s * BQ_BYTES);
+        const uint32_t sDO = smem_u32(sm + BwdSmem::DO + s * BQ_BYTES);
+        // dV += P^T dO and dK += dS^T Q with the A operands read from TMEM:
+        // queries 16k..16k+15 sit at column 32 (k/2) + 8 (k%2) of the buffer
+        // (P^T), 16 further on for dS^T.
 #pragma unroll
-        for (int k = 0; k < BT / 16; ++k)
-          umma_bf16(tDQ, umma_smem_desc(sdSt + k * 2048, BT_BYTES, 1024),
-                    umma_smem_desc(sK + k * 2048, BT_BYTES, 1024), idMN, k > 0);
-        umma_commit(dq_full);
-        // dK += dS^T · Q  (A K-major over queries, B MN-major)
-#pragma unroll
-        for (int k = 0; k < BT / 16; ++k)
-          umma_bf16(tDK, umma_smem_desc(sdSt + (k >> 2) * BT_BYTES + (k & 3) * 32, 16, 1024),
-                    umma_smem_desc(sQ + k * 2048, BT_BYTES, 1024), idKN, (it > 0 || k > 0));
-        umma_commit(&ds_free[s]);
+        for (int k = 0; k < BQ / 16; ++k) {
+          const uint32_t acol = tBuf(bb) + (k >> 1) * 32 + (k & 1) * 8;
+          umma_bf16_ts(tDV, acol, umma_smem_desc(sDO + k * 2048, BQ_BYTES, 1024), idKN,
+                       (it > 0 || k > 0));
+          umma_bf16_ts(tDK, acol + 16, umma_smem_desc(sQ + k * 2048, BQ_BYTES, 1024), idKN,
+                       (it > 0 || k > 0));
+        }
         umma_commit(&q_empty[s]);
-        ATTN_TRACE(64 * it + 4);
+        ATTN_TRACE(64 * it + 7);
+        if ((it & 1) || it == nq - 1) {
+          // dQ of query pair j (tiles 2j, 2j+1) = dS K into the dP^T half of
+          // this buffer: A = the pair's two dS^T tiles of the ring read
+          // MN-major (M = 128 queries, 16 KB apart), B = K tile MN-major.
+          const int j = it >> 1;
+          const uint32_t sd = smem_u32(sm + BwdSmem::DST + ((2 * j) & 3) * BT_BYTES);
+#pragma unroll
+          for (int k = 0; k < BT / 16; ++k)
+            umma_bf16(tBuf(bb) + 64, umma_smem_desc(sd + k * 2048, BT_BYTES, 1024),
+                      umma_smem_desc(sK + k * 2048, BT_BYTES, 1024), idMN, k > 0);
+          umma_commit(&dq_full[j & 1]);
+        }
+        umma_commit(&done[it & 3]);
+        ATTN_TRACE(64 * it + 3);
       }
       umma_commit(fin);
     }
-  } else {
-    // 8 softmax warps: warp w reads TMEM lanes of quadrant w % 4 (key rows)
-    // and the query columns [64*half, 64*half + 64).
+  } else if (warp == kBwdScoreWarp) {
+    // S^T = K Q^T and dP^T = V dO^T of each tile into TMEM buffer it % 3, as
+    // far ahead as the buffers allow. The buffer last served tile it-3: read
+    // by that tile's dV / dK MMAs and, when it-3 closed a query pair, holding
+    // that pair's dQ until the softmax warps have read it out.
+    if (lane == 0) {
+      constexpr uint32_t idS = umma_idesc_bf16(128, BQ, 0, 0);
+      const uint32_t sK = smem_u32(sm + BwdSmem::K), sV = smem_u32(sm + BwdSmem::V);
+      bool ok = mbar_wait(kv_full, 0, abort_flag, err);
+      for (int it = 0; ok && it < nq; ++it) {
+        const int s = it % kQStages;
+        ATTN_TRACE(64 * it + 0);
+        if (it >= 3) {
+          const int o = it - 3;
+          if (!mbar_wait(&done[o & 3], (o >> 2) & 1, abort_flag, err)) break;
+          if ((o & 1) && !mbar_wait(&dq_free[(o >> 1) & 1], (o >> 2) & 1, abort_flag, err)) break;
+        }
+        ATTN_TRACE(64 * it + 4);
+        if (!mbar_wait(&q_full[s], (it / kQStages) & 1, abort_flag, err)) break;
+        ATTN_TRACE(64 * it + 6);
+        tc_fence_after();
+        const uint32_t sQ = smem_u32(sm + BwdSmem::Q + s * BQ_BYTES);
+        const uint32_t sDO = smem_u32(sm + BwdSmem::DO + s * BQ_BYTES);
+        const uint32_t tb = tBuf(it % 3);
+#pragma unroll
+        for (int k = 0; k < HD / 16; ++k) {
+          umma_bf16(tb, umma_smem_desc(sK + k * 32, 16, 1024),
+                    umma_smem_desc(sQ + k * 32, 16, 1024), idS, k > 0);
+          umma_bf16(tb + 64, umma_smem_desc(sV + k * 32, 16, 1024),
+                    umma_smem_desc(sDO + k * 32, 16, 1024), idS, k > 0);
+        }
+        umma_commit(&s_full[it % 3]);
+        umma_commit(&q_empty[s]);
+        ATTN_TRACE(64 * it + 1);
+      }
+    }
+  } else if (warp < 2 + 2 * kBwdWgWarps) {
+    // Two softmax warpgroups take alternate query tiles (wg 0 even, wg 1 odd).
+    // Warp w reads TMEM lanes of quadrant w % 4 (key rows) and the query
+    // columns [32*hf, 32*hf + 32) of the tile. Warpgroup 0 also reads out dQ.
+    const int wg = (warp - 2) >> 3;
+    const int wl = (warp - 2) & 7;
     const int quad = warp & 3;
-    const int half = (warp - 2) >> 2;
+    const int hf = wl >> 2;
     const int r = quad * 32 + lane;
     const int key = k0 + r;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const float c = p.scale * kLog2e;
     const float* Lg = p.lse + (int64_t)bh * p.T;
     const float* Dg = p.delta + (int64_t)bh * p.T;
-    uint8_t* stage = sm + BwdSmem::DQS + (warp - 2) * 4096;
-    // Statistics of this warp's 64 query columns of tile `it`: lane j holds
-    // columns j and 32 + j (broadcast with shuffles in the inner loop).
-    float ls[2], dl[2], nls[2], ndl[2];
-    auto fetch = [&](int it, float* l2, float* d2) {
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const int t = (kt + it) * BT + half * 64 + u * 32 + lane;
-        l2[u] = (t < p.T) ? Lg[t] * kLog2e : INFINITY;  // rows past T: P = 0
-        d2[u] = (t < p.T) ? Dg[t] : 0.f;
-      }
+    uint8_t* stage = sm + BwdSmem::DQS + wl * 4096;  // dQ staging (warpgroup 0)
+    float* stat = reinterpret_cast<float*>(sm + BwdSmem::STAT + (warp - 2) * 256);
+    // lane j fetches the statistics of query column j of tile `it`
+    auto fetch = [&](int it, float& l2, float& d2) {
+      const int t = k0 + it * BQ + hf * 32 + lane;
+      l2 = (t < p.T) ? Lg[t] * kLog2e : INFINITY;  // rows past T: P = 0
+      d2 = (t < p.T) ? Dg[t] : 0.f;
     };
-    fetch(0, ls, dl);
+    float nl = 0.f, nd = 0.f;
+    if (wg < nq) fetch(wg, nl, nd);
     bool ok = true;
-    // dQ rows of query tile `it` (TMEM lane r = query (kt+it)*BT + r): one
-    // 32x32 fp32 sub-tile per warp, reduced into dq_acc by a TMA reduce-add.
-    auto flush_dq = [&](int it) {
+    // dQ rows of query pair j (TMEM lane m = query k0 + 128 j + m) from
+    // buffer bb: one 32x32 fp32 sub-tile per warp, reduced into dq_acc by a
+    // TMA reduce-add (rows past the sequence end are clipped by the map).
+    auto flush_dq = [&](int j, int bb) {
       float v[32];
-      tmem_ld32(tDQ + lane_off + half * 32, v);
+      tmem_ld32(tBuf(bb) + 64 + lane_off + hf * 32, v);
       if (lane == 0) bulk_wait_read();  // the previous reduce has read the staging tile
       __syncwarp();
 #pragma unroll
@@ -514,115 +541,118 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
-        tma_reduce_add_3d(&tmDQ, stage, half * 32, (kt + it) * BT + quad * 32, bh);
+        tma_reduce_add_3d(&tmDQ, stage, hf * 32, k0 + j * BT + quad * 32, bh);
         bulk_commit();
       }
     };
-    for (int it = 0; it < nq && ok; ++it) {
-      if (it + 1 < nq) fetch(it + 1, nls, ndl);
+    for (int it = wg; it < nq && ok; it += 2) {
+      const int bb = it % 3;
+      const uint32_t tb = tBuf(bb);
+      // this tile's statistics, broadcast to the warp through shared memory
+      __syncwarp();
+      stat[lane] = nl;
+      stat[32 + lane] = nd;
+      __syncwarp();
+      if (it + 2 < nq) fetch(it + 2, nl, nd);
       if (threadIdx.x == 64) ATTN_TRACE(64 * it + 11);
-      if (!mbar_wait(s_full, it & 1, abort_flag, err)) {
+      if (!mbar_wait(&s_full[bb], (it / 3) & 1, abort_flag, err)) {
+        ok = false;
+        break;
+      }
+      // The dS^T ring slot of this tile was last read by the dQ MMA of tile it-4.
+      if (it >= 4 && !mbar_wait(&done[(it - 3) & 3], ((it - 3) >> 2) & 1, abort_flag, err)) {
         ok = false;
         break;
       }
       if (threadIdx.x == 64) ATTN_TRACE(64 * it + 12);
-      // P^T of the previous tile has been consumed by its dV MMA; the dS^T
-      // buffer of this tile was last read by the MMAs of tile it-2.
-      if (it > 0 && !mbar_wait(pv_done, (it - 1) & 1, abort_flag, err)) {
-        ok = false;
-        break;
-      }
-      if (it >= 2 && !mbar_wait(&ds_free[it & 1], ((it >> 1) + 1) & 1, abort_flag, err)) {
-        ok = false;
-        break;
-      }
       tc_fence_after();
-      uint8_t* sdSt = sm + BwdSmem::DST + (it & 1) * 2 * BT_BYTES + half * BT_BYTES;
-      const bool diag = (it == 0);
+      uint32_t sraw[32], draw[32];
+      tmem_ld32_nw(tb + lane_off + hf * 32, sraw);
+      tmem_ld32_nw(tb + 64 + lane_off + hf * 32, draw);
+      tmem_wait_ld();
+      const int qbase = it * BQ + hf * 32;  // query index relative to k0
+      const bool diag = (it < 2);           // key r > query masks only near the diagonal
+      uint32_t pk[16], dk[16];
 #pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        float sv[16], dp[16];
-        tmem_ld16(tS + lane_off + half * 64 + cc * 16, sv);
-        tmem_ld16(tDP + lane_off + half * 64 + cc * 16, dp);
-        uint32_t pk[8], dk[8];
+      for (int j4 = 0; j4 < 8; ++j4) {
+        const float4 l4 = reinterpret_cast<const float4*>(stat)[j4];
+        const float4 d4 = reinterpret_cast<const float4*>(stat + 32)[j4];
+        const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
+        const float dl[4] = {d4.x, d4.y, d4.z, d4.w};
+        float pv[4], dv[4];
 #pragma unroll
-        for (int i = 0; i < 16; i += 2) {
-          const int qc = cc * 16 + i;  // column within this warp's 64
-          const float l0 = __shfl_sync(0xffffffffu, ls[qc >> 5], qc & 31);
-          const float l1 = __shfl_sync(0xffffffffu, ls[(qc + 1) >> 5], (qc + 1) & 31);
-          const float d0 = __shfl_sync(0xffffffffu, dl[qc >> 5], qc & 31);
-          const float d1 = __shfl_sync(0xffffffffu, dl[(qc + 1) >> 5], (qc + 1) & 31);
-          float p0 = ex2(fmaf(sv[i], c, -l0));
-          float p1 = ex2(fmaf(sv[i + 1], c, -l1));
-          if (diag && r > half * 64 + qc) p0 = 0.f;
-          if (diag && r > half * 64 + qc + 1) p1 = 0.f;
-          pk[i / 2] = pack_bf16x2(p0, p1);
-          dk[i / 2] = pack_bf16x2(p0 * (dp[i] - d0), p1 * (dp[i + 1] - d1));
+        for (int u = 0; u < 4; ++u) {
+          const int j = 4 * j4 + u;
+          pv[u] = ex2(fmaf(__uint_as_float(sraw[j]), c, -lv[u]));
+          if (diag && r > qbase + j) pv[u] = 0.f;
+          dv[u] = pv[u] * (__uint_as_float(draw[j]) - dl[u]);
         }
-        tmem_st8_nw(tP + lane_off + half * 32 + cc * 8, pk);
-        *reinterpret_cast<uint4*>(sdSt + swz128(r, 2 * cc)) = make_uint4(dk[0], dk[1], dk[2], dk[3]);
-        *reinterpret_cast<uint4*>(sdSt + swz128(r, 2 * cc + 1)) =
-            make_uint4(dk[4], dk[5], dk[6], dk[7]);
+        pk[2 * j4] = pack_bf16x2(pv[0], pv[1]);
+        pk[2 * j4 + 1] = pack_bf16x2(pv[2], pv[3]);
+        dk[2 * j4] = pack_bf16x2(dv[0], dv[1]);
+        dk[2 * j4 + 1] = pack_bf16x2(dv[2], dv[3]);
       }
+      tmem_st8_nw(tb + lane_off + hf * 32, pk);
+      tmem_st8_nw(tb + lane_off + hf * 32 + 8, pk + 8);
+      tmem_st8_nw(tb + lane_off + hf * 32 + 16, dk);
+      tmem_st8_nw(tb + lane_off + hf * 32 + 24, dk + 8);
+      uint8_t* sd = sm + BwdSmem::DST + (it & 3) * BT_BYTES;
+#pragma unroll
+      for (int g = 0; g < 4; ++g)
+        *reinterpret_cast<uint4*>(sd + swz128(r, hf * 4 + g)) =
+            make_uint4(dk[4 * g], dk[4 * g + 1], dk[4 * g + 2], dk[4 * g + 3]);
       tmem_wait_st();
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
+      if (lane == 0) mbar_arrive(&p_full[bb]);
       if (threadIdx.x == 64) ATTN_TRACE(64 * it + 13);
-      // dQ of the previous tile (its MMA ran behind this tile's scores).
-      if (it > 0) {
-        if (!mbar_wait(dq_full, (it - 1) & 1, abort_flag, err)) {
+      if (wg == 0 && it >= 2) {
+        // query pair j = (it-2, it-1) was closed by the previous tile of the
+        // other warpgroup; its dQ MMA has had a whole softmax tile to finish
+        const int j = (it >> 1) - 1;
+        if (!mbar_wait(&dq_full[j & 1], (j >> 1) & 1, abort_flag, err)) {
           ok = false;
           break;
         }
-        if (threadIdx.x == 64) ATTN_TRACE(64 * it + 14);
         tc_fence_after();
-        flush_dq(it - 1);
+        flush_dq(j, (2 * j + 1) % 3);
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(dq_free);
-        if (threadIdx.x == 64) ATTN_TRACE(64 * it + 15);
-      }
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        ls[u] = nls[u];
-        dl[u] = ndl[u];
+        if (lane == 0) mbar_arrive(&dq_free[j & 1]);
       }
     }
-    // dQ of the last tile, then dK and dV.
-    if (ok && mbar_wait(dq_full, (nq - 1) & 1, abort_flag, err)) {
-      tc_fence_after();
-      flush_dq(nq - 1);
+    if (wg == 0) {
+      // the last pair (closed by tile nq-1, which may be its only tile)
+      const int j = (nq - 1) >> 1;
+      if (ok && mbar_wait(&dq_full[j & 1], (j >> 1) & 1, abort_flag, err)) {
+        tc_fence_after();
+        flush_dq(j, (nq - 1) % 3);
+      }
+      if (lane == 0) bulk_wait_all();
     }
-    if (lane == 0) bulk_wait_all();
     if (ok && mbar_wait(fin, 0, abort_flag, err)) {
       tc_fence_after();
-      float kk[32], vv[32];
-      // warp-collective TMEM loads stay outside the per-row guard
-      tmem_ld32(tDK + lane_off + half * 32, kk);
-      tmem_ld32(tDV + lane_off + half * 32, vv);
+      // warpgroup 0 writes dK, warpgroup 1 dV; the warp-collective TMEM load
+      // stays outside the per-row guard
+      float g[32];
+      tmem_ld32((wg == 0 ? tDK : tDV) + lane_off + hf * 32, g);
       if (key < p.T) {
-        bf16* dkrow = p.dk + b * p.sb + h * p.sh + (int64_t)key * p.st + half * 32;
-        bf16* dvrow = p.dv + b * p.sb + h * p.sh + (int64_t)key * p.st + half * 32;
+        bf16* row = (wg == 0 ? p.dk : p.dv) + b * p.sb + h * p.sh + (int64_t)key * p.st + hf * 32;
 #pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          float* kv = kk + 8 * g;
+        for (int q4 = 0; q4 < 4; ++q4) {
+          float* gv = g + 8 * q4;
+          if (wg == 0) {
 #pragma unroll
-          for (int i = 0; i < 8; ++i) kv[i] *= p.scale;
-          if (p.rcos) rope_back(kv, p.rcos, p.rsin, key, half * 4 + g);
-          uint4 qk, qv;
-          qk.x = pack_bf16x2(kv[0], kv[1]);
-          qk.y = pack_bf16x2(kv[2], kv[3]);
-          qk.z = pack_bf16x2(kv[4], kv[5]);
-          qk.w = pack_bf16x2(kv[6], kv[7]);
-          const float* w = vv + 8 * g;
-          qv.x = pack_bf16x2(w[0], w[1]);
-          qv.y = pack_bf16x2(w[2], w[3]);
-          qv.z = pack_bf16x2(w[4], w[5]);
-          qv.w = pack_bf16x2(w[6], w[7]);
-          *reinterpret_cast<uint4*>(dkrow + 8 * g) = qk;
-          *reinterpret_cast<uint4*>(dvrow + 8 * g) = qv;
+            for (int i = 0; i < 8; ++i) gv[i] *= p.scale;
+            if (p.rcos) rope_back(gv, p.rcos, p.rsin, key, hf * 4 + q4);
+          }
+          uint4 o;
+          o.x = pack_bf16x2(gv[0], gv[1]);
+          o.y = pack_bf16x2(gv[2], gv[3]);
+          o.z = pack_bf16x2(gv[4], gv[5]);
+          o.w = pack_bf16x2(gv[6], gv[7]);
+          *reinterpret_cast<uint4*>(row + 8 * q4) = o;
         }
       }
     }
@@ -846,10 +876,10 @@ extern "C" int gptb200_attention_bwd(const void* q, const void* k, const void* v
   auto st = reinterpret_cast<cudaStream_t>(stream);
   const int B = (int)batch, H = (int)heads, T = (int)seq;
   CUtensorMap mq, mk, mv, mdo;
-  if (!make_map4(&mq, q, B, H, T, stride_b, stride_h, stride_t, BT) ||
+  if (!make_map4(&mq, q, B, H, T, stride_b, stride_h, stride_t, BQ) ||
       !make_map4(&mk, k, B, H, T, stride_b, stride_h, stride_t, BT) ||
       !make_map4(&mv, v, B, H, T, stride_b, stride_h, stride_t, BT) ||
-      !make_map4(&mdo, dout, B, H, T, o_stride_b, o_stride_h, o_stride_t, BT))
+      !make_map4(&mdo, dout, B, H, T, o_stride_b, o_stride_h, o_stride_t, BQ))
     return GPTB200_ESHAPE;
   const int64_t rows = batch * heads * seq;
   float* delta = reinterpret_cast<float*>(workspace);

@@ -20,15 +20,19 @@ typedef __nv_bfloat16 bf16;
 // Error codes written by device code into a per-translation-unit flag.
 enum {
   kErrNone = 0,
-  kErrWaitTimeout = 1,   // an mbarrier wait ran out of iterations
+  kErrWaitTimeout = 1,   // an mbarrier wait ran out of time
   kErrTmemAlloc = 2,     // TMEM allocation returned an unexpected address
 };
 
-// Upper bound of try_wait polls before a wait gives up. Each poll can suspend
-// for a hardware-chosen interval, so this is far above any legitimate wait
-// (the longest waits here are one split-K unit, ~100 us) yet a wait that can
-// never complete ends in seconds.
-#define GPTB200_WAIT_LIMIT (1u << 20)
+// Time limit of one mbarrier wait (nanoseconds of %globaltimer). Far above any
+// legitimate wait (the longest here are one split-K unit, ~100 us), yet a wait
+// that can never complete ends in about a second.
+#define GPTB200_WAIT_NS 1000000000ull
+// Suspend-time hint of one try_wait: the waiting thread sleeps until the phase
+// completes or this many nanoseconds pass, instead of re-polling the barrier
+// (polls from many waiting warps would queue ahead of the producer's own
+// shared-memory operations).
+#define GPTB200_WAIT_HINT_NS 100000u
 
 GPTB200_DEV uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -61,21 +65,32 @@ GPTB200_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(GPTB200_WAIT_HINT_NS)
       : "memory");
   return ok != 0;
 }
 
+GPTB200_DEV uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
 // Bounded wait: returns false (and records kErrWaitTimeout once) when the
-// phase did not complete within GPTB200_WAIT_LIMIT polls, or when another
-// role of the same CTA already gave up (*abort != 0).
+// phase did not complete within GPTB200_WAIT_NS, or when another role of the
+// same CTA already gave up (*abort != 0).
 GPTB200_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* err) {
-  for (uint32_t i = 0; i < GPTB200_WAIT_LIMIT; ++i) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 1023u) == 1023u && *abort) return false;
+    if ((i & 15u) == 0) {
+      if (*abort) return false;
+      if (globaltimer_ns() - t0 > GPTB200_WAIT_NS) break;
+    }
   }
   *abort = 1;
   if (err) atomicCAS(err, 0, kErrWaitTimeout);
