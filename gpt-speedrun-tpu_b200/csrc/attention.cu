@@ -1,20 +1,14 @@
 // Causal flash attention (head_dim 64) on the Blackwell tensor cores.
 //
-// Forward (attn_fwd_tc): one CTA per (128-query tile, batch*head), 6 warps:
-//   warp 0  TMA: the Q tile once, then 128-key K/V tiles into a 2-stage ring
-//           (4-D tensor maps over (e, t, h, b), so any [b, t, h, e] strides work
-//           and rows past the sequence end arrive as zeros);
-//   warp 1  one thread issues tcgen05.mma: S = Q·Kᵀ (128x128, fp32 in TMEM),
-//           then O += P·V (128x64, fp32 in TMEM, V as an MN-major operand);
-//   warps 2-5 softmax: thread r owns query row r (TMEM lane r). Two passes
-//           over its S row, 32 TMEM columns at a time (max, then exp + store),
-//           apply scale·log2(e) and the causal mask, and keep a running max
-//           that is only raised when the row max grows by more than 2^8, in
-//           which case O is rescaled in TMEM (tcgen05.ld/st) — otherwise the
-//           stale max is exact because O and the row sum use the same one.
-//           P = exp2(s - m) is written as bf16 into a 128-byte-swizzled K-major
-//           shared tile that the next P·V MMA reads.
-//   Two CTAs fit on an SM (112 KB shared memory, 256 TMEM columns each).
+// Forward (attn_fwd_tc): one CTA per (pair of 128-query tiles, batch*head),
+// 10 warps, all of TMEM: warp 0 loads both Q tiles once and 128-key K/V blocks
+// into a 3-stage ring (4-D tensor maps over (e, t, h, b), so any [b, t, h, e]
+// strides work and rows past the sequence end arrive as zeros); one thread of
+// warp 1 issues the MMAs, S_x = Q_x K^T (128x128 fp32 in TMEM) and
+// O_x += P_x V (P_x read from TMEM, V an MN-major shared operand); two softmax
+// warpgroups own one tile each (thread = query row = TMEM lane) and turn S_x
+// into bf16 P_x in TMEM, so the two tiles ping-pong: while one warpgroup
+// exponentiates, the tensor core runs the other tile's MMAs.
 // Backward (attn_bwd_tc): one CTA per (128-key tile, batch*head), looping over
 // 64-query tiles from the diagonal down. 19 warps: TMA (K, V once; Q/dO into a
 // 4-stage ring), a scores MMA thread (S^T = K Q^T and dP^T = V dO^T into one
@@ -56,7 +50,6 @@ __device__ long long g_attn_trace[4096];
 constexpr int HD = 64;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
-constexpr int kThreads = 192;
 
 struct AttnParams {
   int B, H, T;
@@ -95,22 +88,23 @@ __device__ __forceinline__ void rope_back(float* v, const bf16* rcos, const bf16
 }
 
 // ------------------------------------------------------------------ forward
-constexpr int FQ = 128;                 // queries per forward CTA (TMEM lanes)
-constexpr int FK = 64;                  // keys per K/V tile
+constexpr int FQ = 128;                 // queries per tile (TMEM lanes); two tiles per CTA
+constexpr int FK = 128;                 // keys per K/V block
 constexpr int Q_BYTES = FQ * 128;       // 128 rows x 64 bf16
-constexpr int KV_BYTES = FK * 128;      // 64 rows x 64 bf16
-constexpr int P_BYTES = FQ * FK * 2;    // 128 rows x 64 keys bf16 (one 128-byte-wide block)
+constexpr int KV_BYTES = FK * 128;      // 128 rows x 64 bf16
+constexpr int kKvStages = 5;
+constexpr int kFwdMma1Warp = 10;       // MMA thread of tile 1 (warp 1 serves tile 0)
+constexpr int kFwdThreads = 32 * 11;
 
 struct FwdSmem {
-  static constexpr int Q = 0;
-  static constexpr int K = Q + Q_BYTES;       // 2 stages
-  static constexpr int V = K + 2 * KV_BYTES;  // 2 stages
-  static constexpr int P = V + 2 * KV_BYTES;
-  static constexpr int BAR = P + P_BYTES;
+  static constexpr int Q = 0;                             // 2 tiles
+  static constexpr int K = Q + 2 * Q_BYTES;               // kKvStages
+  static constexpr int V = K + kKvStages * KV_BYTES;      // kKvStages
+  static constexpr int BAR = V + kKvStages * KV_BYTES;
   static constexpr int TOTAL = BAR + 256 + 1024;
 };
 
-__global__ void __launch_bounds__(kThreads, 3)
+__global__ void __launch_bounds__(kFwdThreads, 1)
     attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -118,189 +112,231 @@ __global__ void __launch_bounds__(kThreads, 3)
                                            ~static_cast<uintptr_t>(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + FwdSmem::BAR);
   uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;   // [2]
-  uint64_t* kv_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;
-  uint64_t* s_free = bars + 6;
-  uint64_t* p_full = bars + 7;
-  uint64_t* pv_done = bars + 8;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+  uint64_t* kv_full = bars + 1;                // [kKvStages]
+  uint64_t* kv_empty = kv_full + kKvStages;    // [kKvStages]
+  uint64_t* s_full = kv_empty + kKvStages;     // [2 tiles]: S of the current block is in TMEM
+  uint64_t* p_full = s_full + 2;               // [2]: P written to TMEM
+  uint64_t* pv_done = p_full + 2;              // [2]: the tile's P.V MMA has completed
+  uint64_t* s_free = pv_done + 2;              // [2]: S has been loaded into registers
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_free + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nqt = (p.T + FQ - 1) / FQ;
-  const int qt = nqt - 1 - (int)blockIdx.x;  // heaviest tiles first
+  const int npair = (p.T + 2 * FQ - 1) / (2 * FQ);
+  const int pr = npair - 1 - (int)blockIdx.x;  // heaviest pairs first
   const int bh = blockIdx.y;
   const int b = bh / p.H, h = bh - b * p.H;
-  const int q0 = qt * FQ;
-  const int nkv = min((q0 + FQ) / FK, (p.T + FK - 1) / FK);
+  const int q0 = pr * 2 * FQ;
+  // Causal key blocks per tile (the last one holds the diagonal); tile 1 of
+  // the last pair may lie wholly past the sequence end.
+  const int n0 = q0 / FK + 1;
+  const int n1 = (q0 + FQ < p.T) ? n0 + 1 : 0;
+  const int nkv = n1 > 0 ? n1 : n0;
   int* err = &g_attn_error;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < kKvStages; ++s) {
       mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(&kv_empty[s], n1 > 0 ? 2 : 1);  // released by each tile's MMA thread
     }
-    mbar_init(s_full, 1);
-    mbar_init(s_free, 4);
-    mbar_init(p_full, 4);
-    mbar_init(pv_done, 1);
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(&s_full[x], 1);
+      mbar_init(&p_full[x], 4);
+      mbar_init(&pv_done[x], 1);
+      mbar_init(&s_free[x], 4);
+    }
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 1) tmem_alloc(tmem_slot, 128);
+  if (warp == 1) tmem_alloc(tmem_slot, 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // TMEM columns: S[2] (128 fp32 each) | O[2] (64 fp32) | P[2] (128 keys as bf16 pairs)
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem, tO = tmem + 64;
+  auto tS = [&](int x) { return tmem + 128 * x; };
+  auto tO = [&](int x) { return tmem + 256 + 64 * x; };
+  auto tP = [&](int x) { return tmem + 384 + 64 * x; };
 
   if (warp == 0) {
     if (lane == 0) {
-      mbar_arrive_expect_tx(q_full, Q_BYTES);
+      mbar_arrive_expect_tx(q_full, 2 * Q_BYTES);
       tma_load_4d(sm + FwdSmem::Q, &tmQ, q_full, 0, q0, h, b);
+      tma_load_4d(sm + FwdSmem::Q + Q_BYTES, &tmQ, q_full, 0, q0 + FQ, h, b);
       for (int j = 0; j < nkv; ++j) {
-        const int s = j & 1;
-        if (!mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1, abort_flag, err)) break;
+        const int s = j % kKvStages;
+        if (!mbar_wait(&kv_empty[s], ((j / kKvStages) & 1) ^ 1, abort_flag, err)) break;
         mbar_arrive_expect_tx(&kv_full[s], 2 * KV_BYTES);
         tma_load_4d(sm + FwdSmem::K + s * KV_BYTES, &tmK, &kv_full[s], 0, j * FK, h, b);
         tma_load_4d(sm + FwdSmem::V + s * KV_BYTES, &tmV, &kv_full[s], 0, j * FK, h, b);
       }
     }
-  } else if (warp == 1) {
-    if (lane == 0) {
+  } else if (warp == 1 || warp == kFwdMma1Warp) {
+    // One MMA thread per tile: S_x = Q_x K_j^T (128 x 128 fp32) for the next
+    // block as soon as the softmax holds S_x in registers, O_x += P_x V_j
+    // once P_x is in TMEM. The two tiles progress independently.
+    const int x = warp == 1 ? 0 : 1;
+    const int nb = x == 0 ? n0 : n1;
+    if (lane == 0 && nb > 0) {
       constexpr uint32_t idS = umma_idesc_bf16(128, FK, 0, 0);
-      constexpr uint32_t idO = umma_idesc_bf16(128, HD, 0, 1);
-      const uint32_t sQ = smem_u32(sm + FwdSmem::Q);
-      const uint32_t sP = smem_u32(sm + FwdSmem::P);
-      bool ok = mbar_wait(q_full, 0, abort_flag, err);
-      for (int j = 0; ok && j < nkv; ++j) {
-        const int s = j & 1;
-        if (!mbar_wait(&kv_full[s], (j >> 1) & 1, abort_flag, err)) break;
-        if (j > 0 && !mbar_wait(s_free, (j - 1) & 1, abort_flag, err)) break;
-        tc_fence_after();
-        const uint32_t sK = smem_u32(sm + FwdSmem::K + s * KV_BYTES);
-        const uint32_t sV = smem_u32(sm + FwdSmem::V + s * KV_BYTES);
+      constexpr uint32_t idO = umma_idesc_bf16(128, HD, 0, 1);  // A = P in TMEM, B = V MN-major
+      const uint32_t sQ = smem_u32(sm + FwdSmem::Q + x * Q_BYTES);
+      auto issue_s = [&](int j) {
+        const uint32_t sK = smem_u32(sm + FwdSmem::K + (j % kKvStages) * KV_BYTES);
 #pragma unroll
         for (int k = 0; k < HD / 16; ++k)
-          umma_bf16(tS, umma_smem_desc(sQ + k * 32, 16, 1024), umma_smem_desc(sK + k * 32, 16, 1024),
-                    idS, k > 0);
-        umma_commit(s_full);
-        if (!mbar_wait(p_full, j & 1, abort_flag, err)) break;
+          umma_bf16(tS(x), umma_smem_desc(sQ + k * 32, 16, 1024),
+                    umma_smem_desc(sK + k * 32, 16, 1024), idS, k > 0);
+        umma_commit(&s_full[x]);
+      };
+      bool ok = mbar_wait(q_full, 0, abort_flag, err) && mbar_wait(&kv_full[0], 0, abort_flag, err);
+      if (ok) {
         tc_fence_after();
+        issue_s(0);
+      }
+      for (int j = 0; ok && j < nb; ++j) {
+        if (j + 1 < nb) {
+          if (!mbar_wait(&kv_full[(j + 1) % kKvStages], ((j + 1) / kKvStages) & 1, abort_flag,
+                         err) ||
+              !mbar_wait(&s_free[x], j & 1, abort_flag, err))
+            break;
+          ATTN_TRACE(2048 + 32 * j + 8 * x + 0);
+          tc_fence_after();
+          issue_s(j + 1);
+          ATTN_TRACE(2048 + 32 * j + 8 * x + 1);
+        }
+        if (!mbar_wait(&p_full[x], j & 1, abort_flag, err)) break;
+        ATTN_TRACE(2048 + 32 * j + 8 * x + 2);
+        tc_fence_after();
+        const uint32_t sV = smem_u32(sm + FwdSmem::V + (j % kKvStages) * KV_BYTES);
+        // O_x += P_x V_j, P read from TMEM (keys 16k..16k+15 at column 8k)
 #pragma unroll
         for (int k = 0; k < FK / 16; ++k)
-          umma_bf16(tO, umma_smem_desc(sP + k * 32, 16, 1024),
-                    umma_smem_desc(sV + k * 2048, KV_BYTES, 1024), idO, (j > 0 || k > 0));
-        umma_commit(pv_done);
-        umma_commit(&kv_empty[s]);
+          umma_bf16_ts(tO(x), tP(x) + k * 8, umma_smem_desc(sV + k * 2048, KV_BYTES, 1024), idO,
+                       (j > 0 || k > 0));
+        umma_commit(&pv_done[x]);
+        umma_commit(&kv_empty[j % kKvStages]);
       }
     }
-  } else {
-    // softmax warps: thread owns row r of the tile (TMEM lane r)
+  } else if (warp < kFwdMma1Warp) {
+    // Softmax warpgroup x (warps 2-5: tile 0, 6-9: tile 1); thread = query
+    // row r of the tile (TMEM lane r). Per block: the S row into registers,
+    // its max, then exp + row sum + P, with a running max that is only raised
+    // when the row max grows by more than 2^8; O is then rescaled in TMEM.
+    // Otherwise the stale max is exact because O and the row sum share it.
+    const int x = (warp - 2) >> 2;
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
-    const int qrow = q0 + r;
+    const int qrow = q0 + x * FQ + r;
+    const int nb = x == 0 ? n0 : n1;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const float c = p.scale * kLog2e;
     float m_used = -INFINITY, l = 0.f;
-    uint8_t* sP = sm + FwdSmem::P;
     bool ok = true;
-    for (int j = 0; j < nkv && ok; ++j) {
-      if (!mbar_wait(s_full, j & 1, abort_flag, err)) {
+    for (int j = 0; j < nb && ok; ++j) {
+      if ((threadIdx.x & 127) == 64) ATTN_TRACE(2048 + 32 * j + 8 * x + 3);
+      if (!mbar_wait(&s_full[x], j & 1, abort_flag, err)) {
         ok = false;
         break;
       }
+      if ((threadIdx.x & 127) == 64) ATTN_TRACE(2048 + 32 * j + 8 * x + 4);
       tc_fence_after();
-      const int k0 = j * FK;
-      const bool diag = k0 + FK - 1 > q0;  // tile crosses the causal diagonal
-      const int lim = qrow - k0;           // visible keys: column index <= lim
-      // Pass 1: row max of the scaled, masked scores, straight from TMEM.
-      float mx = -INFINITY;
-#pragma unroll 1
-      for (int cc = 0; cc < FK / 32; ++cc) {
-        float v[32];
-        tmem_ld32(tS + lane_off + cc * 32, v);
+      const bool diag = (j == nb - 1);  // keys past the query (and past T) are masked
+      // The whole 128-column S row in one batch of TMEM loads, then S_x is
+      // handed back so the next block's scores overlap this block's exps.
+      uint32_t v[FK];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float x = (diag && cc * 32 + i > lim) ? -INFINITY : v[i] * c;
-          mx = fmaxf(mx, x);
-        }
+      for (int cc = 0; cc < FK / 32; ++cc) tmem_ld32_nw(tS(x) + lane_off + cc * 32, v + 32 * cc);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[x]);
+      if ((threadIdx.x & 127) == 64) ATTN_TRACE(2048 + 32 * j + 8 * x + 5);
+      // Row max of the raw scores (c > 0 commutes with the max), eight
+      // independent chains; on the diagonal block keys past the query are out.
+      float m8[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) m8[u] = -INFINITY;
+      if (diag) {
+#pragma unroll
+        for (int i = 0; i < FK; i += 2)
+          m8[(i >> 1) & 7] = fmax3(m8[(i >> 1) & 7], i > r ? -INFINITY : __uint_as_float(v[i]),
+                                   i + 1 > r ? -INFINITY : __uint_as_float(v[i + 1]));
+      } else {
+#pragma unroll
+        for (int i = 0; i < FK; i += 2)
+          m8[(i >> 1) & 7] =
+              fmax3(m8[(i >> 1) & 7], __uint_as_float(v[i]), __uint_as_float(v[i + 1]));
       }
-      bool waited_pv = false;
-      // The rescale decision is made per warp: the TMEM loads/stores inside
-      // are warp-collective and must not run in a divergent branch. Rows whose
+      const float mx =
+          fmaxf(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], fmaxf(m8[5], fmaxf(m8[6], m8[7])))) * c;
+      // The rescale decision is made per warp: the TMEM loads/stores of O are
+      // warp-collective and must not run in a divergent branch. Rows whose
       // max did not move rescale by exactly 1.
-      if (__any_sync(0xffffffffu, mx > m_used + 8.0f)) {
+      const bool rescale = __any_sync(0xffffffffu, mx > m_used + 8.0f);
+      float alpha = 1.f;
+      if (rescale) {
         const float m_new = fmaxf(m_used, mx);
-        if (j > 0) {
-          const float alpha = ex2(m_used - m_new);
-          l *= alpha;
-          if (!mbar_wait(pv_done, (j - 1) & 1, abort_flag, err)) {
-            ok = false;
-            break;
-          }
-          waited_pv = true;
-          tc_fence_after();
-          float o[32];
-#pragma unroll
-          for (int cc = 0; cc < HD / 32; ++cc) {
-            tmem_ld32(tO + lane_off + cc * 32, o);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] *= alpha;
-            tmem_st32(tO + lane_off + cc * 32, o);
-          }
-        }
+        alpha = ex2(m_used - m_new);  // 0 on the first block (m_used = -inf)
         m_used = m_new;
       }
-      // P_{j-1} must have been consumed by its P·V MMA before P_j overwrites it.
-      if (j > 0 && !waited_pv) {
-        if (!mbar_wait(pv_done, (j - 1) & 1, abort_flag, err)) {
+      if ((threadIdx.x & 127) == 64) ATTN_TRACE(2048 + 32 * j + 8 * x + 6);
+      // P = exp2(s*c - m) packed to bf16 pairs in registers (the S registers
+      // die as P is produced); four packed partial row sums.
+      const float2 c2 = make_float2(c, c), nm2 = make_float2(-m_used, -m_used);
+      float2 acc[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) acc[u] = make_float2(0.f, 0.f);
+      uint32_t pk[FK / 2];
+#pragma unroll
+      for (int i = 0; i < FK; i += 2) {
+        const float2 t = ffma2(make_float2(__uint_as_float(v[i]), __uint_as_float(v[i + 1])), c2, nm2);
+        float p0 = ex2(t.x), p1 = ex2(t.y);
+        if (diag) {
+          if (i > r) p0 = 0.f;
+          if (i + 1 > r) p1 = 0.f;
+        }
+        acc[(i >> 1) & 3] = fadd2(acc[(i >> 1) & 3], make_float2(p0, p1));
+        pk[i / 2] = pack_bf16x2(p0, p1);
+      }
+      const float2 s01 = fadd2(fadd2(acc[0], acc[1]), fadd2(acc[2], acc[3]));
+      const float sum = s01.x + s01.y;
+      // P and O of the previous block must have been consumed by its P.V MMA.
+      if (j > 0) {
+        if (!mbar_wait(&pv_done[x], (j - 1) & 1, abort_flag, err)) {
           ok = false;
           break;
         }
+        tc_fence_after();
       }
-      // Pass 2: P = exp2(s*c - m) as bf16 into the swizzled K-major P tile.
-      float sum = 0.f;
-#pragma unroll 1
-      for (int cc = 0; cc < FK / 32; ++cc) {
-        float v[32];
-        tmem_ld32(tS + lane_off + cc * 32, v);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          float pv = ex2(fmaf(v[i], c, -m_used));
-          if (diag && cc * 32 + i > lim) pv = 0.f;
-          v[i] = pv;
-          sum += pv;
-        }
+      for (int g = 0; g < FK / 16; ++g) tmem_st8_nw(tP(x) + lane_off + g * 8, pk + 8 * g);
+      l = l * alpha + sum;
+      if (rescale && j > 0) {
+        float o[32];
 #pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          uint4 q;
-          q.x = pack_bf16x2(v[8 * g], v[8 * g + 1]);
-          q.y = pack_bf16x2(v[8 * g + 2], v[8 * g + 3]);
-          q.z = pack_bf16x2(v[8 * g + 4], v[8 * g + 5]);
-          q.w = pack_bf16x2(v[8 * g + 6], v[8 * g + 7]);
-          *reinterpret_cast<uint4*>(sP + swz128(r, cc * 4 + g)) = q;
+        for (int cc = 0; cc < HD / 32; ++cc) {
+          tmem_ld32(tO(x) + lane_off + cc * 32, o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] *= alpha;
+          tmem_st32(tO(x) + lane_off + cc * 32, o);
         }
       }
-      l += sum;
-      fence_proxy_async_smem();
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(s_free);
-        mbar_arrive(p_full);
-      }
+      if (lane == 0) mbar_arrive(&p_full[x]);
+      if ((threadIdx.x & 127) == 64) ATTN_TRACE(2048 + 32 * j + 8 * x + 7);
     }
-    if (ok && mbar_wait(pv_done, (nkv - 1) & 1, abort_flag, err)) {
+    if (ok && nb > 0 && mbar_wait(&pv_done[x], (nb - 1) & 1, abort_flag, err)) {
       tc_fence_after();
       const float inv = 1.f / l;
       float o[32];
       bf16* orow = p.o + b * p.osb + h * p.osh + (int64_t)qrow * p.ost;
 #pragma unroll
       for (int cc = 0; cc < HD / 32; ++cc) {
-        tmem_ld32(tO + lane_off + cc * 32, o);
+        tmem_ld32(tO(x) + lane_off + cc * 32, o);
         if (qrow < p.T) {
 #pragma unroll
           for (int g = 0; g < 4; ++g) {
@@ -320,7 +356,7 @@ __global__ void __launch_bounds__(kThreads, 3)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 128);
+    tmem_dealloc(tmem, 512);
   }
 }
 
@@ -843,8 +879,8 @@ extern "C" int gptb200_attention_fwd(const void* q, const void* k, const void* v
     if (e != cudaSuccess) return -static_cast<int>(e);
     if (dev < 64) cfg[dev] = true;
   }
-  dim3 grid((unsigned)((seq + FQ - 1) / FQ), (unsigned)(batch * heads));
-  attn_fwd_tc<<<grid, kThreads, FwdSmem::TOTAL, reinterpret_cast<cudaStream_t>(stream)>>>(mq, mk,
+  dim3 grid((unsigned)((seq + 2 * FQ - 1) / (2 * FQ)), (unsigned)(batch * heads));
+  attn_fwd_tc<<<grid, kFwdThreads, FwdSmem::TOTAL, reinterpret_cast<cudaStream_t>(stream)>>>(mq, mk,
                                                                                           mv, p);
   GPTB200_CHECK_LAUNCH();
   return 0;
