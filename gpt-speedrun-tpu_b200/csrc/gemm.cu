@@ -102,16 +102,50 @@ template <int EPI>
 constexpr bool kStagedEpi = EPI == EPI_BF16_ || EPI == EPI_BIAS_ROPE_ || EPI == EPI_BIAS_GELU_ ||
                             EPI == EPI_DGELU_ || EPI == EPI_LCE_BWD_;
 
+// Global operands of the bf16-output epilogues for 8 columns [c0, c0+8) of
+// one row: bias, the residual / saved GELU derivative row, RoPE tables.
+// Addresses are clamped into the matrix (N is a multiple of 8 whenever these
+// are read), so a chunk's loads can all be issued before any of its math.
+struct EpiOperands {
+  uint4 b, x;
+  uint2 cs, sn;
+};
+
+template <int EPI>
+__device__ __forceinline__ EpiOperands epi_load8(const GemmParams& p, int row, int c0) {
+  EpiOperands o;
+  o.b = o.x = make_uint4(0u, 0u, 0u, 0u);
+  o.cs = o.sn = make_uint2(0u, 0u);
+  const int cc = min(c0, p.N - 8);
+  const int64_t rr = min(row, p.M - 1);
+  if constexpr (EPI == EPI_BF16_) {
+    if (p.bias) o.b = *reinterpret_cast<const uint4*>(p.bias + cc);
+    if (p.resid) o.x = *reinterpret_cast<const uint4*>(p.resid + rr * p.ld_resid + cc);
+  } else if constexpr (EPI == EPI_BIAS_ROPE_) {
+    o.b = *reinterpret_cast<const uint4*>(p.bias + cc);
+    if (cc < p.rope_cols) {
+      const int64_t pos = rr % p.rope_seq;
+      const int pair0 = (cc & 63) >> 1;
+      o.cs = *reinterpret_cast<const uint2*>(p.rope_cos + pos * 32 + pair0);
+      o.sn = *reinterpret_cast<const uint2*>(p.rope_sin + pos * 32 + pair0);
+    }
+  } else if constexpr (EPI == EPI_BIAS_GELU_) {
+    o.b = *reinterpret_cast<const uint4*>(p.bias + cc);
+  } else if constexpr (EPI == EPI_DGELU_) {
+    o.x = *reinterpret_cast<const uint4*>(p.aux + rr * p.ld_aux + cc);
+  }
+  return o;
+}
+
 // Packed bf16 outputs for 8 consecutive columns [c0, c0+8) of one row of the
 // bf16-output epilogues: o0 = C, o1 = the GELU derivative (EPI_BIAS_GELU only).
 // Each operation rounds where the reference's bf16 op does: bf16(acc), then
 // bias / branch-multiplier / residual as bf16x2 ops with one rounding each.
-// Rows and columns outside the matrix produce zeros without touching memory
-// (the TMA store clips them).
+// Rows and columns outside the matrix produce zeros (the TMA store clips them).
 template <int EPI>
 __device__ __forceinline__ void epi_pack8(const GemmParams& p, int row, int c0, const float* a,
-                                          uint32_t* o0, uint32_t* o1, int target, float lse,
-                                          float cot) {
+                                          const EpiOperands& op, uint32_t* o0, uint32_t* o1,
+                                          int target, float lse, float cot) {
   if (row >= p.M || c0 >= p.N) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) o0[j] = o1[j] = 0u;
@@ -122,8 +156,7 @@ __device__ __forceinline__ void epi_pack8(const GemmParams& p, int row, int c0, 
   for (int j = 0; j < 4; ++j) t[j] = pack_bf16x2(a[2 * j], a[2 * j + 1]);
   if constexpr (EPI == EPI_BF16_) {
     if (p.bias) {
-      const uint4 bq = *reinterpret_cast<const uint4*>(p.bias + c0);
-      const uint32_t* bw = &bq.x;
+      const uint32_t* bw = &op.b.x;
 #pragma unroll
       for (int j = 0; j < 4; ++j) t[j] = hadd2_bf16(t[j], bw[j]);
     }
@@ -133,8 +166,7 @@ __device__ __forceinline__ void epi_pack8(const GemmParams& p, int row, int c0, 
       for (int j = 0; j < 4; ++j) t[j] = hmul2_bf16(t[j], al);
     }
     if (p.resid) {
-      const uint4 rq = *reinterpret_cast<const uint4*>(p.resid + (int64_t)row * p.ld_resid + c0);
-      const uint32_t* rw = &rq.x;
+      const uint32_t* rw = &op.x.x;
 #pragma unroll
       for (int j = 0; j < 4; ++j) t[j] = hadd2_bf16(rw[j], t[j]);
     }
@@ -143,20 +175,15 @@ __device__ __forceinline__ void epi_pack8(const GemmParams& p, int row, int c0, 
   } else if constexpr (EPI == EPI_BIAS_ROPE_) {
     // bias, then the interleaved RoPE rotation of q/k columns at this row's
     // position (rig/nn.py:36-52), one bf16 rounding per value as in the reference.
-    const uint4 bq = *reinterpret_cast<const uint4*>(p.bias + c0);
-    const uint32_t* bw = &bq.x;
+    const uint32_t* bw = &op.b.x;
 #pragma unroll
     for (int j = 0; j < 4; ++j) t[j] = hadd2_bf16(t[j], bw[j]);
     if (c0 < p.rope_cols) {
-      const int pos = row % p.rope_seq;
-      const int pair0 = (c0 & 63) >> 1;
-      const uint2 cq = *reinterpret_cast<const uint2*>(p.rope_cos + (int64_t)pos * 32 + pair0);
-      const uint2 sq = *reinterpret_cast<const uint2*>(p.rope_sin + (int64_t)pos * 32 + pair0);
       float cs[4], sn[4];
-      unpack_bf16x2(cq.x, cs[0], cs[1]);
-      unpack_bf16x2(cq.y, cs[2], cs[3]);
-      unpack_bf16x2(sq.x, sn[0], sn[1]);
-      unpack_bf16x2(sq.y, sn[2], sn[3]);
+      unpack_bf16x2(op.cs.x, cs[0], cs[1]);
+      unpack_bf16x2(op.cs.y, cs[2], cs[3]);
+      unpack_bf16x2(op.sn.x, sn[0], sn[1]);
+      unpack_bf16x2(op.sn.y, sn[2], sn[3]);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         float e, d;
@@ -167,8 +194,7 @@ __device__ __forceinline__ void epi_pack8(const GemmParams& p, int row, int c0, 
 #pragma unroll
     for (int j = 0; j < 4; ++j) o0[j] = t[j];
   } else if constexpr (EPI == EPI_BIAS_GELU_) {
-    const uint4 bq = *reinterpret_cast<const uint4*>(p.bias + c0);
-    const uint32_t* bw = &bq.x;
+    const uint32_t* bw = &op.b.x;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       float u0, u1, g0, g1, d0, d1;
@@ -180,8 +206,7 @@ __device__ __forceinline__ void epi_pack8(const GemmParams& p, int row, int c0, 
     }
   } else if constexpr (EPI == EPI_DGELU_) {
     // du = bf16(alpha * acc) * gelu'(u), the derivative saved by the forward epilogue
-    const uint4 gq = *reinterpret_cast<const uint4*>(p.aux + (int64_t)row * p.ld_aux + c0);
-    const uint32_t* gw = &gq.x;
+    const uint32_t* gw = &op.x.x;
 #pragma unroll
     for (int j = 0; j < 4; ++j)
       o0[j] = hmul2_bf16(pack_bf16x2(p.alpha * a[2 * j], p.alpha * a[2 * j + 1]), gw[j]);
@@ -440,13 +465,21 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c = 0; c < COLS / 32; ++c) {
           uint32_t out0[16], out1[16];
+          // operand loads of PRE groups at a time are issued before their math
+          constexpr int PRE = (EPI == EPI_BF16_ || EPI == EPI_BIAS_ROPE_) ? 2 : 4;
 #pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            float a8[8];
+          for (int g0 = 0; g0 < 4; g0 += PRE) {
+            EpiOperands op[PRE];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) a8[j] = __uint_as_float(raw[c * 32 + g * 8 + j]);
-            epi_pack8<EPI>(p, row, n0 + c * 32 + g * 8, a8, out0 + 4 * g, out1 + 4 * g, target,
-                           lse, cot);
+            for (int g = 0; g < PRE; ++g) op[g] = epi_load8<EPI>(p, row, n0 + c * 32 + (g0 + g) * 8);
+#pragma unroll
+            for (int g = 0; g < PRE; ++g) {
+              float a8[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) a8[j] = __uint_as_float(raw[c * 32 + (g0 + g) * 8 + j]);
+              epi_pack8<EPI>(p, row, n0 + c * 32 + (g0 + g) * 8, a8, op[g], out0 + 4 * (g0 + g),
+                             out1 + 4 * (g0 + g), target, lse, cot);
+            }
           }
 #pragma unroll
           for (int o = 0; o < NOUT; ++o) {
@@ -725,6 +758,9 @@ extern "C" int gptb200_gemm(const void* a, int a_mn_major, int64_t lda, const vo
     default: return GPTB200_EUNSUPPORTED;
   }
   if (e->residual && (e->ld_residual < n || (e->ld_residual % 8))) return GPTB200_EINVAL;
+  // bias / residual / derivative rows are read in 16-byte groups of 8 columns
+  if ((e->bias || e->residual || kind == EPI_BIAS_GELU_ || kind == EPI_DGELU_) && (n % 8))
+    return GPTB200_ESHAPE;
   if (kind == EPI_F32_ || kind == EPI_F32_ATOMIC_) {
     if (ldc % 4) return GPTB200_ESHAPE;
   }
