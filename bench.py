@@ -23,6 +23,7 @@ reference itself is JAX, which this image does not have).
 from __future__ import annotations
 
 import argparse
+import datetime
 import json
 import os
 import pathlib
@@ -61,9 +62,14 @@ def measured_peaks() -> dict:
 
 
 class ClockSampler:
-    """nvidia-smi clock/throttle samples every 200 ms while running."""
+    """nvidia-smi clock/throttle samples every 50 ms, kept for the timed window.
 
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    Started before the warm-up steps; `wait_ready` blocks until the first sample
+    exists, and `stop(t0, t1)` keeps the samples whose timestamps fall inside the
+    host-time window [t0, t1] of the timed region (a region shorter than one
+    sampling interval keeps the single nearest sample, and says so)."""
+
+    QUERY = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -72,12 +78,26 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(gpu_index), f"--query-gpu={self.QUERY}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=self.file, stderr=subprocess.DEVNULL)
         except (FileNotFoundError, OSError):
             self.proc = None
 
-    def stop(self) -> dict:
+    def wait_ready(self, timeout_s: float = 10.0) -> None:
+        t_end = time.time() + timeout_s
+        while self.proc is not None and time.time() < t_end:
+            if os.path.getsize(self.file.name) > 0:
+                return
+            time.sleep(0.02)
+
+    @staticmethod
+    def _ts(text: str) -> float:
+        try:
+            return datetime.datetime.strptime(text, "%Y/%m/%d %H:%M:%S.%f").timestamp()
+        except ValueError:
+            return float("nan")
+
+    def stop(self, t0: float, t1: float) -> dict:
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
@@ -86,17 +106,26 @@ class ClockSampler:
         rows = []
         for line in pathlib.Path(self.file.name).read_text().splitlines():
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 9:
-                rows.append(parts)
+            if len(parts) >= 10:
+                rows.append((self._ts(parts[0]), parts[1:]))
         os.unlink(self.file.name)
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        inside = [r for t, r in rows if t0 <= t <= t1]
+        note = None
+        if not inside:
+            mid = 0.5 * (t0 + t1)
+            inside = [min(rows, key=lambda tr: abs(tr[0] - mid) if tr[0] == tr[0] else 1e30)[1]]
+            note = "timed region shorter than the sampling interval: nearest sample"
+        sm = [float(r[1]) for r in inside if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in inside if r[2].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
+        reasons = sorted({n for r in inside for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        out = {"sm_mhz": statistics.median(sm) if sm else None,
+               "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(inside)}
+        if note:
+            out["note"] = note
+        return out
 
 
 def make_stream(cfg, rank: int, world: int, steps: int, seed: int):
@@ -216,26 +245,29 @@ def main() -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    clocks = ClockSampler(local)
     for i in range(args.warmup):
         trainer.train_step(*dev_batches[i])
         if i == 0 and world == 1 and not args.eager:
             trainer.capture()  # after one eager step; replays the same launches
+    clocks.wait_ready()
     barrier()
 
     # ---- value: inputs resident in HBM
-    clocks = ClockSampler(local)
     launches0 = ops.launch_count()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
+    t_host0 = time.time()
     start.record()
     for i in range(args.steps):
         trainer.train_step(*dev_batches[args.warmup + i])
     end.record()
     barrier()
+    t_host1 = time.time()
     launches = ops.launch_count() - launches0
     if trainer.graph is not None:  # replays do not pass through the host launch counter
         launches += trainer.graph_launches * args.steps
-    clock_info = clocks.stop()
+    clock_info = clocks.stop(t_host0, t_host1)
     ms = max_over_ranks(start.elapsed_time(end))
     global_tokens = cfg.batch_size * cfg.seq_len
     value = global_tokens * args.steps / (ms / 1000.0)

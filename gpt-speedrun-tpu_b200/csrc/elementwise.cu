@@ -205,7 +205,8 @@ static int rms_bwd_launch(const bf16* x, const bf16* s, const float* rstd, const
                           const bf16* dxi, bf16* dxo, float* dscale, float* dcol, float col_alpha,
                           int64_t rows, int d, cudaStream_t st) {
   const int threads = 128;
-  int64_t blocks = std::min<int64_t>((rows + 3) / 4, (int64_t)sms() * 8);
+  // Each block ends in 2 x d column atomics, so blocks stay few (4 per SM).
+  int64_t blocks = std::min<int64_t>((rows + 3) / 4, (int64_t)sms() * 4);
   size_t smem = 2 * (size_t)(threads / 32) * d * sizeof(float);
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(rms_bwd_kernel<CH>,

@@ -671,10 +671,12 @@ int gemm_launch(const void* a, int a_mn, int64_t lda, const void* b, int b_mn, i
   p.num_kb = (int)((K + BK - 1) / BK);
   int splits = 1;
   if (epi == EPI_F32_ATOMIC_) {
-    // Split K until there are about three units per SM, keeping >= 8 k-blocks each.
+    // Split K until there are about three units per SM, keeping >= 32 k-blocks
+    // (2048 of K) per unit: every unit ends in BM x BN fp32 atomics, which a
+    // shorter main loop no longer hides.
     const int tiles = p.tiles_m * p.tiles_n;
     const int target = 3 * sm_count();
-    while (tiles * splits < target && p.num_kb / (splits * 2) >= 8) splits *= 2;
+    while (tiles * splits < target && p.num_kb / (splits * 2) >= 32) splits *= 2;
   }
   p.kb_per_split = (p.num_kb + splits - 1) / splits;
   p.splits = (p.num_kb + p.kb_per_split - 1) / p.kb_per_split;
