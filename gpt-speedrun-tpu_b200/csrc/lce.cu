@@ -79,9 +79,49 @@ __global__ void __launch_bounds__(1024) mean_kernel(const float* __restrict__ x,
   }
 }
 
+// out[0] = sum(losses * mask), out[1] = sum(mask), fp32, one block (fixed
+// summation order, so repeated evaluations agree bit for bit).
+__global__ void __launch_bounds__(1024) masked_sum_kernel(const float* __restrict__ losses,
+                                                          const float* __restrict__ mask,
+                                                          int64_t n, float* __restrict__ out) {
+  __shared__ float red[2][32];
+  float s = 0.f, c = 0.f;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+    const float m = mask[i];
+    s += losses[i] * m;
+    c += m;
+  }
+  s = warp_sum(s);
+  c = warp_sum(c);
+  if ((threadIdx.x & 31) == 0) {
+    red[0][threadIdx.x >> 5] = s;
+    red[1][threadIdx.x >> 5] = c;
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    const bool live = threadIdx.x < (blockDim.x >> 5);
+    float t = live ? red[0][threadIdx.x] : 0.f;
+    float u = live ? red[1][threadIdx.x] : 0.f;
+    t = warp_sum(t);
+    u = warp_sum(u);
+    if (threadIdx.x == 0) {
+      out[0] = t;
+      out[1] = u;
+    }
+  }
+}
+
 }  // namespace gptb200
 
 using namespace gptb200;
+
+extern "C" int gptb200_masked_loss_sum(const float* losses, const float* mask, int64_t n,
+                                       float* out, void* stream) {
+  if (!losses || !mask || !out || n <= 0) return GPTB200_EINVAL;
+  masked_sum_kernel<<<1, 1024, 0, reinterpret_cast<cudaStream_t>(stream)>>>(losses, mask, n, out);
+  GPTB200_CHECK_LAUNCH();
+  return 0;
+}
 
 extern "C" size_t gptb200_lce_fwd_workspace_size(int64_t n, int64_t v_storage) {
   if (n <= 0 || v_storage <= 0) return 0;

@@ -117,6 +117,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp],
     ),
     "gptb200_colsum": (c_int, [c_vp, c_i64, c_i64, c_f32, c_vp, c_vp]),
+    "gptb200_masked_loss_sum": (c_int, [c_vp, c_vp, c_i64, c_vp, c_vp]),
     "gptb200_adamw_workspace_size": (c_size, [c_i64]),
     "gptb200_adamw_step": (
         c_int,

@@ -422,6 +422,49 @@ class GPTTrainer:
         self.graph = graph
         self.graph_launches = ops.launch_count() - before
 
+    def eval_step(self, x: torch.Tensor, y: torch.Tensor, mask: torch.Tensor) -> torch.Tensor:
+        """recipes/reference/train.py:1494-1525: [sum(loss * mask), sum(mask)]
+        over the global batch (fp32, on the device; summed over data-parallel
+        ranks). The forward runs through the same kernels as the training step
+        (tiled cross-entropy losses, never materialized logits); parameters and
+        optimizer state are untouched."""
+
+        if tuple(x.shape) != (self.B, self.T) or tuple(mask.shape) != (self.B, self.T):
+            raise ValueError(f"eval batch must be [{self.B}, {self.T}]; got x {tuple(x.shape)}, "
+                             f"mask {tuple(mask.shape)}")
+        self.set_batch(x, y)
+        self.forward()
+        m = mask.to(device=self.device, dtype=torch.float32)
+        out = ops.masked_loss_sum(self.losses, m.reshape(-1))
+        if self.world_size > 1:
+            import torch.distributed as dist
+
+            dist.all_reduce(out, op=dist.ReduceOp.SUM, group=self.pg)
+        return out
+
+    # ------------------------------------------------------------ artifacts
+    def training_history(self, final_step: int) -> np.ndarray:
+        """Rows 1..final_step of the on-device (loss, lr, grad_norm) history."""
+
+        return self.history[:final_step].detach().cpu().numpy().astype(np.float32)
+
+    def save_checkpoint(self, output_dir, seed: int) -> None:
+        """checkpoint.npz in the rig's layout (fp32 master parameters)."""
+
+        from . import runlog
+
+        tree = runlog.nest_params(self.export(), self.config.layers)
+        runlog.save_checkpoint(output_dir, tree, runlog.checkpoint_metadata(self.config, seed))
+
+    def write_training_log(self, output_dir, final_step: int, flops_per_token: float | None = None):
+        """training.riglog: one record per optimizer step 1..final_step."""
+
+        from . import runlog
+
+        runlog.write_training_log(output_dir, self.training_history(final_step),
+                                  tokens_per_step=self.config.batch_size * self.T,
+                                  final_step=final_step, flops_per_token=flops_per_token)
+
     graph: "torch.cuda.CUDAGraph | None" = None
     graph_launches: int = 0  # libgptb200 kernels inside one replay
 

@@ -278,6 +278,21 @@ def colsum(x: torch.Tensor, out: torch.Tensor, alpha: float = 1.0):
     return out
 
 
+def masked_loss_sum(losses: torch.Tensor, mask: torch.Tensor, out: torch.Tensor | None = None):
+    """out = [sum(losses * mask), sum(mask)] (fp32, deterministic), on the device."""
+
+    _cuda(losses, mask, out)
+    if losses.dtype != F32 or mask.dtype != F32:
+        raise TypeError("masked_loss_sum takes fp32 losses and an fp32 mask")
+    if losses.numel() != mask.numel():
+        raise ValueError(f"losses {tuple(losses.shape)} and mask {tuple(mask.shape)} differ in size")
+    if out is None:
+        out = torch.empty(2, device=losses.device, dtype=F32)
+    call("gptb200_masked_loss_sum", losses.data_ptr(), mask.contiguous().data_ptr(), losses.numel(),
+         out.data_ptr(), _stream())
+    return out
+
+
 def cast_bf16(src: torch.Tensor, dst: torch.Tensor):
     _cuda(src, dst)
     call("gptb200_cast_bf16", src.data_ptr(), dst.data_ptr(), src.numel(), _stream())

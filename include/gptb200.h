@@ -211,6 +211,12 @@ int gptb200_lce_bwd(const void* hidden, const void* embedding, const int32_t* ta
 
 /* ------------------------------------------------------------------ reductions
  * out[j] += sum_i x[i, j] for bf16 x [rows, n] (bias gradients), scaled by alpha. */
+/* Evaluation reduction of recipes/reference/train.py:1494-1525 (eval_step):
+ * out[0] = sum(losses * mask), out[1] = sum(mask), both fp32, over n per-token
+ * losses (from gptb200_lce_fwd) and an fp32 mask. Deterministic (one block). */
+int gptb200_masked_loss_sum(const float* losses, const float* mask, int64_t n, float* out,
+                            void* stream);
+
 int gptb200_colsum(const void* x, int64_t rows, int64_t n, float alpha, float* out, void* stream);
 
 /* ------------------------------------------------------------------ optimizer

@@ -234,6 +234,20 @@ def loss_and_grads(params_np: dict[str, np.ndarray], x, y, cfg, dtype=BF16):
 
 
 # ------------------------------------------------------------------ optimizer
+def eval_step(params_np: dict[str, np.ndarray], x, y, mask, cfg, dtype=BF16) -> tuple[float, float]:
+    """recipes/reference/train.py:1494-1525 (tiled loss backend): the masked
+    per-token loss sum and the mask sum, both fp32."""
+
+    params = {k: torch.from_numpy(np.asarray(v, np.float32)) for k, v in params_np.items()}
+    with torch.no_grad():
+        hidden = gpt_hidden(params, torch.as_tensor(x), cfg, dtype)
+        emb = params.get("output_embedding", params["token_embedding"])
+        losses = TiledLinearCrossEntropy.apply(hidden, emb, torch.as_tensor(y),
+                                               cfg.semantic_vocab_size, dtype).to(F32)
+        m = torch.as_tensor(mask).to(F32)
+        return float((losses * m).sum()), float(m.sum())
+
+
 def learning_rate(step: int, cfg) -> float:
     s = np.float32(step)
     if cfg.warmup_steps:

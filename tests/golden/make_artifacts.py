@@ -1,0 +1,44 @@
+"""Writes tests/golden/training_smoke.riglog with the reference's own
+rig/logpack.py (the training-log columns of rig/runlog.py:132-156) from a fixed
+synthetic history, plus the registry ids it resolves. Run in a checkout where
+the reference project is importable (its logpack/metrics modules need only numpy):
+
+    python tests/golden/make_artifacts.py /path/to/GPT-speedrun-TPU
+"""
+
+import json
+import pathlib
+import sys
+
+import numpy as np
+
+HERE = pathlib.Path(__file__).resolve().parent
+
+
+def history() -> np.ndarray:
+    rng = np.random.default_rng(7)
+    h = np.empty((20, 3), np.float32)
+    h[:, 0] = 10.8 - 0.2 * np.arange(20) + 0.01 * rng.standard_normal(20)
+    h[:, 1] = np.float32(2.0 ** -8) * np.minimum(1.0, (np.arange(20) + 1) / 2.0)
+    h[:, 2] = np.abs(1.0 + rng.standard_normal(20))
+    return h
+
+
+def main(ref_root: str) -> None:
+    sys.path.insert(0, ref_root)
+    from rig import logpack, metrics  # noqa: E402  (the reference's modules)
+
+    cols = [logpack.column("train_loss"), logpack.column("learning_rate"),
+            logpack.column("grad_norm")]
+    out = HERE / "training_smoke.riglog"
+    with logpack.LogWriter(out, cols, tokens_per_step=2048, flops_per_token=123456789.0) as w:
+        for step, row in enumerate(history(), 1):
+            w.append(step, row)
+    ids = {name: metrics.metric(name).id for name in ("train_loss", "learning_rate", "grad_norm")}
+    ids["scope.overall"] = metrics.scope("overall").id
+    (HERE / "riglog_ids.json").write_text(json.dumps(ids, sort_keys=True) + "\n")
+    print(f"wrote {out} ({out.stat().st_size} bytes) and riglog_ids.json")
+
+
+if __name__ == "__main__":
+    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")

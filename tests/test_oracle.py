@@ -114,3 +114,22 @@ def test_learning_rate_schedule():
     assert ref.learning_rate(1, cfg) == pytest.approx(2 ** -8 / 20, rel=1e-6)
     assert ref.learning_rate(20, cfg) == pytest.approx(2 ** -8, rel=1e-6)
     assert ref.learning_rate(200, cfg) == pytest.approx(0.1 * 2 ** -8, rel=1e-5)
+
+
+def test_oracle_eval_step_is_masked_loss_sum():
+    """train.py:1494-1525 restated: with an all-ones mask the loss sum over the
+    token count is the training loss."""
+
+    from rig_b200.model import init_params as b200_init
+
+    cfg = load_config("smoke_parity").replace(batch_size=2, seq_len=32)
+    params = b200_init(cfg, 0)
+    rng = np.random.default_rng(3)
+    x = rng.integers(0, cfg.vocab_size, (2, 32), dtype=np.int32)
+    y = rng.integers(0, cfg.vocab_size, (2, 32), dtype=np.int32)
+    s, n = ref.eval_step(params, x, y, np.ones((2, 32), np.float32), cfg)
+    loss, _ = ref.loss_and_grads(params, x, y, cfg)
+    assert n == 64.0
+    assert abs(s / n - loss) < 1e-5 * abs(loss)
+    s2, n2 = ref.eval_step(params, x, y, np.zeros((2, 32), np.float32), cfg)
+    assert s2 == 0.0 and n2 == 0.0
