@@ -66,6 +66,7 @@ struct AttnParams {
   int64_t sb, sh, st;  // q/k/v (and dq/dk/dv) strides
   const bf16* rcos;    // RoPE tables [T, 32] or null
   const bf16* rsin;
+  const int* seg;      // document segment ids [B, T] or null (causal only)
 };
 
 __device__ __forceinline__ uint32_t swz128(int row, int chunk) {
@@ -87,6 +88,59 @@ __device__ __forceinline__ void rope_back(float* v, const bf16* rcos, const bf16
   }
 }
 
+// ------------------------------------------------------------------ segments
+// Document masking (rig/kernels/tpu_flash_attention.py:171-207 with segment
+// ids): a query sees a key only if the key is not later and both carry the same
+// segment id. Each CTA first reduces the ids of every 64-position chunk of its
+// sequence to a (min, max) range in shared memory; a key block and a query tile
+// whose ranges are disjoint never meet, and when both ranges are one and the
+// same single id no per-element test is needed. Both hold for any ids; with the
+// nondecreasing ids of document_segments (rig/attention.py:205-208) the blocks
+// before a query tile's first document are exactly the ones skipped.
+constexpr int kSegChunk = 64;
+constexpr int kMaxSegChunks = 1024;  // segment ids are supported up to T = 65536
+
+__device__ __forceinline__ int2 rng_merge(int2 a, int2 b) {
+  return make_int2(min(a.x, b.x), max(a.y, b.y));
+}
+__device__ __forceinline__ bool rng_meet(int2 a, int2 b) { return a.x <= b.y && b.x <= a.y; }
+__device__ __forceinline__ bool rng_single(int2 a, int2 b) {
+  return a.x == a.y && b.x == b.y && a.x == b.x;
+}
+
+// tab[c - c0] = (min, max) id of positions [64c, 64c + 64) of seg_row for
+// chunks c0 <= c < c1; positions past T are ignored (an empty chunk is
+// (INT_MAX, INT_MIN)). Every thread of the CTA takes part.
+__device__ void seg_chunk_ranges(const int* __restrict__ seg_row, int T, int c0, int c1,
+                                 int2* tab) {
+  const int warps = blockDim.x >> 5, w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int c = c0 + w; c < c1; c += warps) {
+    int mn = INT_MAX, mx = INT_MIN;
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int t = c * kSegChunk + u * 32 + lane;
+      if (t < T) {
+        const int v = seg_row[t];
+        mn = min(mn, v);
+        mx = max(mx, v);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      mn = min(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+      mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    }
+    if (lane == 0) tab[c - c0] = make_int2(mn, mx);
+  }
+}
+
+// Range of the ids in table entries [c, c + n) (entries at or past nch are empty).
+__device__ __forceinline__ int2 seg_range(const int2* tab, int nch, int c, int n) {
+  int2 r = make_int2(INT_MAX, INT_MIN);
+  for (int i = c; i < c + n && i < nch; ++i) r = rng_merge(r, tab[i]);
+  return r;
+}
+
 // ------------------------------------------------------------------ forward
 constexpr int FQ = 128;                 // queries per tile (TMEM lanes); two tiles per CTA
 constexpr int FK = 128;                 // keys per K/V block
@@ -100,10 +154,14 @@ struct FwdSmem {
   static constexpr int Q = 0;                             // 2 tiles
   static constexpr int K = Q + 2 * Q_BYTES;               // kKvStages
   static constexpr int V = K + kKvStages * KV_BYTES;      // kKvStages
-  static constexpr int BAR = V + kKvStages * KV_BYTES;
+  static constexpr int SEGTAB = V + kKvStages * KV_BYTES; // int2 per 64-position chunk
+  static constexpr int BLOCKS = SEGTAB + kMaxSegChunks * 8;  // key blocks this CTA visits
+  static constexpr int KSEG = BLOCKS + kMaxSegChunks / 2 * 4;  // [tile][2][128] key ids
+  static constexpr int BAR = KSEG + 2 * 2 * FK * 4;
   static constexpr int TOTAL = BAR + 256 + 1024;
 };
 
+template <bool SEG>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
@@ -118,7 +176,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   uint64_t* p_full = s_full + 2;               // [2]: P written to TMEM
   uint64_t* pv_done = p_full + 2;              // [2]: the tile's P.V MMA has completed
   uint64_t* s_free = pv_done + 2;              // [2]: S has been loaded into registers
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_free + 2);
+  uint64_t* kseg_full = s_free + 2;            // [2 tiles][2]: a block's key ids are in smem
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(kseg_full + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -127,24 +186,52 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   const int bh = blockIdx.y;
   const int b = bh / p.H, h = bh - b * p.H;
   const int q0 = pr * 2 * FQ;
-  // Causal key blocks per tile (the last one holds the diagonal); tile 1 of
-  // the last pair may lie wholly past the sequence end.
-  const int n0 = q0 / FK + 1;
-  const int n1 = (q0 + FQ < p.T) ? n0 + 1 : 0;
-  const int nkv = n1 > 0 ? n1 : n0;
+  // Tile x's diagonal key block is d0 + x; tile 1 of the last pair may lie
+  // wholly past the sequence end.
+  const int d0 = q0 / FK;
+  const bool has1 = q0 + FQ < p.T;
+  const int dmax = has1 ? d0 + 1 : d0;
+  const int* segrow = SEG ? p.seg + (int64_t)b * p.T : nullptr;  // null: causal only
+  int2* segtab = reinterpret_cast<int2*>(sm + FwdSmem::SEGTAB);
+  int* blist = reinterpret_cast<int*>(sm + FwdSmem::BLOCKS);
+  int* counts = reinterpret_cast<int*>(tmem_slot + 2);  // [0] blocks, [1] of them <= d0
+  const int nch = min((p.T + kSegChunk - 1) / kSegChunk, 2 * (dmax + 1));
+  if (segrow) seg_chunk_ranges(segrow, p.T, 0, nch, segtab);
+  __syncthreads();
   int* err = &g_attn_error;
 
   if (threadIdx.x == 0) {
+    // The key blocks 0..dmax either query tile can see, in order. Both tiles
+    // walk this one list (tile 0 its prefix up to d0); a block only the other
+    // tile needs is fully masked for a tile, at most costing its exps.
+    const int2 qr0 = segrow ? seg_range(segtab, nch, 2 * d0, 2) : make_int2(0, 0);
+    const int2 qr1 = segrow ? seg_range(segtab, nch, 2 * d0 + 2, 2) : make_int2(0, 0);
+    int n = 0, n_le0 = 0;
+    for (int j = 0; j <= dmax; ++j) {
+      bool need = true;
+      if (segrow) {
+        const int2 kr = seg_range(segtab, nch, 2 * j, 2);
+        need = (j <= d0 && rng_meet(kr, qr0)) || (has1 && rng_meet(kr, qr1));
+      }
+      if (need) {
+        blist[n++] = j;
+        if (j <= d0) ++n_le0;
+      }
+    }
+    counts[0] = n;
+    counts[1] = n_le0;
     mbar_init(q_full, 1);
     for (int s = 0; s < kKvStages; ++s) {
       mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], n1 > 0 ? 2 : 1);  // released by each tile's MMA thread
+      mbar_init(&kv_empty[s], has1 ? 2 : 1);  // released by each tile's MMA thread
     }
     for (int x = 0; x < 2; ++x) {
       mbar_init(&s_full[x], 1);
       mbar_init(&p_full[x], 4);
       mbar_init(&pv_done[x], 1);
       mbar_init(&s_free[x], 4);
+      mbar_init(&kseg_full[2 * x], FQ);
+      mbar_init(&kseg_full[2 * x + 1], FQ);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -153,6 +240,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  const int nkv = counts[0];
+  const int n0 = counts[1];
+  const int n1 = has1 ? nkv : 0;
   // TMEM columns: S[2] (128 fp32 each) | O[2] (64 fp32) | P[2] (128 keys as bf16 pairs)
   const uint32_t tmem = *tmem_slot;
   auto tS = [&](int x) { return tmem + 128 * x; };
@@ -168,8 +258,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         const int s = j % kKvStages;
         if (!mbar_wait(&kv_empty[s], ((j / kKvStages) & 1) ^ 1, abort_flag, err)) break;
         mbar_arrive_expect_tx(&kv_full[s], 2 * KV_BYTES);
-        tma_load_4d(sm + FwdSmem::K + s * KV_BYTES, &tmK, &kv_full[s], 0, j * FK, h, b);
-        tma_load_4d(sm + FwdSmem::V + s * KV_BYTES, &tmV, &kv_full[s], 0, j * FK, h, b);
+        const int key0 = blist[j] * FK;
+        tma_load_4d(sm + FwdSmem::K + s * KV_BYTES, &tmK, &kv_full[s], 0, key0, h, b);
+        tma_load_4d(sm + FwdSmem::V + s * KV_BYTES, &tmV, &kv_full[s], 0, key0, h, b);
       }
     }
   } else if (warp == 1 || warp == kFwdMma1Warp) {
@@ -233,6 +324,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const float c = p.scale * kLog2e;
     float m_used = -INFINITY, l = 0.f;
+    // this row's segment id (rows past T take an id no key has)
+    const int sq = segrow ? (qrow < p.T ? segrow[qrow] : INT_MIN) : 0;
+    const int2 qrng = segrow ? seg_range(segtab, nch, 2 * (d0 + x), 2) : make_int2(0, 0);
+    int* kseg = reinterpret_cast<int*>(sm + FwdSmem::KSEG) + x * 2 * FK;
+    int nseg = 0;  // blocks of this tile that needed the per-element test so far
     bool ok = true;
     for (int j = 0; j < nb && ok; ++j) {
       if ((threadIdx.x & 127) == 64) ATTN_TRACE(2048 + 32 * j + 8 * x + 3);
@@ -242,7 +338,23 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       }
       if ((threadIdx.x & 127) == 64) ATTN_TRACE(2048 + 32 * j + 8 * x + 4);
       tc_fence_after();
-      const bool diag = (j == nb - 1);  // keys past the query (and past T) are masked
+      const int jb = blist[j];
+      const bool diag = (jb == d0 + x);  // keys past the query (and past T) are masked
+      // Per-element segment test unless keys and queries all share one id;
+      // the block's key ids then come through shared memory (double-buffered,
+      // one mbarrier handshake across the warpgroup).
+      const bool segmask = segrow && !rng_single(seg_range(segtab, nch, 2 * jb, 2), qrng);
+      const int* ks = kseg + (nseg & 1) * FK;
+      if (segmask) {
+        const int key = jb * FK + r;
+        kseg[(nseg & 1) * FK + r] = key < p.T ? segrow[key] : INT_MAX;
+        mbar_arrive(&kseg_full[2 * x + (nseg & 1)]);
+        if (!mbar_wait(&kseg_full[2 * x + (nseg & 1)], (nseg >> 1) & 1, abort_flag, err)) {
+          ok = false;
+          break;
+        }
+        ++nseg;
+      }
       // The whole 128-column S row in one batch of TMEM loads, then S_x is
       // handed back so the next block's scores overlap this block's exps.
       uint32_t v[FK];
@@ -258,11 +370,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       float m8[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u) m8[u] = -INFINITY;
-      if (diag) {
+      auto visible = [&](int i) { return (!diag || i <= r) && (!segmask || ks[i] == sq); };
+      if (diag || segmask) {
 #pragma unroll
         for (int i = 0; i < FK; i += 2)
-          m8[(i >> 1) & 7] = fmax3(m8[(i >> 1) & 7], i > r ? -INFINITY : __uint_as_float(v[i]),
-                                   i + 1 > r ? -INFINITY : __uint_as_float(v[i + 1]));
+          m8[(i >> 1) & 7] = fmax3(m8[(i >> 1) & 7], visible(i) ? __uint_as_float(v[i]) : -INFINITY,
+                                   visible(i + 1) ? __uint_as_float(v[i + 1]) : -INFINITY);
       } else {
 #pragma unroll
         for (int i = 0; i < FK; i += 2)
@@ -277,8 +390,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const bool rescale = __any_sync(0xffffffffu, mx > m_used + 8.0f);
       float alpha = 1.f;
       if (rescale) {
+        // 0 on a row's first visible block (m_used = -inf); a row with no
+        // visible key yet (document masking) keeps its -inf max and alpha 1
         const float m_new = fmaxf(m_used, mx);
-        alpha = ex2(m_used - m_new);  // 0 on the first block (m_used = -inf)
+        alpha = m_new == -INFINITY ? 1.f : ex2(m_used - m_new);
         m_used = m_new;
       }
       if ((threadIdx.x & 127) == 64) ATTN_TRACE(2048 + 32 * j + 8 * x + 6);
@@ -293,9 +408,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       for (int i = 0; i < FK; i += 2) {
         const float2 t = ffma2(make_float2(__uint_as_float(v[i]), __uint_as_float(v[i + 1])), c2, nm2);
         float p0 = ex2(t.x), p1 = ex2(t.y);
-        if (diag) {
-          if (i > r) p0 = 0.f;
-          if (i + 1 > r) p1 = 0.f;
+        if (diag || segmask) {
+          if (!visible(i)) p0 = 0.f;
+          if (!visible(i + 1)) p1 = 0.f;
         }
         acc[(i >> 1) & 3] = fadd2(acc[(i >> 1) & 3], make_float2(p0, p1));
         pk[i / 2] = pack_bf16x2(p0, p1);
@@ -377,11 +492,14 @@ struct BwdSmem {
   static constexpr int DO = Q + kQStages * BQ_BYTES;    // kQStages tiles
   static constexpr int DST = DO + kQStages * BQ_BYTES;  // ring of 4 dS^T tiles [128 keys x 64 queries]
   static constexpr int DQS = DST + 4 * BT_BYTES;        // dQ staging: 8 warps x (32 x 32 fp32)
-  static constexpr int STAT = DQS + 8 * 4096;           // per warp: 32 x lse*log2(e), 32 x delta
-  static constexpr int BAR = STAT + 16 * 256;
+  static constexpr int STAT = DQS + 8 * 4096;           // per warp: 32 lse*log2(e), delta, seg id
+  static constexpr int SEGTAB = STAT + 16 * 384;        // int2 per 64-position chunk from k0
+  static constexpr int QLIST = SEGTAB + kMaxSegChunks * 8;  // query tiles this CTA visits
+  static constexpr int BAR = QLIST + kMaxSegChunks * 4;
   static constexpr int TOTAL = BAR + 256 + 1023;
 };
 
+template <bool SEG>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
@@ -407,10 +525,24 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const int bh = blockIdx.y;
   const int b = bh / p.H, h = bh - b * p.H;
   const int k0 = kt * BT;
-  const int nq = (p.T - k0 + BQ - 1) / BQ;  // 64-query tiles from the diagonal to the end
+  const int nq_all = (p.T - k0 + BQ - 1) / BQ;  // 64-query tiles from the diagonal to the end
+  const int* segrow = SEG ? p.seg + (int64_t)b * p.T : nullptr;  // null: causal only
+  int2* segtab = reinterpret_cast<int2*>(sm + BwdSmem::SEGTAB);  // chunk c at [c - 2 kt]
+  int* qlist = reinterpret_cast<int*>(sm + BwdSmem::QLIST);
+  int* counts = reinterpret_cast<int*>(bars + 26);
+  const int nch = (p.T + kSegChunk - 1) / kSegChunk - 2 * kt;
+  if (segrow) seg_chunk_ranges(segrow, p.T, 2 * kt, 2 * kt + nch, segtab);
+  __syncthreads();
   int* err = &g_attn_error;
 
   if (threadIdx.x == 0) {
+    // The query tiles (one 64-position chunk each) that can see this key tile,
+    // in order; every role walks this list.
+    const int2 kr = segrow ? seg_range(segtab, nch, 0, 2) : make_int2(0, 0);
+    int n = 0;
+    for (int it = 0; it < nq_all; ++it)
+      if (!segrow || rng_meet(seg_range(segtab, nch, it, 1), kr)) qlist[n++] = it;
+    counts[0] = n;
     mbar_init(kv_full, 1);
     for (int s = 0; s < kQStages; ++s) {
       mbar_init(&q_full[s], 1);
@@ -433,6 +565,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  const int nq = counts[0];
   // TMEM columns: three tile buffers of 128 columns, then dV | dK. In buffer
   // b, columns [0, 64) receive S^T and [64, 128) dP^T (fp32, lane = key). The
   // softmax writes P^T and dS^T as bf16 pairs over the S^T half (warp half hf
@@ -451,7 +584,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const int s = it % kQStages;
         if (!mbar_wait(&q_empty[s], ((it / kQStages) & 1) ^ 1, abort_flag, err)) break;
         mbar_arrive_expect_tx(&q_full[s], 2 * BQ_BYTES);
-        const int qq = k0 + it * BQ;
+        const int qq = k0 + qlist[it] * BQ;
         tma_load_4d(sm + BwdSmem::Q + s * BQ_BYTES, &tmQ, &q_full[s], 0, qq, h, b);
         tma_load_4d(sm + BwdSmem::DO + s * BQ_BYTES, &tmDO, &q_full[s], 0, qq, h, b);
       }
@@ -552,20 +685,30 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const float* Lg = p.lse + (int64_t)bh * p.T;
     const float* Dg = p.delta + (int64_t)bh * p.T;
     uint8_t* stage = sm + BwdSmem::DQS + wl * 4096;  // dQ staging (warpgroup 0)
-    float* stat = reinterpret_cast<float*>(sm + BwdSmem::STAT + (warp - 2) * 256);
-    // lane j fetches the statistics of query column j of tile `it`
-    auto fetch = [&](int it, float& l2, float& d2) {
-      const int t = k0 + it * BQ + hf * 32 + lane;
+    float* stat = reinterpret_cast<float*>(sm + BwdSmem::STAT + (warp - 2) * 384);
+    int* stat_seg = reinterpret_cast<int*>(stat + 64);
+    // this key row's segment id (rows past T take an id no query has)
+    const int sk = segrow ? (key < p.T ? segrow[key] : INT_MAX) : 0;
+    const int2 krng = segrow ? seg_range(segtab, nch, 0, 2) : make_int2(0, 0);
+    // lane j fetches the statistics of query column j of list entry `it`
+    auto fetch = [&](int it, float& l2, float& d2, int& s2) {
+      const int t = k0 + qlist[it] * BQ + hf * 32 + lane;
       l2 = (t < p.T) ? Lg[t] * kLog2e : INFINITY;  // rows past T: P = 0
       d2 = (t < p.T) ? Dg[t] : 0.f;
+      s2 = (segrow && t < p.T) ? segrow[t] : INT_MIN;
     };
     float nl = 0.f, nd = 0.f;
-    if (wg < nq) fetch(wg, nl, nd);
+    int ns = 0;
+    if (wg < nq) fetch(wg, nl, nd, ns);
     bool ok = true;
-    // dQ rows of query pair j (TMEM lane m = query k0 + 128 j + m) from
-    // buffer bb: one 32x32 fp32 sub-tile per warp, reduced into dq_acc by a
-    // TMA reduce-add (rows past the sequence end are clipped by the map).
+    // dQ rows of query pair j (list entries 2j, 2j+1; TMEM lane m is row m of
+    // the pair, quadrants 0-1 the first tile, 2-3 the second) from buffer bb:
+    // one 32x32 fp32 sub-tile per warp, reduced into dq_acc by a TMA reduce-add
+    // (rows past the sequence end are clipped by the map).
     auto flush_dq = [&](int j, int bb) {
+      const int e = 2 * j + (quad >> 1);
+      if (e >= nq) return;  // a last pair of one tile (warp-uniform)
+      const int row0 = k0 + qlist[e] * BQ + (quad & 1) * 32;
       float v[32];
       tmem_ld32(tBuf(bb) + 64 + lane_off + hf * 32, v);
       if (lane == 0) bulk_wait_read();  // the previous reduce has read the staging tile
@@ -577,7 +720,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
-        tma_reduce_add_3d(&tmDQ, stage, hf * 32, k0 + j * BT + quad * 32, bh);
+        tma_reduce_add_3d(&tmDQ, stage, hf * 32, row0, bh);
         bulk_commit();
       }
     };
@@ -585,11 +728,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const int bb = it % 3;
       const uint32_t tb = tBuf(bb);
       // this tile's statistics, broadcast to the warp through shared memory
+      const int qt = qlist[it];  // query tile index (64 positions) past k0
       __syncwarp();
       stat[lane] = nl;
       stat[32 + lane] = nd;
+      stat_seg[lane] = ns;
       __syncwarp();
-      if (it + 2 < nq) fetch(it + 2, nl, nd);
+      if (it + 2 < nq) fetch(it + 2, nl, nd, ns);
       if (threadIdx.x == 64) ATTN_TRACE(64 * it + 11);
       if (!mbar_wait(&s_full[bb], (it / 3) & 1, abort_flag, err)) {
         ok = false;
@@ -606,8 +751,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tmem_ld32_nw(tb + lane_off + hf * 32, sraw);
       tmem_ld32_nw(tb + 64 + lane_off + hf * 32, draw);
       tmem_wait_ld();
-      const int qbase = it * BQ + hf * 32;  // query index relative to k0
-      const bool diag = (it < 2);           // key r > query masks only near the diagonal
+      const int qbase = qt * BQ + hf * 32;  // query index relative to k0
+      const bool diag = (qt < 2);           // key r > query masks only near the diagonal
+      // per-element segment test unless this key tile and query tile share one id
+      const bool segmask = segrow && !rng_single(seg_range(segtab, nch, qt, 1), krng);
       uint32_t pk[16], dk[16];
 #pragma unroll
       for (int j4 = 0; j4 < 8; ++j4) {
@@ -621,6 +768,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           const int j = 4 * j4 + u;
           pv[u] = ex2(fmaf(__uint_as_float(sraw[j]), c, -lv[u]));
           if (diag && r > qbase + j) pv[u] = 0.f;
+          if (segmask && stat_seg[j] != sk) pv[u] = 0.f;
           dv[u] = pv[u] * (__uint_as_float(draw[j]) - dl[u]);
         }
         pk[2 * j4] = pack_bf16x2(pv[0], pv[1]);
@@ -849,11 +997,14 @@ extern "C" int gptb200_attention_fwd(const void* q, const void* k, const void* v
                                      int64_t stride_h, int64_t stride_t, void* o,
                                      int64_t o_stride_b, int64_t o_stride_h, int64_t o_stride_t,
                                      float* lse, int64_t batch, int64_t heads, int64_t seq,
-                                     int64_t head_dim, float softmax_scale, void* stream) {
+                                     int64_t head_dim, float softmax_scale,
+                                     const int32_t* segment_ids, void* stream) {
   int s = check_attn(q, k, v, stride_b, stride_h, stride_t, o_stride_b, o_stride_h, o_stride_t,
                      batch, heads, seq, head_dim);
   if (s) return s;
   if (!o || !lse || !(softmax_scale > 0.f)) return GPTB200_EINVAL;
+  if (segment_ids && seq > (int64_t)kMaxSegChunks * kSegChunk) return GPTB200_EUNSUPPORTED;
+  if (reinterpret_cast<uintptr_t>(segment_ids) & 3) return GPTB200_ESHAPE;
   if (reinterpret_cast<uintptr_t>(o) & 15) return GPTB200_ESHAPE;
   CUtensorMap mq, mk, mv;
   if (!make_map4(&mq, q, (int)batch, (int)heads, (int)seq, stride_b, stride_h, stride_t, FQ) ||
@@ -870,18 +1021,21 @@ extern "C" int gptb200_attention_fwd(const void* q, const void* k, const void* v
   p.osh = o_stride_h;
   p.ost = o_stride_t;
   p.lse = lse;
-  static bool cfg[64] = {false};
+  p.seg = segment_ids;
+  static bool cfg[64][2] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 64 || !cfg[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(attn_fwd_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  const int seg = segment_ids != nullptr;
+  auto kern = seg ? attn_fwd_tc<true> : attn_fwd_tc<false>;
+  if (dev >= 64 || !cfg[dev][seg]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          FwdSmem::TOTAL);
     if (e != cudaSuccess) return -static_cast<int>(e);
-    if (dev < 64) cfg[dev] = true;
+    if (dev < 64) cfg[dev][seg] = true;
   }
   dim3 grid((unsigned)((seq + 2 * FQ - 1) / (2 * FQ)), (unsigned)(batch * heads));
-  attn_fwd_tc<<<grid, kFwdThreads, FwdSmem::TOTAL, reinterpret_cast<cudaStream_t>(stream)>>>(mq, mk,
-                                                                                          mv, p);
+  kern<<<grid, kFwdThreads, FwdSmem::TOTAL, reinterpret_cast<cudaStream_t>(stream)>>>(mq, mk, mv,
+                                                                                      p);
   GPTB200_CHECK_LAUNCH();
   return 0;
 }
@@ -898,12 +1052,15 @@ extern "C" int gptb200_attention_bwd(const void* q, const void* k, const void* v
                                      int64_t o_stride_t, const float* lse, void* dq, void* dk,
                                      void* dv, int64_t batch, int64_t heads, int64_t seq,
                                      int64_t head_dim, float softmax_scale, const void* rope_cos,
-                                     const void* rope_sin, void* workspace, void* stream) {
+                                     const void* rope_sin, const int32_t* segment_ids,
+                                     void* workspace, void* stream) {
   int s = check_attn(q, k, v, stride_b, stride_h, stride_t, o_stride_b, o_stride_h, o_stride_t,
                      batch, heads, seq, head_dim);
   if (s) return s;
   if (!o || !dout || !lse || !dq || !dk || !dv || !workspace || !(softmax_scale > 0.f))
     return GPTB200_EINVAL;
+  if (segment_ids && seq > (int64_t)kMaxSegChunks * kSegChunk) return GPTB200_EUNSUPPORTED;
+  if (reinterpret_cast<uintptr_t>(segment_ids) & 3) return GPTB200_ESHAPE;
   if ((rope_cos == nullptr) != (rope_sin == nullptr)) return GPTB200_EINVAL;
   if ((reinterpret_cast<uintptr_t>(dout) | reinterpret_cast<uintptr_t>(dq) |
        reinterpret_cast<uintptr_t>(dk) | reinterpret_cast<uintptr_t>(dv) |
@@ -940,19 +1097,22 @@ extern "C" int gptb200_attention_bwd(const void* q, const void* k, const void* v
   p.st = stride_t;
   p.rcos = reinterpret_cast<const bf16*>(rope_cos);
   p.rsin = reinterpret_cast<const bf16*>(rope_sin);
-  static bool cfg[64] = {false};
+  p.seg = segment_ids;
+  static bool cfg[64][2] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 64 || !cfg[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(attn_bwd_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  const int seg = segment_ids != nullptr;
+  auto kern = seg ? attn_bwd_tc<true> : attn_bwd_tc<false>;
+  if (dev >= 64 || !cfg[dev][seg]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          BwdSmem::TOTAL);
     if (e != cudaSuccess) return -static_cast<int>(e);
-    if (dev < 64) cfg[dev] = true;
+    if (dev < 64) cfg[dev][seg] = true;
   }
   dim3 grid((unsigned)((seq + BT - 1) / BT), (unsigned)(batch * heads));
   CUtensorMap mdq;
   if (!make_dq_map(&mdq, dq_acc, B * H, T)) return GPTB200_ESHAPE;
-  attn_bwd_tc<<<grid, kBwdThreads, BwdSmem::TOTAL, st>>>(mq, mk, mv, mdo, mdq, p);
+  kern<<<grid, kBwdThreads, BwdSmem::TOTAL, st>>>(mq, mk, mv, mdo, mdq, p);
   GPTB200_CHECK_LAUNCH();
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);

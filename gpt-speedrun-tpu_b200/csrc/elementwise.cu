@@ -265,6 +265,46 @@ extern "C" int gptb200_rms_norm_bwd(const void* x, const void* scale, const floa
   return rms_bwd_launch<8>(X, S, rstd, DY, DXI, DXO, dscale, dx_colsum, colsum_alpha, rows, (int)d, st);
 }
 
+// ------------------------------------------------------------------ document segments
+// out[b, t] = number of boundary tokens in tokens[b, 0..t] (rig/attention.py:
+// 205-208): one block per sequence, each thread a contiguous run of positions,
+// a block-wide exclusive scan of the run counts, then the running count.
+__global__ void __launch_bounds__(256) doc_segments_kernel(const int* __restrict__ tokens,
+                                                           int64_t seq, int boundary,
+                                                           int* __restrict__ out) {
+  __shared__ int part[256];
+  const int64_t row = blockIdx.x;
+  const int64_t per = (seq + blockDim.x - 1) / blockDim.x;
+  const int64_t t0 = threadIdx.x * per, t1 = min(seq, t0 + per);
+  const int* tk = tokens + row * seq;
+  int n = 0;
+  for (int64_t t = t0; t < t1; ++t) n += tk[t] == boundary;
+  part[threadIdx.x] = n;
+  __syncthreads();
+  // inclusive Hillis-Steele scan over the 256 run counts
+  for (int o = 1; o < (int)blockDim.x; o <<= 1) {
+    const int v = threadIdx.x >= o ? part[threadIdx.x - o] : 0;
+    __syncthreads();
+    part[threadIdx.x] += v;
+    __syncthreads();
+  }
+  int run = part[threadIdx.x] - n;
+  int* o = out + row * seq;
+  for (int64_t t = t0; t < t1; ++t) {
+    run += tk[t] == boundary;
+    o[t] = run;
+  }
+}
+
+extern "C" int gptb200_document_segments(const int32_t* tokens, int64_t batch, int64_t seq,
+                                         int32_t boundary_token, int32_t* out, void* stream) {
+  if (!tokens || !out || batch <= 0 || seq <= 0 || batch > INT32_MAX) return GPTB200_EINVAL;
+  doc_segments_kernel<<<(unsigned)batch, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      tokens, seq, boundary_token, out);
+  GPTB200_CHECK_LAUNCH();
+  return 0;
+}
+
 // ------------------------------------------------------------------ embedding
 __global__ void embed_fwd_kernel(const int32_t* __restrict__ tok, const bf16* __restrict__ table,
                                  bf16* __restrict__ out, int64_t n, int d, int64_t vocab) {

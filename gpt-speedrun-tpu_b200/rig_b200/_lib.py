@@ -91,18 +91,19 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "gptb200_embedding_fwd": (c_int, [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp]),
     "gptb200_embedding_bwd": (c_int, [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp]),
     "gptb200_rope_tables": (c_int, [c_vp, c_vp, c_i64, c_i64, c_vp]),
+    "gptb200_document_segments": (c_int, [c_vp, c_i64, c_i64, ctypes.c_int32, c_vp, c_vp]),
     "gptb200_rope_apply": (
         c_int, [c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_int, c_vp]),
     "gptb200_attention_fwd": (
         c_int,
         [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_i64, c_vp,
-         c_i64, c_i64, c_i64, c_i64, c_f32, c_vp],
+         c_i64, c_i64, c_i64, c_i64, c_f32, c_vp, c_vp],
     ),
     "gptb200_attention_bwd_workspace_size": (c_size, [c_i64, c_i64, c_i64]),
     "gptb200_attention_bwd": (
         c_int,
         [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp,
-         c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_f32, c_vp, c_vp, c_vp, c_vp],
+         c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_f32, c_vp, c_vp, c_vp, c_vp, c_vp],
     ),
     "gptb200_lce_fwd_workspace_size": (c_size, [c_i64, c_i64]),
     "gptb200_lce_fwd": (

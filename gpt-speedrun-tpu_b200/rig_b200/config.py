@@ -55,6 +55,8 @@ class Config:
     normalization: str = "rms_norm"
     position_encoding: str = "rope_base_10000"
     mlp_activation: str = "gelu"
+    document_masking: bool = False        # the context preset's document-attention policy
+    document_boundary_token: int = 50256  # recipes/reference/train.py:234-235
 
     @property
     def width_multiplier(self) -> float:
@@ -179,6 +181,7 @@ def resolve_config(
         dtype_name=str(training["dtype"]),
         sampling=str(training.get("sampling", "shuffled_epochs")),
         tier=tier_name,
+        document_masking=bool(ctx.get("document_masking", False)),
     )
 
 

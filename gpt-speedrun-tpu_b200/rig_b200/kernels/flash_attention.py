@@ -5,8 +5,9 @@ Drop-in for rig/kernels/tpu_flash_attention.py:75-97 (`AttentionConfig`) and
 (bf16, head_dim 64) and returns BHSD output, differentiable through the
 libgptb200 forward/backward kernels. Validation follows `_validate_qkv`
 (:145-168). Tiles are chosen by the kernel; the `tiles` field is accepted and
-ignored. Segment ids (document masking, 8k preset) are not supported yet and
-raise.
+ignored. Optional segment ids ([batch, seq] int32, e.g. from
+`rig_b200.attention.document_segments`) restrict attention to each document
+(reference_causal_attention's segment_ids, :171-207).
 """
 
 from __future__ import annotations
@@ -52,7 +53,7 @@ def _validate_qkv(q, k, v) -> None:
 
 class _Attention(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, q, k, v, scale, rope):
+    def forward(ctx, q, k, v, scale, rope, segment_ids):
         q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
         if rope is not None:  # rotate copies of q and k (BHSD viewed as BTHD)
             q, k = q.clone(), k.clone()
@@ -61,9 +62,9 @@ class _Attention(torch.autograd.Function):
         b, h, t, _ = q.shape
         o = torch.empty_like(q)
         lse = torch.empty(b, h, t, dtype=torch.float32, device=q.device)
-        ops.attention_fwd(q, k, v, o, lse, scale=scale)
+        ops.attention_fwd(q, k, v, o, lse, scale=scale, segment_ids=segment_ids)
         ctx.save_for_backward(q, k, v, o, lse)
-        ctx.scale, ctx.rope = scale, rope
+        ctx.scale, ctx.rope, ctx.segment_ids = scale, rope, segment_ids
         return o
 
     @staticmethod
@@ -71,8 +72,9 @@ class _Attention(torch.autograd.Function):
         q, k, v, o, lse = ctx.saved_tensors
         do = do.contiguous().to(torch.bfloat16)
         dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
-        ops.attention_bwd(q, k, v, o, do, lse, dq, dk, dv, scale=ctx.scale, rope=ctx.rope)
-        return dq, dk, dv, None, None
+        ops.attention_bwd(q, k, v, o, do, lse, dq, dk, dv, scale=ctx.scale, rope=ctx.rope,
+                          segment_ids=ctx.segment_ids)
+        return dq, dk, dv, None, None, None
 
 
 def make_causal_attention(config: AttentionConfig = AttentionConfig(), *,
@@ -84,10 +86,13 @@ def make_causal_attention(config: AttentionConfig = AttentionConfig(), *,
     """
 
     def attention(q, k, v, segment_ids=None):
-        if segment_ids is not None:
-            raise NotImplementedError("document masking (segment ids) is not supported yet")
         _validate_qkv(q, k, v)
+        if segment_ids is not None:
+            if tuple(segment_ids.shape) != (q.shape[0], q.shape[2]):
+                raise ValueError(f"segment_ids must be [batch, seq] = {(q.shape[0], q.shape[2])}, "
+                                 f"got {tuple(segment_ids.shape)}")
+            segment_ids = segment_ids.to(device=q.device, dtype=torch.int32).contiguous()
         scale = config.softmax_scale if config.softmax_scale is not None else q.shape[-1] ** -0.5
-        return _Attention.apply(q, k, v, float(scale), rope_tables)
+        return _Attention.apply(q, k, v, float(scale), rope_tables, segment_ids)
 
     return attention

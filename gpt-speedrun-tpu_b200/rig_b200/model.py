@@ -263,6 +263,8 @@ class GPTTrainer:
         self.lnf = torch.empty(N, d, **bf)
         self.rstdf = torch.empty(N, **f32)
         self.losses = torch.empty(N, **f32)
+        self.segments = (torch.empty(self.B, self.T, dtype=torch.int32, device=dev)
+                         if c.document_masking else None)
         self.lse_ce = torch.empty(N, **f32)
         self.loss = torch.zeros(1, **f32)
         self.cot = torch.full((N,), 1.0 / (N * self.world_size), **f32)
@@ -321,6 +323,9 @@ class GPTTrainer:
         d, h, N = c.d_model, c.hidden, self.N
         a = c.branch_scale
         ops.embedding_fwd(self.tokens.view(-1), self.tok_emb, self.x[0])
+        if self.segments is not None:  # document masking (train.py:1127-1131)
+            ops.document_segments(self.tokens.view(self.B, self.T), c.document_boundary_token,
+                                  self.segments)
         for l, blk in enumerate(self.blocks):
             ops.rms_norm_fwd(self.x[l], blk.ln1_scale, self.ln1[l], self.rstd1[l])
             # QKV projection with bias and RoPE on the q/k columns in the epilogue
@@ -328,7 +333,7 @@ class GPTTrainer:
                        kind=_lib.EPI_BIAS_ROPE, rope=self.rope, rope_cols=2 * d)
             q, k, v = self._qkv_views(self.qkv[l])
             ops.attention_fwd(q, k, v, self._bthd(self.att[l]), self.lse[l], scale=c.softmax_scale,
-                              layout="bthd")
+                              layout="bthd", segment_ids=self.segments)
             ops.matmul(self.att[l], blk.attn_w, bias=blk.attn_b, alpha=a, residual=self.x[l],
                        out=self.xm[l])
             ops.rms_norm_fwd(self.xm[l], blk.ln2_scale, self.ln2[l], self.rstd2[l])
@@ -381,7 +386,7 @@ class GPTTrainer:
             dq, dk, dv = self._qkv_views(self.dqkv)
             ops.attention_bwd(q, k, v, self._bthd(self.att[l]), self._bthd(self.datt), self.lse[l],
                               dq, dk, dv, scale=c.softmax_scale, layout="bthd", rope=self.rope,
-                              workspace=self.attn_ws)
+                              workspace=self.attn_ws, segment_ids=self.segments)
             self._wgrad(self.ln1[l], self.dqkv, blk.g_qkv_w, 1.0)
             ops.colsum(self.dqkv, blk.g_qkv_b, 1.0)
             self._dgrad(self.dqkv, blk.qkv_w, self.dln)

@@ -176,6 +176,21 @@ def rope_tables(seq: int, head_dim: int, device) -> tuple[torch.Tensor, torch.Te
     return cos, sin
 
 
+def document_segments(tokens: torch.Tensor, boundary_token: int,
+                      out: torch.Tensor | None = None) -> torch.Tensor:
+    """rig/attention.py:205-208 on the device: cumulative boundary count per row."""
+
+    _cuda(tokens, out)
+    if tokens.dtype != torch.int32 or tokens.dim() != 2:
+        raise TypeError("tokens must be an int32 [batch, seq] tensor")
+    tokens = tokens.contiguous()
+    if out is None:
+        out = torch.empty_like(tokens)
+    call("gptb200_document_segments", tokens.data_ptr(), tokens.shape[0], tokens.shape[1],
+         int(boundary_token), out.data_ptr(), _stream())
+    return out
+
+
 # ----------------------------------------------------------------- attention
 def _strides4(t: torch.Tensor, layout: str) -> tuple[int, int, int]:
     """Element strides (batch, head, time) of a rank-4 view, inner dim contiguous."""
@@ -187,9 +202,20 @@ def _strides4(t: torch.Tensor, layout: str) -> tuple[int, int, int]:
     return t.stride(0), t.stride(2), t.stride(1)  # bthd
 
 
-def attention_fwd(q, k, v, o, lse, *, scale: float, layout: str = "bhsd"):
+def _segments(segment_ids, b: int, t: int):
+    if segment_ids is None:
+        return None
+    _cuda(segment_ids)
+    if segment_ids.dtype != torch.int32 or tuple(segment_ids.shape) != (b, t):
+        raise ValueError(f"segment_ids must be int32 [{b}, {t}], got {segment_ids.dtype} "
+                         f"{tuple(segment_ids.shape)}")
+    return segment_ids.contiguous()
+
+
+def attention_fwd(q, k, v, o, lse, *, scale: float, layout: str = "bhsd", segment_ids=None):
     """Causal attention; q/k/v/o are rank-4 views in `layout` ('bhsd' or 'bthd').
-    q and k are used as given (apply RoPE before, e.g. with `rope_apply`)."""
+    q and k are used as given (apply RoPE before, e.g. with `rope_apply`).
+    segment_ids: optional int32 [B, T] document ids (same-document attention)."""
 
     _cuda(q, k, v, o, lse)
     sb, sh, st = _strides4(q, layout)
@@ -200,8 +226,10 @@ def attention_fwd(q, k, v, o, lse, *, scale: float, layout: str = "bhsd"):
         b, h, t, dh = q.shape
     else:
         b, t, h, dh = q.shape
+    seg = _segments(segment_ids, b, t)
     call("gptb200_attention_fwd", q.data_ptr(), k.data_ptr(), v.data_ptr(), sb, sh, st,
-         o.data_ptr(), osb, osh, ost, lse.data_ptr(), b, h, t, dh, float(scale), _stream())
+         o.data_ptr(), osb, osh, ost, lse.data_ptr(), b, h, t, dh, float(scale), _ptr(seg),
+         _stream())
     return o, lse
 
 
@@ -211,7 +239,7 @@ def attention_workspace(b: int, h: int, t: int, device) -> torch.Tensor:
 
 
 def attention_bwd(q, k, v, o, do, lse, dq, dk, dv, *, scale: float, layout="bhsd", rope=None,
-                  workspace=None):
+                  workspace=None, segment_ids=None):
     _cuda(q, k, v, o, do, lse, dq, dk, dv)
     sb, sh, st = _strides4(q, layout)
     for t_ in (k, v, dq, dk, dv):
@@ -227,10 +255,11 @@ def attention_bwd(q, k, v, o, do, lse, dq, dk, dv, *, scale: float, layout="bhsd
     if workspace is None:
         workspace = attention_workspace(b, h, t, q.device)
     cos, sin = rope if rope is not None else (None, None)
+    seg = _segments(segment_ids, b, t)
     call("gptb200_attention_bwd", q.data_ptr(), k.data_ptr(), v.data_ptr(), sb, sh, st,
          o.data_ptr(), do.data_ptr(), osb, osh, ost, lse.data_ptr(), dq.data_ptr(),
          dk.data_ptr(), dv.data_ptr(), b, h, t, dh, float(scale), _ptr(cos), _ptr(sin),
-         workspace.data_ptr(), _stream())
+         _ptr(seg), workspace.data_ptr(), _stream())
     return dq, dk, dv
 
 

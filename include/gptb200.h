@@ -135,6 +135,11 @@ int gptb200_rope_apply(void* x, int64_t stride_b, int64_t stride_t, int64_t stri
                        int64_t batch, int64_t seq, int64_t heads, int64_t head_dim,
                        const void* rope_cos, const void* rope_sin, int inverse, void* stream);
 
+/* Document ids for attention masking (rig/attention.py:205-208): out[b, t] =
+ * count of boundary_token in tokens[b, 0..t] (int32 [batch, seq] both). */
+int gptb200_document_segments(const int32_t* tokens, int64_t batch, int64_t seq,
+                              int32_t boundary_token, int32_t* out, void* stream);
+
 /* ------------------------------------------------------------------ attention
  * Causal softmax attention on tcgen05 tensor cores, fp32 statistics, bf16 P
  * before P·V. q and k are taken as given (already rotated: in the training
@@ -143,6 +148,11 @@ int gptb200_rope_apply(void* x, int64_t stride_b, int64_t stride_t, int64_t stri
  * (element strides); q, k, v share (stride_b, stride_h, stride_t), o and do
  * share (o_stride_*). lse: fp32 [batch, heads, seq] (natural-log units of the
  * scaled scores). head_dim must be 64; strides multiples of 8 elements.
+ * segment_ids: NULL (causal only) or int32 [batch, seq] document ids: a query
+ * then sees a key only if both carry the same id (block-diagonal over
+ * documents on top of the causal mask, reference_causal_attention's
+ * segment_ids); key blocks whose id range misses a query tile's are skipped.
+ * With segment ids, seq <= 65536 (GPTB200_EUNSUPPORTED otherwise).
  * Replaces rig/kernels/tpu_flash_attention.py:236-348 (forward kernel) behind
  * make_causal_attention (:962-1164); semantics of reference_causal_attention
  * (:171-207).
@@ -151,11 +161,12 @@ int gptb200_attention_fwd(const void* q, const void* k, const void* v, int64_t s
                           int64_t stride_h, int64_t stride_t, void* o, int64_t o_stride_b,
                           int64_t o_stride_h, int64_t o_stride_t, float* lse, int64_t batch,
                           int64_t heads, int64_t seq, int64_t head_dim, float softmax_scale,
-                          void* stream);
+                          const int32_t* segment_ids, void* stream);
 
 size_t gptb200_attention_bwd_workspace_size(int64_t batch, int64_t heads, int64_t seq);
 
 /* Backward: dq, dk, dv are written (not accumulated) with the q/k/v strides.
+ * segment_ids: as in the forward (the same ids, or NULL).
  * With rope tables (the ones q and k were rotated with), dq and dk are rotated
  * back, i.e. they are gradients with respect to the unrotated q and k.
  * Replaces rig/kernels/tpu_flash_attention.py:479-575 (dQ) and :578-701 (dK/dV). */
@@ -164,8 +175,8 @@ int gptb200_attention_bwd(const void* q, const void* k, const void* v, int64_t s
                           int64_t o_stride_b, int64_t o_stride_h, int64_t o_stride_t,
                           const float* lse, void* dq, void* dk, void* dv, int64_t batch,
                           int64_t heads, int64_t seq, int64_t head_dim, float softmax_scale,
-                          const void* rope_cos, const void* rope_sin, void* workspace,
-                          void* stream);
+                          const void* rope_cos, const void* rope_sin, const int32_t* segment_ids,
+                          void* workspace, void* stream);
 
 /* ------------------------------------------------------------------ linear cross-entropy
  * Tied-embedding cross entropy without materializing [n, vocab] logits:

@@ -87,12 +87,18 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, dtype=BF16
     return bf16_dot(x, weight, dtype) + bias.to(dtype)
 
 
-def causal_attention(q, k, v, scale: float) -> torch.Tensor:
-    """reference_causal_attention on BHSD tensors."""
+def causal_attention(q, k, v, scale: float, segment_ids=None) -> torch.Tensor:
+    """reference_causal_attention on BHSD tensors
+    (rig/kernels/tpu_flash_attention.py:171-207): with segment_ids [B, T], a
+    query sees only keys of its own segment, on top of the causal mask."""
 
     t = q.shape[2]
     scores = (q.to(F32) @ k.to(F32).transpose(-1, -2)) * scale
     visible = torch.ones(t, t, dtype=torch.bool).tril()
+    if segment_ids is not None:
+        seg = torch.as_tensor(segment_ids)
+        same = seg[:, None, :, None] == seg[:, None, None, :]
+        visible = visible[None, None] & same
     scores = torch.where(visible, scores, torch.tensor(-0.7 * torch.finfo(F32).max))
     probabilities = torch.softmax(scores, dim=-1).to(v.dtype)
     return (probabilities.to(F32) @ v.to(F32)).to(q.dtype)
@@ -156,6 +162,13 @@ def tiled_tied_cross_entropy(hidden, embedding, targets, semantic_vocab_size, dt
 
 
 # ------------------------------------------------------------------ model
+def document_segments(tokens, boundary_token: int):
+    """rig/attention.py:205-208: each token's document index inside its window
+    (cumulative count of boundary tokens, the boundary opening a new document)."""
+
+    return np.cumsum(np.asarray(tokens) == boundary_token, axis=1).astype(np.int32)
+
+
 def init_params(cfg: Any, seed: int) -> dict[str, np.ndarray]:
     """train.py:865-901 with rig/nn.py:20-23's normal()."""
 
@@ -198,6 +211,8 @@ def gpt_hidden(params: dict[str, torch.Tensor], tokens: torch.Tensor, cfg, dtype
     head_dim = cfg.d_model // heads
     mult = (cfg.layers / float(cfg.base_depth)) ** (-cfg.depth_alpha)
     scale = softmax_scale(cfg)
+    segments = (document_segments(tokens.numpy(), cfg.document_boundary_token)
+                if getattr(cfg, "document_masking", False) else None)  # train.py:1127-1131
     x = params["token_embedding"][tokens.long()].to(dtype)
     for b in range(cfg.layers):
         p = {k: params[f"blocks/{b}/{k}"] for k in BLOCK_FIELDS}
@@ -208,7 +223,8 @@ def gpt_hidden(params: dict[str, torch.Tensor], tokens: torch.Tensor, cfg, dtype
         q = apply_rotary(q.reshape(batch, length, heads, head_dim))
         k = apply_rotary(k.reshape(batch, length, heads, head_dim))
         v = v.reshape(batch, length, heads, head_dim)
-        att = causal_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), scale)
+        att = causal_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), scale,
+                               segments)
         att = att.transpose(1, 2).reshape(batch, length, cfg.d_model)
         x = residual + mult * linear(att, p["attn_w"], p["attn_b"], dtype)
         residual = x

@@ -1,6 +1,7 @@
 """Flash attention (RoPE fused on load) vs the dense restatement of
 reference_causal_attention (rig/kernels/tpu_flash_attention.py:171-207)."""
 
+import numpy as np
 import pytest
 import torch
 
@@ -103,3 +104,52 @@ def test_qkv_rope_epilogue(cuda):
     ops.rope_apply(pl[:, :, 1], tables)
     o = out.view_as(pl).float()
     assert ((o - pl.float()).abs() <= 2 ** -7 * pl.float().abs() + 1e-6).all()
+
+
+def _segments(b, t, kind, seed):
+    rng = np.random.default_rng(seed)
+    if kind == "one":
+        return np.zeros((b, t), np.int32)
+    if kind == "random":  # arbitrary ids: the semantics are plain id equality
+        return rng.integers(0, 3, (b, t)).astype(np.int32)
+    p = {"docs300": 1 / 300, "docs40": 1 / 40}[kind]
+    return ref.document_segments(rng.random((b, t)) < p, True)
+
+
+@pytest.mark.parametrize("kind", ["one", "docs300", "docs40", "random"])
+@pytest.mark.parametrize("b,h,t", [(2, 2, 1024), (1, 2, 1000), (1, 1, 200), (2, 1, 2048)])
+def test_document_masking_vs_restatement(cuda, kind, b, h, t):
+    """Segment ids (rig/attention.py:205-208; reference_causal_attention's
+    segment_ids): forward and all three gradients, with and without block
+    skipping, including ids that are not monotone."""
+
+    g = torch.Generator().manual_seed(11)
+    q, k, v, do = (torch.randn(b, h, t, 64, generator=g).bfloat16() for _ in range(4))
+    seg = _segments(b, t, kind, 5)
+    qq, kk, vv = (x.float().requires_grad_(True) for x in (q, k, v))
+    o_ref = ref.causal_attention(qq.bfloat16(), kk.bfloat16(), vv.bfloat16(), 1 / 64, seg)
+    (o_ref.float() * do.float()).sum().backward()
+    qd, kd, vd, dod = (x.to(cuda) for x in (q, k, v, do))
+    segd = torch.from_numpy(seg).to(cuda)
+    o = torch.empty_like(qd)
+    lse = torch.empty(b, h, t, device=cuda)
+    ops.attention_fwd(qd, kd, vd, o, lse, scale=1 / 64, segment_ids=segd)
+    dq, dk, dv = torch.empty_like(qd), torch.empty_like(kd), torch.empty_like(vd)
+    ops.attention_bwd(qd, kd, vd, o, dod, lse, dq, dk, dv, scale=1 / 64, segment_ids=segd)
+    torch.cuda.synchronize()
+    assert ops.device_error() == 0
+    for name, x, y in zip(("o", "dq", "dk", "dv"), (o, dq, dk, dv),
+                          (o_ref, qq.grad, kk.grad, vv.grad)):
+        assert _rel(x.cpu(), y) < 2e-2, (name, _rel(x.cpu(), y))
+
+
+def test_single_segment_equals_causal(cuda):
+    g = torch.Generator().manual_seed(2)
+    q, k, v = (torch.randn(1, 2, 512, 64, generator=g).bfloat16().to(cuda) for _ in range(3))
+    outs = []
+    for seg in (None, torch.full((1, 512), 7, dtype=torch.int32, device=cuda)):
+        o = torch.empty_like(q)
+        lse = torch.empty(1, 2, 512, device=cuda)
+        ops.attention_fwd(q, k, v, o, lse, scale=1 / 64, segment_ids=seg)
+        outs.append((o.cpu(), lse.cpu()))
+    assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])

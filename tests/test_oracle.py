@@ -133,3 +133,23 @@ def test_oracle_eval_step_is_masked_loss_sum():
     assert abs(s / n - loss) < 1e-5 * abs(loss)
     s2, n2 = ref.eval_step(params, x, y, np.zeros((2, 32), np.float32), cfg)
     assert s2 == 0.0 and n2 == 0.0
+
+
+def test_document_segments_golden():
+    """tests/test_attention.py:206-211 of the reference (known answer)."""
+
+    tokens = np.asarray([[9, 1, 2, 9, 3], [4, 9, 5, 9, 9]], np.int32)
+    np.testing.assert_array_equal(ref.document_segments(tokens, 9),
+                                  np.asarray([[1, 1, 1, 2, 2], [0, 1, 1, 2, 3]], np.int32))
+
+
+def test_segment_attention_is_blockwise_causal():
+    """With segments, each document attends as if it were its own sequence."""
+
+    g = torch.Generator().manual_seed(0)
+    q, k, v = (torch.randn(1, 2, 12, 8, generator=g) for _ in range(3))
+    seg = np.asarray([[0] * 5 + [1] * 7], np.int32)
+    out = ref.causal_attention(q, k, v, 0.3, seg)
+    a = ref.causal_attention(q[:, :, :5], k[:, :, :5], v[:, :, :5], 0.3)
+    b = ref.causal_attention(q[:, :, 5:], k[:, :, 5:], v[:, :, 5:], 0.3)
+    torch.testing.assert_close(out, torch.cat([a, b], dim=2))
