@@ -3,6 +3,7 @@
 MFU of the 125M tier, bf16, seq 1024, global batch 128, at 1/2/4/8 GPUs).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+    python bench.py --op attention|lce|gelu_gemm   (op configurations, 1 GPU)
 
 One process per GPU (torchrun for N > 1). A "step" is one full training step
 (forward, backward, gradient all-reduce, AdamW) over the rank's share of the
@@ -189,6 +190,108 @@ def run_reference(args, cfg, rank: int, world: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_op(args) -> None:
+    """Op-level configurations of the same kernels (one GPU, rank 0):
+
+    * attention: SURVEY config 3 -- q, k, v, dO [16, 12, 1024, 64] bf16 ~ N(0, 1)
+      (seeds 0..2), RoPE on q and k, scale 1/64; one step = forward + backward;
+      algorithmic FLOPs (causal) 6 B H T^2 D = 7.73e10 per step.
+    * lce: config 2 -- hidden [65536, 768] bf16 ~ N(0, 1), embedding
+      [50304, 768] bf16 ~ N(0, 0.02), Zipf(1.1) labels (seed 1); one step = mean
+      loss + dH + dE; algorithmic FLOPs 6 N V D = 1.519e13 per step.
+    * gelu_gemm: the MLP up projection of the step (M = 131072, K = 768,
+      N = 3072) with the bias + GELU epilogue (writes g and gelu').
+    Each timed iteration is bracketed by CUDA events on the launching stream;
+    a 256 MB buffer is rewritten between iterations (outside the events) so no
+    input is served from the 126 MB L2.
+    """
+
+    from rig_b200 import _lib, ops
+    from rig_b200.tokens import zipf_tokens
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    gen = lambda seed: torch.Generator(device="cpu").manual_seed(seed)  # noqa: E731
+    if args.op == "attention":
+        b, h, t, d = 16, 12, 1024, 64
+        q, k, v = (torch.randn(b, h, t, d, generator=gen(i)).bfloat16().to(dev) for i in range(3))
+        do = torch.randn(b, h, t, d, generator=gen(2)).bfloat16().to(dev)
+        rope = ops.rope_tables(t, d, dev)
+        ops.rope_apply(q.transpose(1, 2), rope)
+        ops.rope_apply(k.transpose(1, 2), rope)
+        o, lse = torch.empty_like(q), torch.empty(b, h, t, device=dev)
+        dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+        ws = ops.attention_workspace(b, h, t, dev)
+        fwd = lambda: ops.attention_fwd(q, k, v, o, lse, scale=1 / 64)  # noqa: E731
+        bwd = lambda: ops.attention_bwd(q, k, v, o, do, lse, dq, dk, dv, scale=1 / 64,  # noqa
+                                        rope=rope, workspace=ws)
+        # causal algorithmic FLOPs: forward 2 B H T^2 D, backward 4 B H T^2 D
+        parts = {"fwd": (fwd, 2.0 * b * h * t * t * d), "bwd": (bwd, 4.0 * b * h * t * t * d)}
+        config = {"workload": "config 3: causal attention fwd+bwd", "batch": b, "heads": h,
+                  "seq_len": t, "head_dim": d, "rope": True, "scale": "1/64"}
+    elif args.op == "lce":
+        n, vocab, d = 65536, 50304, 768
+        hid = torch.randn(n, d, generator=gen(0)).bfloat16().to(dev)
+        emb = (0.02 * torch.randn(vocab, d, generator=gen(1))).bfloat16().to(dev)
+        tgt = torch.from_numpy(zipf_tokens(n, vocab, 1).astype("int32")).to(dev)
+        losses, lse = torch.empty(n, device=dev), torch.empty(n, device=dev)
+        mean = torch.empty(1, device=dev)
+        cot = torch.full((n,), 1.0 / n, device=dev)
+        dh = torch.empty_like(hid)
+        de = torch.zeros(vocab, d, device=dev)
+        fws, bws = ops.lce_fwd_workspace(n, vocab, dev), ops.lce_bwd_workspace(n, vocab, dev)
+        fwd = lambda: ops.lce_fwd(hid, emb, tgt, vocab, losses, lse, mean, workspace=fws)  # noqa
+        bwd = lambda: ops.lce_bwd(hid, emb, tgt, lse, cot, vocab, dh, de, workspace=bws)  # noqa
+        parts = {"fwd": (fwd, 2.0 * n * vocab * d), "bwd": (bwd, 4.0 * n * vocab * d)}
+        config = {"workload": "config 2: tied linear cross-entropy loss + dH + dE", "tokens": n,
+                  "vocab": vocab, "d_model": d}
+    elif args.op == "gelu_gemm":
+        m, kk, nn = 131072, 768, 3072
+        x = torch.randn(m, kk, generator=gen(0)).bfloat16().to(dev)
+        w = (0.02 * torch.randn(kk, nn, generator=gen(1))).bfloat16().to(dev)
+        bias = torch.zeros(nn, dtype=torch.bfloat16, device=dev)
+        g, gp = (torch.empty(m, nn, dtype=torch.bfloat16, device=dev) for _ in range(2))
+        run = lambda: ops.matmul(x, w, bias=bias, out=g, kind=_lib.EPI_BIAS_GELU, aux=gp)  # noqa
+        parts = {"gemm": (run, 2.0 * m * nn * kk)}
+        config = {"workload": "MLP up projection + bias + GELU (writes g and gelu')", "M": m,
+                  "K": kk, "N": nn}
+    else:
+        raise SystemExit(f"unknown --op {args.op}")
+
+    for _ in range(args.warmup):
+        for fn, _fl in parts.values():
+            fn()
+    torch.cuda.synchronize()
+    times = {name: 0.0 for name in parts}
+    for _ in range(args.steps):
+        for name, (fn, _fl) in parts.items():
+            flush.fill_(1)
+            st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            st.record()
+            fn()
+            en.record()
+            torch.cuda.synchronize()
+            times[name] += st.elapsed_time(en)
+    if ops.device_error() != 0:
+        raise RuntimeError("device-side error flag set during the benchmark")
+    ms = sum(times.values()) / args.steps
+    flops = sum(fl for _fn, fl in parts.values())
+    peaks = measured_peaks()
+    tflops = flops / (ms / 1e3) / 1e12
+    print(json.dumps({
+        "metric": f"{args.op} TFLOP/s (algorithmic)", "value": tflops, "unit": "TFLOP/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "none", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded, shapes and distributions of the op configuration)",
+        "config": {**config, "l2": "256 MB buffer rewritten between timed iterations"},
+        "parts_ms": {k: v / args.steps for k, v in times.items()},
+        "roofline": {"bound": "tensor", "achieved": tflops, "peak": peaks["bf16"],
+                     "unit": "TFLOP/s", "frac": tflops / peaks["bf16"],
+                     "peak_source": f"{peaks['source']} bf16 burst (kernel timed alone)"},
+    }), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -199,7 +302,12 @@ def main() -> None:
     ap.add_argument("--seed", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--eager", action="store_true", help="no CUDA graph replay")
+    ap.add_argument("--op", choices=["step", "attention", "lce", "gelu_gemm"], default="step",
+                    help="op-level configuration instead of the training step (1 GPU)")
     args = ap.parse_args()
+    if args.op != "step":
+        run_op(args)
+        return
 
     from rig_b200.config import load_config
     from rig_b200.mesh import initialize_distributed_runtime
