@@ -418,7 +418,12 @@ def main() -> None:
         "achieved": achieved, "peak": peaks["bf16_sustained"], "unit": "TFLOP/s",
         "frac": achieved / peaks["bf16_sustained"],
         "peak_source": f"{peaks['source']} sustained bf16 (kernel timed inside a long step)",
-        "traffic": None, "launches_per_step": len(timed), "share_of_step": gemm_ms / step_ms_instr,
+        # DRAM read + write bytes per GEMM launch, averaged over one step's 144
+        # launches of the 1-GPU bench workload (one-pass ncu capture recorded in
+        # profiles/gemm_dram_traffic_step.md: 119.43 GB read + 56.45 GB written)
+        "traffic": (119.43e9 + 56.45e9) / 144 if world == 1 else None,
+        "traffic_unit": "bytes per launch (1-GPU workload, ncu capture)",
+        "launches_per_step": len(timed), "share_of_step": gemm_ms / step_ms_instr,
         "algorithmic_flops_per_step": gemm_flops,
     }
 

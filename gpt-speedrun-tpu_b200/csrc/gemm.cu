@@ -63,13 +63,23 @@ struct TileCoord {
   int tm, tn, ks;
 };
 
+// Work unit u -> (M tile, N tile, K split). Within a split the tiles are
+// rastered in groups of group_m M tiles: consecutive units walk down the
+// group's M tiles, then to the next N tile. The CTAs in flight at any moment
+// then share a few A stripes and a few B panels, which stay in L2, instead of
+// all sweeping the full width of B (re-fetched from DRAM for every M tile).
 __device__ __forceinline__ TileCoord decode_unit(const GemmParams& p, int u) {
   TileCoord c;
-  int per_split = p.tiles_m * p.tiles_n;
+  const int per_split = p.tiles_m * p.tiles_n;
   c.ks = u / per_split;
-  int r = u - c.ks * per_split;
-  c.tm = r / p.tiles_n;
-  c.tn = r - c.tm * p.tiles_n;
+  const int r = u - c.ks * per_split;
+  const int per_group = p.group_m * p.tiles_n;
+  const int g = r / per_group;
+  const int first_m = g * p.group_m;
+  const int gm = min(p.group_m, p.tiles_m - first_m);
+  const int w = r - g * per_group;
+  c.tm = first_m + w % gm;
+  c.tn = w / gm;
   return c;
 }
 
@@ -677,6 +687,13 @@ int gemm_launch(const void* a, int a_mn, int64_t lda, const void* b, int b_mn, i
     const int tiles = p.tiles_m * p.tiles_n;
     const int target = 3 * sm_count();
     while (tiles * splits < target && p.num_kb / (splits * 2) >= 32) splits *= 2;
+  }
+  // Raster groups: enough M tiles that a wave of CTAs spans few N tiles, with
+  // the group's A stripe (group_m x BM rows of K) at most ~16 MB of L2.
+  {
+    const int64_t stripe = (int64_t)BM * K * 2;
+    int g = (int)std::max<int64_t>(1, std::min<int64_t>(32, (16ll << 20) / stripe));
+    p.group_m = std::min(g, p.tiles_m);
   }
   p.kb_per_split = (p.num_kb + splits - 1) / splits;
   p.splits = (p.num_kb + p.kb_per_split - 1) / p.kb_per_split;

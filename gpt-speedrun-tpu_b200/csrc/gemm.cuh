@@ -22,6 +22,7 @@ struct GemmParams {
   // filled by gemm_launch
   int M, N, K;
   int tiles_m, tiles_n, num_kb, kb_per_split, splits, num_units;
+  int group_m;  // M tiles per raster group (consecutive units sweep a group's N tiles)
   // output + generic epilogue operands
   void* C;
   int64_t ldc;
