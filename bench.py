@@ -419,8 +419,8 @@ def main() -> None:
         "frac": achieved / peaks["bf16_sustained"],
         "peak_source": f"{peaks['source']} sustained bf16 (kernel timed inside a long step)",
         # DRAM read + write bytes per GEMM launch, averaged over one step's 144
-        # launches of the 1-GPU bench workload (one-pass ncu capture recorded in
-        # profiles/gemm_dram_traffic_step.md: 119.43 GB read + 56.45 GB written)
+        # launches of the 1-GPU bench workload (one-pass ncu capture of
+        # dram__bytes_read.sum / dram__bytes_write.sum: 119.43 GB + 56.45 GB)
         "traffic": (119.43e9 + 56.45e9) / 144 if world == 1 else None,
         "traffic_unit": "bytes per launch (1-GPU workload, ncu capture)",
         "launches_per_step": len(timed), "share_of_step": gemm_ms / step_ms_instr,
