@@ -339,6 +339,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   int* err = &g_gemm_error;
+  // device-side M or K range (see GemmParams::range)
+  int m_off = 0, tiles_m_eff = p.tiles_m, k_off = 0, kb_eff = p.num_kb;
+  if (p.range) {
+    const int2 rg = *p.range;
+    if (p.range_dim == 1) {
+      m_off = rg.x;
+      tiles_m_eff = min(p.tiles_m, rg.y / BM);
+    } else {
+      k_off = rg.x;
+      kb_eff = min(p.num_kb, rg.y / BK);
+    }
+  }
+  auto unit_kb = [&](const TileCoord& tc, int& kb0, int& kb1) {
+    kb0 = tc.ks * p.kb_per_split;
+    kb1 = min(kb_eff, kb0 + p.kb_per_split);
+    return tc.tm < tiles_m_eff && kb0 < kb1;  // false: nothing to do in this unit
+  };
 
   if (warp == 0) {
     if (lane == 0) {
@@ -347,15 +364,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       for (int u = blockIdx.x; u < p.num_units; u += gridDim.x) {
         TileCoord tc = decode_unit(p, u);
-        const int m0 = tc.tm * BM, n0 = tc.tn * BN;
-        const int kb0 = tc.ks * p.kb_per_split;
-        const int kb1 = min(p.num_kb, kb0 + p.kb_per_split);
+        int kb0, kb1;
+        if (!unit_kb(tc, kb0, kb1)) continue;
+        const int m0 = m_off + tc.tm * BM, n0 = tc.tn * BN;
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, err)) goto producer_done;
           uint8_t* sa = smem + stage * L::STAGE_BYTES;
           uint8_t* sb = sa + L::A_BYTES;
           mbar_arrive_expect_tx(&full[stage], L::STAGE_BYTES);
-          const int k0 = kb * BK;
+          const int k0 = k_off + kb * BK;
           if constexpr (!A_MN) {
             tma_load_2d(sa, &tmA, &full[stage], k0, m0);
           } else {
@@ -388,8 +405,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t acc_phase = 0;
       for (int u = blockIdx.x; u < p.num_units; u += gridDim.x) {
         TileCoord tc = decode_unit(p, u);
-        const int kb0 = tc.ks * p.kb_per_split;
-        const int kb1 = min(p.num_kb, kb0 + p.kb_per_split);
+        int kb0, kb1;
+        if (!unit_kb(tc, kb0, kb1)) continue;
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, err)) break;
         tc_fence_after();
         const uint32_t dtmem = tmem_base + acc * BN;
@@ -442,7 +459,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t acc_phase = 0;
     for (int u = blockIdx.x; u < p.num_units; u += gridDim.x) {
       TileCoord tc = decode_unit(p, u);
-      const int row = tc.tm * BM + r_in_tile;
+      int kb0, kb1;
+      if (!unit_kb(tc, kb0, kb1)) continue;
+      const int row = m_off + tc.tm * BM + r_in_tile;
       const int n0 = tc.tn * BN + part * COLS;
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, err)) break;
       tc_fence_after();
@@ -503,7 +522,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
-              tma_store_2d(o ? &maps.aux : &maps.c, stage, n0 + c * 32, tc.tm * BM + quad * 32);
+              tma_store_2d(o ? &maps.aux : &maps.c, stage, n0 + c * 32, m_off + tc.tm * BM + quad * 32);
               bulk_commit();
             }
           }
@@ -777,6 +796,12 @@ extern "C" int gptb200_gemm(const void* a, int a_mn_major, int64_t lda, const vo
     default: return GPTB200_EUNSUPPORTED;
   }
   if (e->residual && (e->ld_residual < n || (e->ld_residual % 8))) return GPTB200_EINVAL;
+  if (e->range_dim < 0 || e->range_dim > 2 || (e->range_dim != 0) != (e->row_range != nullptr))
+    return GPTB200_EINVAL;
+  if (e->range_dim == 2 && !(a_mn_major && b_mn_major)) return GPTB200_EUNSUPPORTED;
+  if (e->range_dim == 1 && a_mn_major) return GPTB200_EUNSUPPORTED;
+  p.range = reinterpret_cast<const int2*>(e->row_range);
+  p.range_dim = e->range_dim;
   // bias / residual / derivative rows are read in 16-byte groups of 8 columns
   if ((e->bias || e->residual || kind == EPI_BIAS_GELU_ || kind == EPI_DGELU_) && (n % 8))
     return GPTB200_ESHAPE;

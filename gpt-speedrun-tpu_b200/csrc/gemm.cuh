@@ -23,6 +23,13 @@ struct GemmParams {
   int M, N, K;
   int tiles_m, tiles_n, num_kb, kb_per_split, splits, num_units;
   int group_m;  // M tiles per raster group (consecutive units sweep a group's N tiles)
+  // Optional device-side row range {offset, count} (count a multiple of 128)
+  // read at kernel start: range_dim 1 restricts the M rows (A and C rows
+  // offset, tiles past the count do nothing), 2 the K rows of MN-major
+  // operands. Lets a segment of a buffer whose bounds live on the device (an
+  // expert's tokens) be multiplied without a host round trip.
+  const int2* range;
+  int range_dim;
   // output + generic epilogue operands
   void* C;
   int64_t ldc;

@@ -1,0 +1,619 @@
+// Top-k routed MLP (recipes/reference_moe/train.py:1230-1345, routed_mlp_local)
+// around the tcgen05 GEMM: routing, dropless dispatch into expert segments,
+// gather / combine and their backward, router backward, per-expert bias
+// gradients and the balance-loss statistics.
+//
+// Layout of one layer's routed buffers (N tokens, k = top-k, E experts):
+//   assignment a = i * k + j (token i, choice j); the assignments are stably
+//   sorted by expert into one row buffer where expert e owns the segment
+//   [seg[e].x, seg[e].x + seg[e].y), seg[e].y = its count rounded up to 128
+//   (padding rows hold zeros on the way in and are ignored on the way out), so
+//   every 128-row GEMM tile belongs to one expert and the expert GEMMs take
+//   their bounds from `seg` on the device (GemmParams::range).
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace gptb200 {
+
+constexpr int kMoeMaxE = 16;
+constexpr int kMoeMaxK = 4;
+constexpr int kDispatchBlock = 1024;  // assignments per dispatch block
+
+// Per layer statistics, fp32: [0, E) router probability sums, [E, 2E) counts,
+// 2E entropy sum, 2E+1 top-1 gate sum, 2E+2 sum of squared logits.
+__host__ __device__ constexpr int moe_stat_width(int E) { return 2 * E + 3; }
+
+// ------------------------------------------------------------------ routing
+// One warp per token: logits = x(fp32) . W_router (fp32) -- the reference
+// promotes the bf16 activations to fp32 -- softmax probabilities, the top-k
+// logits (ties: lower expert first, like lax.top_k) and the gates (softmax of
+// the chosen logits). Block-level partial statistics, one atomic each.
+__global__ void __launch_bounds__(256) moe_route_kernel(
+    const bf16* __restrict__ x, const float* __restrict__ w, int64_t n, int d, int E, int k,
+    float* __restrict__ logits, int* __restrict__ chosen, float* __restrict__ gate,
+    float* __restrict__ stats) {
+  extern __shared__ float wsm[];  // [d][E] router weights, then [E + E + 3] block stats
+  float* bst = wsm + (size_t)d * E;
+  for (int i = threadIdx.x; i < d * E; i += blockDim.x) wsm[i] = w[i];
+  for (int i = threadIdx.x; i < moe_stat_width(E); i += blockDim.x) bst[i] = 0.f;
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < n;
+       t += warps) {
+    float acc[kMoeMaxE];
+#pragma unroll
+    for (int e = 0; e < kMoeMaxE; ++e) acc[e] = 0.f;
+    const bf16* row = x + t * d;
+    for (int c = lane; c < d / 8; c += 32) {
+      const uint4 q = *reinterpret_cast<const uint4*>(row + c * 8);
+      const uint32_t* qw = &q.x;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float a0, a1;
+        unpack_bf16x2(qw[j], a0, a1);
+        const float* w0 = wsm + (size_t)(c * 8 + 2 * j) * E;
+#pragma unroll
+        for (int e = 0; e < kMoeMaxE; ++e)
+          if (e < E) acc[e] = fmaf(a0, w0[e], fmaf(a1, w0[E + e], acc[e]));
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < kMoeMaxE; ++e)
+      if (e < E) acc[e] = warp_sum(acc[e]);
+    if (lane == 0) {
+      float mx = -INFINITY;
+      for (int e = 0; e < E; ++e) {
+        logits[t * E + e] = acc[e];
+        mx = fmaxf(mx, acc[e]);
+      }
+      float p[kMoeMaxE], z = 0.f, sq = 0.f;
+      for (int e = 0; e < E; ++e) {
+        p[e] = expf(acc[e] - mx);
+        z += p[e];
+        sq += acc[e] * acc[e];
+      }
+      float ent = 0.f;
+      for (int e = 0; e < E; ++e) {
+        p[e] /= z;
+        ent -= p[e] * logf(p[e] + 1.0e-9f);
+        atomicAdd(&bst[e], p[e]);
+      }
+      // top-k by repeated arg-max; the first maximum wins ties
+      int sel[kMoeMaxK];
+      float lv[kMoeMaxK];
+      unsigned used = 0u;
+      for (int j = 0; j < k; ++j) {
+        int best = -1;
+        float bv = -INFINITY;
+        for (int e = 0; e < E; ++e)
+          if (!(used >> e & 1u) && (best < 0 || acc[e] > bv)) {
+            best = e;
+            bv = acc[e];
+          }
+        used |= 1u << best;
+        sel[j] = best;
+        lv[j] = bv;
+      }
+      float gz = 0.f, g[kMoeMaxK];
+      for (int j = 0; j < k; ++j) {
+        g[j] = expf(lv[j] - lv[0]);
+        gz += g[j];
+      }
+      float top1 = 0.f;
+      for (int j = 0; j < k; ++j) {
+        g[j] /= gz;
+        top1 = fmaxf(top1, g[j]);
+        chosen[t * k + j] = sel[j];
+        gate[t * k + j] = g[j];
+        atomicAdd(&bst[E + sel[j]], 1.f);
+      }
+      atomicAdd(&bst[2 * E], ent);
+      atomicAdd(&bst[2 * E + 1], top1);
+      atomicAdd(&bst[2 * E + 2], sq);
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < moe_stat_width(E); i += blockDim.x) atomicAdd(&stats[i], bst[i]);
+}
+
+// ------------------------------------------------------------------ dispatch
+// Stable counting sort of the assignments by expert. Pass 1: per-block
+// counts. Pass 2 (one block): segment offsets (counts rounded up to 128) and
+// each block's starting rank per expert. Pass 3: per-warp ballots give each
+// assignment its rank among equal experts in flat order.
+__global__ void __launch_bounds__(256) moe_count_kernel(const int* __restrict__ chosen,
+                                                        int64_t na, int E,
+                                                        int* __restrict__ block_counts) {
+  __shared__ int c[kMoeMaxE];
+  if (threadIdx.x < E) c[threadIdx.x] = 0;
+  __syncthreads();
+  const int64_t a0 = (int64_t)blockIdx.x * kDispatchBlock;
+  for (int64_t a = a0 + threadIdx.x; a < min(na, a0 + kDispatchBlock); a += blockDim.x)
+    atomicAdd(&c[chosen[a]], 1);
+  __syncthreads();
+  if (threadIdx.x < E) block_counts[(int64_t)blockIdx.x * E + threadIdx.x] = c[threadIdx.x];
+}
+
+__global__ void moe_offsets_kernel(int* __restrict__ block_counts, int nblocks, int E,
+                                   int2* __restrict__ seg, int* __restrict__ total) {
+  // thread e scans expert e's column of block counts (in place: exclusive)
+  __shared__ int cnt[kMoeMaxE];
+  const int e = threadIdx.x;
+  if (e < E) {
+    int run = 0;
+    for (int b = 0; b < nblocks; ++b) {
+      const int v = block_counts[(int64_t)b * E + e];
+      block_counts[(int64_t)b * E + e] = run;
+      run += v;
+    }
+    cnt[e] = run;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int off = 0;
+    for (int x = 0; x < E; ++x) {
+      const int padded = (cnt[x] + 127) / 128 * 128;
+      seg[x] = make_int2(off, padded);
+      off += padded;
+    }
+    *total = off;
+  }
+}
+
+__global__ void __launch_bounds__(kDispatchBlock) moe_place_kernel(
+    const int* __restrict__ chosen, int64_t na, int E, int k,
+    const int* __restrict__ block_base, const int2* __restrict__ seg, int* __restrict__ pos,
+    int* __restrict__ src) {
+  __shared__ int wc[kDispatchBlock / 32][kMoeMaxE];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t a = (int64_t)blockIdx.x * kDispatchBlock + threadIdx.x;
+  const int ex = a < na ? chosen[a] : -1;
+  int rank = 0;
+  for (int e = 0; e < E; ++e) {
+    const unsigned m = __ballot_sync(0xffffffffu, ex == e);
+    if (ex == e) rank = __popc(m & ((1u << lane) - 1u));
+    if (lane == 0) wc[warp][e] = __popc(m);
+  }
+  __syncthreads();
+  if (threadIdx.x < E) {  // exclusive scan over the block's warps, expert = thread
+    int run = 0;
+    for (int w = 0; w < kDispatchBlock / 32; ++w) {
+      const int v = wc[w][threadIdx.x];
+      wc[w][threadIdx.x] = run;
+      run += v;
+    }
+  }
+  __syncthreads();
+  if (ex >= 0) {
+    const int p = seg[ex].x + block_base[(int64_t)blockIdx.x * E + ex] + wc[warp][ex] + rank;
+    pos[a] = p;
+    src[p] = (int)(a / k);
+  }
+}
+
+// grouped[r] = x[src[r]] (zeros on padding rows), rows < total.
+__global__ void moe_gather_kernel(const bf16* __restrict__ x, const int* __restrict__ src,
+                                  const int* __restrict__ total, int d, bf16* __restrict__ out) {
+  const int64_t rows = *total;
+  const int nch = d / 8;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < rows * nch;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / nch;
+    const int c = (int)(i - r * nch);
+    const int s = src[r];
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (s >= 0) v = *reinterpret_cast<const uint4*>(x + (int64_t)s * d + c * 8);
+    *reinterpret_cast<uint4*>(out + r * d + c * 8) = v;
+  }
+}
+
+// ------------------------------------------------------------------ combine
+// x_out[i] = resid[i] + alpha * sum_j bf16(out[pos(i,j)] * bf16(gate(i,j))),
+// each product and sum rounded to bf16 as the reference's bf16 scatter-add.
+__global__ void moe_combine_kernel(const bf16* __restrict__ out, const int* __restrict__ pos,
+                                   const float* __restrict__ gate, const bf16* __restrict__ resid,
+                                   float alpha, int64_t n, int d, int k,
+                                   bf16* __restrict__ x_out) {
+  const int nch = d / 8;
+  const uint32_t al = pack_bf16x2(alpha, alpha);
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n * nch;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = i / nch;
+    const int c = (int)(i - t * nch);
+    uint32_t acc[4] = {0u, 0u, 0u, 0u};
+    for (int j = 0; j < k; ++j) {
+      const float g = gate[t * k + j];
+      const uint32_t gb = pack_bf16x2(g, g);
+      const uint4 o = *reinterpret_cast<const uint4*>(out + (int64_t)pos[t * k + j] * d + c * 8);
+      const uint32_t* ow = &o.x;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint32_t w = hmul2_bf16(ow[q], gb);
+        acc[q] = j == 0 ? w : hadd2_bf16(acc[q], w);
+      }
+    }
+    const uint4 rq = *reinterpret_cast<const uint4*>(resid + t * d + c * 8);
+    const uint32_t* rw = &rq.x;
+    uint4 res;
+    uint32_t* ow = &res.x;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) ow[q] = hadd2_bf16(rw[q], hmul2_bf16(acc[q], al));
+    *reinterpret_cast<uint4*>(x_out + t * d + c * 8) = res;
+  }
+}
+
+// Backward of the combine: d_mlp = bf16(alpha * dx); d_out[pos(i,j)] =
+// bf16(d_mlp * bf16(gate)); d_gate(i,j) = bf16-rounded sum_d d_mlp * out.
+// One warp per token. Padding rows of d_out are zeroed by moe_zero_pad_kernel.
+__global__ void moe_combine_bwd_kernel(const bf16* __restrict__ dx, float alpha,
+                                       const bf16* __restrict__ out, const int* __restrict__ pos,
+                                       const float* __restrict__ gate, int64_t n, int d, int k,
+                                       bf16* __restrict__ d_out, float* __restrict__ d_gate) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const uint32_t al = pack_bf16x2(alpha, alpha);
+  for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < n;
+       t += warps) {
+    float dg[kMoeMaxK];
+    for (int j = 0; j < k; ++j) dg[j] = 0.f;
+    for (int c = lane; c < d / 8; c += 32) {
+      const uint4 q = *reinterpret_cast<const uint4*>(dx + t * d + c * 8);
+      const uint32_t* qw = &q.x;
+      uint32_t dm[4];
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) dm[q4] = hmul2_bf16(qw[q4], al);
+      for (int j = 0; j < k; ++j) {
+        const int64_t r = pos[t * k + j];
+        const float g = gate[t * k + j];
+        const uint32_t gb = pack_bf16x2(g, g);
+        const uint4 o = *reinterpret_cast<const uint4*>(out + r * d + c * 8);
+        const uint32_t* ow = &o.x;
+        uint4 w;
+        uint32_t* ww = &w.x;
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          ww[q4] = hmul2_bf16(dm[q4], gb);
+          float a0, a1, b0, b1;
+          unpack_bf16x2(dm[q4], a0, a1);
+          unpack_bf16x2(ow[q4], b0, b1);
+          dg[j] = fmaf(a0, b0, fmaf(a1, b1, dg[j]));
+        }
+        *reinterpret_cast<uint4*>(d_out + r * d + c * 8) = w;
+      }
+    }
+    for (int j = 0; j < k; ++j) {
+      const float s = warp_sum(dg[j]);
+      if (lane == 0) d_gate[t * k + j] = bf16r(s);
+    }
+  }
+}
+
+__global__ void moe_zero_pad_kernel(const int* __restrict__ src, const int* __restrict__ total,
+                                    int d, bf16* __restrict__ buf) {
+  const int64_t rows = *total;
+  const int nch = d / 8;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < rows * nch;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / nch;
+    if (src[r] < 0)
+      *reinterpret_cast<uint4*>(buf + r * d + (i - r * nch) * 8) = make_uint4(0u, 0u, 0u, 0u);
+  }
+}
+
+// ------------------------------------------------------------------ router backward
+// d_logits from the gates (softmax of the chosen logits) and from the balance
+// loss through the router probabilities (d prob_e = bal[e], the same for every
+// token); then d_x = bf16(bf16(sum_j d_grouped[pos(i,j)]) + bf16(d_logits . W^T))
+// and d_W += x^T d_logits (block partials in shared memory, one atomic each).
+__global__ void __launch_bounds__(256) moe_route_bwd_kernel(
+    const bf16* __restrict__ x, const float* __restrict__ w, const float* __restrict__ logits,
+    const int* __restrict__ chosen, const float* __restrict__ gate,
+    const float* __restrict__ d_gate, const float* __restrict__ bal,
+    const bf16* __restrict__ d_grouped, const int* __restrict__ pos, int64_t n, int d, int E,
+    int k, float* __restrict__ d_w, bf16* __restrict__ d_x) {
+  extern __shared__ float sm[];  // [d][E] weights, then [d][E] partial d_W
+  float* dws = sm + (size_t)d * E;
+  for (int i = threadIdx.x; i < d * E; i += blockDim.x) {
+    sm[i] = w[i];
+    dws[i] = 0.f;
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < n;
+       t += warps) {
+    // every lane recomputes the token's E-wide gradient (E <= 16 values)
+    float lg[kMoeMaxE], pr[kMoeMaxE], dl[kMoeMaxE];
+    float mx = -INFINITY;
+    for (int e = 0; e < E; ++e) {
+      lg[e] = logits[t * E + e];
+      mx = fmaxf(mx, lg[e]);
+    }
+    float z = 0.f;
+    for (int e = 0; e < E; ++e) {
+      pr[e] = expf(lg[e] - mx);
+      z += pr[e];
+    }
+    float dot = 0.f;
+    for (int e = 0; e < E; ++e) {
+      pr[e] /= z;
+      dot += pr[e] * bal[e];
+    }
+    for (int e = 0; e < E; ++e) dl[e] = pr[e] * (bal[e] - dot);
+    float gd = 0.f;
+    for (int j = 0; j < k; ++j) gd += gate[t * k + j] * d_gate[t * k + j];
+    for (int j = 0; j < k; ++j) {
+      const int e = chosen[t * k + j];
+      const float gj = gate[t * k + j];
+      for (int x2 = 0; x2 < E; ++x2)
+        if (x2 == e) dl[x2] += gj * (d_gate[t * k + j] - gd);
+    }
+    for (int c = lane; c < d / 8; c += 32) {
+      const uint4 q = *reinterpret_cast<const uint4*>(x + t * d + c * 8);
+      const uint32_t* qw = &q.x;
+      uint32_t sumg[4];
+      for (int j = 0; j < k; ++j) {
+        const uint4 g4 = *reinterpret_cast<const uint4*>(d_grouped + (int64_t)pos[t * k + j] * d +
+                                                         c * 8);
+        const uint32_t* gw = &g4.x;
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) sumg[q4] = j == 0 ? gw[q4] : hadd2_bf16(sumg[q4], gw[q4]);
+      }
+      uint4 o;
+      uint32_t* ow = &o.x;
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {
+        float a0, a1;
+        unpack_bf16x2(qw[q4], a0, a1);
+        const int r0 = c * 8 + 2 * q4;
+        float* d0 = dws + (size_t)r0 * E;
+        float v0 = 0.f, v1 = 0.f;
+        for (int e = 0; e < E; ++e) {
+          v0 = fmaf(dl[e], sm[(size_t)r0 * E + e], v0);
+          v1 = fmaf(dl[e], sm[(size_t)(r0 + 1) * E + e], v1);
+          atomicAdd(&d0[e], a0 * dl[e]);
+          atomicAdd(&d0[E + e], a1 * dl[e]);
+        }
+        ow[q4] = hadd2_bf16(sumg[q4], pack_bf16x2(v0, v1));
+      }
+      *reinterpret_cast<uint4*>(d_x + t * d + c * 8) = o;
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < d * E; i += blockDim.x) atomicAdd(&d_w[i], dws[i]);
+}
+
+// out[e][c] += sum of buf rows [seg[e].x, seg[e].x + seg[e].y), column c.
+__global__ void moe_seg_colsum_kernel(const bf16* __restrict__ buf, const int2* __restrict__ seg,
+                                      int w, float* __restrict__ out) {
+  const int e = blockIdx.y;
+  const int col = blockIdx.x * blockDim.x + threadIdx.x;
+  if (col >= w) return;
+  const int2 sg = seg[e];
+  const int chunk = (sg.y + gridDim.z - 1) / gridDim.z;
+  const int r0 = sg.x + blockIdx.z * chunk, r1 = min(sg.x + sg.y, r0 + chunk);
+  float s = 0.f;
+  for (int r = r0; r < r1; ++r) s += __bfloat162float(buf[(int64_t)r * w + col]);
+  if (r1 > r0) atomicAdd(&out[(int64_t)e * w + col], s);
+}
+
+// ------------------------------------------------------------------ statistics
+// After the per-rank statistics have been summed over ranks: per layer load
+// = count / (tokens * k), mean probability = prob sum / tokens, balance =
+// E * sum(load * mean prob) (recipes/reference_moe/train.py:1347-1372), the
+// backward coefficient of each router probability, the router history row
+// (train.py:1881-1915) and loss += coef * mean balance.
+__global__ void moe_finalize_kernel(const float* __restrict__ stats, int layers, int E,
+                                    float tokens, int k, float coef, float bwd_scale,
+                                    float* __restrict__ bal_grad, float* __restrict__ loss,
+                                    float* __restrict__ history, int history_rows,
+                                    const int* __restrict__ step) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  // this step's row: the optimizer's step counter before its increment
+  const int s = *step;
+  float scratch[6 + 64 * (3 + kMoeMaxE)];
+  const int width = 6 + layers * (3 + E);
+  float* row = (s >= 0 && s < history_rows) ? history + (int64_t)s * width : scratch;
+  if (row == scratch && layers > 64) return;
+  const int W = moe_stat_width(E);
+  float bal_sum = 0.f, lmax = -INFINITY, lmin = INFINITY, sm0 = 0.f, sm1 = 0.f, sm2 = 0.f;
+  for (int l = 0; l < layers; ++l) {
+    const float* s = stats + (size_t)l * W;
+    float b = 0.f;
+    for (int e = 0; e < E; ++e) {
+      const float load = s[E + e] / (tokens * (float)k);
+      const float mp = s[e] / tokens;
+      b += load * mp;
+      lmax = fmaxf(lmax, load);
+      lmin = fminf(lmin, load);
+      bal_grad[l * E + e] = coef / (float)layers * (float)E * load * bwd_scale;
+    }
+    bal_sum += (float)E * b;
+    const float ent = s[2 * E] / tokens, top1 = s[2 * E + 1] / tokens;
+    const float rms = sqrtf(s[2 * E + 2] / (tokens * (float)E));
+    sm0 += ent;
+    sm1 += top1;
+    sm2 += rms;
+    float* pl = row + 6 + l * (3 + E);
+    pl[0] = ent;
+    pl[1] = top1;
+    pl[2] = rms;
+    for (int e = 0; e < E; ++e) pl[3 + e] = s[E + e] / (tokens * (float)k);
+  }
+  const float balance = bal_sum / (float)layers;
+  row[0] = balance;
+  row[1] = lmax;
+  row[2] = lmin;
+  row[3] = sm0 / (float)layers;
+  row[4] = sm1 / (float)layers;
+  row[5] = sm2 / (float)layers;
+  if (coef != 0.f) *loss += coef * balance;
+}
+
+}  // namespace gptb200
+
+using namespace gptb200;
+
+extern "C" size_t gptb200_moe_rows(int64_t tokens, int32_t top_k, int32_t experts) {
+  if (tokens <= 0 || top_k <= 0 || experts <= 0) return 0;
+  return (size_t)((tokens * top_k + (int64_t)experts * 127 + 127) / 128 * 128);
+}
+
+extern "C" size_t gptb200_moe_dispatch_workspace_size(int64_t tokens, int32_t top_k,
+                                                      int32_t experts) {
+  if (tokens <= 0 || top_k <= 0 || experts <= 0) return 0;
+  const int64_t nblocks = (tokens * top_k + kDispatchBlock - 1) / kDispatchBlock;
+  return (size_t)(nblocks * experts * 4 + 256);
+}
+
+extern "C" int gptb200_moe_route(const void* x, const float* router_w, int64_t tokens,
+                                 int64_t d, int32_t experts, int32_t top_k, float* logits,
+                                 int32_t* chosen, float* gate, float* stats, void* stream) {
+  if (!x || !router_w || !logits || !chosen || !gate || !stats || tokens <= 0) return GPTB200_EINVAL;
+  if (experts < 1 || experts > kMoeMaxE || top_k < 1 || top_k > kMoeMaxK || top_k > experts)
+    return GPTB200_EUNSUPPORTED;
+  if (d % 8 || d * experts * 4 + moe_stat_width(experts) * 4 > 200 * 1024) return GPTB200_ESHAPE;
+  auto st = reinterpret_cast<cudaStream_t>(stream);
+  const size_t smem = (size_t)(d * experts + moe_stat_width(experts)) * 4;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(moe_route_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return -static_cast<int>(e);
+  }
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int blocks = (int)std::min<int64_t>((tokens + 7) / 8, (int64_t)sms * 2);
+  moe_route_kernel<<<blocks, 256, smem, st>>>(reinterpret_cast<const bf16*>(x), router_w, tokens,
+                                               (int)d, experts, top_k, logits, chosen, gate,
+                                               stats);
+  GPTB200_CHECK_LAUNCH();
+  return 0;
+}
+
+extern "C" int gptb200_moe_dispatch(const int32_t* chosen, int64_t tokens, int32_t top_k,
+                                    int32_t experts, const void* x, int64_t d, int32_t* seg,
+                                    int32_t* total, int32_t* pos, int32_t* src, void* grouped,
+                                    void* workspace, void* stream) {
+  if (!chosen || !x || !seg || !total || !pos || !src || !grouped || !workspace || tokens <= 0)
+    return GPTB200_EINVAL;
+  if (experts < 1 || experts > kMoeMaxE || top_k < 1 || top_k > kMoeMaxK) return GPTB200_EUNSUPPORTED;
+  if (d % 8) return GPTB200_ESHAPE;
+  auto st = reinterpret_cast<cudaStream_t>(stream);
+  const int64_t na = tokens * top_k;
+  const int nblocks = (int)((na + kDispatchBlock - 1) / kDispatchBlock);
+  int* bc = reinterpret_cast<int*>(workspace);
+  const int64_t rows = (int64_t)gptb200_moe_rows(tokens, top_k, experts);
+  cudaError_t e = cudaMemsetAsync(src, 0xff, (size_t)rows * 4, st);  // -1: padding
+  if (e != cudaSuccess) return -static_cast<int>(e);
+  moe_count_kernel<<<nblocks, 256, 0, st>>>(chosen, na, experts, bc);
+  GPTB200_CHECK_LAUNCH();
+  moe_offsets_kernel<<<1, 32, 0, st>>>(bc, nblocks, experts, reinterpret_cast<int2*>(seg), total);
+  GPTB200_CHECK_LAUNCH();
+  moe_place_kernel<<<nblocks, kDispatchBlock, 0, st>>>(chosen, na, experts, top_k, bc,
+                                                       reinterpret_cast<const int2*>(seg), pos,
+                                                       src);
+  GPTB200_CHECK_LAUNCH();
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  moe_gather_kernel<<<sms * 8, 256, 0, st>>>(reinterpret_cast<const bf16*>(x), src, total, (int)d,
+                                             reinterpret_cast<bf16*>(grouped));
+  GPTB200_CHECK_LAUNCH();
+  return 0;
+}
+
+extern "C" int gptb200_moe_combine(const void* out, const int32_t* pos, const float* gate,
+                                   const void* residual, float alpha, int64_t tokens, int64_t d,
+                                   int32_t top_k, void* x_out, void* stream) {
+  if (!out || !pos || !gate || !residual || !x_out || tokens <= 0) return GPTB200_EINVAL;
+  if (top_k < 1 || top_k > kMoeMaxK) return GPTB200_EUNSUPPORTED;
+  if (d % 8) return GPTB200_ESHAPE;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  moe_combine_kernel<<<sms * 8, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const bf16*>(out), pos, gate, reinterpret_cast<const bf16*>(residual),
+      alpha, tokens, (int)d, top_k, reinterpret_cast<bf16*>(x_out));
+  GPTB200_CHECK_LAUNCH();
+  return 0;
+}
+
+extern "C" int gptb200_moe_combine_bwd(const void* dx, float alpha, const void* out,
+                                       const int32_t* pos, const float* gate,
+                                       const int32_t* src, const int32_t* total, int64_t tokens,
+                                       int64_t d, int32_t top_k, void* d_out, float* d_gate,
+                                       void* stream) {
+  if (!dx || !out || !pos || !gate || !src || !total || !d_out || !d_gate || tokens <= 0)
+    return GPTB200_EINVAL;
+  if (top_k < 1 || top_k > kMoeMaxK) return GPTB200_EUNSUPPORTED;
+  if (d % 8) return GPTB200_ESHAPE;
+  auto st = reinterpret_cast<cudaStream_t>(stream);
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  moe_combine_bwd_kernel<<<sms * 4, 256, 0, st>>>(
+      reinterpret_cast<const bf16*>(dx), alpha, reinterpret_cast<const bf16*>(out), pos, gate,
+      tokens, (int)d, top_k, reinterpret_cast<bf16*>(d_out), d_gate);
+  GPTB200_CHECK_LAUNCH();
+  moe_zero_pad_kernel<<<sms * 4, 256, 0, st>>>(src, total, (int)d, reinterpret_cast<bf16*>(d_out));
+  GPTB200_CHECK_LAUNCH();
+  return 0;
+}
+
+extern "C" int gptb200_moe_route_bwd(const void* x, const float* router_w, const float* logits,
+                                     const int32_t* chosen, const float* gate,
+                                     const float* d_gate, const float* bal_grad,
+                                     const void* d_grouped, const int32_t* pos, int64_t tokens,
+                                     int64_t d, int32_t experts, int32_t top_k, float* d_router_w,
+                                     void* d_x, void* stream) {
+  if (!x || !router_w || !logits || !chosen || !gate || !d_gate || !bal_grad || !d_grouped ||
+      !pos || !d_router_w || !d_x || tokens <= 0)
+    return GPTB200_EINVAL;
+  if (experts < 1 || experts > kMoeMaxE || top_k < 1 || top_k > kMoeMaxK) return GPTB200_EUNSUPPORTED;
+  const size_t smem = (size_t)2 * d * experts * 4;
+  if (d % 8 || smem > 200 * 1024) return GPTB200_ESHAPE;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(moe_route_bwd_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return -static_cast<int>(e);
+  }
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int blocks = (int)std::min<int64_t>((tokens + 7) / 8, (int64_t)sms);
+  moe_route_bwd_kernel<<<blocks, 256, smem, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const bf16*>(x), router_w, logits, chosen, gate, d_gate, bal_grad,
+      reinterpret_cast<const bf16*>(d_grouped), pos, tokens, (int)d, experts, top_k, d_router_w,
+      reinterpret_cast<bf16*>(d_x));
+  GPTB200_CHECK_LAUNCH();
+  return 0;
+}
+
+extern "C" int gptb200_moe_segment_colsum(const void* buf, const int32_t* seg, int32_t experts,
+                                          int64_t width, float* out, void* stream) {
+  if (!buf || !seg || !out || width <= 0) return GPTB200_EINVAL;
+  if (experts < 1 || experts > kMoeMaxE) return GPTB200_EUNSUPPORTED;
+  dim3 grid((unsigned)((width + 255) / 256), (unsigned)experts, 16);
+  moe_seg_colsum_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const bf16*>(buf), reinterpret_cast<const int2*>(seg), (int)width, out);
+  GPTB200_CHECK_LAUNCH();
+  return 0;
+}
+
+extern "C" int gptb200_moe_finalize(const float* stats, int32_t layers, int32_t experts,
+                                    int64_t tokens, int32_t top_k, float coefficient,
+                                    float bwd_scale, float* bal_grad, float* loss,
+                                    float* history, int32_t history_rows, const int32_t* step,
+                                    void* stream) {
+  if (!stats || !bal_grad || !loss || !history || !step || layers <= 0 || tokens <= 0)
+    return GPTB200_EINVAL;
+  if (experts < 1 || experts > kMoeMaxE || layers > 64) return GPTB200_EUNSUPPORTED;
+  moe_finalize_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      stats, layers, experts, (float)tokens, top_k, coefficient, bwd_scale, bal_grad, loss,
+      history, history_rows, step);
+  GPTB200_CHECK_LAUNCH();
+  return 0;
+}

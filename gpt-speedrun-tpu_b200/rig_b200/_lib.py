@@ -35,6 +35,8 @@ class Epilogue(ctypes.Structure):
         ("rope_sin", c_vp),
         ("rope_seq", c_i64),
         ("rope_cols", c_i64),
+        ("row_range", c_vp),
+        ("range_dim", c_int),
     ]
 
 
@@ -118,6 +120,26 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp],
     ),
     "gptb200_colsum": (c_int, [c_vp, c_i64, c_i64, c_f32, c_vp, c_vp]),
+    "gptb200_moe_rows": (c_size, [c_i64, ctypes.c_int32, ctypes.c_int32]),
+    "gptb200_moe_dispatch_workspace_size": (c_size, [c_i64, ctypes.c_int32, ctypes.c_int32]),
+    "gptb200_moe_route": (
+        c_int, [c_vp, c_vp, c_i64, c_i64, ctypes.c_int32, ctypes.c_int32, c_vp, c_vp, c_vp, c_vp,
+                c_vp]),
+    "gptb200_moe_dispatch": (
+        c_int, [c_vp, c_i64, ctypes.c_int32, ctypes.c_int32, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp,
+                c_vp, c_vp, c_vp]),
+    "gptb200_moe_combine": (
+        c_int, [c_vp, c_vp, c_vp, c_vp, c_f32, c_i64, c_i64, ctypes.c_int32, c_vp, c_vp]),
+    "gptb200_moe_combine_bwd": (
+        c_int, [c_vp, c_f32, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, ctypes.c_int32, c_vp,
+                c_vp, c_vp]),
+    "gptb200_moe_route_bwd": (
+        c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64,
+                ctypes.c_int32, ctypes.c_int32, c_vp, c_vp, c_vp]),
+    "gptb200_moe_segment_colsum": (c_int, [c_vp, c_vp, ctypes.c_int32, c_i64, c_vp, c_vp]),
+    "gptb200_moe_finalize": (
+        c_int, [c_vp, ctypes.c_int32, ctypes.c_int32, c_i64, ctypes.c_int32, c_f32, c_f32, c_vp,
+                c_vp, c_vp, ctypes.c_int32, c_vp, c_vp]),
     "gptb200_masked_loss_sum": (c_int, [c_vp, c_vp, c_i64, c_vp, c_vp]),
     "gptb200_adamw_workspace_size": (c_size, [c_i64]),
     "gptb200_adamw_step": (

@@ -57,6 +57,11 @@ class Config:
     mlp_activation: str = "gelu"
     document_masking: bool = False        # the context preset's document-attention policy
     document_boundary_token: int = 50256  # recipes/reference/train.py:234-235
+    # routed MLP (recipes/reference_moe/train.py:242-245); experts = 0: dense MLP
+    experts: int = 0
+    expert_top_k: int = 2
+    expert_mult: int = 2
+    router_aux_coefficient: float = 0.01
 
     @property
     def width_multiplier(self) -> float:
@@ -182,6 +187,10 @@ def resolve_config(
         sampling=str(training.get("sampling", "shuffled_epochs")),
         tier=tier_name,
         document_masking=bool(ctx.get("document_masking", False)),
+        experts=int(model.get("experts", 0)),
+        expert_top_k=int(model.get("expert_top_k", 2)),
+        expert_mult=int(model.get("expert_mult", 2)),
+        router_aux_coefficient=float(model.get("router_aux_coefficient", 0.01)),
     )
 
 

@@ -49,11 +49,21 @@ BLOCK_FIELDS = (
     "ln1_scale", "qkv_w", "qkv_b", "attn_w", "attn_b",
     "ln2_scale", "mlp_up_w", "mlp_up_b", "mlp_down_w", "mlp_down_b",
 )
+# A routed block (recipes/reference_moe/train.py:905-931), in its init order.
+MOE_BLOCK_FIELDS = (
+    "ln1_scale", "qkv_w", "qkv_b", "attn_w", "attn_b", "ln2_scale",
+    "router_w", "expert_up_w", "expert_up_b", "expert_down_w", "expert_down_b",
+)
 ALIGN = 64
+
+
+def block_fields(config: Config) -> tuple[str, ...]:
+    return MOE_BLOCK_FIELDS if config.experts else BLOCK_FIELDS
 
 
 def block_shapes(config: Config) -> dict[str, tuple[int, ...]]:
     d, h = config.d_model, config.hidden
+    E, eh = config.experts, config.expert_mult * config.d_model
     return {
         "ln1_scale": (d,),
         "qkv_w": (d, 3 * d),
@@ -65,6 +75,11 @@ def block_shapes(config: Config) -> dict[str, tuple[int, ...]]:
         "mlp_up_b": (h,),
         "mlp_down_w": (h, d),
         "mlp_down_b": (d,),
+        "router_w": (d, E),
+        "expert_up_w": (E, d, eh),
+        "expert_up_b": (E, eh),
+        "expert_down_w": (E, eh, d),
+        "expert_down_b": (E, d),
     }
 
 
@@ -99,7 +114,7 @@ class ParamLayout:
         self.block_ranges: list[tuple[int, int]] = []
         for b in range(config.layers):
             start = off
-            for leaf in BLOCK_FIELDS:
+            for leaf in block_fields(config):
                 add(f"blocks/{b}/{leaf}", leaf, b, shapes[leaf])
             self.block_ranges.append((start, off))
         tail = off
@@ -138,7 +153,7 @@ def init_params(config: Config, seed: int) -> dict[str, np.ndarray]:
     shapes = block_shapes(config)
     out: dict[str, np.ndarray] = {}
     for b in range(config.layers):
-        for leaf in BLOCK_FIELDS:
+        for leaf in block_fields(config):
             shape = shapes[leaf]
             if leaf.endswith("_scale"):
                 value = np.ones(shape, dtype=np.float32)
@@ -160,10 +175,12 @@ class _Block:
     """Views of one block's parameters, bf16 mirrors and gradients."""
 
     def __init__(self, trainer: "GPTTrainer", b: int):
-        for leaf in BLOCK_FIELDS:
+        for leaf in block_fields(trainer.config):
             name = f"blocks/{b}/{leaf}"
             setattr(self, leaf, trainer.param_view(name, bf16=True))
             setattr(self, "g_" + leaf, trainer.grad_view(name))
+        if trainer.config.experts:  # the router computes in fp32 (train.py:1258-1263)
+            self.router_w32 = trainer.param_view(f"blocks/{b}/router_w")
 
 
 class GPTTrainer:
@@ -258,8 +275,11 @@ class GPTTrainer:
         self.xm = [torch.empty(N, d, **bf) for _ in range(L)]
         self.ln2 = [torch.empty(N, d, **bf) for _ in range(L)]
         self.rstd2 = [torch.empty(N, **f32) for _ in range(L)]
-        self.gelu_grad = [torch.empty(N, h, **bf) for _ in range(L)]  # gelu'(u), saved by the forward
-        self.g = [torch.empty(N, h, **bf) for _ in range(L)]
+        if c.experts:
+            self._alloc_moe()
+        else:
+            self.gelu_grad = [torch.empty(N, h, **bf) for _ in range(L)]  # gelu'(u), saved
+            self.g = [torch.empty(N, h, **bf) for _ in range(L)]
         self.lnf = torch.empty(N, d, **bf)
         self.rstdf = torch.empty(N, **f32)
         self.losses = torch.empty(N, **f32)
@@ -271,7 +291,7 @@ class GPTTrainer:
         # backward scratch
         self.dx = torch.empty(N, d, **bf)
         self.dln = torch.empty(N, d, **bf)
-        self.du = torch.empty(N, h, **bf)
+        self.du = None if c.experts else torch.empty(N, h, **bf)
         self.datt = torch.empty(N, d, **bf)
         self.dqkv = torch.empty(N, 3 * d, **bf)
         self.attn_ws = ops.attention_workspace(self.B, c.heads, self.T, dev)
@@ -279,6 +299,108 @@ class GPTTrainer:
         self.lce_bwd_ws = ops.lce_bwd_workspace(N, c.vocab_size, dev)
         self.tokens = torch.empty(self.B, self.T, dtype=torch.int32, device=dev)
         self.targets = torch.empty(self.B, self.T, dtype=torch.int32, device=dev)
+
+    def _alloc_moe(self) -> None:
+        """Per-layer routed buffers (kept for the backward) and shared scratch."""
+
+        c, dev, N, L = self.config, self.device, self.N, self.config.layers
+        d, E, k, eh = c.d_model, c.experts, c.expert_top_k, c.expert_mult * c.d_model
+        R = ops.moe_rows(N, k, E)
+        bf = dict(dtype=torch.bfloat16, device=dev)
+        f32 = dict(dtype=torch.float32, device=dev)
+        i32 = dict(dtype=torch.int32, device=dev)
+        self.moe_R = R
+        self.m_logits = [torch.empty(N, E, **f32) for _ in range(L)]
+        self.m_chosen = [torch.empty(N, k, **i32) for _ in range(L)]
+        self.m_gate = [torch.empty(N, k, **f32) for _ in range(L)]
+        self.m_pos = [torch.empty(N, k, **i32) for _ in range(L)]
+        self.m_src = [torch.empty(R, **i32) for _ in range(L)]
+        self.m_seg = [torch.zeros(E, 2, **i32) for _ in range(L)]
+        self.m_total = [torch.zeros(1, **i32) for _ in range(L)]
+        self.m_grouped = [torch.empty(R, d, **bf) for _ in range(L)]
+        self.m_hidden = [torch.empty(R, eh, **bf) for _ in range(L)]
+        self.m_gelu = [torch.empty(R, eh, **bf) for _ in range(L)]
+        self.m_out = [torch.empty(R, d, **bf) for _ in range(L)]
+        width = 2 * E + 3
+        self.m_stats = torch.zeros(L, width, **f32)
+        self.m_bal = torch.zeros(L, E, **f32)
+        self.m_dout = torch.empty(R, d, **bf)
+        self.m_dhidden = torch.empty(R, eh, **bf)
+        self.m_dgrouped = torch.empty(R, d, **bf)
+        self.m_dgate = torch.empty(N, k, **f32)
+        self.m_ws = ops.moe_dispatch_workspace(N, k, E, dev)
+        self.router_history = torch.zeros(self.history.shape[0], 6 + L * (3 + E), **f32)
+
+    def _moe_forward(self, l: int, blk) -> None:
+        """Routed MLP of block l (recipes/reference_moe/train.py:1230-1311):
+        route, dispatch into padded expert segments, per-expert up (bias + GELU)
+        and down GEMMs over the device-side segment bounds, gate-weighted combine
+        with the residual branch."""
+
+        c = self.config
+        E, eh, d = c.experts, c.expert_mult * c.d_model, c.d_model
+        ops.moe_route(self.ln2[l], blk.router_w32, self.m_logits[l], self.m_chosen[l],
+                      self.m_gate[l], self.m_stats[l])
+        ops.moe_dispatch(self.m_chosen[l], self.ln2[l], E, self.m_seg[l], self.m_total[l],
+                         self.m_pos[l], self.m_src[l], self.m_grouped[l], self.m_ws)
+        R = self.moe_R
+        for e in range(E):
+            rr = self.m_seg[l][e]
+            ops.gemm(self.m_grouped[l], blk.expert_up_w[e], self.m_hidden[l], b_mn_major=True,
+                     m=R, n=eh, k=d, kind=_lib.EPI_BIAS_GELU, bias=blk.expert_up_b[e],
+                     aux=self.m_gelu[l], row_range=rr, range_dim=1)
+        for e in range(E):
+            rr = self.m_seg[l][e]
+            ops.gemm(self.m_hidden[l], blk.expert_down_w[e], self.m_out[l], b_mn_major=True,
+                     m=R, n=d, k=eh, bias=blk.expert_down_b[e], row_range=rr, range_dim=1)
+        ops.moe_combine(self.m_out[l], self.m_pos[l], self.m_gate[l], self.xm[l],
+                        c.branch_scale, self.x[l + 1])
+
+    def _moe_backward(self, l: int, blk, dx: torch.Tensor) -> None:
+        """Backward of _moe_forward: dx (gradient of the block output) in,
+        self.dln (gradient of the routed MLP's input) out; expert, router and
+        bias gradients accumulated."""
+
+        c = self.config
+        E, eh, d, R = c.experts, c.expert_mult * c.d_model, c.d_model, self.moe_R
+        ops.moe_combine_bwd(dx, c.branch_scale, self.m_out[l], self.m_pos[l], self.m_gate[l],
+                            self.m_src[l], self.m_total[l], self.m_dout, self.m_dgate)
+        for e in range(E):
+            rr = self.m_seg[l][e]
+            # d_hidden = dGELU(d_out . W_down[e]^T)
+            ops.gemm(self.m_dout, blk.expert_down_w[e], self.m_dhidden, m=R, n=eh, k=d,
+                     kind=_lib.EPI_DGELU, aux=self.m_gelu[l], row_range=rr, range_dim=1)
+            # dW_down[e] += hidden^T d_out over the expert's rows
+            ops.gemm(self.m_hidden[l], self.m_dout, blk.g_expert_down_w[e], a_mn_major=True,
+                     b_mn_major=True, m=eh, n=d, k=R, kind=_lib.EPI_F32_ATOMIC, row_range=rr,
+                     range_dim=2)
+        ops.moe_segment_colsum(self.m_dout, self.m_seg[l], E, blk.g_expert_down_b)
+        for e in range(E):
+            rr = self.m_seg[l][e]
+            ops.gemm(self.m_dhidden, blk.expert_up_w[e], self.m_dgrouped, m=R, n=d, k=eh,
+                     row_range=rr, range_dim=1)
+            ops.gemm(self.m_grouped[l], self.m_dhidden, blk.g_expert_up_w[e], a_mn_major=True,
+                     b_mn_major=True, m=d, n=eh, k=R, kind=_lib.EPI_F32_ATOMIC, row_range=rr,
+                     range_dim=2)
+        ops.moe_segment_colsum(self.m_dhidden, self.m_seg[l], E, blk.g_expert_up_b)
+        ops.moe_route_bwd(self.ln2[l], blk.router_w32, self.m_logits[l], self.m_chosen[l],
+                          self.m_gate[l], self.m_dgate, self.m_bal[l], self.m_dgrouped,
+                          self.m_pos[l], blk.g_router_w, self.dln)
+
+    def _moe_finalize(self) -> None:
+        """Balance loss and router statistics over all ranks (the reference
+        pmeans them, train.py:1302-1305), added to the loss; backward
+        coefficients of the router probabilities."""
+
+        c = self.config
+        if self.world_size > 1:
+            import torch.distributed as dist
+
+            dist.all_reduce(self.m_stats, op=dist.ReduceOp.SUM, group=self.pg)
+        ops.moe_finalize(self.m_stats, c.layers, c.experts, self.N * self.world_size,
+                         c.expert_top_k, c.router_aux_coefficient,
+                         1.0 / (self.N * self.world_size), self.m_bal, self.loss,
+                         self.router_history, self.step_dev)
 
     def _build_optimizer(self) -> None:
         c = self.config
@@ -323,6 +445,8 @@ class GPTTrainer:
         d, h, N = c.d_model, c.hidden, self.N
         a = c.branch_scale
         ops.embedding_fwd(self.tokens.view(-1), self.tok_emb, self.x[0])
+        if c.experts:
+            self.m_stats.zero_()
         if self.segments is not None:  # document masking (train.py:1127-1131)
             ops.document_segments(self.tokens.view(self.B, self.T), c.document_boundary_token,
                                   self.segments)
@@ -337,6 +461,9 @@ class GPTTrainer:
             ops.matmul(self.att[l], blk.attn_w, bias=blk.attn_b, alpha=a, residual=self.x[l],
                        out=self.xm[l])
             ops.rms_norm_fwd(self.xm[l], blk.ln2_scale, self.ln2[l], self.rstd2[l])
+            if c.experts:
+                self._moe_forward(l, blk)
+                continue
             ops.matmul(self.ln2[l], blk.mlp_up_w, bias=blk.mlp_up_b, kind=_lib.EPI_BIAS_GELU,
                        aux=self.gelu_grad[l], out=self.g[l])
             ops.matmul(self.g[l], blk.mlp_down_w, bias=blk.mlp_down_b, alpha=a,
@@ -344,6 +471,8 @@ class GPTTrainer:
         ops.rms_norm_fwd(self.x[c.layers], self.final_scale, self.lnf, self.rstdf)
         ops.lce_fwd(self.lnf, self.out_emb, self.targets.view(-1), c.semantic_vocab_size,
                     self.losses, self.lse_ce, self.loss, workspace=self.lce_fwd_ws)
+        if c.experts:
+            self._moe_finalize()
         return self.loss
 
     def _wgrad(self, act: torch.Tensor, dy: torch.Tensor, gview: torch.Tensor, alpha: float):
@@ -366,17 +495,23 @@ class GPTTrainer:
                     c.semantic_vocab_size, self.dln, self.g_out_emb, workspace=self.lce_bwd_ws)
         # The residual-stream gradient each RMSNorm backward produces is also the
         # gradient of the bias of the branch below it; its column sums are fused.
+        # (a routed MLP's biases are per expert: their sums come from moe_segment_colsum)
+        mlp_bias = (lambda l: None) if c.experts else (lambda l: self.blocks[l].g_mlp_down_b)
         ops.rms_norm_bwd(self.x[c.layers], self.final_scale, self.rstdf, self.dln, None, self.dx,
-                         self.g_final_scale, self.blocks[c.layers - 1].g_mlp_down_b, a)
+                         self.g_final_scale, mlp_bias(c.layers - 1), a)
         dx = self.dx
         for l in reversed(range(c.layers)):
             blk = self.blocks[l]
-            # MLP: x[l+1] = xm + a * (gelu(ln2 Wu + bu) Wd + bd)
-            self._dgrad(dx, blk.mlp_down_w, self.du, kind=_lib.EPI_DGELU, alpha=a, aux=self.gelu_grad[l])
-            self._wgrad(self.g[l], dx, blk.g_mlp_down_w, a)
-            self._wgrad(self.ln2[l], self.du, blk.g_mlp_up_w, 1.0)
-            ops.colsum(self.du, blk.g_mlp_up_b, 1.0)
-            self._dgrad(self.du, blk.mlp_up_w, self.dln)
+            if c.experts:
+                self._moe_backward(l, blk, dx)
+            else:
+                # MLP: x[l+1] = xm + a * (gelu(ln2 Wu + bu) Wd + bd)
+                self._dgrad(dx, blk.mlp_down_w, self.du, kind=_lib.EPI_DGELU, alpha=a,
+                            aux=self.gelu_grad[l])
+                self._wgrad(self.g[l], dx, blk.g_mlp_down_w, a)
+                self._wgrad(self.ln2[l], self.du, blk.g_mlp_up_w, 1.0)
+                ops.colsum(self.du, blk.g_mlp_up_b, 1.0)
+                self._dgrad(self.du, blk.mlp_up_w, self.dln)
             ops.rms_norm_bwd(self.xm[l], blk.ln2_scale, self.rstd2[l], self.dln, dx, dx,
                              blk.g_ln2_scale, blk.g_attn_b, a)
             # attention: xm = x + a * (att Wo + bo)
@@ -390,7 +525,7 @@ class GPTTrainer:
             self._wgrad(self.ln1[l], self.dqkv, blk.g_qkv_w, 1.0)
             ops.colsum(self.dqkv, blk.g_qkv_b, 1.0)
             self._dgrad(self.dqkv, blk.qkv_w, self.dln)
-            below = self.blocks[l - 1].g_mlp_down_b if l > 0 else None
+            below = mlp_bias(l - 1) if l > 0 else None
             ops.rms_norm_bwd(self.x[l], blk.ln1_scale, self.rstd1[l], self.dln, dx, dx,
                              blk.g_ln1_scale, below, a)
             if reduce_hook is not None:

@@ -60,10 +60,14 @@ def gemm(
     accumulate: bool = False,
     rope: tuple[torch.Tensor, torch.Tensor] | None = None,
     rope_cols: int = 0,
+    row_range: torch.Tensor | None = None,
+    range_dim: int = 0,
 ) -> torch.Tensor:
-    """out[m, n] = epilogue(sum_k A[m, k] B[n, k]); see include/gptb200.h."""
+    """out[m, n] = epilogue(sum_k A[m, k] B[n, k]); see include/gptb200.h.
+    row_range: optional int32 device tensor {offset, count} restricting the M
+    rows (range_dim 1) or the K rows (range_dim 2) that take part."""
 
-    _cuda(a, b, out, bias, residual, aux)
+    _cuda(a, b, out, bias, residual, aux, row_range)
     if a.dtype != BF16 or b.dtype != BF16:
         raise TypeError("GEMM operands must be bfloat16")
     lda, ldb, ldc = _row_major(a, "a"), _row_major(b, "b"), _row_major(out, "out")
@@ -80,6 +84,8 @@ def gemm(
         rope_sin=None if rope is None else rope[1].data_ptr(),
         rope_seq=0 if rope is None else rope[0].shape[0],
         rope_cols=int(rope_cols),
+        row_range=_ptr(row_range),
+        range_dim=int(range_dim) if row_range is not None else 0,
     )
     if gemm_timer is not None:
         start = torch.cuda.Event(enable_timing=True)
@@ -343,3 +349,73 @@ def adamw_step(params, m, v, grads, groups_dev, n_groups, cfg, step, loss, histo
 
 def device_error(clear: bool = True) -> int:
     return _lib.load().gptb200_device_error(int(clear))
+
+
+# ----------------------------------------------------------------- routed MLP (MoE)
+def moe_rows(tokens: int, top_k: int, experts: int) -> int:
+    """Rows of the expert-sorted buffer (assignments + per-expert padding to 128)."""
+
+    return int(_lib.load().gptb200_moe_rows(tokens, top_k, experts))
+
+
+def moe_dispatch_workspace(tokens: int, top_k: int, experts: int, device) -> torch.Tensor:
+    n = _lib.load().gptb200_moe_dispatch_workspace_size(tokens, top_k, experts)
+    return torch.empty(n, dtype=torch.uint8, device=device)
+
+
+def moe_route(x, router_w, logits, chosen, gate, stats):
+    """logits = x . router_w (fp32), top-k `chosen` experts and their `gate`s;
+    accumulates the layer's routing statistics into `stats`."""
+
+    _cuda(x, router_w, logits, chosen, gate, stats)
+    n, d = x.shape
+    e = router_w.shape[1]
+    call("gptb200_moe_route", x.data_ptr(), router_w.data_ptr(), n, d, e, chosen.shape[1],
+         logits.data_ptr(), chosen.data_ptr(), gate.data_ptr(), stats.data_ptr(), _stream())
+
+
+def moe_dispatch(chosen, x, experts, seg, total, pos, src, grouped, workspace):
+    _cuda(chosen, x, seg, total, pos, src, grouped, workspace)
+    n, k = chosen.shape
+    call("gptb200_moe_dispatch", chosen.data_ptr(), n, k, experts, x.data_ptr(), x.shape[1],
+         seg.data_ptr(), total.data_ptr(), pos.data_ptr(), src.data_ptr(), grouped.data_ptr(),
+         workspace.data_ptr(), _stream())
+
+
+def moe_combine(out, pos, gate, residual, alpha, x_out):
+    _cuda(out, pos, gate, residual, x_out)
+    n, k = pos.shape
+    call("gptb200_moe_combine", out.data_ptr(), pos.data_ptr(), gate.data_ptr(),
+         residual.data_ptr(), float(alpha), n, residual.shape[1], k, x_out.data_ptr(), _stream())
+
+
+def moe_combine_bwd(dx, alpha, out, pos, gate, src, total, d_out, d_gate):
+    _cuda(dx, out, pos, gate, src, total, d_out, d_gate)
+    n, k = pos.shape
+    call("gptb200_moe_combine_bwd", dx.data_ptr(), float(alpha), out.data_ptr(), pos.data_ptr(),
+         gate.data_ptr(), src.data_ptr(), total.data_ptr(), n, dx.shape[1], k, d_out.data_ptr(),
+         d_gate.data_ptr(), _stream())
+
+
+def moe_route_bwd(x, router_w, logits, chosen, gate, d_gate, bal_grad, d_grouped, pos,
+                  d_router_w, d_x):
+    _cuda(x, router_w, logits, chosen, gate, d_gate, bal_grad, d_grouped, pos, d_router_w, d_x)
+    n, d = x.shape
+    call("gptb200_moe_route_bwd", x.data_ptr(), router_w.data_ptr(), logits.data_ptr(),
+         chosen.data_ptr(), gate.data_ptr(), d_gate.data_ptr(), bal_grad.data_ptr(),
+         d_grouped.data_ptr(), pos.data_ptr(), n, d, router_w.shape[1], chosen.shape[1],
+         d_router_w.data_ptr(), d_x.data_ptr(), _stream())
+
+
+def moe_segment_colsum(buf, seg, experts, out):
+    _cuda(buf, seg, out)
+    call("gptb200_moe_segment_colsum", buf.data_ptr(), seg.data_ptr(), experts, buf.shape[1],
+         out.data_ptr(), _stream())
+
+
+def moe_finalize(stats, layers, experts, tokens, top_k, coefficient, bwd_scale, bal_grad, loss,
+                 history, step):
+    _cuda(stats, bal_grad, loss, history, step)
+    call("gptb200_moe_finalize", stats.data_ptr(), layers, experts, tokens, top_k,
+         float(coefficient), float(bwd_scale), bal_grad.data_ptr(), loss.data_ptr(),
+         history.data_ptr(), history.shape[0], step.data_ptr(), _stream())

@@ -83,6 +83,14 @@ typedef struct gptb200_epilogue {
   const void* rope_sin;
   int64_t rope_seq;      /* rows are token positions row % rope_seq */
   int64_t rope_cols;     /* columns [0, rope_cols) are rotated (q and k: 2 * d_model) */
+  /* Optional device-resident row range: int32 {offset, count} with count a
+   * multiple of 128, read when the kernel starts. range_dim 1: only rows
+   * [offset, offset + count) of A and C take part (m = the buffer's rows);
+   * range_dim 2: only K rows [offset, offset + count) of MN-major A and B
+   * (k = the buffer's rows). 0: no range. Used for per-expert segments of a
+   * token buffer whose sizes are only known on the device. */
+  const int32_t* row_range;
+  int range_dim;
 } gptb200_epilogue;
 
 int gptb200_gemm(const void* a, int a_mn_major, int64_t lda, const void* b, int b_mn_major,
@@ -177,6 +185,64 @@ int gptb200_attention_bwd(const void* q, const void* k, const void* v, int64_t s
                           int64_t heads, int64_t seq, int64_t head_dim, float softmax_scale,
                           const void* rope_cos, const void* rope_sin, const int32_t* segment_ids,
                           void* workspace, void* stream);
+
+/* ------------------------------------------------------------------ routed MLP (MoE)
+ * recipes/reference_moe/train.py:1230-1372 (routed_mlp_local, load_balance_loss)
+ * as kernels around gptb200_gemm. Assignment a = token * top_k + choice; the
+ * assignments are stably sorted by expert into one row buffer of
+ * gptb200_moe_rows() rows, expert e owning rows [seg[2e], seg[2e] + seg[2e+1])
+ * (its count rounded up to 128; padding rows are zero on the way in and
+ * ignored on the way out). The expert GEMMs read seg[2e..2e+1] on the device
+ * (gptb200_epilogue.row_range), so no host synchronisation is needed.
+ * stats (fp32, per layer, accumulated): [0, E) router-probability sums,
+ * [E, 2E) assignment counts, entropy sum, top-1 gate sum, sum of squared
+ * logits. E <= 16, top_k <= 4. */
+size_t gptb200_moe_rows(int64_t tokens, int32_t top_k, int32_t experts);
+size_t gptb200_moe_dispatch_workspace_size(int64_t tokens, int32_t top_k, int32_t experts);
+/* logits fp32 [tokens, E] = x (bf16 [tokens, d], promoted to fp32) . router_w
+ * (fp32 [d, E]); chosen/gate [tokens, top_k]: top-k experts (ties: lower
+ * index first) and the softmax of their logits. */
+int gptb200_moe_route(const void* x, const float* router_w, int64_t tokens, int64_t d,
+                      int32_t experts, int32_t top_k, float* logits, int32_t* chosen, float* gate,
+                      float* stats, void* stream);
+/* seg int32 [E, 2], total int32 [1] (rows in use), pos int32 [tokens, top_k]
+ * (row of each assignment), src int32 [rows] (token of each row, -1 padding),
+ * grouped bf16 [rows, d] = x[src]. */
+int gptb200_moe_dispatch(const int32_t* chosen, int64_t tokens, int32_t top_k, int32_t experts,
+                         const void* x, int64_t d, int32_t* seg, int32_t* total, int32_t* pos,
+                         int32_t* src, void* grouped, void* workspace, void* stream);
+/* x_out = residual + alpha * sum_j bf16(out[pos(t, j)] * bf16(gate(t, j))) (bf16). */
+int gptb200_moe_combine(const void* out, const int32_t* pos, const float* gate,
+                        const void* residual, float alpha, int64_t tokens, int64_t d,
+                        int32_t top_k, void* x_out, void* stream);
+/* Backward of the combine for dx = d x_out: d_out rows (zero on padding) and
+ * d_gate fp32 [tokens, top_k]. */
+int gptb200_moe_combine_bwd(const void* dx, float alpha, const void* out, const int32_t* pos,
+                            const float* gate, const int32_t* src, const int32_t* total,
+                            int64_t tokens, int64_t d, int32_t top_k, void* d_out, float* d_gate,
+                            void* stream);
+/* Router backward: d_logits from the gates and from the balance loss (bal_grad
+ * fp32 [E]: d loss / d router probability, equal for every token); d_router_w
+ * += x^T d_logits (fp32); d_x = bf16(sum_j d_grouped[pos] + d_logits router_w^T). */
+int gptb200_moe_route_bwd(const void* x, const float* router_w, const float* logits,
+                          const int32_t* chosen, const float* gate, const float* d_gate,
+                          const float* bal_grad, const void* d_grouped, const int32_t* pos,
+                          int64_t tokens, int64_t d, int32_t experts, int32_t top_k,
+                          float* d_router_w, void* d_x, void* stream);
+/* out fp32 [E, width] += column sums of buf (bf16 [rows, width]) over each
+ * expert's segment (per-expert bias gradients). */
+int gptb200_moe_segment_colsum(const void* buf, const int32_t* seg, int32_t experts,
+                               int64_t width, float* out, void* stream);
+/* From the (rank-summed) stats of all layers: balance loss per layer, the
+ * backward coefficients bal_grad [layers, E] (= coefficient / layers * E * load
+ * * bwd_scale), loss += coefficient * mean balance, and the router history row
+ * (train.py:1881-1915: balance, max load, min load, mean entropy / top-1 gate /
+ * logit RMS, then per layer those three and the load vector) written to row
+ * *step of history [history_rows, 6 + layers * (3 + E)]. */
+int gptb200_moe_finalize(const float* stats, int32_t layers, int32_t experts, int64_t tokens,
+                         int32_t top_k, float coefficient, float bwd_scale, float* bal_grad,
+                         float* loss, float* history, int32_t history_rows, const int32_t* step,
+                         void* stream);
 
 /* ------------------------------------------------------------------ linear cross-entropy
  * Tied-embedding cross entropy without materializing [n, vocab] logits:

@@ -189,6 +189,15 @@ def init_params(cfg: Any, seed: int) -> dict[str, np.ndarray]:
         out[f"blocks/{b}/attn_w"] = normal((d, d), hidden_scale)
         out[f"blocks/{b}/attn_b"] = np.zeros((d,), np.float32)
         out[f"blocks/{b}/ln2_scale"] = np.ones((d,), np.float32)
+        experts = getattr(cfg, "experts", 0)
+        if experts:  # recipes/reference_moe/train.py:905-931 (router, then experts)
+            eh = cfg.expert_mult * d
+            out[f"blocks/{b}/router_w"] = normal((d, experts), hidden_scale)
+            out[f"blocks/{b}/expert_up_w"] = normal((experts, d, eh), hidden_scale)
+            out[f"blocks/{b}/expert_up_b"] = np.zeros((experts, eh), np.float32)
+            out[f"blocks/{b}/expert_down_w"] = normal((experts, eh, d), hidden_scale)
+            out[f"blocks/{b}/expert_down_b"] = np.zeros((experts, d), np.float32)
+            continue
         out[f"blocks/{b}/mlp_up_w"] = normal((d, hidden), hidden_scale)
         out[f"blocks/{b}/mlp_up_b"] = np.zeros((hidden,), np.float32)
         out[f"blocks/{b}/mlp_down_w"] = normal((hidden, d), hidden_scale)
@@ -205,7 +214,58 @@ def softmax_scale(cfg) -> float:
     return 1.0 / head_dim if cfg.attention_scale == "inverse_head_dim" else head_dim ** -0.5
 
 
-def gpt_hidden(params: dict[str, torch.Tensor], tokens: torch.Tensor, cfg, dtype=BF16):
+def routed_mlp(x, router_w, up_w, up_b, down_w, down_b, experts: int, top_k: int, dtype=BF16):
+    """recipes/reference_moe/train.py:1230-1311 (routed_mlp_local, one device):
+    fp32 router logits, softmax probabilities, top-k logits and their softmax
+    gates, stable sort of the assignments by expert, per-expert bf16 matmuls
+    with fp32 accumulation (megablox.gmm), bias, tanh GELU, bias, gate weighting
+    in bf16 and a bf16 scatter-add back to the tokens. Returns the output and
+    the per-expert mean probability, load and (entropy, top-1 gate, logit RMS)."""
+
+    batch, length, width = x.shape
+    n = batch * length
+    flat = x.reshape(n, width)
+    logits = flat.to(F32) @ router_w.to(F32)
+    probabilities = torch.softmax(logits, dim=-1)
+    chosen_logits, chosen = torch.topk(logits, top_k, dim=-1)
+    gate = torch.softmax(chosen_logits, dim=-1)
+    assignments = chosen.reshape(-1)
+    order = torch.argsort(assignments, stable=True)
+    sorted_assignments = assignments[order]
+    counts = torch.bincount(assignments, minlength=experts)
+    rows = torch.arange(n).repeat_interleave(top_k)[order]
+    grouped = flat[rows].to(dtype)
+    hidden_parts, out_parts = [], []
+    start = 0
+    for e in range(experts):
+        seg = grouped[start:start + int(counts[e])]
+        hidden_parts.append(bf16_dot(seg, up_w[e], dtype))
+        start += int(counts[e])
+    hidden = torch.cat(hidden_parts) + up_b[sorted_assignments].to(dtype)
+    hidden = F.gelu(hidden.to(F32), approximate="tanh").to(dtype)
+    start = 0
+    for e in range(experts):
+        out_parts.append(bf16_dot(hidden[start:start + int(counts[e])], down_w[e], dtype))
+        start += int(counts[e])
+    out = torch.cat(out_parts) + down_b[sorted_assignments].to(dtype)
+    weighted = out * gate.reshape(-1)[order][:, None].to(dtype)
+    combined = torch.zeros(n, width, dtype=dtype).index_add(0, rows, weighted)
+    mean_probability = probabilities.mean(dim=0)
+    load = counts.to(F32) / float(n * top_k)
+    entropy = -(probabilities * torch.log(probabilities + 1.0e-9)).sum(-1).mean()
+    summary = torch.stack((entropy, gate.max(dim=-1).values.mean(),
+                           torch.sqrt(torch.mean(logits * logits))))
+    return combined.reshape(batch, length, width), mean_probability, load, summary
+
+
+def load_balance_loss(mean_probability, load):
+    """recipes/reference_moe/train.py:1347-1372: E * sum(load * mean probability)."""
+
+    return float(load.shape[0]) * torch.sum(load * mean_probability)
+
+
+def gpt_hidden(params: dict[str, torch.Tensor], tokens: torch.Tensor, cfg, dtype=BF16,
+               router_out: list | None = None):
     batch, length = tokens.shape
     heads = cfg.heads
     head_dim = cfg.d_model // heads
@@ -215,7 +275,8 @@ def gpt_hidden(params: dict[str, torch.Tensor], tokens: torch.Tensor, cfg, dtype
                 if getattr(cfg, "document_masking", False) else None)  # train.py:1127-1131
     x = params["token_embedding"][tokens.long()].to(dtype)
     for b in range(cfg.layers):
-        p = {k: params[f"blocks/{b}/{k}"] for k in BLOCK_FIELDS}
+        p = {k: v for k, v in ((f.split("/")[-1], params[f]) for f in params
+                                if f.startswith(f"blocks/{b}/"))}
         residual = x
         xn = rms_norm(x, p["ln1_scale"], dtype)
         qkv = linear(xn, p["qkv_w"], p["qkv_b"], dtype)
@@ -229,6 +290,14 @@ def gpt_hidden(params: dict[str, torch.Tensor], tokens: torch.Tensor, cfg, dtype
         x = residual + mult * linear(att, p["attn_w"], p["attn_b"], dtype)
         residual = x
         xn = rms_norm(x, p["ln2_scale"], dtype)
+        if getattr(cfg, "experts", 0):
+            mlp_out, mean_p, load, summary = routed_mlp(
+                xn, p["router_w"], p["expert_up_w"], p["expert_up_b"], p["expert_down_w"],
+                p["expert_down_b"], cfg.experts, cfg.expert_top_k, dtype)
+            if router_out is not None:
+                router_out.append((mean_p, load, summary))
+            x = residual + mult * mlp_out
+            continue
         hidden = linear(xn, p["mlp_up_w"], p["mlp_up_b"], dtype)
         hidden = F.gelu(hidden.to(F32), approximate="tanh").to(dtype)
         x = residual + mult * linear(hidden, p["mlp_down_w"], p["mlp_down_b"], dtype)
@@ -236,9 +305,18 @@ def gpt_hidden(params: dict[str, torch.Tensor], tokens: torch.Tensor, cfg, dtype
 
 
 def loss_fn(params, x, y, cfg, dtype=BF16):
-    hidden = gpt_hidden(params, x, cfg, dtype)
+    """recipes/reference/train.py:1194-1216; for routed models plus the
+    coefficient times the layer-mean balance loss
+    (recipes/reference_moe/train.py:1562-1602)."""
+
+    router: list = []
+    hidden = gpt_hidden(params, x, cfg, dtype, router)
     emb = params.get("output_embedding", params["token_embedding"])
-    return tiled_tied_cross_entropy(hidden, emb, y, cfg.semantic_vocab_size, dtype)
+    loss = tiled_tied_cross_entropy(hidden, emb, y, cfg.semantic_vocab_size, dtype)
+    if router and cfg.router_aux_coefficient:
+        balance = torch.stack([load_balance_loss(mp, ld) for mp, ld, _ in router]).mean()
+        loss = loss + cfg.router_aux_coefficient * balance
+    return loss
 
 
 def loss_and_grads(params_np: dict[str, np.ndarray], x, y, cfg, dtype=BF16):

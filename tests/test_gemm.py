@@ -102,3 +102,33 @@ def test_rejects_bad_arguments(cuda):
     c = torch.zeros(64, 64, device=cuda, dtype=torch.bfloat16)
     with pytest.raises(_lib.GptB200Error):
         ops.gemm(a, b, c, m=64, n=64, k=60)
+
+
+def test_device_row_range(cuda):
+    """M rows (range_dim 1) and K rows (range_dim 2) bounded by an int32
+    {offset, count} pair that lives on the device: rows outside stay untouched."""
+
+    g = torch.Generator().manual_seed(5)
+    R, K, N = 1024, 192, 256
+    a = torch.randn(R, K, generator=g).bfloat16().to(cuda)
+    b = (0.1 * torch.randn(K, N, generator=g)).bfloat16().to(cuda)  # [K, N]: MN-major operand
+    c = torch.full((R, N), 7.0, device=cuda).bfloat16()
+    rr = torch.tensor([256, 384], dtype=torch.int32, device=cuda)
+    ops.gemm(a, b, c, b_mn_major=True, m=R, n=N, k=K, row_range=rr, range_dim=1)
+    ref = (a.float() @ b.float())
+    assert _rel(c[256:640], ref[256:640]) < 4e-3
+    assert torch.all(c[:256] == 7.0) and torch.all(c[640:] == 7.0)
+    # K range: out[M, N] = A[K rows]^T B[K rows] with A, B MN-major [R, M] / [R, N]
+    am = torch.randn(R, 128, generator=g).bfloat16().to(cuda)
+    bm = torch.randn(R, N, generator=g).bfloat16().to(cuda)
+    out = torch.zeros(128, N, device=cuda)
+    kr = torch.tensor([128, 512], dtype=torch.int32, device=cuda)
+    ops.gemm(am, bm, out, a_mn_major=True, b_mn_major=True, m=128, n=N, k=R,
+             kind=_lib.EPI_F32_ATOMIC, row_range=kr, range_dim=2)
+    want = am[128:640].float().t() @ bm[128:640].float()
+    assert _rel(out, want) < 4e-3
+    empty = torch.tensor([0, 0], dtype=torch.int32, device=cuda)
+    c2 = torch.full((R, N), 3.0, device=cuda).bfloat16()
+    ops.gemm(a, b, c2, b_mn_major=True, m=R, n=N, k=K, row_range=empty, range_dim=1)
+    torch.cuda.synchronize()
+    assert torch.all(c2 == 3.0) and ops.device_error() == 0
