@@ -50,7 +50,12 @@ def flops_per_token(cfg) -> int:
     parameters (incl. the tied head) + full-square attention 12*L*H*T*Dh."""
 
     d, L = cfg.d_model, cfg.layers
-    return 6 * (L * 12 * d * d + cfg.vocab_size * d) + 12 * L * cfg.heads * cfg.seq_len * cfg.head_dim
+    if cfg.experts:  # active parameters: top_k experts of width expert_mult*d, plus the router
+        mlp = 2 * cfg.expert_top_k * d * cfg.expert_mult * d + d * cfg.experts
+    else:
+        mlp = 2 * d * cfg.mlp_mult * d
+    return (6 * (L * (4 * d * d + mlp) + cfg.vocab_size * d)
+            + 12 * L * cfg.heads * cfg.seq_len * cfg.head_dim)
 
 
 def measured_peaks() -> dict:
@@ -436,8 +441,10 @@ def main() -> None:
         "data": "synthetic: Zipf(s=1.1) token ids (seed 3) in an llm.c uint16 shard, read "
                 "through the shuffled-epoch stream; random-init weights (CompleteP init)",
         "config": {"workload": f"{cfg.tier} training step (fwd+bwd+allreduce+AdamW)",
-                   "model": f"GPT {cfg.layers}L/{cfg.d_model}d/{cfg.heads}H tied vocab "
-                            f"{cfg.vocab_size}", "global_batch": cfg.batch_size,
+                   "model": f"GPT {cfg.layers}L/{cfg.d_model}d/{cfg.heads}H "
+                            + ("tied" if cfg.tied else "untied") + f" vocab {cfg.vocab_size}"
+                            + (f", {cfg.experts} experts top-{cfg.expert_top_k}"
+                               if cfg.experts else ""), "global_batch": cfg.batch_size,
                    "seq_len": cfg.seq_len, "parallelism": f"dp{world}",
                    "l2": "working set (activations ~40 GB/GPU at dp1) far larger than L2"},
         "mfu": mfu, "mfu_peak_tflops": peaks["bf16"], "mfu_peak_source": peaks["source"],

@@ -33,9 +33,9 @@ __global__ void __launch_bounds__(256) moe_route_kernel(
     const bf16* __restrict__ x, const float* __restrict__ w, int64_t n, int d, int E, int k,
     float* __restrict__ logits, int* __restrict__ chosen, float* __restrict__ gate,
     float* __restrict__ stats) {
-  extern __shared__ float wsm[];  // [d][E] router weights, then [E + E + 3] block stats
+  extern __shared__ float wsm[];  // [E][d] router weights (transposed), then the block stats
   float* bst = wsm + (size_t)d * E;
-  for (int i = threadIdx.x; i < d * E; i += blockDim.x) wsm[i] = w[i];
+  for (int i = threadIdx.x; i < d * E; i += blockDim.x) wsm[(i % E) * d + i / E] = w[i];
   for (int i = threadIdx.x; i < moe_stat_width(E); i += blockDim.x) bst[i] = 0.f;
   __syncthreads();
   const int lane = threadIdx.x & 31;
@@ -49,14 +49,17 @@ __global__ void __launch_bounds__(256) moe_route_kernel(
     for (int c = lane; c < d / 8; c += 32) {
       const uint4 q = *reinterpret_cast<const uint4*>(row + c * 8);
       const uint32_t* qw = &q.x;
+      float a[8];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        float a0, a1;
-        unpack_bf16x2(qw[j], a0, a1);
-        const float* w0 = wsm + (size_t)(c * 8 + 2 * j) * E;
+      for (int j = 0; j < 4; ++j) unpack_bf16x2(qw[j], a[2 * j], a[2 * j + 1]);
 #pragma unroll
-        for (int e = 0; e < kMoeMaxE; ++e)
-          if (e < E) acc[e] = fmaf(a0, w0[e], fmaf(a1, w0[E + e], acc[e]));
+      for (int e = 0; e < kMoeMaxE; ++e) {
+        if (e < E) {
+          const float4* we = reinterpret_cast<const float4*>(wsm + (size_t)e * d + c * 8);
+          const float4 w0 = we[0], w1 = we[1];
+          acc[e] = fmaf(a[0], w0.x, fmaf(a[1], w0.y, fmaf(a[2], w0.z, fmaf(a[3], w0.w, acc[e]))));
+          acc[e] = fmaf(a[4], w1.x, fmaf(a[5], w1.y, fmaf(a[6], w1.z, fmaf(a[7], w1.w, acc[e]))));
+        }
       }
     }
 #pragma unroll
@@ -306,83 +309,88 @@ __global__ void moe_zero_pad_kernel(const int* __restrict__ src, const int* __re
 // d_logits from the gates (softmax of the chosen logits) and from the balance
 // loss through the router probabilities (d prob_e = bal[e], the same for every
 // token); then d_x = bf16(bf16(sum_j d_grouped[pos(i,j)]) + bf16(d_logits . W^T))
-// and d_W += x^T d_logits (block partials in shared memory, one atomic each).
-__global__ void __launch_bounds__(256) moe_route_bwd_kernel(
+// and d_W += x^T d_logits. Tokens go in chunks of 64: the warps first form the
+// chunk's d_logits in shared memory (lane e = expert), then every thread owns a
+// few features (all E weights of them in registers) and walks the chunk's
+// tokens with coalesced row reads, accumulating its d_W entries in registers
+// (one atomic per entry per block at the end). One feature per thread up to
+// d = 1024 threads, two beyond.
+constexpr int kRbChunk = 64;
+constexpr int kRbMaxF = 2;  // features per thread: d <= 2 * 1024
+
+template <int E>
+__global__ void __launch_bounds__(1024, 1) moe_route_bwd_kernel(
     const bf16* __restrict__ x, const float* __restrict__ w, const float* __restrict__ logits,
     const int* __restrict__ chosen, const float* __restrict__ gate,
     const float* __restrict__ d_gate, const float* __restrict__ bal,
-    const bf16* __restrict__ d_grouped, const int* __restrict__ pos, int64_t n, int d, int E,
-    int k, float* __restrict__ d_w, bf16* __restrict__ d_x) {
-  extern __shared__ float sm[];  // [d][E] weights, then [d][E] partial d_W
-  float* dws = sm + (size_t)d * E;
-  for (int i = threadIdx.x; i < d * E; i += blockDim.x) {
-    sm[i] = w[i];
-    dws[i] = 0.f;
+    const bf16* __restrict__ d_grouped, const int* __restrict__ pos, int64_t n, int d, int k,
+    float* __restrict__ d_w, bf16* __restrict__ d_x) {
+  __shared__ float dl[kRbChunk][E];
+  __shared__ int ps[kRbChunk][kMoeMaxK];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // features of this thread: f = tid + i * blockDim.x, i < kRbMaxF
+  float wreg[kRbMaxF][E], acc[kRbMaxF][E];
+#pragma unroll
+  for (int i = 0; i < kRbMaxF; ++i) {
+    const int f = threadIdx.x + i * blockDim.x;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      wreg[i][e] = f < d ? w[(int64_t)f * E + e] : 0.f;
+      acc[i][e] = 0.f;
+    }
   }
-  __syncthreads();
-  const int lane = threadIdx.x & 31;
-  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
-  for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < n;
-       t += warps) {
-    // every lane recomputes the token's E-wide gradient (E <= 16 values)
-    float lg[kMoeMaxE], pr[kMoeMaxE], dl[kMoeMaxE];
-    float mx = -INFINITY;
-    for (int e = 0; e < E; ++e) {
-      lg[e] = logits[t * E + e];
-      mx = fmaxf(mx, lg[e]);
-    }
-    float z = 0.f;
-    for (int e = 0; e < E; ++e) {
-      pr[e] = expf(lg[e] - mx);
-      z += pr[e];
-    }
-    float dot = 0.f;
-    for (int e = 0; e < E; ++e) {
-      pr[e] /= z;
-      dot += pr[e] * bal[e];
-    }
-    for (int e = 0; e < E; ++e) dl[e] = pr[e] * (bal[e] - dot);
-    float gd = 0.f;
-    for (int j = 0; j < k; ++j) gd += gate[t * k + j] * d_gate[t * k + j];
-    for (int j = 0; j < k; ++j) {
-      const int e = chosen[t * k + j];
-      const float gj = gate[t * k + j];
-      for (int x2 = 0; x2 < E; ++x2)
-        if (x2 == e) dl[x2] += gj * (d_gate[t * k + j] - gd);
-    }
-    for (int c = lane; c < d / 8; c += 32) {
-      const uint4 q = *reinterpret_cast<const uint4*>(x + t * d + c * 8);
-      const uint32_t* qw = &q.x;
-      uint32_t sumg[4];
-      for (int j = 0; j < k; ++j) {
-        const uint4 g4 = *reinterpret_cast<const uint4*>(d_grouped + (int64_t)pos[t * k + j] * d +
-                                                         c * 8);
-        const uint32_t* gw = &g4.x;
+  for (int64_t c0 = (int64_t)blockIdx.x * kRbChunk; c0 < n; c0 += (int64_t)gridDim.x * kRbChunk) {
+    const int nt = (int)(n - c0 < kRbChunk ? n - c0 : kRbChunk);
+    // (a) d_logits of the chunk: warp per token, lane e per expert
+    for (int tt = warp; tt < nt; tt += blockDim.x >> 5) {
+      const int64_t t = c0 + tt;
+      const float lg = lane < E ? logits[t * E + lane] : -INFINITY;
+      float mx = lg;
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) sumg[q4] = j == 0 ? gw[q4] : hadd2_bf16(sumg[q4], gw[q4]);
-      }
-      uint4 o;
-      uint32_t* ow = &o.x;
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      const float ex = lane < E ? expf(lg - mx) : 0.f;
+      const float z = warp_sum(ex);
+      const float pr = ex / z;
+      const float b = lane < E ? bal[lane] : 0.f;
+      const float dot = warp_sum(pr * b);
+      float g = pr * (b - dot);
+      float gd = 0.f;
+      for (int j = 0; j < k; ++j) gd += gate[t * k + j] * d_gate[t * k + j];
+      for (int j = 0; j < k; ++j)
+        if (chosen[t * k + j] == lane) g += gate[t * k + j] * (d_gate[t * k + j] - gd);
+      if (lane < E) dl[tt][lane] = g;
+      if (lane < k) ps[tt][lane] = pos[t * k + lane];
+    }
+    __syncthreads();
+    // (b) features: d_W accumulation and d_x
+    for (int tt = 0; tt < nt; ++tt) {
+      const int64_t t = c0 + tt;
 #pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) {
-        float a0, a1;
-        unpack_bf16x2(qw[q4], a0, a1);
-        const int r0 = c * 8 + 2 * q4;
-        float* d0 = dws + (size_t)r0 * E;
-        float v0 = 0.f, v1 = 0.f;
+      for (int i = 0; i < kRbMaxF; ++i) {
+        const int f = threadIdx.x + i * blockDim.x;
+        if (f >= d) break;
+        const float xv = __bfloat162float(x[t * d + f]);
+        float v = 0.f;
+#pragma unroll
         for (int e = 0; e < E; ++e) {
-          v0 = fmaf(dl[e], sm[(size_t)r0 * E + e], v0);
-          v1 = fmaf(dl[e], sm[(size_t)(r0 + 1) * E + e], v1);
-          atomicAdd(&d0[e], a0 * dl[e]);
-          atomicAdd(&d0[E + e], a1 * dl[e]);
+          const float de = dl[tt][e];
+          acc[i][e] = fmaf(xv, de, acc[i][e]);
+          v = fmaf(de, wreg[i][e], v);
         }
-        ow[q4] = hadd2_bf16(sumg[q4], pack_bf16x2(v0, v1));
+        bf16 sg = d_grouped[(int64_t)ps[tt][0] * d + f];
+        for (int j = 1; j < k; ++j) sg = __hadd(sg, d_grouped[(int64_t)ps[tt][j] * d + f]);
+        d_x[t * d + f] = __hadd(sg, __float2bfloat16(v));
       }
-      *reinterpret_cast<uint4*>(d_x + t * d + c * 8) = o;
     }
+    __syncthreads();
   }
-  __syncthreads();
-  for (int i = threadIdx.x; i < d * E; i += blockDim.x) atomicAdd(&d_w[i], dws[i]);
+#pragma unroll
+  for (int i = 0; i < kRbMaxF; ++i) {
+    const int f = threadIdx.x + i * blockDim.x;
+    if (f >= d) break;
+#pragma unroll
+    for (int e = 0; e < E; ++e) atomicAdd(&d_w[(int64_t)f * E + e], acc[i][e]);
+  }
 }
 
 // out[e][c] += sum of buf rows [seg[e].x, seg[e].x + seg[e].y), column c.
@@ -485,7 +493,7 @@ extern "C" int gptb200_moe_route(const void* x, const float* router_w, int64_t t
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int blocks = (int)std::min<int64_t>((tokens + 7) / 8, (int64_t)sms * 2);
+  const int blocks = (int)std::min<int64_t>((tokens + 7) / 8, (int64_t)sms * 4);
   moe_route_kernel<<<blocks, 256, smem, st>>>(reinterpret_cast<const bf16*>(x), router_w, tokens,
                                                (int)d, experts, top_k, logits, chosen, gate,
                                                stats);
@@ -573,21 +581,27 @@ extern "C" int gptb200_moe_route_bwd(const void* x, const float* router_w, const
       !pos || !d_router_w || !d_x || tokens <= 0)
     return GPTB200_EINVAL;
   if (experts < 1 || experts > kMoeMaxE || top_k < 1 || top_k > kMoeMaxK) return GPTB200_EUNSUPPORTED;
-  const size_t smem = (size_t)2 * d * experts * 4;
-  if (d % 8 || smem > 200 * 1024) return GPTB200_ESHAPE;
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(moe_route_bwd_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return -static_cast<int>(e);
-  }
+  if (d % 8 || d > kRbMaxF * 1024) return GPTB200_ESHAPE;
+  // the backward is instantiated for 2, 4, 8 and 16 experts
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int blocks = (int)std::min<int64_t>((tokens + 7) / 8, (int64_t)sms);
-  moe_route_bwd_kernel<<<blocks, 256, smem, reinterpret_cast<cudaStream_t>(stream)>>>(
-      reinterpret_cast<const bf16*>(x), router_w, logits, chosen, gate, d_gate, bal_grad,
-      reinterpret_cast<const bf16*>(d_grouped), pos, tokens, (int)d, experts, top_k, d_router_w,
-      reinterpret_cast<bf16*>(d_x));
+  const int threads = (int)std::min<int64_t>(1024, (d + 31) / 32 * 32);  // a feature per thread
+  const int blocks = (int)std::min<int64_t>((tokens + kRbChunk - 1) / kRbChunk, (int64_t)sms * 2);
+  auto st = reinterpret_cast<cudaStream_t>(stream);
+  auto run = [&](auto kern) {
+    kern<<<blocks, threads, 0, st>>>(reinterpret_cast<const bf16*>(x), router_w, logits, chosen,
+                                     gate, d_gate, bal_grad,
+                                     reinterpret_cast<const bf16*>(d_grouped), pos, tokens,
+                                     (int)d, top_k, d_router_w, reinterpret_cast<bf16*>(d_x));
+  };
+  switch (experts) {
+    case 2: run(moe_route_bwd_kernel<2>); break;
+    case 4: run(moe_route_bwd_kernel<4>); break;
+    case 8: run(moe_route_bwd_kernel<8>); break;
+    case 16: run(moe_route_bwd_kernel<16>); break;
+    default: return GPTB200_EUNSUPPORTED;
+  }
   GPTB200_CHECK_LAUNCH();
   return 0;
 }
@@ -596,7 +610,7 @@ extern "C" int gptb200_moe_segment_colsum(const void* buf, const int32_t* seg, i
                                           int64_t width, float* out, void* stream) {
   if (!buf || !seg || !out || width <= 0) return GPTB200_EINVAL;
   if (experts < 1 || experts > kMoeMaxE) return GPTB200_EUNSUPPORTED;
-  dim3 grid((unsigned)((width + 255) / 256), (unsigned)experts, 16);
+  dim3 grid((unsigned)((width + 255) / 256), (unsigned)experts, 128);
   moe_seg_colsum_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<const bf16*>(buf), reinterpret_cast<const int2*>(seg), (int)width, out);
   GPTB200_CHECK_LAUNCH();

@@ -95,7 +95,7 @@ def gemm(
         a.data_ptr(), int(a_mn_major), lda, b.data_ptr(), int(b_mn_major), ldb,
         out.data_ptr(), ldc, m, n, k, ctypes.byref(epi), _stream(),
     )
-    if gemm_timer is not None:
+    if gemm_timer is not None and row_range is None:  # a range GEMM's work is device-side
         end = torch.cuda.Event(enable_timing=True)
         end.record()
         gemm_timer.append((start, end, 2.0 * m * n * k))

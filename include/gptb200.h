@@ -196,7 +196,7 @@ int gptb200_attention_bwd(const void* q, const void* k, const void* v, int64_t s
  * (gptb200_epilogue.row_range), so no host synchronisation is needed.
  * stats (fp32, per layer, accumulated): [0, E) router-probability sums,
  * [E, 2E) assignment counts, entropy sum, top-1 gate sum, sum of squared
- * logits. E <= 16, top_k <= 4. */
+ * logits. E <= 16, top_k <= 4; the backward supports E in {2, 4, 8, 16}. */
 size_t gptb200_moe_rows(int64_t tokens, int32_t top_k, int32_t experts);
 size_t gptb200_moe_dispatch_workspace_size(int64_t tokens, int32_t top_k, int32_t experts);
 /* logits fp32 [tokens, E] = x (bf16 [tokens, d], promoted to fp32) . router_w
