@@ -307,8 +307,6 @@ def main() -> None:
     ap.add_argument("--seed", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--eager", action="store_true", help="no CUDA graph replay")
-    ap.add_argument("--dp-graph", action="store_true",
-                    help="also replay the data-parallel step (kernels + NCCL) as a CUDA graph")
     ap.add_argument("--op", choices=["step", "attention", "lce", "gelu_gemm"], default="step",
                     help="op-level configuration instead of the training step (1 GPU)")
     args = ap.parse_args()
@@ -363,7 +361,7 @@ def main() -> None:
     clocks = ClockSampler(local)
     for i in range(args.warmup):
         trainer.train_step(*dev_batches[i])
-        if i == 0 and (world == 1 or args.dp_graph) and not args.eager:
+        if i == 0 and world == 1 and not args.eager:
             trainer.capture()  # after one eager step; replays the same launches
     clocks.wait_ready()
     barrier()

@@ -546,11 +546,11 @@ class GPTTrainer:
         warm-up step (which also sets every kernel's shared-memory attribute)
         the graph replays the identical launch sequence; the batch is read from
         `self.tokens` / `self.targets` and the step counter lives on the device.
-        With data parallelism the bucketed NCCL all-reduces are captured with
-        the kernels (every rank records the same sequence, so replays stay
-        matched across ranks).
+        Single-process only: with data parallelism the step runs eagerly.
         """
 
+        if self.world_size != 1:
+            raise ValueError("graph capture is used for the single-GPU step only")
         side = torch.cuda.Stream(self.device)
         side.wait_stream(torch.cuda.current_stream(self.device))
         graph = torch.cuda.CUDAGraph()
