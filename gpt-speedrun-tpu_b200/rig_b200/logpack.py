@@ -26,10 +26,13 @@ SUFFIX = ".riglog"
 
 # Permanent registry ids of rig/metrics.py (add-only upstream).
 METRIC_IDS = {"step": 1, "tokens_processed": 2, "cumulative_flops": 3, "train_loss": 4,
-              "learning_rate": 5, "grad_norm": 6}
-# scope name -> (id, layered)
-SCOPE_IDS = {"overall": (1, False), "embeddings": (2, False), "unembedding": (3, False),
-             "block": (4, True), "final_norm": (5, False)}
+              "learning_rate": 5, "grad_norm": 6, "router.balance_loss": 7,
+              "router.max_load": 8, "router.min_load": 9, "router.load": 10,
+              "router.entropy": 11, "router.top1_gate": 12, "router.logit_rms": 13}
+# scope name -> (id, layered, indexed); "expert" is one routed expert of one block
+SCOPE_IDS = {"overall": (1, False, False), "embeddings": (2, False, False),
+             "unembedding": (3, False, False), "block": (4, True, False),
+             "final_norm": (5, False, False), "expert": (6, True, True)}
 
 _HEADER = struct.Struct("<i4xqd")          # column_count, pad, tokens_per_step, flops_per_token
 _ENTRY = struct.Struct("<iiiiq")           # metric, scope, layer, index, element_count
@@ -46,18 +49,22 @@ class Column:
 
 
 def column(metric_name: str, scope_name: str = "overall", layer: int | None = None,
-           element_count: int = 0) -> Column:
+           element_count: int = 0, index: int | None = None) -> Column:
     if metric_name not in METRIC_IDS:
         raise KeyError(f"unregistered metric {metric_name!r}")
     if scope_name not in SCOPE_IDS:
         raise KeyError(f"unregistered scope {scope_name!r}")
-    scope_id, layered = SCOPE_IDS[scope_name]
+    scope_id, layered, indexed = SCOPE_IDS[scope_name]
     if layered and layer is None:
         raise ValueError(f"scope {scope_name!r} requires a layer index")
     if not layered and layer is not None:
         raise ValueError(f"scope {scope_name!r} does not take a layer index")
-    return Column(METRIC_IDS[metric_name], scope_id, -1 if layer is None else int(layer), -1,
-                  int(element_count))
+    if indexed and index is None:
+        raise ValueError(f"scope {scope_name!r} requires a second index")
+    if not indexed and index is not None:
+        raise ValueError(f"scope {scope_name!r} does not take a second index")
+    return Column(METRIC_IDS[metric_name], scope_id, -1 if layer is None else int(layer),
+                  -1 if index is None else int(index), int(element_count))
 
 
 class LogWriter:

@@ -584,9 +584,14 @@ class GPTTrainer:
 
     # ------------------------------------------------------------ artifacts
     def training_history(self, final_step: int) -> np.ndarray:
-        """Rows 1..final_step of the on-device (loss, lr, grad_norm) history."""
+        """Rows 1..final_step of the on-device (loss, lr, grad_norm) history,
+        followed for a routed model by that step's router statistics row
+        (the column order of `runlog.training_log_columns`)."""
 
-        return self.history[:final_step].detach().cpu().numpy().astype(np.float32)
+        rows = self.history[:final_step]
+        if self.config.experts:
+            rows = torch.cat((rows, self.router_history[:final_step]), dim=1)
+        return rows.detach().cpu().numpy().astype(np.float32)
 
     def save_checkpoint(self, output_dir, seed: int) -> None:
         """checkpoint.npz in the rig's layout (fp32 master parameters)."""
@@ -601,9 +606,12 @@ class GPTTrainer:
 
         from . import runlog
 
+        c = self.config
+        columns = runlog.training_log_columns(c.layers if c.experts else 0, c.experts)
         runlog.write_training_log(output_dir, self.training_history(final_step),
-                                  tokens_per_step=self.config.batch_size * self.T,
-                                  final_step=final_step, flops_per_token=flops_per_token)
+                                  tokens_per_step=c.batch_size * self.T,
+                                  final_step=final_step, flops_per_token=flops_per_token,
+                                  columns=columns)
 
     graph: "torch.cuda.CUDAGraph | None" = None
     graph_launches: int = 0  # libgptb200 kernels inside one replay

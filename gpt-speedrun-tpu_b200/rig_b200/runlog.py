@@ -8,8 +8,9 @@ verification tools read a B200 run like one of their own.
   description as UTF-8 JSON bytes under `metadata.json`; it is written to a
   temporary file, fsynced and renamed, so a reader never sees a partial file.
 * The training log has three `overall` columns, `train_loss`,
-  `learning_rate`, `grad_norm`: one record per optimizer step 1..final_step,
-  exactly the rows of the on-device history the AdamW kernel fills.
+  `learning_rate`, `grad_norm`, plus, for a routed (MoE) model, the router
+  statistics columns: one record per optimizer step 1..final_step, exactly the
+  rows of the on-device histories the AdamW and router kernels fill.
 """
 
 from __future__ import annotations
@@ -85,9 +86,27 @@ def load_checkpoint(path: pathlib.Path) -> tuple[dict[str, np.ndarray], dict[str
     return flat, meta
 
 
-def training_log_columns() -> tuple[logpack.Column, ...]:
-    return (logpack.column("train_loss"), logpack.column("learning_rate"),
-            logpack.column("grad_norm"))
+ROUTER_SUMMARY_METRICS = ("router.entropy", "router.top1_gate", "router.logit_rms")
+
+
+def training_log_columns(routing_layers: int = 0, experts: int = 0) -> tuple[logpack.Column, ...]:
+    """The per-step columns in the order of the history rows
+    (rig/runlog.py:133-174): loss, learning rate, gradient norm; a routed run
+    appends the balance loss, the max / min expert load and the three router
+    summaries averaged over layers, then per layer its three summaries and its
+    per-expert load vector (scope "expert", indexed by expert)."""
+
+    cols = [logpack.column("train_loss"), logpack.column("learning_rate"),
+            logpack.column("grad_norm")]
+    if not routing_layers:
+        return tuple(cols)
+    cols += [logpack.column("router.balance_loss"), logpack.column("router.max_load"),
+             logpack.column("router.min_load")]
+    cols += [logpack.column(name) for name in ROUTER_SUMMARY_METRICS]
+    for layer in range(routing_layers):
+        cols += [logpack.column(name, "block", layer) for name in ROUTER_SUMMARY_METRICS]
+        cols += [logpack.column("router.load", "expert", layer, index=e) for e in range(experts)]
+    return tuple(cols)
 
 
 def write_training_log(output_dir: pathlib.Path, history: np.ndarray, *, tokens_per_step: int,

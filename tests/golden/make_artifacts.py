@@ -1,6 +1,9 @@
 """Writes tests/golden/training_smoke.riglog with the reference's own
 rig/logpack.py (the training-log columns of rig/runlog.py:132-156) from a fixed
-synthetic history, plus the registry ids it resolves. Run in a checkout where
+synthetic history, and tests/golden/training_moe.riglog with the routed-model
+columns (rig/runlog.py:152-173, restated here in the same order because
+rig/runlog.py itself imports jax) for 2 layers x 4 experts, plus the registry
+ids they resolve. Run in a checkout where
 the reference project is importable (its logpack/metrics modules need only numpy):
 
     python tests/golden/make_artifacts.py /path/to/GPT-speedrun-TPU
@@ -24,6 +27,18 @@ def history() -> np.ndarray:
     return h
 
 
+MOE_LAYERS, MOE_EXPERTS = 2, 4
+ROUTER_SUMMARY = ("router.entropy", "router.top1_gate", "router.logit_rms")
+
+
+def moe_history() -> np.ndarray:
+    rng = np.random.default_rng(11)
+    width = 3 + 6 + MOE_LAYERS * (3 + MOE_EXPERTS)
+    h = np.abs(rng.standard_normal((20, width))).astype(np.float32)
+    h[:, :3] = history()
+    return h
+
+
 def main(ref_root: str) -> None:
     sys.path.insert(0, ref_root)
     from rig import logpack, metrics  # noqa: E402  (the reference's modules)
@@ -34,8 +49,23 @@ def main(ref_root: str) -> None:
     with logpack.LogWriter(out, cols, tokens_per_step=2048, flops_per_token=123456789.0) as w:
         for step, row in enumerate(history(), 1):
             w.append(step, row)
-    ids = {name: metrics.metric(name).id for name in ("train_loss", "learning_rate", "grad_norm")}
-    ids["scope.overall"] = metrics.scope("overall").id
+    moe_cols = cols + [logpack.column("router.balance_loss"), logpack.column("router.max_load"),
+                       logpack.column("router.min_load")]
+    moe_cols += [logpack.column(name) for name in ROUTER_SUMMARY]
+    for layer in range(MOE_LAYERS):
+        moe_cols += [logpack.column(name, "block", layer) for name in ROUTER_SUMMARY]
+        moe_cols += [logpack.column("router.load", "expert", layer, index=e)
+                     for e in range(MOE_EXPERTS)]
+    moe_out = HERE / "training_moe.riglog"
+    with logpack.LogWriter(moe_out, moe_cols, tokens_per_step=4096,
+                           flops_per_token=987654321.0) as w:
+        for step, row in enumerate(moe_history(), 1):
+            w.append(step, row)
+    names = ("train_loss", "learning_rate", "grad_norm", "router.balance_loss", "router.max_load",
+             "router.min_load", "router.load", *ROUTER_SUMMARY)
+    ids = {name: metrics.metric(name).id for name in names}
+    for scope in ("overall", "block", "expert"):
+        ids["scope." + scope] = metrics.scope(scope).id
     (HERE / "riglog_ids.json").write_text(json.dumps(ids, sort_keys=True) + "\n")
     print(f"wrote {out} ({out.stat().st_size} bytes) and riglog_ids.json")
 

@@ -16,20 +16,55 @@ from rig_b200.model import init_params
 GOLDEN = pathlib.Path(__file__).resolve().parent / "golden"
 
 
-def _history():
+def _maker():
     import importlib.util
 
     spec = importlib.util.spec_from_file_location("make_artifacts", GOLDEN / "make_artifacts.py")
     mod = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(mod)
-    return mod.history()
+    return mod
+
+
+def _history():
+    return _maker().history()
 
 
 def test_registry_ids_match_reference():
     ids = json.loads((GOLDEN / "riglog_ids.json").read_text())
-    for name in ("train_loss", "learning_rate", "grad_norm"):
-        assert logpack.METRIC_IDS[name] == ids[name]
-    assert logpack.SCOPE_IDS["overall"][0] == ids["scope.overall"]
+    for name, value in ids.items():
+        if name.startswith("scope."):
+            assert logpack.SCOPE_IDS[name[len("scope."):]][0] == value, name
+        else:
+            assert logpack.METRIC_IDS[name] == value, name
+
+
+def test_routed_training_log_bytes_match_reference_writer(tmp_path):
+    """A routed model's log: the router statistics columns after the dense
+    three, per layer the summaries and the per-expert load (scope "expert")."""
+
+    mk = _maker()
+    cols = runlog.training_log_columns(mk.MOE_LAYERS, mk.MOE_EXPERTS)
+    assert len(cols) == 3 + 6 + mk.MOE_LAYERS * (3 + mk.MOE_EXPERTS)
+    runlog.write_training_log(tmp_path, mk.moe_history(), tokens_per_step=4096, final_step=20,
+                              flops_per_token=987654321.0, columns=cols)
+    ours = (tmp_path / runlog.TRAINING_LOG_NAME).read_bytes()
+    assert ours == (GOLDEN / "training_moe.riglog").read_bytes()
+    log = logpack.read_log(GOLDEN / "training_moe.riglog")
+    assert log.columns == cols
+    loads = [c for c in log.columns if c.scope_id == logpack.SCOPE_IDS["expert"][0]]
+    assert [(c.layer, c.index) for c in loads] == [(l, e) for l in range(mk.MOE_LAYERS)
+                                                  for e in range(mk.MOE_EXPERTS)]
+
+
+def test_column_scope_rules():
+    with pytest.raises(ValueError):
+        logpack.column("router.load", "expert", 0)  # expert scope needs an index
+    with pytest.raises(ValueError):
+        logpack.column("router.entropy", "block", 0, index=1)
+    with pytest.raises(ValueError):
+        logpack.column("router.entropy", "block")
+    with pytest.raises(KeyError):
+        logpack.column("router.unknown")
 
 
 def test_training_log_bytes_match_reference_writer(tmp_path):

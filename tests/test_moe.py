@@ -89,8 +89,9 @@ def test_router_statistics_row(cuda):
         assert abs(per[3:].sum() - 1.0) < 1e-6  # every assignment counted once
 
 
-def test_moe_steps_train(cuda):
-    """A few optimizer steps stay finite and the loss drops (graph capture too)."""
+def test_moe_steps_train(cuda, tmp_path):
+    """A few optimizer steps stay finite and the loss drops (graph capture too);
+    the training log carries the router statistics columns of every step."""
 
     cfg = _cfg()
     tr = GPTTrainer(cfg, cfg.batch_size, cuda)
@@ -105,6 +106,18 @@ def test_moe_steps_train(cuda):
     h = tr.history[:6, 0].cpu().numpy()
     assert np.all(np.isfinite(h)) and h[-1] < h[0], h
     assert ops.device_error() == 0
+    from rig_b200 import logpack, runlog
+
+    tr.write_training_log(tmp_path, 6)
+    log = logpack.read_log(tmp_path / runlog.TRAINING_LOG_NAME)
+    assert log.columns == runlog.training_log_columns(cfg.layers, cfg.experts)
+    want = np.concatenate((tr.history[:6].cpu().numpy(), tr.router_history[:6].cpu().numpy()), 1)
+    np.testing.assert_array_equal(log.values, want)
+    assert np.all(log.values[:, 3] > 0)  # the balance loss of every step
+    E = cfg.experts
+    for layer in range(cfg.layers):
+        c0 = 9 + layer * (3 + E) + 3
+        np.testing.assert_allclose(log.values[:, c0:c0 + E].sum(1), 1.0, atol=1e-5)
 
 
 def test_routed_mlp_op(cuda):
