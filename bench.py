@@ -198,7 +198,7 @@ def run_reference(args, cfg, rank: int, world: int) -> None:
 def run_op(args) -> None:
     """Op-level configurations of the same kernels (one GPU, rank 0):
 
-    * attention: SURVEY config 3 -- q, k, v, dO [16, 12, 1024, 64] bf16 ~ N(0, 1)
+    * attention: benchmark config 3 -- q, k, v, dO [16, 12, 1024, 64] bf16 ~ N(0, 1)
       (seeds 0..2), RoPE on q and k, scale 1/64; one step = forward + backward;
       algorithmic FLOPs (causal) 6 B H T^2 D = 7.73e10 per step.
     * lce: config 2 -- hidden [65536, 768] bf16 ~ N(0, 1), embedding
