@@ -307,6 +307,8 @@ def main() -> None:
     ap.add_argument("--seed", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--eager", action="store_true", help="no CUDA graph replay")
+    ap.add_argument("--atomic-wgrad", action="store_true",
+                    help="fp32 atomics for split-K weight gradients (not bit-reproducible)")
     ap.add_argument("--op", choices=["step", "attention", "lce", "gelu_gemm"], default="step",
                     help="op-level configuration instead of the training step (1 GPU)")
     args = ap.parse_args()
@@ -342,7 +344,8 @@ def main() -> None:
     dev_batches = [(x.to(device), y.to(device)) for x, y in pinned[: args.warmup + args.steps]]
 
     trainer = GPTTrainer(cfg, local_batch, device, process_group=None, world_size=world,
-                         history_steps=max(cfg.steps, total_steps + 1))
+                         history_steps=max(cfg.steps, total_steps + 1),
+                         deterministic=not args.atomic_wgrad)
     trainer.load_params(init_params(cfg, args.seed))
     torch.cuda.synchronize()
 
@@ -446,6 +449,7 @@ def main() -> None:
                             + (f", {cfg.experts} experts top-{cfg.expert_top_k}"
                                if cfg.experts else ""), "global_batch": cfg.batch_size,
                    "seq_len": cfg.seq_len, "parallelism": f"dp{world}",
+                   "bit_reproducible": trainer.deterministic,
                    "l2": "working set (activations ~40 GB/GPU at dp1) far larger than L2"},
         "mfu": mfu, "mfu_peak_tflops": peaks["bf16"], "mfu_peak_source": peaks["source"],
         "mfu_vs_nominal_2250": value * fpt / (world * NOMINAL_BF16_TFLOPS * 1e12),

@@ -33,19 +33,6 @@ namespace gptb200 {
 
 static __device__ int g_attn_error;
 
-#ifdef GPTB200_TRACE
-// Per-phase clock stamps of CTA (0, 0), for performance diagnostics builds.
-__device__ long long g_attn_trace[4096];
-#define ATTN_TRACE(slot)                                                  \
-  do {                                                                    \
-    if (blockIdx.x == 0 && blockIdx.y == 0 && (slot) < 4096)              \
-      g_attn_trace[(slot)] = clock64();                                   \
-  } while (0)
-#else
-#define ATTN_TRACE(slot) \
-  do {                   \
-  } while (0)
-#endif
 
 constexpr int HD = 64;
 constexpr float kLog2e = 1.4426950408889634f;
@@ -292,13 +279,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                          err) ||
               !mbar_wait(&s_free[x], j & 1, abort_flag, err))
             break;
-          ATTN_TRACE(2048 + 32 * j + 8 * x + 0);
           tc_fence_after();
           issue_s(j + 1);
-          ATTN_TRACE(2048 + 32 * j + 8 * x + 1);
         }
         if (!mbar_wait(&p_full[x], j & 1, abort_flag, err)) break;
-        ATTN_TRACE(2048 + 32 * j + 8 * x + 2);
         tc_fence_after();
         const uint32_t sV = smem_u32(sm + FwdSmem::V + (j % kKvStages) * KV_BYTES);
         // O_x += P_x V_j, P read from TMEM (keys 16k..16k+15 at column 8k)
@@ -331,12 +315,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     int nseg = 0;  // blocks of this tile that needed the per-element test so far
     bool ok = true;
     for (int j = 0; j < nb && ok; ++j) {
-      if ((threadIdx.x & 127) == 64) ATTN_TRACE(2048 + 32 * j + 8 * x + 3);
       if (!mbar_wait(&s_full[x], j & 1, abort_flag, err)) {
         ok = false;
         break;
       }
-      if ((threadIdx.x & 127) == 64) ATTN_TRACE(2048 + 32 * j + 8 * x + 4);
       tc_fence_after();
       const int jb = blist[j];
       const bool diag = (jb == d0 + x);  // keys past the query (and past T) are masked
@@ -364,7 +346,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_free[x]);
-      if ((threadIdx.x & 127) == 64) ATTN_TRACE(2048 + 32 * j + 8 * x + 5);
       // Row max of the raw scores (c > 0 commutes with the max), eight
       // independent chains; on the diagonal block keys past the query are out.
       float m8[8];
@@ -396,7 +377,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         alpha = m_new == -INFINITY ? 1.f : ex2(m_used - m_new);
         m_used = m_new;
       }
-      if ((threadIdx.x & 127) == 64) ATTN_TRACE(2048 + 32 * j + 8 * x + 6);
       // P = exp2(s*c - m) packed to bf16 pairs in registers (the S registers
       // die as P is produced); four packed partial row sums.
       const float2 c2 = make_float2(c, c), nm2 = make_float2(-m_used, -m_used);
@@ -442,7 +422,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[x]);
-      if ((threadIdx.x & 127) == 64) ATTN_TRACE(2048 + 32 * j + 8 * x + 7);
     }
     if (ok && nb > 0 && mbar_wait(&pv_done[x], (nb - 1) & 1, abort_flag, err)) {
       tc_fence_after();
@@ -600,7 +579,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       for (int it = 0; it < nq; ++it) {
         const int bb = it % 3, s = it % kQStages;
         if (!mbar_wait(&p_full[bb], (it / 3) & 1, abort_flag, err)) break;
-        ATTN_TRACE(64 * it + 2);
         tc_fence_after();
         const uint32_t sQ = smem_u32(sm + BwdSmem::Q + s * BQ_BYTES);
         const uint32_t sDO = smem_u32(sm + BwdSmem::DO + s * BQ_BYTES);
@@ -616,7 +594,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                        (it > 0 || k > 0));
         }
         umma_commit(&q_empty[s]);
-        ATTN_TRACE(64 * it + 7);
         if ((it & 1) || it == nq - 1) {
           // dQ of query pair j (tiles 2j, 2j+1) = dS K into the dP^T half of
           // this buffer: A = the pair's two dS^T tiles of the ring read
@@ -630,7 +607,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           umma_commit(&dq_full[j & 1]);
         }
         umma_commit(&done[it & 3]);
-        ATTN_TRACE(64 * it + 3);
       }
       umma_commit(fin);
     }
@@ -645,15 +621,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       bool ok = mbar_wait(kv_full, 0, abort_flag, err);
       for (int it = 0; ok && it < nq; ++it) {
         const int s = it % kQStages;
-        ATTN_TRACE(64 * it + 0);
         if (it >= 3) {
           const int o = it - 3;
           if (!mbar_wait(&done[o & 3], (o >> 2) & 1, abort_flag, err)) break;
           if ((o & 1) && !mbar_wait(&dq_free[(o >> 1) & 1], (o >> 2) & 1, abort_flag, err)) break;
         }
-        ATTN_TRACE(64 * it + 4);
         if (!mbar_wait(&q_full[s], (it / kQStages) & 1, abort_flag, err)) break;
-        ATTN_TRACE(64 * it + 6);
         tc_fence_after();
         const uint32_t sQ = smem_u32(sm + BwdSmem::Q + s * BQ_BYTES);
         const uint32_t sDO = smem_u32(sm + BwdSmem::DO + s * BQ_BYTES);
@@ -667,7 +640,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
         umma_commit(&s_full[it % 3]);
         umma_commit(&q_empty[s]);
-        ATTN_TRACE(64 * it + 1);
       }
     }
   } else if (warp < 2 + 2 * kBwdWgWarps) {
@@ -735,7 +707,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       stat_seg[lane] = ns;
       __syncwarp();
       if (it + 2 < nq) fetch(it + 2, nl, nd, ns);
-      if (threadIdx.x == 64) ATTN_TRACE(64 * it + 11);
       if (!mbar_wait(&s_full[bb], (it / 3) & 1, abort_flag, err)) {
         ok = false;
         break;
@@ -745,7 +716,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         ok = false;
         break;
       }
-      if (threadIdx.x == 64) ATTN_TRACE(64 * it + 12);
       tc_fence_after();
       uint32_t sraw[32], draw[32];
       tmem_ld32_nw(tb + lane_off + hf * 32, sraw);
@@ -790,7 +760,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[bb]);
-      if (threadIdx.x == 64) ATTN_TRACE(64 * it + 13);
       if (wg == 0 && it >= 2) {
         // query pair j = (it-2, it-1) was closed by the previous tile of the
         // other warpgroup; its dQ MMA has had a whole softmax tile to finish
@@ -910,12 +879,6 @@ __global__ void attn_dq_store_kernel(const float* __restrict__ dq_acc, bf16* __r
     *reinterpret_cast<uint4*>(dq + b * sb + h * sh + (int64_t)t * st + c * 8) = q;
   }
 }
-
-#ifdef GPTB200_TRACE
-extern "C" int gptb200_attention_trace(long long* out, int n) {
-  return (int)cudaMemcpyFromSymbol(out, g_attn_trace, sizeof(long long) * (n < 4096 ? n : 4096));
-}
-#endif
 
 int attention_read_error(int clear) {
   int hv = 0;

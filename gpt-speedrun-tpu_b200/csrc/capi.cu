@@ -6,6 +6,8 @@
 
 namespace gptb200 {
 int attention_read_error(int clear);
+int embed_read_error(int clear);
+int optim_read_error(int clear);
 static std::atomic<uint64_t> g_launches{0};
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 }  // namespace gptb200
@@ -31,9 +33,16 @@ extern "C" const char* gptb200_status_string(int status) {
   }
 }
 
-extern "C" int gptb200_device_error(int clear) {
+extern "C" int gptb200_device_error_flags(int clear) {
   cudaDeviceSynchronize();
-  int e = gptb200::gemm_read_error(clear);
-  e |= gptb200::attention_read_error(clear);
-  return e ? GPTB200_EDEVICE : GPTB200_OK;
+  int f = 0;
+  if (gptb200::gemm_read_error(clear)) f |= GPTB200_DEVERR_GEMM;
+  if (gptb200::attention_read_error(clear)) f |= GPTB200_DEVERR_ATTENTION;
+  if (gptb200::embed_read_error(clear)) f |= GPTB200_DEVERR_TOKEN_RANGE;
+  if (gptb200::optim_read_error(clear)) f |= GPTB200_DEVERR_NONFINITE;
+  return f;
+}
+
+extern "C" int gptb200_device_error(int clear) {
+  return gptb200_device_error_flags(clear) ? GPTB200_EDEVICE : GPTB200_OK;
 }

@@ -22,6 +22,8 @@ enum {
   kErrNone = 0,
   kErrWaitTimeout = 1,   // an mbarrier wait ran out of time
   kErrTmemAlloc = 2,     // TMEM allocation returned an unexpected address
+  kErrTokenRange = 3,    // a token id outside [0, vocab) reached the embedding gather
+  kErrNonFinite = 4,     // the loss or the gradient norm is NaN or infinite
 };
 
 // Time limit of one mbarrier wait (nanoseconds of %globaltimer). Far above any

@@ -1,5 +1,5 @@
 // Memory-bound kernels of the step: RMSNorm forward/backward, embedding
-// gather/scatter, RoPE tables, bias-gradient column sums and the fp32->bf16
+// gather (the scatter is in embedding.cu), RoPE tables, bias-gradient column sums and the fp32->bf16
 // cast. All of them move 16-byte vectors (8 bf16 / 4 fp32) per thread access,
 // reduce with warp shuffles and size their grids from the SM count.
 #include <algorithm>
@@ -83,8 +83,8 @@ __global__ void __launch_bounds__(256) rms_fwd_kernel(const bf16* __restrict__ x
 template <int CH>
 __global__ void __launch_bounds__(128, 6) rms_bwd_kernel(
     const bf16* __restrict__ x, const bf16* __restrict__ scale, const float* __restrict__ rstd_in,
-    const bf16* __restrict__ dy, const bf16* dx_in, bf16* dx_out, float* __restrict__ dscale,
-    float* __restrict__ dcol, float col_alpha, int64_t rows, int d) {
+    const bf16* __restrict__ dy, const bf16* dx_in, bf16* dx_out, float* __restrict__ part,
+    bool want_col, int64_t rows, int d) {
   extern __shared__ float red[];  // [2][warps_per_block][d]: dscale, then column sums of dx_out
   const int lane = threadIdx.x & 31;
   const int wib = threadIdx.x >> 5;
@@ -164,7 +164,7 @@ __global__ void __launch_bounds__(128, 6) rms_bwd_kernel(
           ow[j] = pack_bf16x2(v0, v1);
         }
         *reinterpret_cast<uint4*>(dx_out + r * d + ch * 8) = o;
-        if (dcol) {  // column sums of the stored (bf16) gradient, for a bias gradient
+        if (want_col) {  // column sums of the stored (bf16) gradient, for a bias gradient
           float4* cs = reinterpret_cast<float4*>(mycol + ch * 8);
           float4 c0 = cs[0], c1 = cs[1];
           float f[8];
@@ -178,17 +178,61 @@ __global__ void __launch_bounds__(128, 6) rms_bwd_kernel(
       }
     }
   }
-  // Reduce the per-warp dscale partials inside the block, then one atomic per column.
+  // Reduce the per-warp partials inside the block (warp order) and store the
+  // block's row: part[block][0][:] = dscale partial, part[block][1][:] = column
+  // sums. colred_kernel adds the rows in block order, so the result does not
+  // depend on which block finished first.
   __syncthreads();
+  float* prow = part + (int64_t)blockIdx.x * 2 * d;
   for (int col = threadIdx.x; col < d; col += blockDim.x) {
     float s = 0.f, c = 0.f;
     for (int w = 0; w < wpb; ++w) {
       s += red[w * d + col];
       c += red[(wpb + w) * d + col];
     }
-    atomicAdd(dscale + col, s);
-    if (dcol) atomicAdd(dcol + col, col_alpha * c);
+    prow[col] = s;
+    prow[d + col] = c;
   }
+}
+
+// out_j[c] += alpha_j * sum_p part[p * pstride + j * n + c] for j < nout,
+// summed in a fixed order: thread row y adds partials y, y + 16, ... in turn,
+// then the 16 row sums are added in y order. Block = 32 columns x 16 rows.
+__global__ void __launch_bounds__(512) colred_kernel(const float* __restrict__ part, int nparts,
+                                                     int64_t pstride, int n, float* out0,
+                                                     float alpha0, float* out1, float alpha1) {
+  __shared__ float red[16][33];
+  const int c = blockIdx.x * 32 + threadIdx.x;
+  const int j = blockIdx.y;  // 0: out0, 1: out1
+  float s = 0.f;
+  if (c < n) {
+    const float* src = part + (int64_t)j * n + c;
+    int p = threadIdx.y;
+#pragma unroll 4
+    for (; p < nparts; p += 16) s += __ldg(src + (int64_t)p * pstride);
+  }
+  red[threadIdx.y][threadIdx.x] = s;
+  __syncthreads();
+  if (threadIdx.y == 0 && c < n) {
+    float t = 0.f;
+#pragma unroll
+    for (int y = 0; y < 16; ++y) t += red[y][threadIdx.x];
+    if (j == 0) out0[c] += alpha0 * t;
+    else out1[c] += alpha1 * t;
+  }
+}
+
+static int colred_launch(const float* part, int nparts, int64_t pstride, int n, float* out0,
+                         float alpha0, float* out1, float alpha1, cudaStream_t st) {
+  dim3 grid((n + 31) / 32, out1 ? 2 : 1), block(32, 16);
+  colred_kernel<<<grid, block, 0, st>>>(part, nparts, pstride, n, out0, alpha0, out1, alpha1);
+  GPTB200_CHECK_LAUNCH();
+  return 0;
+}
+
+// Blocks of the RMSNorm backward: each ends in one row of 2 x d partials.
+static int64_t rms_bwd_blocks(int64_t rows) {
+  return std::min<int64_t>((rows + 3) / 4, (int64_t)sms() * 4);
 }
 
 template <int CH>
@@ -203,20 +247,19 @@ static int rms_fwd_launch(const bf16* x, const bf16* s, bf16* y, float* rstd, in
 template <int CH>
 static int rms_bwd_launch(const bf16* x, const bf16* s, const float* rstd, const bf16* dy,
                           const bf16* dxi, bf16* dxo, float* dscale, float* dcol, float col_alpha,
-                          int64_t rows, int d, cudaStream_t st) {
+                          int64_t rows, int d, float* part, cudaStream_t st) {
   const int threads = 128;
-  // Each block ends in 2 x d column atomics, so blocks stay few (4 per SM).
-  int64_t blocks = std::min<int64_t>((rows + 3) / 4, (int64_t)sms() * 4);
+  const int64_t blocks = rms_bwd_blocks(rows);
   size_t smem = 2 * (size_t)(threads / 32) * d * sizeof(float);
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(rms_bwd_kernel<CH>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return -static_cast<int>(e);
   }
-  rms_bwd_kernel<CH><<<(int)blocks, threads, smem, st>>>(x, s, rstd, dy, dxi, dxo, dscale, dcol,
-                                                       col_alpha, rows, d);
+  rms_bwd_kernel<CH><<<(int)blocks, threads, smem, st>>>(x, s, rstd, dy, dxi, dxo, part,
+                                                       dcol != nullptr, rows, d);
   GPTB200_CHECK_LAUNCH();
-  return 0;
+  return colred_launch(part, (int)blocks, 2 * (int64_t)d, d, dscale, 1.f, dcol, col_alpha, st);
 }
 
 }  // namespace gptb200
@@ -242,11 +285,16 @@ extern "C" int gptb200_rms_norm_fwd(const void* x, const void* scale, void* y, f
   return rms_fwd_launch<16>(X, S, Y, rstd, rows, (int)d, st);
 }
 
+extern "C" size_t gptb200_rms_norm_bwd_workspace_size(int64_t rows, int64_t d) {
+  if (rows <= 0 || d <= 0) return 0;
+  return (size_t)rms_bwd_blocks(rows) * 2 * (size_t)d * sizeof(float);
+}
+
 extern "C" int gptb200_rms_norm_bwd(const void* x, const void* scale, const float* rstd,
                                     const void* dy, const void* dx_in, void* dx_out,
                                     float* dscale, float* dx_colsum, float colsum_alpha,
-                                    int64_t rows, int64_t d, void* stream) {
-  if (!x || !scale || !rstd || !dy || !dx_out || !dscale || rows <= 0 || d <= 0)
+                                    int64_t rows, int64_t d, void* workspace, void* stream) {
+  if (!x || !scale || !rstd || !dy || !dx_out || !dscale || !workspace || rows <= 0 || d <= 0)
     return GPTB200_EINVAL;
   if (d % 8 || d > 2048 || !aligned16(x) || !aligned16(dy) || !aligned16(dx_out) ||
       (dx_in && !aligned16(dx_in)))
@@ -257,12 +305,13 @@ extern "C" int gptb200_rms_norm_bwd(const void* x, const void* scale, const floa
   auto DY = reinterpret_cast<const bf16*>(dy);
   auto DXI = reinterpret_cast<const bf16*>(dx_in);
   auto DXO = reinterpret_cast<bf16*>(dx_out);
+  auto W = reinterpret_cast<float*>(workspace);
   int ch = (int)((d / 8 + 31) / 32);
-  if (ch <= 1) return rms_bwd_launch<1>(X, S, rstd, DY, DXI, DXO, dscale, dx_colsum, colsum_alpha, rows, (int)d, st);
-  if (ch <= 2) return rms_bwd_launch<2>(X, S, rstd, DY, DXI, DXO, dscale, dx_colsum, colsum_alpha, rows, (int)d, st);
-  if (ch <= 3) return rms_bwd_launch<3>(X, S, rstd, DY, DXI, DXO, dscale, dx_colsum, colsum_alpha, rows, (int)d, st);
-  if (ch <= 4) return rms_bwd_launch<4>(X, S, rstd, DY, DXI, DXO, dscale, dx_colsum, colsum_alpha, rows, (int)d, st);
-  return rms_bwd_launch<8>(X, S, rstd, DY, DXI, DXO, dscale, dx_colsum, colsum_alpha, rows, (int)d, st);
+  if (ch <= 1) return rms_bwd_launch<1>(X, S, rstd, DY, DXI, DXO, dscale, dx_colsum, colsum_alpha, rows, (int)d, W, st);
+  if (ch <= 2) return rms_bwd_launch<2>(X, S, rstd, DY, DXI, DXO, dscale, dx_colsum, colsum_alpha, rows, (int)d, W, st);
+  if (ch <= 3) return rms_bwd_launch<3>(X, S, rstd, DY, DXI, DXO, dscale, dx_colsum, colsum_alpha, rows, (int)d, W, st);
+  if (ch <= 4) return rms_bwd_launch<4>(X, S, rstd, DY, DXI, DXO, dscale, dx_colsum, colsum_alpha, rows, (int)d, W, st);
+  return rms_bwd_launch<8>(X, S, rstd, DY, DXI, DXO, dscale, dx_colsum, colsum_alpha, rows, (int)d, W, st);
 }
 
 // ------------------------------------------------------------------ document segments
@@ -306,6 +355,8 @@ extern "C" int gptb200_document_segments(const int32_t* tokens, int64_t batch, i
 }
 
 // ------------------------------------------------------------------ embedding
+static __device__ int g_embed_error;
+
 __global__ void embed_fwd_kernel(const int32_t* __restrict__ tok, const bf16* __restrict__ table,
                                  bf16* __restrict__ out, int64_t n, int d, int64_t vocab) {
   const int nch = d >> 3;
@@ -315,27 +366,12 @@ __global__ void embed_fwd_kernel(const int32_t* __restrict__ tok, const bf16* __
     int64_t r = i / nch;
     int c = (int)(i - r * nch);
     int64_t t = tok[r];
-    t = t < 0 ? 0 : (t >= vocab ? vocab - 1 : t);
+    if (t < 0 || t >= vocab) {
+      if (c == 0) atomicCAS(&g_embed_error, 0, kErrTokenRange);
+      t = t < 0 ? 0 : vocab - 1;
+    }
     *reinterpret_cast<uint4*>(out + r * d + c * 8) =
         *reinterpret_cast<const uint4*>(table + t * d + c * 8);
-  }
-}
-
-__global__ void embed_bwd_kernel(const int32_t* __restrict__ tok, const bf16* __restrict__ dout,
-                                 float* __restrict__ dtable, int64_t n, int d, int64_t vocab) {
-  const int nch = d >> 2;
-  const int64_t total = n * nch;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    int64_t r = i / nch;
-    int c = (int)(i - r * nch);
-    int64_t t = tok[r];
-    if (t < 0 || t >= vocab) continue;
-    uint2 q = *reinterpret_cast<const uint2*>(dout + r * d + c * 4);
-    float a, b, e, f;
-    unpack_bf16x2(q.x, a, b);
-    unpack_bf16x2(q.y, e, f);
-    atomicAdd(reinterpret_cast<float4*>(dtable + t * d + c * 4), make_float4(a, b, e, f));
   }
 }
 
@@ -347,18 +383,6 @@ extern "C" int gptb200_embedding_fwd(const int32_t* tokens, const void* table, v
   int blocks = (int)std::min<int64_t>((total + 255) / 256, (int64_t)sms() * 16);
   embed_fwd_kernel<<<blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       tokens, reinterpret_cast<const bf16*>(table), reinterpret_cast<bf16*>(out), n, (int)d, vocab);
-  GPTB200_CHECK_LAUNCH();
-  return 0;
-}
-
-extern "C" int gptb200_embedding_bwd(const int32_t* tokens, const void* dout, float* dtable,
-                                     int64_t n, int64_t d, int64_t vocab, void* stream) {
-  if (!tokens || !dout || !dtable || n <= 0 || d <= 0 || vocab <= 0) return GPTB200_EINVAL;
-  if (d % 4 || !aligned16(dtable)) return GPTB200_ESHAPE;
-  int64_t total = n * (d / 4);
-  int blocks = (int)std::min<int64_t>((total + 255) / 256, (int64_t)sms() * 16);
-  embed_bwd_kernel<<<blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      tokens, reinterpret_cast<const bf16*>(dout), dtable, n, (int)d, vocab);
   GPTB200_CHECK_LAUNCH();
   return 0;
 }
@@ -390,10 +414,12 @@ extern "C" int gptb200_rope_tables(void* cos_out, void* sin_out, int64_t seq, in
 
 // ------------------------------------------------------------------ column sums
 // Block = 8 warps. Lane l of every warp owns columns [8l, 8l+8) of a 256-wide
-// strip; the warps of the block split the rows of the block's row range.
+// strip; the warps of the block split the rows of the block's row range
+// (blockIdx.y). Each block stores its strip's sums as row blockIdx.y of the
+// partials; colred_kernel adds the rows in order (deterministic).
 __global__ void __launch_bounds__(256) colsum_kernel(const bf16* __restrict__ x, int64_t rows,
-                                                     int n, int64_t rows_per_block, float alpha,
-                                                     float* __restrict__ out) {
+                                                     int n, int64_t rows_per_block,
+                                                     float* __restrict__ part) {
   __shared__ float red[8][256];
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int col = blockIdx.x * 256 + lane * 8;
@@ -416,23 +442,39 @@ __global__ void __launch_bounds__(256) colsum_kernel(const bf16* __restrict__ x,
     float s = 0.f;
 #pragma unroll
     for (int k = 0; k < 8; ++k) s += red[k][c];
-    atomicAdd(out + blockIdx.x * 256 + c, alpha * s);
+    part[(int64_t)blockIdx.y * n + blockIdx.x * 256 + c] = s;
   }
 }
 
+// Row split of gptb200_colsum: about 4 blocks per SM, >= 64 rows per block.
+static void colsum_split(int64_t rows, int64_t n, int64_t* rpb, int* ysplit) {
+  const int strips = (int)((n + 255) / 256);
+  const int64_t want = std::max<int64_t>(1, (int64_t)sms() * 4 / strips);
+  *rpb = std::max<int64_t>(64, (rows + want - 1) / want);
+  *ysplit = (int)((rows + *rpb - 1) / *rpb);
+}
+
+extern "C" size_t gptb200_colsum_workspace_size(int64_t rows, int64_t n) {
+  if (rows <= 0 || n <= 0) return 0;
+  int64_t rpb;
+  int ysplit;
+  colsum_split(rows, n, &rpb, &ysplit);
+  return (size_t)ysplit * (size_t)n * sizeof(float);
+}
+
 extern "C" int gptb200_colsum(const void* x, int64_t rows, int64_t n, float alpha, float* out,
-                              void* stream) {
-  if (!x || !out || rows <= 0 || n <= 0) return GPTB200_EINVAL;
+                              void* workspace, void* stream) {
+  if (!x || !out || !workspace || rows <= 0 || n <= 0) return GPTB200_EINVAL;
   if (n % 8 || !aligned16(x)) return GPTB200_ESHAPE;
-  int strips = (int)((n + 255) / 256);
-  int64_t want = std::max<int64_t>(1, (int64_t)sms() * 4 / strips);
-  int64_t rpb = std::max<int64_t>(64, (rows + want - 1) / want);
-  int ysplit = (int)((rows + rpb - 1) / rpb);
-  dim3 grid(strips, ysplit);
-  colsum_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      reinterpret_cast<const bf16*>(x), rows, (int)n, rpb, alpha, out);
+  auto st = reinterpret_cast<cudaStream_t>(stream);
+  int64_t rpb;
+  int ysplit;
+  colsum_split(rows, n, &rpb, &ysplit);
+  dim3 grid((int)((n + 255) / 256), ysplit);
+  float* part = reinterpret_cast<float*>(workspace);
+  colsum_kernel<<<grid, 256, 0, st>>>(reinterpret_cast<const bf16*>(x), rows, (int)n, rpb, part);
   GPTB200_CHECK_LAUNCH();
-  return 0;
+  return colred_launch(part, ysplit, n, (int)n, out, alpha, nullptr, 0.f, st);
 }
 
 // ------------------------------------------------------------------ cast
@@ -508,3 +550,15 @@ extern "C" int gptb200_rope_apply(void* x, int64_t stride_b, int64_t stride_t, i
   GPTB200_CHECK_LAUNCH();
   return 0;
 }
+
+namespace gptb200 {
+int embed_read_error(int clear) {
+  int h = 0;
+  cudaMemcpyFromSymbol(&h, g_embed_error, sizeof(int));
+  if (clear) {
+    int z = 0;
+    cudaMemcpyToSymbol(g_embed_error, &z, sizeof(int));
+  }
+  return h;
+}
+}  // namespace gptb200

@@ -238,12 +238,32 @@ __device__ __forceinline__ void epi_pack8(const GemmParams& p, int row, int c0, 
 // Applies the fp32 / cross-entropy-forward epilogues to 32 accumulator
 // columns [col, col+32) of one row (bf16 outputs go through epi_value8).
 template <int EPI>
-__device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int row, int col, float* v,
-                                               EpilogueRowState<EPI>& st, int target,
+__device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int row, int col, int ks,
+                                               float* v, EpilogueRowState<EPI>& st, int target,
                                                float lse, float cot) {
   const bool row_ok = row < p.M;
   if constexpr (kStagedEpi<EPI>) {
     return;
+  } else if constexpr (EPI == EPI_F32_SPLITK_) {
+    // One split: C += alpha * acc directly. Several: this split's raw partial
+    // goes to its own slab; splitk_reduce_kernel adds the slabs in split order.
+    if (!row_ok) return;
+    const bool direct = p.splits == 1;
+    float* dst_row = direct ? reinterpret_cast<float*>(p.C) + (int64_t)row * p.ldc
+                            : p.slab + ((int64_t)ks * p.M + row) * p.N;
+#pragma unroll
+    for (int g = 0; g < 8; ++g) {
+      int c0 = col + 4 * g;
+      if (c0 >= p.N) break;
+      float4* dst = reinterpret_cast<float4*>(dst_row + c0);
+      if (direct) {
+        float4 o = *dst;
+        *dst = make_float4(o.x + p.alpha * v[4 * g], o.y + p.alpha * v[4 * g + 1],
+                           o.z + p.alpha * v[4 * g + 2], o.w + p.alpha * v[4 * g + 3]);
+      } else {
+        *dst = make_float4(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]);
+      }
+    }
   } else if constexpr (EPI == EPI_F32_) {
     if (!row_ok) return;
     float* C = reinterpret_cast<float*>(p.C);
@@ -533,7 +553,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           float v[32];
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(raw[c * 32 + i]);
-          epilogue_chunk<EPI>(p, row, n0 + c * 32, v, st, target, lse, cot);
+          epilogue_chunk<EPI>(p, row, n0 + c * 32, tc.ks, v, st, target, lse, cot);
         }
       }
       if constexpr (EPI == EPI_LCE_FWD_) {
@@ -570,6 +590,34 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, 2 * BN);
+  }
+}
+
+// C[r, c] += alpha * (((slab_0 + slab_1) + slab_2) + ...)[r, c]: the K splits of
+// an EPI_F32_SPLITK_ product, added in split order so that the result is the
+// same whichever CTA finished first. One float4 of C per thread.
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ slab,
+                                                            int splits, int64_t M, int N,
+                                                            float* __restrict__ C, int64_t ldc,
+                                                            float alpha) {
+  const int64_t per = M * (int64_t)N;
+  const int64_t n4 = per >> 2;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t e = i << 2;
+    const int64_t r = e / N;
+    const int c = (int)(e - r * N);
+    float4 s = __ldcs(reinterpret_cast<const float4*>(slab + e));
+    for (int k = 1; k < splits; ++k) {
+      const float4 t = __ldcs(reinterpret_cast<const float4*>(slab + k * per + e));
+      s.x += t.x;
+      s.y += t.y;
+      s.z += t.z;
+      s.w += t.w;
+    }
+    float4* dst = reinterpret_cast<float4*>(C + r * ldc + c);
+    const float4 o = *dst;
+    *dst = make_float4(o.x + alpha * s.x, o.y + alpha * s.y, o.z + alpha * s.z, o.w + alpha * s.w);
   }
 }
 
@@ -666,6 +714,8 @@ static int dispatch_layout(int a_mn, int b_mn, const CUtensorMap& ta, const CUte
   return launch_variant<kBN, kStages, EPI, 1, 1>(ta, tb, em, p, s);
 }
 
+static int gemm_split_request(int64_t M, int64_t N, int64_t K);
+
 int gemm_launch(const void* a, int a_mn, int64_t lda, const void* b, int b_mn, int64_t ldb,
                 int64_t M, int64_t N, int64_t K, int epi, GemmParams p, cudaStream_t stream) {
   if (!a || !b || !p.C) return GPTB200_EINVAL;
@@ -699,14 +749,7 @@ int gemm_launch(const void* a, int a_mn, int64_t lda, const void* b, int b_mn, i
   p.tiles_n = (int)((N + kBN - 1) / kBN);
   p.num_kb = (int)((K + BK - 1) / BK);
   int splits = 1;
-  if (epi == EPI_F32_ATOMIC_) {
-    // Split K until there are about three units per SM, keeping >= 32 k-blocks
-    // (2048 of K) per unit: every unit ends in BM x BN fp32 atomics, which a
-    // shorter main loop no longer hides.
-    const int tiles = p.tiles_m * p.tiles_n;
-    const int target = 3 * sm_count();
-    while (tiles * splits < target && p.num_kb / (splits * 2) >= 32) splits *= 2;
-  }
+  if (epi == EPI_F32_ATOMIC_ || epi == EPI_F32_SPLITK_) splits = gemm_split_request(M, N, K);
   // Raster groups: enough M tiles that a wave of CTAs spans few N tiles, with
   // the group's A stripe (group_m x BM rows of K) at most ~16 MB of L2.
   {
@@ -722,6 +765,18 @@ int gemm_launch(const void* a, int a_mn, int64_t lda, const void* b, int b_mn, i
     case EPI_BF16_: return dispatch_layout<EPI_BF16_>(a_mn, b_mn, ta, tb, em, p, stream);
     case EPI_F32_: return dispatch_layout<EPI_F32_>(a_mn, b_mn, ta, tb, em, p, stream);
     case EPI_F32_ATOMIC_: return dispatch_layout<EPI_F32_ATOMIC_>(a_mn, b_mn, ta, tb, em, p, stream);
+    case EPI_F32_SPLITK_: {
+      if (p.splits > 1 && !p.slab) return GPTB200_EINVAL;
+      int s = dispatch_layout<EPI_F32_SPLITK_>(a_mn, b_mn, ta, tb, em, p, stream);
+      if (s || p.splits == 1) return s;
+      const int64_t n4 = (int64_t)p.M * p.N / 4;
+      const int blocks = (int)std::min<int64_t>((n4 + 255) / 256, (int64_t)sm_count() * 8);
+      splitk_reduce_kernel<<<blocks, 256, 0, stream>>>(p.slab, p.splits, p.M, p.N,
+                                                      reinterpret_cast<float*>(p.C), p.ldc,
+                                                      p.alpha);
+      GPTB200_CHECK_LAUNCH();
+      return GPTB200_OK;
+    }
     case EPI_BIAS_ROPE_:
       if (a_mn || !b_mn) return GPTB200_EUNSUPPORTED;
       return launch_variant<kBN, kStages, EPI_BIAS_ROPE_, 0, 1>(ta, tb, em, p, stream);
@@ -742,6 +797,25 @@ int gemm_launch(const void* a, int a_mn, int64_t lda, const void* b, int b_mn, i
 }
 
 int gemm_tile_n() { return kBN; }
+
+static int gemm_split_request(int64_t M, int64_t N, int64_t K) {
+  // Split K until there are about three units per SM, keeping >= 32 k-blocks
+  // (2048 of K) per unit: every unit ends in a BM x BN fp32 write-out (atomics
+  // or a partial slab), which a shorter main loop no longer hides.
+  const int64_t tiles = ((M + BM - 1) / BM) * ((N + kBN - 1) / kBN);
+  const int64_t num_kb = (K + BK - 1) / BK;
+  const int64_t target = 3 * (int64_t)sm_count();
+  int splits = 1;
+  while (tiles * splits < target && num_kb / (splits * 2) >= 32) splits *= 2;
+  return splits;
+}
+
+// Splits that actually run: k-blocks are dealt in runs of ceil(num_kb / request).
+int gemm_splits(int64_t M, int64_t N, int64_t K) {
+  const int64_t num_kb = (K + BK - 1) / BK;
+  const int64_t per = (num_kb + gemm_split_request(M, N, K) - 1) / gemm_split_request(M, N, K);
+  return (int)((num_kb + per - 1) / per);
+}
 
 int gemm_read_error(int clear) {
   int h = 0;
@@ -793,6 +867,12 @@ extern "C" int gptb200_gemm(const void* a, int a_mn_major, int64_t lda, const vo
       break;
     case GPTB200_EPI_F32: kind = EPI_F32_; break;
     case GPTB200_EPI_F32_ATOMIC: kind = EPI_F32_ATOMIC_; break;
+    case GPTB200_EPI_F32_SPLITK:
+      kind = EPI_F32_SPLITK_;
+      p.slab = reinterpret_cast<float*>(e->workspace);
+      if (e->row_range) return GPTB200_EUNSUPPORTED;
+      if (e->workspace && (reinterpret_cast<uintptr_t>(e->workspace) & 15)) return GPTB200_ESHAPE;
+      break;
     default: return GPTB200_EUNSUPPORTED;
   }
   if (e->residual && (e->ld_residual < n || (e->ld_residual % 8))) return GPTB200_EINVAL;
@@ -805,9 +885,15 @@ extern "C" int gptb200_gemm(const void* a, int a_mn_major, int64_t lda, const vo
   // bias / residual / derivative rows are read in 16-byte groups of 8 columns
   if ((e->bias || e->residual || kind == EPI_BIAS_GELU_ || kind == EPI_DGELU_) && (n % 8))
     return GPTB200_ESHAPE;
-  if (kind == EPI_F32_ || kind == EPI_F32_ATOMIC_) {
+  if (kind == EPI_F32_ || kind == EPI_F32_ATOMIC_ || kind == EPI_F32_SPLITK_) {
     if (ldc % 4) return GPTB200_ESHAPE;
   }
   return gemm_launch(a, a_mn_major, lda, b, b_mn_major, ldb, m, n, k, kind, p,
                      reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" size_t gptb200_gemm_workspace_size(int64_t m, int64_t n, int64_t k, int kind) {
+  if (m <= 0 || n <= 0 || k <= 0 || kind != GPTB200_EPI_F32_SPLITK) return 0;
+  const int splits = gptb200::gemm_splits(m, n, k);
+  return splits > 1 ? (size_t)splits * (size_t)m * (size_t)n * sizeof(float) : 0;
 }

@@ -14,6 +14,7 @@ enum {
   EPI_F32_ = 3,
   EPI_F32_ATOMIC_ = 4,
   EPI_BIAS_ROPE_ = 5,
+  EPI_F32_SPLITK_ = 6,  // C fp32 += alpha * acc, K splits reduced in a fixed order
   EPI_LCE_FWD_ = 10,  // per (row, N-tile) partial (max, sum exp) + target logit
   EPI_LCE_BWD_ = 11,  // bf16 (softmax - onehot) * cotangent
 };
@@ -52,12 +53,16 @@ struct GemmParams {
   float2* partial;    // [M, tiles_n]
   float* tgt_logit;   // [M]
   int v_sem;
+  // EPI_F32_SPLITK_: per-split fp32 partial products [splits][M][N]
+  float* slab;
 };
 
 // Validates shapes, encodes the TMA maps and launches the persistent kernel.
 int gemm_launch(const void* a, int a_mn, int64_t lda, const void* b, int b_mn, int64_t ldb,
                 int64_t M, int64_t N, int64_t K, int epi, GemmParams p, cudaStream_t stream);
 int gemm_tile_n();
+// K splits the weight-gradient epilogues use for an M x N x K product.
+int gemm_splits(int64_t M, int64_t N, int64_t K);
 int gemm_read_error(int clear);
 
 }  // namespace gptb200

@@ -582,7 +582,7 @@ extern "C" int gptb200_moe_route_bwd(const void* x, const float* router_w, const
     return GPTB200_EINVAL;
   if (experts < 1 || experts > kMoeMaxE || top_k < 1 || top_k > kMoeMaxK) return GPTB200_EUNSUPPORTED;
   if (d % 8 || d > kRbMaxF * 1024) return GPTB200_ESHAPE;
-  // the backward is instantiated for 2, 4, 8 and 16 experts
+  // the backward is instantiated for every expert count 1..16
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -596,10 +596,15 @@ extern "C" int gptb200_moe_route_bwd(const void* x, const float* router_w, const
                                      (int)d, top_k, d_router_w, reinterpret_cast<bf16*>(d_x));
   };
   switch (experts) {
-    case 2: run(moe_route_bwd_kernel<2>); break;
-    case 4: run(moe_route_bwd_kernel<4>); break;
-    case 8: run(moe_route_bwd_kernel<8>); break;
-    case 16: run(moe_route_bwd_kernel<16>); break;
+#define GPTB200_ROUTE_BWD_CASE(E) \
+  case E: run(moe_route_bwd_kernel<E>); break;
+    GPTB200_ROUTE_BWD_CASE(1) GPTB200_ROUTE_BWD_CASE(2) GPTB200_ROUTE_BWD_CASE(3)
+    GPTB200_ROUTE_BWD_CASE(4) GPTB200_ROUTE_BWD_CASE(5) GPTB200_ROUTE_BWD_CASE(6)
+    GPTB200_ROUTE_BWD_CASE(7) GPTB200_ROUTE_BWD_CASE(8) GPTB200_ROUTE_BWD_CASE(9)
+    GPTB200_ROUTE_BWD_CASE(10) GPTB200_ROUTE_BWD_CASE(11) GPTB200_ROUTE_BWD_CASE(12)
+    GPTB200_ROUTE_BWD_CASE(13) GPTB200_ROUTE_BWD_CASE(14) GPTB200_ROUTE_BWD_CASE(15)
+    GPTB200_ROUTE_BWD_CASE(16)
+#undef GPTB200_ROUTE_BWD_CASE
     default: return GPTB200_EUNSUPPORTED;
   }
   GPTB200_CHECK_LAUNCH();

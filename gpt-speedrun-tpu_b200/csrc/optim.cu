@@ -60,6 +60,8 @@ __global__ void __launch_bounds__(kNormThreads) sqnorm_partial_kernel(const floa
   }
 }
 
+static __device__ int g_optim_error;
+
 __global__ void adamw_scalars_kernel(const double* __restrict__ part, int nparts,
                                      const gptb200_adamw_config cfg, int32_t* step_io,
                                      const float* loss, float* history, AdamScalars* out) {
@@ -97,6 +99,9 @@ __global__ void adamw_scalars_kernel(const double* __restrict__ part, int nparts
   a.step = step;
   *out = a;
   *step_io = step;
+  // A non-finite loss or gradient norm is the reference's FloatingPointError
+  // (rig/mesh.py finite_metric); record it for gptb200_device_error().
+  if (!isfinite(grad_norm) || (loss && !isfinite(*loss))) g_optim_error = kErrNonFinite;
   if (history && step >= 1 && step <= cfg.total_steps) {
     float* row = history + (int64_t)(step - 1) * 3;
     row[0] = loss ? *loss : 0.f;
@@ -237,3 +242,15 @@ extern "C" int gptb200_adamw_step(float* params, float* m, float* v, const float
   GPTB200_CHECK_LAUNCH();
   return 0;
 }
+
+namespace gptb200 {
+int optim_read_error(int clear) {
+  int h = 0;
+  cudaMemcpyFromSymbol(&h, g_optim_error, sizeof(int));
+  if (clear) {
+    int z = 0;
+    cudaMemcpyToSymbol(g_optim_error, &z, sizeof(int));
+  }
+  return h;
+}
+}  // namespace gptb200

@@ -5,14 +5,16 @@
 // walking (rig/tokens.py:136-168), SplitMix64 round keys (:127-133), then a
 // binary search over the epoch's shard order (:239-254). That per-row Python
 // loop is the data loader's hot spot; here it runs as plain C++ over all rows
-// of a local batch, and the windows are copied straight from the (memory
-// mapped) uint16 shards into the int32 batch. The epoch plan (shard order
-// from numpy's Generator, rig/tokens.py:222-236) stays with the Python caller
-// because it depends on numpy's PCG64 stream.
+// of a local batch: the epoch's window table (per-shard window counts in the
+// epoch's shard order), the epoch key and the window copy from the (memory
+// mapped) shards into the int32 batch. Only the shard order itself comes from
+// the caller, because it is a draw of numpy's PCG64 Generator
+// (rig/tokens.py:222-236).
 #include <stdint.h>
 #include <string.h>
 
 #include <algorithm>
+#include <vector>
 
 #include "../../include/gptb200.h"
 
@@ -68,46 +70,61 @@ extern "C" uint64_t gptb200_permute_bounded(uint64_t value, uint64_t size, uint6
   }
 }
 
-extern "C" int gptb200_gather_windows(const uint16_t* const* shard_data,
-                                      const int64_t* shard_lengths, const int64_t* ordered_shards,
-                                      const int64_t* ordered_cumulative, int64_t n_shards,
-                                      int64_t windows_per_epoch, uint64_t epoch_key,
-                                      int64_t first_epoch_ordinal, int64_t rows, int64_t seq_len,
-                                      int64_t vocab, int32_t* out) {
-  if (!shard_data || !shard_lengths || !ordered_shards || !ordered_cumulative || !out)
+namespace {
+
+// Reads element i of a shard of element type `dtype` (GPTB200_TOKENS_*).
+inline int64_t token_at(const void* shard, int dtype, int64_t i) {
+  switch (dtype) {
+    case GPTB200_TOKENS_U8: return static_cast<const uint8_t*>(shard)[i];
+    case GPTB200_TOKENS_U16: return static_cast<const uint16_t*>(shard)[i];
+    case GPTB200_TOKENS_I32: return static_cast<const int32_t*>(shard)[i];
+    case GPTB200_TOKENS_U32: return static_cast<const uint32_t*>(shard)[i];
+    default: return static_cast<const int64_t*>(shard)[i];
+  }
+}
+
+}  // namespace
+
+extern "C" int gptb200_epoch_windows(const void* const* shards, const int64_t* lengths,
+                                     int64_t n_shards, int dtype, const int64_t* order,
+                                     int64_t seq_len, uint64_t seed, int64_t epoch,
+                                     int64_t first, int64_t rows, int64_t vocab, int32_t* out) {
+  if (!shards || !lengths || !order || !out || n_shards <= 0 || seq_len <= 0 || rows < 0 ||
+      first < 0 || epoch < 0 || vocab <= 0)
     return GPTB200_EINVAL;
-  if (n_shards <= 0 || windows_per_epoch <= 0 || rows < 0 || seq_len <= 0)
-    return GPTB200_EINVAL;
-  if (first_epoch_ordinal < 0 || first_epoch_ordinal + rows > windows_per_epoch)
-    return GPTB200_EINVAL;
-  const uint64_t size = (uint64_t)windows_per_epoch;
-  Feistel f(size, epoch_key);
+  if (dtype < GPTB200_TOKENS_U8 || dtype > GPTB200_TOKENS_I64) return GPTB200_EINVAL;
+  // The epoch's plan: shards visited in `order`, each contributing
+  // floor((len - 1) / seq_len) whole windows; ends[j] = windows of the first
+  // j + 1 shards of the order.
+  std::vector<int64_t> ends(n_shards);
+  int64_t total = 0;
+  for (int64_t j = 0; j < n_shards; ++j) {
+    const int64_t s = order[j];
+    if (s < 0 || s >= n_shards) return GPTB200_EINVAL;
+    total += std::max<int64_t>(0, (lengths[s] - 1) / seq_len);
+    ends[j] = total;
+  }
+  if (total <= 0 || first + rows > total) return GPTB200_EINVAL;
+  const uint64_t size = (uint64_t)total;
+  const Feistel f(size, mix64(seed ^ mix64((uint64_t)epoch)));
   int status = GPTB200_OK;
   for (int64_t r = 0; r < rows; ++r) {
-    uint64_t c = (uint64_t)(first_epoch_ordinal + r);
-    if (size > 1) {
-      do {
-        c = f.apply(c);
-      } while (c >= size);
+    uint64_t w = (uint64_t)(first + r);
+    if (size == 1) {
+      w = 0;
     } else {
-      c = 0;
+      do w = f.apply(w);
+      while (w >= size);  // cycle walking back into [0, size)
     }
-    const int64_t permuted = (int64_t)c;
-    // searchsorted(cumulative, permuted, side="right")
-    const int64_t* it =
-        std::upper_bound(ordered_cumulative, ordered_cumulative + n_shards, permuted);
-    const int64_t oi = it - ordered_cumulative;
-    if (oi >= n_shards) return GPTB200_EINVAL;
-    const int64_t prev = oi ? ordered_cumulative[oi - 1] : 0;
-    const int64_t shard = ordered_shards[oi];
-    const int64_t start = (permuted - prev) * seq_len;
-    if (start + seq_len + 1 > shard_lengths[shard]) return GPTB200_EINVAL;
-    const uint16_t* src = shard_data[shard] + start;
+    // the shard of the order whose window range holds w
+    const int64_t j = std::upper_bound(ends.begin(), ends.end(), (int64_t)w) - ends.begin();
+    const int64_t s = order[j];
+    const int64_t start = ((int64_t)w - (j ? ends[j - 1] : 0)) * seq_len;
     int32_t* dst = out + r * (seq_len + 1);
     for (int64_t t = 0; t <= seq_len; ++t) {
-      const int32_t v = (int32_t)src[t];
-      if (v >= vocab) status = GPTB200_ERANGE;
-      dst[t] = v;
+      const int64_t v = token_at(shards[s], dtype, start + t);
+      if (v < 0 || v >= vocab) status = GPTB200_ERANGE;
+      dst[t] = (int32_t)v;
     }
   }
   return status;

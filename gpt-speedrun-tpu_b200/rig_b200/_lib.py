@@ -37,6 +37,7 @@ class Epilogue(ctypes.Structure):
         ("rope_cols", c_i64),
         ("row_range", c_vp),
         ("range_dim", c_int),
+        ("workspace", c_vp),
     ]
 
 
@@ -75,12 +76,19 @@ EPI_DGELU = 2
 EPI_F32 = 3
 EPI_F32_ATOMIC = 4
 EPI_BIAS_ROPE = 5
+EPI_F32_SPLITK = 6
+
+DEVERR_GEMM = 1
+DEVERR_ATTENTION = 2
+DEVERR_TOKEN_RANGE = 4
+DEVERR_NONFINITE = 8
 
 # name -> (restype, argtypes). Mirrors include/gptb200.h one to one.
 SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "gptb200_version": (ctypes.c_char_p, []),
     "gptb200_status_string": (ctypes.c_char_p, [c_int]),
     "gptb200_device_error": (c_int, [c_int]),
+    "gptb200_device_error_flags": (c_int, [c_int]),
     "gptb200_launch_count": (ctypes.c_uint64, []),
     "gptb200_gemm": (
         c_int,
@@ -88,10 +96,13 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
          ctypes.POINTER(Epilogue), c_vp],
     ),
     "gptb200_rms_norm_fwd": (c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_vp]),
+    "gptb200_gemm_workspace_size": (c_size, [c_i64, c_i64, c_i64, c_int]),
+    "gptb200_rms_norm_bwd_workspace_size": (c_size, [c_i64, c_i64]),
     "gptb200_rms_norm_bwd": (
-        c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_f32, c_i64, c_i64, c_vp]),
+        c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_f32, c_i64, c_i64, c_vp, c_vp]),
     "gptb200_embedding_fwd": (c_int, [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp]),
-    "gptb200_embedding_bwd": (c_int, [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp]),
+    "gptb200_embedding_bwd_workspace_size": (c_size, [c_i64, c_i64, c_i64]),
+    "gptb200_embedding_bwd": (c_int, [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_vp]),
     "gptb200_rope_tables": (c_int, [c_vp, c_vp, c_i64, c_i64, c_vp]),
     "gptb200_document_segments": (c_int, [c_vp, c_i64, c_i64, ctypes.c_int32, c_vp, c_vp]),
     "gptb200_rope_apply": (
@@ -119,7 +130,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         c_int,
         [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp],
     ),
-    "gptb200_colsum": (c_int, [c_vp, c_i64, c_i64, c_f32, c_vp, c_vp]),
+    "gptb200_colsum_workspace_size": (c_size, [c_i64, c_i64]),
+    "gptb200_colsum": (c_int, [c_vp, c_i64, c_i64, c_f32, c_vp, c_vp, c_vp]),
     "gptb200_moe_rows": (c_size, [c_i64, ctypes.c_int32, ctypes.c_int32]),
     "gptb200_moe_dispatch_workspace_size": (c_size, [c_i64, ctypes.c_int32, ctypes.c_int32]),
     "gptb200_moe_route": (
@@ -151,9 +163,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "gptb200_mix_uint64": (ctypes.c_uint64, [ctypes.c_uint64]),
     "gptb200_permute_bounded": (
         ctypes.c_uint64, [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64]),
-    "gptb200_gather_windows": (
+    "gptb200_epoch_windows": (
         c_int,
-        [ctypes.POINTER(c_vp), c_vp, c_vp, c_vp, c_i64, c_i64, ctypes.c_uint64, c_i64, c_i64,
+        [ctypes.POINTER(c_vp), c_vp, c_i64, c_int, c_vp, c_i64, ctypes.c_uint64, c_i64, c_i64,
          c_i64, c_i64, c_vp],
     ),
 }

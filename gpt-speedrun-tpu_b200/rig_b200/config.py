@@ -62,6 +62,10 @@ class Config:
     expert_top_k: int = 2
     expert_mult: int = 2
     router_aux_coefficient: float = 0.01
+    # fixed tokens-per-parameter horizon (train.py:745-751): the tier's declared
+    # parameter denominator and the requested TPP; None for a fixed-step run
+    declared_parameters: int | None = None
+    target_tokens_per_parameter: float | None = None
 
     @property
     def width_multiplier(self) -> float:
@@ -70,6 +74,14 @@ class Config:
     @property
     def depth_multiplier(self) -> float:
         return self.layers / float(self.base_depth)
+
+    @property
+    def tokens_per_parameter(self) -> float | None:
+        """Achieved full-schedule TPP after rounding to whole steps (train.py:255-266)."""
+
+        if self.declared_parameters is None:
+            return None
+        return self.steps * self.batch_size * self.seq_len / float(self.declared_parameters)
 
     @property
     def head_dim(self) -> int:
@@ -109,18 +121,30 @@ def _require(mapping: Mapping[str, Any], key: str, where: str) -> Any:
     return mapping[key]
 
 
+def tpp_parameters(model: Mapping[str, Any]) -> int:
+    """Parameter denominator of the fixed-TPP ladder (train.py:355-364): two
+    vocabulary tables, per block 12 d^2 + 11 d, and the final norm."""
+
+    d, layers, vocab = int(model["d_model"]), int(model["layers"]), int(model["vocab_size"])
+    return 2 * vocab * d + layers * (12 * d * d + 11 * d) + d
+
+
 def resolve_config(
     document: Mapping[str, Any],
     *,
     tier: str | None = None,
     context: str | None = None,
     batch_size: int | None = None,
+    tokens_per_parameter: float | None = None,
 ) -> Config:
     """Resolves a schema-6 experiment document into a step Config.
 
-    Supports the fixed-step duration (``run.training.duration.steps``); a
-    fixed tokens-per-parameter horizon resolves its step count the same way as
-    train.py:749-756.
+    The duration is either a fixed step count (``run.training.duration.steps``)
+    or a fixed tokens-per-parameter horizon (``tokens_per_parameter``): then
+    steps = max(1, floor(tpp_parameters * tpp / tokens_per_step + 0.5)) and the
+    CompleteP data multiplier is the tier's tpp_parameters over the base
+    tier's (train.py:745-751, 792-800). `tokens_per_parameter` overrides the
+    document's horizon like the reference's --tokens-per-parameter flag.
     """
 
     if int(_require(document, "schema_version", "config")) != 6:
@@ -141,18 +165,30 @@ def resolve_config(
     kernels = run["kernels"]
     if model.get("normalization", "rms_norm") != "rms_norm":
         raise ValueError("only rms_norm is supported (train.py:323)")
+    _check_routing(model, tier_name)
 
     batch = int(batch_size or ctx["reference_batch_size"])
     seq_len = int(ctx["seq_len"])
     duration = training["duration"]
-    if "steps" in duration and duration["steps"] is not None:
-        steps = int(duration["steps"])
+    fixed_steps = duration.get("steps")
+    doc_tpp = duration.get("tokens_per_parameter")
+    if (fixed_steps is None) == (doc_tpp is None):
+        raise ValueError("run.training.duration must define exactly one of steps and "
+                         "tokens_per_parameter")
+    declared = None
+    requested_tpp = None
+    if fixed_steps is not None:
+        if tokens_per_parameter is not None:
+            raise ValueError("tokens_per_parameter cannot override a fixed-step configuration")
+        steps = int(fixed_steps)
         data_multiplier = 1.0
     else:
-        raise ValueError(
-            "fixed tokens-per-parameter horizons need the tier's declared parameter count; "
-            "use a fixed `steps` duration"
-        )
+        requested_tpp = float(tokens_per_parameter if tokens_per_parameter is not None else doc_tpp)
+        if not math.isfinite(requested_tpp) or requested_tpp <= 0.0:
+            raise ValueError(f"tokens_per_parameter must be positive and finite, got {requested_tpp}")
+        declared = tpp_parameters(model)
+        steps = max(1, int(math.floor(declared * requested_tpp / (batch * seq_len) + 0.5)))
+        data_multiplier = declared / float(tpp_parameters(base))
     warmup = int(math.floor(steps * float(optimizer["warmup_ratio"]) + 0.5))
     warmup = min(warmup, steps - 1) if steps > 1 else 0
     return Config(
@@ -191,7 +227,32 @@ def resolve_config(
         expert_top_k=int(model.get("expert_top_k", 2)),
         expert_mult=int(model.get("expert_mult", 2)),
         router_aux_coefficient=float(model.get("router_aux_coefficient", 0.01)),
+        declared_parameters=declared,
+        target_tokens_per_parameter=requested_tpp,
     )
+
+
+MOE_MAX_EXPERTS = 16  # gptb200_moe_* kernels: 1 <= experts <= 16, top_k <= min(4, experts)
+MOE_MAX_TOP_K = 4
+
+
+def _check_routing(model: Mapping[str, Any], label: str) -> None:
+    """The routed tier's rules (recipes/reference_moe/train.py:362-371) plus
+    the limits of the routing kernels, checked before anything is built."""
+
+    experts = int(model.get("experts", 0))
+    if not experts:
+        return
+    top_k = int(model.get("expert_top_k", 2))
+    mult = int(model.get("expert_mult", 2))
+    if top_k > experts:
+        raise ValueError(f"{label}.expert_top_k must not exceed experts")
+    if top_k * mult != int(model["mlp_mult"]):
+        raise ValueError(f"{label} must satisfy expert_top_k * expert_mult == mlp_mult so active "
+                         "MLP FLOPs match the dense tier")
+    if experts > MOE_MAX_EXPERTS or top_k > MOE_MAX_TOP_K:
+        raise ValueError(f"{label}: the routing kernels support up to {MOE_MAX_EXPERTS} experts "
+                         f"and top-{MOE_MAX_TOP_K}, got {experts} experts top-{top_k}")
 
 
 def load_config(name_or_path: str | pathlib.Path, **overrides: Any) -> Config:

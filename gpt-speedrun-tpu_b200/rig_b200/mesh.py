@@ -18,6 +18,7 @@ compute stream wait for all of them before the optimizer runs.
 from __future__ import annotations
 
 import datetime
+import math
 import os
 
 import torch
@@ -87,3 +88,16 @@ class GradientReducer:
 def barrier() -> None:
     if dist.is_initialized():
         dist.barrier()
+
+
+def finite_metric(name: str, value: float, *, positive: bool = False) -> float:
+    """A host-side metric checked before it is logged (rig/mesh.py:214-223):
+    NaN, infinities, negatives, and zero when `positive`, raise
+    FloatingPointError, which ends the run the way the reference's does."""
+
+    value = float(value)
+    low_ok = value > 0.0 if positive else value >= 0.0
+    if math.isfinite(value) and low_ok:
+        return value
+    need = "finite and positive" if positive else "finite and nonnegative"
+    raise FloatingPointError(f"{name} must be {need}, got {value!r}")

@@ -195,6 +195,7 @@ class GPTTrainer:
         process_group=None,
         world_size: int = 1,
         history_steps: int | None = None,
+        deterministic: bool = True,
     ):
         if config.dtype_name != "bfloat16":
             raise ValueError("the B200 step computes in bfloat16")
@@ -209,7 +210,17 @@ class GPTTrainer:
         self.N = self.B * self.T
         self.world_size = int(world_size)
         self.pg = process_group
+        # Bit-reproducible gradients: weight gradients split over K are summed
+        # from per-split slabs in a fixed order (EPI_F32_SPLITK) instead of with
+        # fp32 atomics. The other reductions of the step are always ordered.
+        self.deterministic = bool(deterministic)
+        self.wgrad_kind = _lib.EPI_F32_SPLITK if deterministic else _lib.EPI_F32_ATOMIC
         self.layout = ParamLayout(config)
+        if (config.declared_parameters is not None
+                and self.layout.parameter_count() != config.declared_parameters):
+            # recipes/reference/train.py:1672-1678
+            raise ValueError(f"tier {config.tier} declares {config.declared_parameters:,} "
+                             f"parameters, but initialized {self.layout.parameter_count():,}")
         dev = self.device
         n = self.layout.numel
         self.params = torch.zeros(n, dtype=torch.float32, device=dev)
@@ -299,6 +310,14 @@ class GPTTrainer:
         self.lce_bwd_ws = ops.lce_bwd_workspace(N, c.vocab_size, dev)
         self.tokens = torch.empty(self.B, self.T, dtype=torch.int32, device=dev)
         self.targets = torch.empty(self.B, self.T, dtype=torch.int32, device=dev)
+        # One scratch buffer shared by the backward's ordered reductions (they
+        # run one after another on the step's stream).
+        wgrad_shapes = [(d, 3 * d), (d, d)] + ([] if c.experts else [(d, h), (h, d)])
+        need = [ops.rms_norm_bwd_workspace_size(N, d),
+                ops.embedding_bwd_workspace_size(N, d, c.vocab_size)]
+        need += [ops.colsum_workspace_size(N, w) for w in (3 * d, h)]
+        need += [ops.gemm_workspace_size(m, n, N, self.wgrad_kind) for m, n in wgrad_shapes]
+        self.scratch = torch.empty(max(need), dtype=torch.uint8, device=dev)
 
     def _alloc_moe(self) -> None:
         """Per-layer routed buffers (kept for the backward) and shared scratch."""
@@ -476,11 +495,12 @@ class GPTTrainer:
         return self.loss
 
     def _wgrad(self, act: torch.Tensor, dy: torch.Tensor, gview: torch.Tensor, alpha: float):
-        """gview[K_in, N_out] += alpha * act^T dy (fp32, split-K atomics)."""
+        """gview[K_in, N_out] += alpha * act^T dy (fp32; K split over CTAs, the
+        splits summed in a fixed order unless the trainer runs with atomics)."""
 
         m, n = act.shape[1], dy.shape[1]
         ops.gemm(act, dy, gview, a_mn_major=True, b_mn_major=True, m=m, n=n, k=self.N,
-                 kind=_lib.EPI_F32_ATOMIC, alpha=alpha)
+                 kind=self.wgrad_kind, alpha=alpha, workspace=self.scratch)
 
     def _dgrad(self, dy: torch.Tensor, w: torch.Tensor, out: torch.Tensor, **kw):
         """out[N, in] = epilogue(dy[N, out] @ w[in, out]^T)."""
@@ -498,7 +518,7 @@ class GPTTrainer:
         # (a routed MLP's biases are per expert: their sums come from moe_segment_colsum)
         mlp_bias = (lambda l: None) if c.experts else (lambda l: self.blocks[l].g_mlp_down_b)
         ops.rms_norm_bwd(self.x[c.layers], self.final_scale, self.rstdf, self.dln, None, self.dx,
-                         self.g_final_scale, mlp_bias(c.layers - 1), a)
+                         self.g_final_scale, mlp_bias(c.layers - 1), a, workspace=self.scratch)
         dx = self.dx
         for l in reversed(range(c.layers)):
             blk = self.blocks[l]
@@ -510,10 +530,10 @@ class GPTTrainer:
                             aux=self.gelu_grad[l])
                 self._wgrad(self.g[l], dx, blk.g_mlp_down_w, a)
                 self._wgrad(self.ln2[l], self.du, blk.g_mlp_up_w, 1.0)
-                ops.colsum(self.du, blk.g_mlp_up_b, 1.0)
+                ops.colsum(self.du, blk.g_mlp_up_b, 1.0, workspace=self.scratch)
                 self._dgrad(self.du, blk.mlp_up_w, self.dln)
             ops.rms_norm_bwd(self.xm[l], blk.ln2_scale, self.rstd2[l], self.dln, dx, dx,
-                             blk.g_ln2_scale, blk.g_attn_b, a)
+                             blk.g_ln2_scale, blk.g_attn_b, a, workspace=self.scratch)
             # attention: xm = x + a * (att Wo + bo)
             self._dgrad(dx, blk.attn_w, self.datt, alpha=a)
             self._wgrad(self.att[l], dx, blk.g_attn_w, a)
@@ -523,14 +543,14 @@ class GPTTrainer:
                               dq, dk, dv, scale=c.softmax_scale, layout="bthd", rope=self.rope,
                               workspace=self.attn_ws, segment_ids=self.segments)
             self._wgrad(self.ln1[l], self.dqkv, blk.g_qkv_w, 1.0)
-            ops.colsum(self.dqkv, blk.g_qkv_b, 1.0)
+            ops.colsum(self.dqkv, blk.g_qkv_b, 1.0, workspace=self.scratch)
             self._dgrad(self.dqkv, blk.qkv_w, self.dln)
             below = mlp_bias(l - 1) if l > 0 else None
             ops.rms_norm_bwd(self.x[l], blk.ln1_scale, self.rstd1[l], self.dln, dx, dx,
-                             blk.g_ln1_scale, below, a)
+                             blk.g_ln1_scale, below, a, workspace=self.scratch)
             if reduce_hook is not None:
                 reduce_hook(*self.layout.block_ranges[l])
-        ops.embedding_bwd(self.tokens.view(-1), dx, self.g_tok_emb)
+        ops.embedding_bwd(self.tokens.view(-1), dx, self.g_tok_emb, workspace=self.scratch)
         if reduce_hook is not None:
             reduce_hook(*self.layout.tail_range)
 
@@ -581,6 +601,28 @@ class GPTTrainer:
 
             dist.all_reduce(out, op=dist.ReduceOp.SUM, group=self.pg)
         return out
+
+    def checked_metrics(self, step: int) -> dict[str, float]:
+        """Synchronizes, then checks and returns step `step`'s history row.
+
+        Raises GptB200Error when a kernel set a device-side error flag (a wait
+        that ran out, a token id outside the vocabulary, a non-finite gradient
+        norm), and FloatingPointError when the loss or gradient norm is not
+        finite or the learning rate is negative, as the reference's logging
+        path does through finite_metric (rig/mesh.py:214-223). Call it on log
+        steps; it costs one device synchronisation."""
+
+        from .mesh import finite_metric
+
+        flags = _lib.load().gptb200_device_error_flags(1)
+        if flags:
+            raise _lib.GptB200Error(f"device-side error flags 0x{flags:x} after step {step}")
+        if not 1 <= step <= self.history.shape[0]:
+            raise ValueError(f"step {step} is outside the history (1..{self.history.shape[0]})")
+        loss, lr, gn = (float(v) for v in self.history[step - 1].tolist())
+        return {"train_loss": finite_metric("train_loss", loss),
+                "learning_rate": finite_metric("learning_rate", lr),
+                "grad_norm": finite_metric("grad_norm", gn)}
 
     # ------------------------------------------------------------ artifacts
     def training_history(self, final_step: int) -> np.ndarray:

@@ -1,7 +1,7 @@
 """Layer building blocks with the signatures of the reference's rig/nn.py.
 
-`rms_norm` (rig/nn.py:26-33) and `linear` (:55-56) are differentiable
-(torch.autograd) wrappers over the libgptb200 kernels; `normal`,
+`rms_norm` (rig/nn.py:26-33), `apply_rotary` (:36-52) and `linear` (:55-56)
+are differentiable (torch.autograd) wrappers over the libgptb200 kernels; `normal`,
 `parameter_count` and `flatten_arrays` are the reference's host helpers
 (:20-23, :59-77). Inputs are CUDA tensors; there is no CPU path.
 """
@@ -59,6 +59,47 @@ def rms_norm(x: torch.Tensor, scale: torch.Tensor, dtype: Any = torch.bfloat16) 
     return _RmsNorm.apply(x.to(torch.bfloat16), scale)
 
 
+_ROPE_TABLES: dict[tuple, tuple[torch.Tensor, torch.Tensor]] = {}
+
+
+def _rope(length: int, head_dim: int, device) -> tuple[torch.Tensor, torch.Tensor]:
+    key = (length, head_dim, str(device))
+    if key not in _ROPE_TABLES:
+        _ROPE_TABLES[key] = ops.rope_tables(length, head_dim, device)
+    return _ROPE_TABLES[key]
+
+
+class _Rotary(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x):
+        y = x.contiguous().clone()
+        rope = _rope(x.shape[1], x.shape[-1], x.device)
+        ops.rope_apply(y, rope)
+        ctx.rope = rope
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        # the rotation is orthogonal: its transpose (inverse = 1) is the backward
+        dx = dy.to(torch.bfloat16).contiguous().clone()
+        ops.rope_apply(dx, ctx.rope, inverse=True)
+        return dx
+
+
+def apply_rotary(x: torch.Tensor) -> torch.Tensor:
+    """Interleaved base-10,000 rotary positions on one [B, T, H, D] tensor.
+
+    Pairs (2i, 2i+1) of the head dimension are rotated by the angle
+    t * 10000^(-2i/D) at sequence position t, with bf16 cos/sin tables, like
+    rig/nn.py:36-52. Computes in bfloat16 on the GPU (rope_apply kernel)."""
+
+    if x.dim() != 4:
+        raise ValueError(f"apply_rotary expects a [batch, seq, heads, head_dim] tensor, got {tuple(x.shape)}")
+    if x.shape[-1] % 2:
+        raise ValueError("rotary attention requires an even head dimension")
+    return _Rotary.apply(x.to(torch.bfloat16))
+
+
 class _Linear(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, weight, bias):
@@ -81,7 +122,7 @@ class _Linear(torch.autograd.Function):
         ops.gemm(dy2, w16, dx, m=m, n=k, k=n)
         dw = torch.zeros(k, n, dtype=torch.float32, device=x2.device)
         ops.gemm(x2, dy2, dw, a_mn_major=True, b_mn_major=True, m=k, n=n, k=m,
-                 kind=_lib.EPI_F32_ATOMIC)
+                 kind=_lib.EPI_F32_SPLITK)
         db = torch.zeros(n, dtype=torch.float32, device=x2.device)
         ops.colsum(dy2, db)
         return dx.reshape(ctx.shape), dw.to(ctx.dtypes[0]), db.to(ctx.dtypes[1])

@@ -62,12 +62,16 @@ def gemm(
     rope_cols: int = 0,
     row_range: torch.Tensor | None = None,
     range_dim: int = 0,
+    workspace: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """out[m, n] = epilogue(sum_k A[m, k] B[n, k]); see include/gptb200.h.
     row_range: optional int32 device tensor {offset, count} restricting the M
-    rows (range_dim 1) or the K rows (range_dim 2) that take part."""
+    rows (range_dim 1) or the K rows (range_dim 2) that take part.
+    workspace: scratch of EPI_F32_SPLITK (allocated here when not given)."""
 
-    _cuda(a, b, out, bias, residual, aux, row_range)
+    _cuda(a, b, out, bias, residual, aux, row_range, workspace)
+    if kind == _lib.EPI_F32_SPLITK and workspace is None:
+        workspace = _scratch(gemm_workspace_size(m, n, k, kind), out.device)
     if a.dtype != BF16 or b.dtype != BF16:
         raise TypeError("GEMM operands must be bfloat16")
     lda, ldb, ldc = _row_major(a, "a"), _row_major(b, "b"), _row_major(out, "out")
@@ -86,6 +90,7 @@ def gemm(
         rope_cols=int(rope_cols),
         row_range=_ptr(row_range),
         range_dim=int(range_dim) if row_range is not None else 0,
+        workspace=_ptr(workspace),
     )
     if gemm_timer is not None:
         start = torch.cuda.Event(enable_timing=True)
@@ -100,6 +105,16 @@ def gemm(
         end.record()
         gemm_timer.append((start, end, 2.0 * m * n * k))
     return out
+
+
+def gemm_workspace_size(m: int, n: int, k: int, kind: int) -> int:
+    return int(_lib.load().gptb200_gemm_workspace_size(m, n, k, kind))
+
+
+def _scratch(nbytes: int, device) -> torch.Tensor | None:
+    """A fresh uint8 workspace (None when no scratch is needed)."""
+
+    return torch.empty(max(int(nbytes), 16), dtype=torch.uint8, device=device) if nbytes else None
 
 
 # When set to a list, every gemm() call appends (start_event, end_event, flops)
@@ -147,14 +162,21 @@ def rms_norm_fwd(x: torch.Tensor, scale: torch.Tensor, y: torch.Tensor, rstd: to
     return y, rstd
 
 
-def rms_norm_bwd(x, scale, rstd, dy, dx_in, dx_out, dscale, dx_colsum=None, colsum_alpha=1.0):
+def rms_norm_bwd_workspace_size(rows: int, d: int) -> int:
+    return int(_lib.load().gptb200_rms_norm_bwd_workspace_size(rows, d))
+
+
+def rms_norm_bwd(x, scale, rstd, dy, dx_in, dx_out, dscale, dx_colsum=None, colsum_alpha=1.0,
+                 workspace=None):
     """dx_out = dx_in + d(rms_norm)/dx . dy; dscale +=; dx_colsum += alpha * colsum(dx_out)."""
 
-    _cuda(x, scale, rstd, dy, dx_in, dx_out, dscale, dx_colsum)
+    _cuda(x, scale, rstd, dy, dx_in, dx_out, dscale, dx_colsum, workspace)
     rows, d = x.shape
+    if workspace is None:
+        workspace = _scratch(rms_norm_bwd_workspace_size(rows, d), x.device)
     call("gptb200_rms_norm_bwd", x.data_ptr(), scale.data_ptr(), rstd.data_ptr(), dy.data_ptr(),
          _ptr(dx_in), dx_out.data_ptr(), dscale.data_ptr(), _ptr(dx_colsum),
-         float(colsum_alpha), rows, d, _stream())
+         float(colsum_alpha), rows, d, workspace.data_ptr(), _stream())
     return dx_out
 
 
@@ -168,10 +190,21 @@ def embedding_fwd(tokens: torch.Tensor, table: torch.Tensor, out: torch.Tensor):
     return out
 
 
-def embedding_bwd(tokens: torch.Tensor, dout: torch.Tensor, dtable: torch.Tensor):
-    _cuda(tokens, dout, dtable)
+def embedding_bwd_workspace_size(n: int, d: int, vocab: int) -> int:
+    return int(_lib.load().gptb200_embedding_bwd_workspace_size(n, d, vocab))
+
+
+def embedding_bwd(tokens: torch.Tensor, dout: torch.Tensor, dtable: torch.Tensor, workspace=None):
+    """dtable[tokens[i]] += dout[i] in a fixed (token, row) order (bit-reproducible)."""
+
+    _cuda(tokens, dout, dtable, workspace)
+    if tokens.dtype != torch.int32:
+        raise TypeError("token ids must be int32")
+    n, (v, d) = tokens.numel(), dtable.shape
+    if workspace is None:
+        workspace = _scratch(embedding_bwd_workspace_size(n, d, v), dtable.device)
     call("gptb200_embedding_bwd", tokens.data_ptr(), dout.data_ptr(), dtable.data_ptr(),
-         tokens.numel(), dtable.shape[1], dtable.shape[0], _stream())
+         n, d, v, workspace.data_ptr(), _stream())
     return dtable
 
 
@@ -306,10 +339,19 @@ def lce_bwd(hidden, embedding, targets, lse, dlosses, v_semantic, dhidden, dembe
 
 
 # ----------------------------------------------------------------- misc
-def colsum(x: torch.Tensor, out: torch.Tensor, alpha: float = 1.0):
-    _cuda(x, out)
+def colsum_workspace_size(rows: int, n: int) -> int:
+    return int(_lib.load().gptb200_colsum_workspace_size(rows, n))
+
+
+def colsum(x: torch.Tensor, out: torch.Tensor, alpha: float = 1.0, workspace=None):
+    """out += alpha * x.sum(0) (fp32, fixed summation order)."""
+
+    _cuda(x, out, workspace)
     rows, n = x.shape
-    call("gptb200_colsum", x.data_ptr(), rows, n, float(alpha), out.data_ptr(), _stream())
+    if workspace is None:
+        workspace = _scratch(colsum_workspace_size(rows, n), x.device)
+    call("gptb200_colsum", x.data_ptr(), rows, n, float(alpha), out.data_ptr(),
+         workspace.data_ptr(), _stream())
     return out
 
 

@@ -62,19 +62,43 @@ def nest_params(flat: Mapping[str, np.ndarray], layers: int) -> dict[str, Any]:
     return tree
 
 
+def _atomic_write(dest: pathlib.Path, write) -> None:
+    """Runs write(binary file) into a temporary file beside `dest`, flushes it
+    to disk, then renames it over `dest` (and syncs the directory entry), so a
+    reader sees either the old file or the complete new one."""
+
+    import tempfile
+
+    dest = pathlib.Path(dest)
+    fd, tmp_name = tempfile.mkstemp(prefix=f".{dest.name}.", suffix=".partial", dir=dest.parent)
+    try:
+        with os.fdopen(fd, "wb") as fh:
+            write(fh)
+            fh.flush()
+            os.fsync(fh.fileno())
+        os.replace(tmp_name, dest)
+    except BaseException:
+        if os.path.exists(tmp_name):
+            os.unlink(tmp_name)
+        raise
+    dir_fd = os.open(dest.parent, os.O_RDONLY)
+    try:
+        os.fsync(dir_fd)
+    finally:
+        os.close(dir_fd)
+
+
 def save_checkpoint(output_dir: pathlib.Path, params: Any, metadata: Mapping[str, Any]) -> None:
+    """checkpoint.npz in `output_dir`: the flattened fp32 parameters under
+    `params/...` plus `metadata.json` (UTF-8 JSON with sorted keys, stored as
+    uint8), the archive layout of rig/runlog.py:96-115."""
+
     output_dir = pathlib.Path(output_dir)
     output_dir.mkdir(parents=True, exist_ok=True)
-    arrays = flatten_arrays(params)
-    arrays["metadata.json"] = np.frombuffer(
-        json.dumps(metadata, sort_keys=True).encode("utf-8"), dtype=np.uint8)
-    dest = output_dir / CHECKPOINT_NAME
-    tmp = output_dir / f".{CHECKPOINT_NAME}.tmp"
-    with tmp.open("wb") as fh:
-        np.savez(fh, **arrays)
-        fh.flush()
-        os.fsync(fh.fileno())
-    os.replace(tmp, dest)
+    entries = flatten_arrays(params)
+    blob = json.dumps(metadata, sort_keys=True).encode("utf-8")
+    entries["metadata.json"] = np.frombuffer(blob, dtype=np.uint8)
+    _atomic_write(output_dir / CHECKPOINT_NAME, lambda fh: np.savez(fh, **entries))
 
 
 def load_checkpoint(path: pathlib.Path) -> tuple[dict[str, np.ndarray], dict[str, Any]]:

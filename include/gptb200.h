@@ -43,6 +43,13 @@ const char* gptb200_status_string(int status);
  * error, else GPTB200_EDEVICE. Synchronizes the device. */
 int gptb200_device_error(int clear);
 
+/* The same flags as a bit mask (0: none). Synchronizes the device. */
+#define GPTB200_DEVERR_GEMM 1         /* a GEMM / cross-entropy wait ran out of time */
+#define GPTB200_DEVERR_ATTENTION 2    /* an attention wait ran out of time */
+#define GPTB200_DEVERR_TOKEN_RANGE 4  /* the embedding gather saw an id outside [0, vocab) */
+#define GPTB200_DEVERR_NONFINITE 8    /* the optimizer saw a NaN/inf loss or gradient norm */
+int gptb200_device_error_flags(int clear);
+
 /* Number of kernels this library has launched in this process (all devices).
  * Used by the benchmark to report how many native launches a step makes; no
  * reference counterpart. */
@@ -69,6 +76,10 @@ uint64_t gptb200_launch_count(void);
 #define GPTB200_EPI_BIAS_ROPE 5  /* C bf16 = bf16(acc)+bias, then columns < rope_cols rotated by
                                     RoPE at position (row % rope_seq), pairs (2i, 2i+1) within
                                     each 64-wide head (the QKV projection + apply_rotary) */
+#define GPTB200_EPI_F32_SPLITK 6 /* C fp32 += alpha*acc; K may be split across CTAs, each split
+                                    writing its partial product to its own slab of `workspace`
+                                    (gptb200_gemm_workspace_size bytes, 0 when K is not split),
+                                    the slabs then added in split order: bit-reproducible */
 
 typedef struct gptb200_epilogue {
   int kind;              /* GPTB200_EPI_* */
@@ -91,7 +102,13 @@ typedef struct gptb200_epilogue {
    * token buffer whose sizes are only known on the device. */
   const int32_t* row_range;
   int range_dim;
+  void* workspace;       /* EPI_F32_SPLITK: scratch of gptb200_gemm_workspace_size bytes */
 } gptb200_epilogue;
+
+/* Scratch bytes gptb200_gemm needs for an m x n x k product with epilogue
+ * `kind` on the current device (0 for every kind but EPI_F32_SPLITK, and for
+ * that one when K is not split). */
+size_t gptb200_gemm_workspace_size(int64_t m, int64_t n, int64_t k, int kind);
 
 int gptb200_gemm(const void* a, int a_mn_major, int64_t lda, const void* b, int b_mn_major,
                  int64_t ldb, void* c, int64_t ldc, int64_t m, int64_t n, int64_t k,
@@ -111,10 +128,14 @@ int gptb200_rms_norm_fwd(const void* x, const void* scale, void* y, float* rstd,
  * dscale (fp32 [d]) is accumulated into (+=). With dx_colsum != NULL the column
  * sums of dx_out times colsum_alpha are accumulated into dx_colsum (fp32 [d]):
  * the bias gradient of the residual branch that consumed this gradient.
- * Replaces the XLA autodiff of rig/nn.py:26-33. */
+ * Both column reductions add per-block partials (kept in `workspace`, sized by
+ * gptb200_rms_norm_bwd_workspace_size) in a fixed order: repeated calls give
+ * bit-identical results. Replaces the XLA autodiff of rig/nn.py:26-33. */
+size_t gptb200_rms_norm_bwd_workspace_size(int64_t rows, int64_t d);
 int gptb200_rms_norm_bwd(const void* x, const void* scale, const float* rstd, const void* dy,
                          const void* dx_in, void* dx_out, float* dscale, float* dx_colsum,
-                         float colsum_alpha, int64_t rows, int64_t d, void* stream);
+                         float colsum_alpha, int64_t rows, int64_t d, void* workspace,
+                         void* stream);
 
 /* ------------------------------------------------------------------ embedding
  * out[i, :] = bf16(table[tokens[i], :]); Replaces recipes/reference/train.py:1107
@@ -123,9 +144,14 @@ int gptb200_rms_norm_bwd(const void* x, const void* scale, const float* rstd, co
  * rig/tokens.py:262-268). */
 int gptb200_embedding_fwd(const int32_t* tokens, const void* table, void* out, int64_t n,
                           int64_t d, int64_t vocab, void* stream);
-/* dtable[tokens[i], :] += dout[i, :] (fp32 atomics). Backward of the gather. */
+/* dtable[tokens[i], :] += dout[i, :] (fp32). Backward of the gather. The rows
+ * are sorted by (token, row) on the device and each token's rows are added in
+ * that order, so the result is bit-identical from run to run (no atomics).
+ * Tokens outside [0, vocab) contribute nothing. d must be a multiple of 8;
+ * workspace of gptb200_embedding_bwd_workspace_size bytes, 16-byte aligned. */
+size_t gptb200_embedding_bwd_workspace_size(int64_t n, int64_t d, int64_t vocab);
 int gptb200_embedding_bwd(const int32_t* tokens, const void* dout, float* dtable, int64_t n,
-                          int64_t d, int64_t vocab, void* stream);
+                          int64_t d, int64_t vocab, void* workspace, void* stream);
 
 /* ------------------------------------------------------------------ RoPE
  * Tables of the interleaved base-10000 rotary embedding of rig/nn.py:36-52:
@@ -196,7 +222,7 @@ int gptb200_attention_bwd(const void* q, const void* k, const void* v, int64_t s
  * (gptb200_epilogue.row_range), so no host synchronisation is needed.
  * stats (fp32, per layer, accumulated): [0, E) router-probability sums,
  * [E, 2E) assignment counts, entropy sum, top-1 gate sum, sum of squared
- * logits. E <= 16, top_k <= 4; the backward supports E in {2, 4, 8, 16}. */
+ * logits. 1 <= E <= 16, 1 <= top_k <= min(4, E). */
 size_t gptb200_moe_rows(int64_t tokens, int32_t top_k, int32_t experts);
 size_t gptb200_moe_dispatch_workspace_size(int64_t tokens, int32_t top_k, int32_t experts);
 /* logits fp32 [tokens, E] = x (bf16 [tokens, d], promoted to fp32) . router_w
@@ -287,14 +313,19 @@ int gptb200_lce_bwd(const void* hidden, const void* embedding, const int32_t* ta
                     void* workspace, void* stream);
 
 /* ------------------------------------------------------------------ reductions
- * out[j] += sum_i x[i, j] for bf16 x [rows, n] (bias gradients), scaled by alpha. */
-/* Evaluation reduction of recipes/reference/train.py:1494-1525 (eval_step):
+ * Evaluation reduction of recipes/reference/train.py:1494-1525 (eval_step):
  * out[0] = sum(losses * mask), out[1] = sum(mask), both fp32, over n per-token
  * losses (from gptb200_lce_fwd) and an fp32 mask. Deterministic (one block). */
 int gptb200_masked_loss_sum(const float* losses, const float* mask, int64_t n, float* out,
                             void* stream);
 
-int gptb200_colsum(const void* x, int64_t rows, int64_t n, float alpha, float* out, void* stream);
+/* out[j] += alpha * sum_i x[i, j] for bf16 x [rows, n] (the bias gradients of
+ * recipes/reference/train.py's projections, XLA's reduction of the bias
+ * cotangent). Per-block partials in `workspace` (gptb200_colsum_workspace_size
+ * bytes) are added in a fixed order: bit-identical from run to run. */
+size_t gptb200_colsum_workspace_size(int64_t rows, int64_t n);
+int gptb200_colsum(const void* x, int64_t rows, int64_t n, float alpha, float* out,
+                   void* workspace, void* stream);
 
 /* ------------------------------------------------------------------ optimizer
  * CompleteP AdamW over one flat fp32 parameter buffer, replacing
@@ -353,17 +384,25 @@ uint64_t gptb200_mix_uint64(uint64_t value);
 /* Keyed bounded Feistel permutation of rig/tokens.py:136-168. Returns the
  * image of `value` in [0, size), or UINT64_MAX for value >= size. */
 uint64_t gptb200_permute_bounded(uint64_t value, uint64_t size, uint64_t key);
-/* Copies `rows` windows of seq_len+1 tokens for global ordinals
- * first_ordinal.. into out (int32 [rows, seq_len+1]), given one epoch's plan:
- * ordered_shards[i] / ordered_cumulative[i] (int64, n_shards entries) from
- * rig/tokens.py:222-236, and the shard data pointers/lengths (uint16 tokens).
- * All ordinals must belong to the epoch `epoch_ordinal_base / windows_per_epoch`
- * whose key is epoch_key. Returns 0, or GPTB200_ERANGE if a token is >= vocab. */
-int gptb200_gather_windows(const uint16_t* const* shard_data, const int64_t* shard_lengths,
-                           const int64_t* ordered_shards, const int64_t* ordered_cumulative,
-                           int64_t n_shards, int64_t windows_per_epoch, uint64_t epoch_key,
-                           int64_t first_epoch_ordinal, int64_t rows, int64_t seq_len,
-                           int64_t vocab, int32_t* out);
+/* Element types of token shards. */
+#define GPTB200_TOKENS_U8 0
+#define GPTB200_TOKENS_U16 1
+#define GPTB200_TOKENS_I32 2
+#define GPTB200_TOKENS_U32 3
+#define GPTB200_TOKENS_I64 4
+/* Windows first .. first + rows - 1 of epoch `epoch` of the shuffled stream
+ * (rig/tokens.py:221-254), each seq_len + 1 tokens, into out (int32
+ * [rows, seq_len + 1]). shards/lengths: n_shards host arrays of element type
+ * `dtype`; order: the epoch's shard order (int64 permutation of
+ * 0..n_shards-1, the caller's numpy PCG64 draw of rig/tokens.py:222-227).
+ * Computes the epoch's window table, the epoch key mix(seed ^ mix(epoch)),
+ * the keyed permutation of each window ordinal and the copy. The ordinals
+ * must lie inside the epoch. Returns 0, GPTB200_ERANGE if a token lies
+ * outside [0, vocab) (the window is still copied), or GPTB200_EINVAL. */
+int gptb200_epoch_windows(const void* const* shards, const int64_t* lengths, int64_t n_shards,
+                          int dtype, const int64_t* order, int64_t seq_len, uint64_t seed,
+                          int64_t epoch, int64_t first, int64_t rows, int64_t vocab,
+                          int32_t* out);
 
 #ifdef __cplusplus
 }

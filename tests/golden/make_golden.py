@@ -70,8 +70,25 @@ def main(reference_root: str) -> None:
         **{f"shard_{i}": s for i, s in enumerate(shards)},
         **streams,
     )
-    print("wrote", out / "tokens_hash.npz", out / "tokens_stream.npz")
+    # ShardedTokens.sample (random windows, rig/tokens.py:81-105) and
+    # ShardedTokens.sequential (:107-124) over the same ragged shards plus a
+    # shard too short to hold a window.
+    short = rng.integers(0, vocab, size=40, dtype=np.uint16)
+    split = rt.ShardedTokens(shards + [short])
+    sampled = {"short_shard": short}
+    for seed, (batch, seq) in enumerate([(8, 64), (33, 100), (5, 2000), (1, 4096)]):
+        draw = np.random.default_rng(1000 + seed)
+        sampled[f"sample_{seed}"] = np.stack([split.sample(draw, batch, seq) for _ in range(4)])
+        sampled[f"sample_shape_{seed}"] = np.array([batch, seq], np.int64)
+    for i, (index, batch, seq) in enumerate([(0, 8, 64), (5, 8, 64), (1000, 3, 500),
+                                             (7, 16, 1000)]):
+        sampled[f"seq_{i}"] = split.sequential(index, batch, seq)
+        sampled[f"seq_args_{i}"] = np.array([index, batch, seq], np.int64)
+    np.savez_compressed(out / "tokens_sample.npz", **sampled)
+    print("wrote", out / "tokens_hash.npz", out / "tokens_stream.npz", out / "tokens_sample.npz")
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit(f"usage: python {sys.argv[0]} <path of the reference checkout>")
+    main(sys.argv[1])

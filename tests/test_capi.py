@@ -42,3 +42,9 @@ def test_argument_errors_are_status_codes():
     assert lib.gptb200_lce_fwd(None, None, None, 1, 8, 8, 8, None, None, None, None, None) == 1
     assert lib.gptb200_attention_bwd_workspace_size(0, 1, 1) == 0
     assert lib.gptb200_lce_fwd_workspace_size(131072, 50304) > 131072 * 197 * 8
+    # scratch sizes are pure host arithmetic
+    assert lib.gptb200_gemm_workspace_size(768, 768, 131072, _lib.EPI_F32) == 0
+    assert lib.gptb200_gemm_workspace_size(768, 768, 64, _lib.EPI_F32_SPLITK) == 0
+    assert lib.gptb200_embedding_bwd_workspace_size(131072, 768, 50304) >= 4 * 131072 * 4
+    assert lib.gptb200_embedding_bwd(None, None, None, 8, 8, 8, None, None) == 1
+    assert lib.gptb200_colsum(None, 8, 8, 1.0, None, None, None) == 1

@@ -54,3 +54,19 @@ def test_local_batch_slices_partition_the_global_batch():
     assert all(s.stop - s.start == 16 for s in rows)
     with pytest.raises(ValueError):
         local_batch_slice(128, 0, 3)
+
+
+def test_finite_metric_raises_like_the_reference():
+    import math
+
+    import pytest
+
+    from rig_b200.mesh import finite_metric
+
+    assert finite_metric("loss", 2.5) == 2.5
+    assert finite_metric("lr", 0.0) == 0.0
+    for bad in (math.nan, math.inf, -1.0):
+        with pytest.raises(FloatingPointError):
+            finite_metric("loss", bad)
+    with pytest.raises(FloatingPointError):
+        finite_metric("tokens_per_second", 0.0, positive=True)

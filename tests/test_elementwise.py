@@ -67,6 +67,41 @@ def test_embedding(cuda):
     assert torch.allclose(dt.cpu(), expect, atol=1e-4)
 
 
+def _skewed_tokens(n, vocab, seed):
+    """Zipf-like ids (a few tokens own long runs that cross many blocks of the
+    sorted order), plus a block of one repeated id and a few invalid ids."""
+
+    g = torch.Generator().manual_seed(seed)
+    ranks = torch.multinomial(1.0 / torch.arange(1, vocab + 1).float() ** 1.1, n, replacement=True,
+                              generator=g)
+    tok = ranks.to(torch.int32)
+    tok[n // 3 : n // 3 + 3000] = 7  # one id in 3000 consecutive rows
+    tok[5] = -1
+    tok[n - 2] = vocab  # outside [0, vocab): contributes nothing
+    return tok
+
+
+@pytest.mark.parametrize("n,d,vocab", [(131072, 768, 50304), (5000, 8, 70000), (333, 64, 256),
+                                       (1, 16, 10)])
+def test_embedding_bwd_ordered(cuda, n, d, vocab):
+    """The sorted scatter matches an fp64 index_add (invalid ids dropped), adds
+    into the existing table, and repeats bit for bit."""
+
+    tok = _skewed_tokens(n, vocab, 3) if n > 1 else torch.tensor([4], dtype=torch.int32)
+    dout = torch.randn(n, d, generator=torch.Generator().manual_seed(4)).bfloat16()
+    base = torch.randn(vocab, d, generator=torch.Generator().manual_seed(5))
+    outs = []
+    for _ in range(2):
+        dt = base.to(cuda)
+        ops.embedding_bwd(tok.to(cuda), dout.to(cuda), dt)
+        outs.append(dt.cpu())
+    torch.cuda.synchronize()
+    valid = (tok >= 0) & (tok < vocab)
+    expect = base.double().index_add_(0, tok[valid].long(), dout[valid].double())
+    assert torch.allclose(outs[0].double(), expect, atol=2e-3 + 1e-5 * expect.abs().max().item())
+    assert torch.equal(outs[0], outs[1])
+
+
 def test_rope_tables(cuda):
     cos, sin = ops.rope_tables(1024, 64, cuda)
     ec, es = ref.rope_tables(1024, 64)
@@ -82,6 +117,32 @@ def test_colsum(cuda, rows, n):
     out = torch.full((n,), 1.0, device=cuda)
     ops.colsum(x.to(cuda), out, alpha=0.5)
     assert torch.allclose(out.cpu(), 1.0 + 0.5 * x.float().sum(0), atol=1e-3, rtol=1e-4)
+
+
+def test_reductions_repeat_bit_for_bit(cuda):
+    """RMSNorm-backward column reductions and colsum add per-block partials in
+    a fixed order: two calls on the same inputs agree exactly."""
+
+    rows, d = 131072, 768
+    g = torch.Generator().manual_seed(9)
+    x = torch.randn(rows, d, generator=g).bfloat16().to(cuda)
+    s = (1 + 0.1 * torch.randn(d, generator=g)).bfloat16().to(cuda)
+    dy = torch.randn(rows, d, generator=g).bfloat16().to(cuda)
+    y = torch.empty_like(x)
+    r = torch.empty(rows, device=cuda)
+    ops.rms_norm_fwd(x, s, y, r)
+    res = []
+    for _ in range(2):
+        dx = torch.empty_like(x)
+        dscale = torch.zeros(d, device=cuda)
+        col = torch.zeros(d, device=cuda)
+        ops.rms_norm_bwd(x, s, r, dy, None, dx, dscale, col, 0.5)
+        cs = torch.zeros(3 * d, device=cuda)
+        ops.colsum(torch.cat([dx, dx, dx], 1), cs, 2.0)
+        res.append((dscale.cpu(), col.cpu(), cs.cpu()))
+    for a, b in zip(*res):
+        assert torch.equal(a, b)
+    assert torch.allclose(res[0][2], 4.0 * res[0][1].repeat(3), rtol=1e-5, atol=1e-2)
 
 
 @pytest.mark.parametrize("n", [1, 7, 4096, 100003])

@@ -84,6 +84,30 @@ def test_f32_atomic_split_k(cuda, k):
     assert _rel(c, ref) < 1e-5
 
 
+@pytest.mark.parametrize("m,n,k", [(768, 2304, 64), (768, 2304, 4096), (768, 768, 131072),
+                                   (3072, 768, 16384), (200, 136, 9000)])
+def test_f32_splitk_ordered(cuda, m, n, k):
+    """Weight-gradient epilogue with K split over CTAs: each split's partial
+    goes to its own slab and the slabs are added in split order, so the result
+    equals the fp32 product and repeats bit for bit."""
+
+    a, b, a_st, b_st = _operands(m, n, k, 1, 1, cuda, 7)
+    ws = ops.gemm_workspace_size(m, n, k, _lib.EPI_F32_SPLITK)
+    if k >= 4096 * 2:
+        assert ws >= 2 * m * n * 4  # K is split
+    outs = []
+    for _ in range(2):
+        c = torch.ones(m, n, device=cuda)
+        ops.gemm(a_st, b_st, c, a_mn_major=True, b_mn_major=True, m=m, n=n, k=k,
+                 kind=_lib.EPI_F32_SPLITK, alpha=0.5)
+        outs.append(c)
+    torch.cuda.synchronize()
+    assert ops.device_error() == 0
+    ref = 1.0 + 0.5 * (a.float() @ b.float().t())
+    assert _rel(outs[0], ref) < 1e-5
+    assert torch.equal(outs[0], outs[1])
+
+
 def test_f32_store_and_accumulate(cuda):
     m, n, k = 600, 768, 512
     a, b, a_st, b_st = _operands(m, n, k, 1, 1, cuda, 4)
