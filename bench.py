@@ -297,6 +297,156 @@ def run_op(args) -> None:
     }), flush=True)
 
 
+def run_kernels(args) -> None:
+    """Memory-bound kernels of the step, one entry point at a time, at the
+    shapes of the 125M step on one GPU (N = 131,072 tokens, d 768, hidden
+    3072, vocabulary 50,304, 123.7 M parameters) and of a routed layer of the
+    same width (8 experts, top-2, expert width 1536). Each timed call is
+    bracketed by CUDA events on the launching stream after a 256 MB L2 flush;
+    achieved GB/s = the entry point's algorithmic bytes (stated per case:
+    every input read once, every output written once) / its mean time,
+    against the measured HBM copy bandwidth. One JSON line per case, then a
+    summary line."""
+
+    from rig_b200 import _lib, ops
+    from rig_b200.config import load_config
+    from rig_b200.model import ParamLayout
+    from rig_b200.tokens import zipf_tokens
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    peaks = measured_peaks()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    N, d, h, V = 131072, 768, 3072, 50304
+    g = torch.Generator(device="cpu").manual_seed(0)
+    bf = lambda *shape: torch.randn(*shape, generator=g).bfloat16().to(dev)  # noqa: E731
+    x, dy, dxi = bf(N, d), bf(N, d), bf(N, d)
+    scale = (1 + 0.1 * torch.randn(d, generator=g)).bfloat16().to(dev)
+    y, dx = torch.empty_like(x), torch.empty_like(x)
+    rstd = torch.empty(N, device=dev)
+    dscale, dcol = torch.zeros(d, device=dev), torch.zeros(d, device=dev)
+    ops.rms_norm_fwd(x, scale, y, rstd)
+    rws = ops._scratch(ops.rms_norm_bwd_workspace_size(N, d), dev)
+    u = bf(N, h)
+    bgrad = torch.zeros(h, device=dev)
+    cws = ops._scratch(ops.colsum_workspace_size(N, h), dev)
+    tok = torch.from_numpy(zipf_tokens(N, V, 3).astype(np.int32)).to(dev)
+    table = bf(V, d)
+    emb = torch.empty(N, d, dtype=torch.bfloat16, device=dev)
+    dtable = torch.zeros(V, d, device=dev)
+    ews = ops._scratch(ops.embedding_bwd_workspace_size(N, d, V), dev)
+    uniq = int(torch.unique(tok).numel())
+    cfg = load_config("baseline_125m")
+    layout = ParamLayout(cfg)
+    P = layout.numel
+    params = (0.02 * torch.randn(P, generator=g)).to(dev)
+    grads = (1e-3 * torch.randn(P, generator=g)).to(dev)
+    m1, v1 = torch.zeros_like(params), torch.zeros_like(params)
+    pbf = torch.empty(P, dtype=torch.bfloat16, device=dev)
+    groups = (_lib.TensorGroup * 1)(_lib.TensorGroup(offset=0, size=P, lr_mult=1.0, eps_mult=1.0,
+                                                      wd_mult=1.0, decay=1))
+    groups_dev = torch.frombuffer(bytearray(bytes(groups)), dtype=torch.uint8).to(dev)
+    adam_cfg = _lib.AdamWConfig(learning_rate=2 ** -8, horizon_lr_scale=1.0, min_lr_ratio=0.1,
+                                warmup_steps=10, total_steps=10 ** 6, beta1=0.9, beta2=0.95,
+                                eps=1e-8, eps_horizon_scale=1.0, weight_decay=0.1,
+                                wd_horizon_scale=1.0, grad_clip=0.0, grad_scale=1.0)
+    step = torch.zeros(1, dtype=torch.int32, device=dev)
+    aws = ops.adamw_workspace(P, dev)
+    # split-K reduction of the QKV weight gradient (768 x 2304 over K = N)
+    slabs = ops.gemm_workspace_size(d, 3 * d, N, _lib.EPI_F32_SPLITK) // (d * 3 * d * 4)
+    # routed layer: 8 experts, top-2, expert width 1536
+    E, k, eh = 8, 2, 2 * d
+    R = ops.moe_rows(N, k, E)
+    router_w = (0.02 * torch.randn(d, E, generator=g)).to(dev)
+    logits = torch.empty(N, E, device=dev)
+    chosen = torch.empty(N, k, dtype=torch.int32, device=dev)
+    gate = torch.empty(N, k, device=dev)
+    stats = torch.zeros(2 * E + 3, device=dev)
+    seg = torch.zeros(E, 2, dtype=torch.int32, device=dev)
+    total = torch.zeros(1, dtype=torch.int32, device=dev)
+    pos = torch.empty(N, k, dtype=torch.int32, device=dev)
+    src = torch.empty(R, dtype=torch.int32, device=dev)
+    grouped = torch.empty(R, d, dtype=torch.bfloat16, device=dev)
+    mws = ops.moe_dispatch_workspace(N, k, E, dev)
+    ops.moe_route(x, router_w, logits, chosen, gate, stats)
+    ops.moe_dispatch(chosen, x, E, seg, total, pos, src, grouped, mws)
+    out_rows = bf(R, d)
+    xo = torch.empty_like(x)
+    dout_rows = torch.empty(R, d, dtype=torch.bfloat16, device=dev)
+    dgate = torch.empty(N, k, device=dev)
+    bal = torch.zeros(E, device=dev)
+    dgrouped = bf(R, d)
+    drw = torch.zeros(d, E, device=dev)
+    dxr = torch.empty_like(x)
+    hid = bf(R, eh)
+    bexp = torch.zeros(E, eh, device=dev)
+
+    B2 = 2  # bf16 bytes
+    cases = [
+        ("rms_norm_fwd", lambda: ops.rms_norm_fwd(x, scale, y, rstd), 2 * N * d * B2 + 4 * N,
+         "read x, write y + rstd"),
+        ("rms_norm_bwd", lambda: ops.rms_norm_bwd(x, scale, rstd, dy, dxi, dx, dscale, dcol, 1.0,
+                                                  workspace=rws), 4 * N * d * B2 + 4 * N,
+         "read x, dy, dx_in, rstd; write dx (dscale and column sums fused)"),
+        ("colsum", lambda: ops.colsum(u, bgrad, 1.0, workspace=cws), N * h * B2,
+         "read the [N, 3072] bias-gradient source once"),
+        ("embedding_fwd", lambda: ops.embedding_fwd(tok, table, emb), 2 * N * d * B2 + 4 * N,
+         "gather N rows, write N rows"),
+        ("embedding_bwd", lambda: ops.embedding_bwd(tok, dy, dtable, workspace=ews),
+         N * d * B2 + 4 * N + 2 * uniq * d * 4,
+         f"read dout and ids, read+write the {uniq} touched fp32 rows"),
+        ("adamw_step", lambda: ops.adamw_step(params, m1, v1, grads, groups_dev, 1, adam_cfg, step,
+                                              None, None, pbf, aws), 30 * P,
+         "p, m, v read+write, g read (fp32), bf16 mirror write: 30 B/param"),
+        ("cast_bf16", lambda: ops.cast_bf16(params, pbf), 6 * P, "fp32 read, bf16 write"),
+        ("moe_route", lambda: ops.moe_route(x, router_w, logits, chosen, gate, stats),
+         N * d * B2 + N * E * 4 + N * k * 8, "read x; write logits, choices, gates"),
+        ("moe_dispatch", lambda: ops.moe_dispatch(chosen, x, E, seg, total, pos, src, grouped, mws),
+         N * k * 4 + N * d * B2 * k + R * d * B2 + N * k * 4 + R * 4,
+         "read choices and x rows (k per token); write grouped rows, positions, sources"),
+        ("moe_combine", lambda: ops.moe_combine(out_rows, pos, gate, x, 1.0, xo),
+         N * k * d * B2 + 2 * N * d * B2 + N * k * 8, "read k expert rows + residual, write x"),
+        ("moe_combine_bwd", lambda: ops.moe_combine_bwd(dy, 1.0, out_rows, pos, gate, src, total,
+                                                        dout_rows, dgate),
+         N * d * B2 + 2 * R * d * B2 + N * k * 12, "read dx and expert rows, write d_out rows"),
+        ("moe_route_bwd", lambda: ops.moe_route_bwd(x, router_w, logits, chosen, gate, dgate, bal,
+                                                    dgrouped, pos, drw, dxr),
+         2 * N * d * B2 + N * k * d * B2 + N * E * 4, "read x, logits, k grouped-gradient rows; write dx"),
+        ("moe_segment_colsum", lambda: ops.moe_segment_colsum(hid, seg, E, bexp), R * eh * B2,
+         "read the [rows, 1536] expert buffer once"),
+    ]
+    results = []
+    for name, fn, nbytes, what in cases:
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        t = 0.0
+        for _ in range(args.steps):
+            flush.fill_(1)
+            st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            st.record()
+            fn()
+            en.record()
+            torch.cuda.synchronize()
+            t += st.elapsed_time(en)
+        ms = t / args.steps
+        gbs = nbytes / (ms / 1e3) / 1e9
+        results.append({"kernel": name, "ms": ms, "bytes": nbytes, "bytes_are": what,
+                        "achieved_gbs": gbs, "frac": gbs / peaks["hbm_gbs"]})
+        print(json.dumps(results[-1]), flush=True)
+    if ops.device_error() != 0:
+        raise RuntimeError("device-side error flag set during the kernel benchmark")
+    print(json.dumps({
+        "metric": "memory-bound kernels, achieved HBM GB/s", "unit": "GB/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "peak": peaks["hbm_gbs"],
+        "peak_source": f"{peaks['source']} HBM copy", "splitk_slabs_qkv_wgrad": slabs,
+        "config": {"workload": "125M step shapes: N 131072, d 768, hidden 3072, V 50304; "
+                               "routed layer 8 experts top-2 width 1536",
+                   "l2": "256 MB buffer rewritten between timed calls"},
+        "kernels": {r["kernel"]: round(r["achieved_gbs"], 1) for r in results},
+    }), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -305,13 +455,22 @@ def main() -> None:
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--config", default="baseline_125m")
     ap.add_argument("--seed", type=int, default=3)
+    ap.add_argument("--batch", type=int, default=None,
+                    help="global batch override (reduced cases for profiling; default: the "
+                         "config's 128)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--eager", action="store_true", help="no CUDA graph replay")
+    ap.add_argument("--single-update", action="store_true",
+                    help="one AdamW pass after the backward instead of per-bucket updates")
     ap.add_argument("--atomic-wgrad", action="store_true",
                     help="fp32 atomics for split-K weight gradients (not bit-reproducible)")
-    ap.add_argument("--op", choices=["step", "attention", "lce", "gelu_gemm"], default="step",
+    ap.add_argument("--op", choices=["step", "attention", "lce", "gelu_gemm", "kernels"],
+                    default="step",
                     help="op-level configuration instead of the training step (1 GPU)")
     args = ap.parse_args()
+    if args.op == "kernels":
+        run_kernels(args)
+        return
     if args.op != "step":
         run_op(args)
         return
@@ -319,7 +478,7 @@ def main() -> None:
     from rig_b200.config import load_config
     from rig_b200.mesh import initialize_distributed_runtime
 
-    cfg = load_config(args.config)
+    cfg = load_config(args.config, batch_size=args.batch)
     if args.impl == "reference":
         rank = int(os.environ.get("RANK", "0"))
         run_reference(args, cfg, rank, int(os.environ.get("WORLD_SIZE", "1")))
@@ -345,7 +504,8 @@ def main() -> None:
 
     trainer = GPTTrainer(cfg, local_batch, device, process_group=None, world_size=world,
                          history_steps=max(cfg.steps, total_steps + 1),
-                         deterministic=not args.atomic_wgrad)
+                         deterministic=not args.atomic_wgrad,
+                         overlap_optimizer=False if args.single_update else None)
     trainer.load_params(init_params(cfg, args.seed))
     torch.cuda.synchronize()
 
@@ -450,6 +610,8 @@ def main() -> None:
                                if cfg.experts else ""), "global_batch": cfg.batch_size,
                    "seq_len": cfg.seq_len, "parallelism": f"dp{world}",
                    "bit_reproducible": trainer.deterministic,
+                   "optimizer": "per-bucket AdamW overlapped with the backward"
+                                if trainer.overlap_optimizer else "one AdamW pass after the backward",
                    "l2": "working set (activations ~40 GB/GPU at dp1) far larger than L2"},
         "mfu": mfu, "mfu_peak_tflops": peaks["bf16"], "mfu_peak_source": peaks["source"],
         "mfu_vs_nominal_2250": value * fpt / (world * NOMINAL_BF16_TFLOPS * 1e12),

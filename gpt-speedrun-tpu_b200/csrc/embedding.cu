@@ -59,26 +59,56 @@ __global__ void __launch_bounds__(kSortThreads) radix_upsweep(const int32_t* __r
   hist[(int64_t)threadIdx.x * tiles + blockIdx.x] = cnt[threadIdx.x];
 }
 
-// In-place exclusive scan of `total` ints with one block of 1024 threads.
+// In-place exclusive scan of `total` ints with one block of 1024 threads:
+// the counts go through shared memory in coalesced chunks of 8192, each
+// thread scans 8 consecutive entries, the 1024 sums are scanned by warps.
+constexpr int kScanChunk = 8192;
+
 __global__ void __launch_bounds__(1024) radix_scan(int* __restrict__ h, int64_t total) {
-  __shared__ int part[1024];
-  const int64_t per = (total + 1023) / 1024;
-  const int64_t a = threadIdx.x * per, b = min(total, a + per);
-  int s = 0;
-  for (int64_t i = a; i < b; ++i) s += h[i];
-  part[threadIdx.x] = s;
-  __syncthreads();
-  for (int o = 1; o < 1024; o <<= 1) {
-    const int v = threadIdx.x >= o ? part[threadIdx.x - o] : 0;
+  __shared__ int buf[kScanChunk];
+  __shared__ int wsum[32];
+  __shared__ int carry_s;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  if (threadIdx.x == 0) carry_s = 0;
+  for (int64_t base = 0; base < total; base += kScanChunk) {
+    const int n = (int)min(total - base, (int64_t)kScanChunk);
+    for (int i = threadIdx.x; i < kScanChunk; i += 1024) buf[i] = i < n ? h[base + i] : 0;
     __syncthreads();
-    part[threadIdx.x] += v;
+    int v[8], s = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      v[j] = buf[threadIdx.x * 8 + j];
+      s += v[j];
+    }
+    // inclusive warp scan of the per-thread sums
+    int x = s;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) wsum[w] = x;
     __syncthreads();
-  }
-  int run = part[threadIdx.x] - s;
-  for (int64_t i = a; i < b; ++i) {
-    const int v = h[i];
-    h[i] = run;
-    run += v;
+    if (w == 0) {
+      int t = wsum[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, t, o);
+        if (lane >= o) t += y;
+      }
+      wsum[lane] = t;  // inclusive over warps
+    }
+    __syncthreads();
+    int run = carry_s + (w ? wsum[w - 1] : 0) + x - s;  // exclusive prefix of this thread
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      buf[threadIdx.x * 8 + j] = run;
+      run += v[j];
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += 1024) h[base + i] = buf[i];
+    if (threadIdx.x == 0) carry_s += wsum[31];
+    __syncthreads();
   }
 }
 
@@ -224,32 +254,60 @@ __global__ void __launch_bounds__(kSegThreads) embed_segsum(
   flush(cur, first_run, cur == after);
 }
 
-// Block x finishes the token whose rows start in block x and run past its end.
+// Block x finishes the token whose rows start in block x and run past its
+// end: it adds its tail and the heads of the following blocks the token
+// covers, in block order. The block's threads first find how many blocks the
+// token covers (each thread tests its own candidates), so that the head rows
+// can then be loaded independently of one another.
 __global__ void __launch_bounds__(kSegThreads) embed_fixup(const uint32_t* __restrict__ keys,
                                                            int64_t n, int d, int64_t vocab,
                                                            const float* __restrict__ head,
                                                            const float* __restrict__ tail,
                                                            float* __restrict__ dtable) {
-  const int c8 = (blockIdx.y * kSegThreads + threadIdx.x) * 8;
-  if (c8 >= d) return;
+  __shared__ int last_s;
   const int64_t p0 = (int64_t)blockIdx.x * kSeg, p1 = min(n, p0 + kSeg);
   if (p1 >= n) return;
   const uint32_t k = keys[p1 - 1];
-  if (k >= (uint32_t)vocab || keys[p1] != k) return;     // nothing crosses the end
+  if (k >= (uint32_t)vocab || keys[p1] != k) return;          // nothing crosses the end
   if (keys[p0] == k && p0 > 0 && keys[p0 - 1] == k) return;  // started earlier: not the owner
+  // blocks x > blockIdx.x that the token reaches: those whose first key is k
+  const int64_t nblocks = (n + kSeg - 1) / kSeg;
+  if (threadIdx.x == 0) last_s = (int)blockIdx.x + 1;
+  __syncthreads();
+  for (int64_t base = blockIdx.x + 1;; base += kSegThreads) {
+    const int64_t x = base + threadIdx.x;
+    const bool reach = x < nblocks && keys[x * kSeg] == k;
+    if (reach) atomicMax(&last_s, (int)x);
+    if (!__syncthreads_or(x < nblocks && !reach) && base + kSegThreads < nblocks) continue;
+    break;
+  }
+  __syncthreads();
+  const int last = last_s;
+  const int c8 = (blockIdx.y * kSegThreads + threadIdx.x) * 8;
+  if (c8 >= d) return;
   float acc[8];
   const float4* t4 = reinterpret_cast<const float4*>(tail + blockIdx.x * (int64_t)d + c8);
   float4 a = t4[0], b = t4[1];
   acc[0] = a.x; acc[1] = a.y; acc[2] = a.z; acc[3] = a.w;
   acc[4] = b.x; acc[5] = b.y; acc[6] = b.z; acc[7] = b.w;
-  for (int64_t x = blockIdx.x + 1;; ++x) {
-    const float4* h4 = reinterpret_cast<const float4*>(head + x * (int64_t)d + c8);
-    a = h4[0];
-    b = h4[1];
-    acc[0] += a.x; acc[1] += a.y; acc[2] += a.z; acc[3] += a.w;
-    acc[4] += b.x; acc[5] += b.y; acc[6] += b.z; acc[7] += b.w;
-    const int64_t e = min(n, (x + 1) * kSeg);
-    if (e >= n || keys[e] != k) break;  // the token ends inside block x
+  for (int x = (int)blockIdx.x + 1; x <= last; x += 4) {
+    float4 hv[4][2];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {  // independent loads, then the adds in block order
+      const float4* h4 = reinterpret_cast<const float4*>(head + (int64_t)(x + u) * d + c8);
+      if (x + u <= last) {
+        hv[u][0] = h4[0];
+        hv[u][1] = h4[1];
+      } else {
+        hv[u][0] = hv[u][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (x + u > last) break;
+      acc[0] += hv[u][0].x; acc[1] += hv[u][0].y; acc[2] += hv[u][0].z; acc[3] += hv[u][0].w;
+      acc[4] += hv[u][1].x; acc[5] += hv[u][1].y; acc[6] += hv[u][1].z; acc[7] += hv[u][1].w;
+    }
   }
   add_to_row(dtable + (int64_t)k * d + c8, acc);
 }

@@ -159,6 +159,14 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [c_vp, c_vp, c_vp, c_vp, c_i64, c_vp, ctypes.c_int32, ctypes.POINTER(AdamWConfig),
          c_vp, c_vp, c_vp, c_vp, c_vp, c_vp],
     ),
+    "gptb200_adamw_begin": (c_int, [ctypes.POINTER(AdamWConfig), c_vp, c_vp, c_vp]),
+    "gptb200_adamw_update_range": (
+        c_int,
+        [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_vp, ctypes.c_int32, ctypes.POINTER(AdamWConfig),
+         ctypes.c_int32, c_vp, c_vp, c_vp],
+    ),
+    "gptb200_adamw_end": (
+        c_int, [ctypes.c_int32, ctypes.POINTER(AdamWConfig), c_vp, c_vp, c_vp, c_vp, c_vp]),
     "gptb200_cast_bf16": (c_int, [c_vp, c_vp, c_i64, c_vp]),
     "gptb200_mix_uint64": (ctypes.c_uint64, [ctypes.c_uint64]),
     "gptb200_permute_bounded": (

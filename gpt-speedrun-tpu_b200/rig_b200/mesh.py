@@ -61,16 +61,20 @@ def local_batch_slice(global_batch: int, rank: int, world: int) -> slice:
 class GradientReducer:
     """Bucketed, backward-overlapped SUM all-reduce over a flat gradient buffer."""
 
-    def __init__(self, grads: torch.Tensor, group=None):
+    def __init__(self, grads: torch.Tensor, group=None, on_reduced=None):
         self.grads = grads
         self.group = group
         self.works = []
+        # on_reduced(start, end, work): called right after a bucket's
+        # all-reduce is launched, e.g. to queue its optimizer update behind it
+        self.on_reduced = on_reduced
 
     def launch(self, start: int, end: int) -> None:
-        self.works.append(
-            dist.all_reduce(self.grads[start:end], op=dist.ReduceOp.SUM, group=self.group,
-                            async_op=True)
-        )
+        work = dist.all_reduce(self.grads[start:end], op=dist.ReduceOp.SUM, group=self.group,
+                               async_op=True)
+        self.works.append(work)
+        if self.on_reduced is not None:
+            self.on_reduced(start, end, work)
 
     def finish(self, loss: torch.Tensor | None = None) -> None:
         """Waits for every bucket; `loss` (this rank's mean) becomes the global mean."""

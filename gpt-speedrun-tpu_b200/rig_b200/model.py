@@ -196,6 +196,7 @@ class GPTTrainer:
         world_size: int = 1,
         history_steps: int | None = None,
         deterministic: bool = True,
+        overlap_optimizer: bool | None = None,
     ):
         if config.dtype_name != "bfloat16":
             raise ValueError("the B200 step computes in bfloat16")
@@ -215,6 +216,16 @@ class GPTTrainer:
         # fp32 atomics. The other reductions of the step are always ordered.
         self.deterministic = bool(deterministic)
         self.wgrad_kind = _lib.EPI_F32_SPLITK if deterministic else _lib.EPI_F32_ATOMIC
+        # Without gradient clipping the AdamW update of a bucket does not wait
+        # for the global norm, so with data parallelism each bucket is updated
+        # on a side stream as soon as its all-reduce completes, overlapping the
+        # rest of the backward pass. On one GPU the update only competes with
+        # the backward for HBM bandwidth (measured: no gain), so it stays off.
+        if overlap_optimizer is None:
+            overlap_optimizer = config.grad_clip <= 0.0 and self.world_size > 1
+        if overlap_optimizer and config.grad_clip > 0.0:
+            raise ValueError("overlap_optimizer needs grad_clip <= 0 (clipping needs the global norm)")
+        self.overlap_optimizer = bool(overlap_optimizer)
         self.layout = ParamLayout(config)
         if (config.declared_parameters is not None
                 and self.layout.parameter_count() != config.declared_parameters):
@@ -243,6 +254,7 @@ class GPTTrainer:
             self.g_out_emb = self.grad_view("output_embedding")
         self._alloc_activations()
         self._build_optimizer()
+        self.opt_stream = torch.cuda.Stream(self.device) if self.overlap_optimizer else None
         self.rope = ops.rope_tables(self.T, config.head_dim, dev)
 
     # ------------------------------------------------------------ state views
@@ -316,8 +328,10 @@ class GPTTrainer:
         need = [ops.rms_norm_bwd_workspace_size(N, d),
                 ops.embedding_bwd_workspace_size(N, d, c.vocab_size)]
         need += [ops.colsum_workspace_size(N, w) for w in (3 * d, h)]
-        need += [ops.gemm_workspace_size(m, n, N, self.wgrad_kind) for m, n in wgrad_shapes]
         self.scratch = torch.empty(max(need), dtype=torch.uint8, device=dev)
+        # per-split partial slabs of the ordered split-K weight gradients
+        self.splitk_ws = ops.splitk_workspace(
+            max(ops.gemm_workspace_size(m, n, N, self.wgrad_kind) for m, n in wgrad_shapes), dev)
 
     def _alloc_moe(self) -> None:
         """Per-layer routed buffers (kept for the backward) and shared scratch."""
@@ -500,7 +514,7 @@ class GPTTrainer:
 
         m, n = act.shape[1], dy.shape[1]
         ops.gemm(act, dy, gview, a_mn_major=True, b_mn_major=True, m=m, n=n, k=self.N,
-                 kind=self.wgrad_kind, alpha=alpha, workspace=self.scratch)
+                 kind=self.wgrad_kind, alpha=alpha, workspace=self.splitk_ws)
 
     def _dgrad(self, dy: torch.Tensor, w: torch.Tensor, out: torch.Tensor, **kw):
         """out[N, in] = epilogue(dy[N, out] @ w[in, out]^T)."""
@@ -670,6 +684,9 @@ class GPTTrainer:
 
     def _eager_step(self) -> None:
         self.forward()
+        if self.overlap_optimizer:
+            self._overlapped_backward_and_update()
+            return
         if self.world_size > 1:
             from .mesh import GradientReducer
 
@@ -679,3 +696,41 @@ class GPTTrainer:
         else:
             self.backward()
         self.optimizer_step()
+
+    def _overlapped_backward_and_update(self) -> None:
+        """Backward with each bucket (a block's parameters, then the final norm
+        and embeddings) updated on the optimizer stream once its gradient is
+        final: right after its all-reduce with data parallelism, right after
+        its backward kernels on one GPU. The compute stream waits for the
+        optimizer stream before the next step reads the new parameters."""
+
+        compute = torch.cuda.current_stream(self.device)
+        opt = self.opt_stream
+        ops.adamw_begin(self.adam_cfg, self.step_dev, self.adam_ws)
+        opt.wait_stream(compute)  # the step's scalars
+        slots = []
+
+        def update(start: int, end: int, work=None) -> None:
+            if work is None:
+                opt.wait_stream(compute)
+            with torch.cuda.stream(opt):
+                if work is not None:
+                    work.wait()
+                ops.adamw_update_range(self.params, self.m, self.v, self.grads, start, end,
+                                       self.groups_dev, self.n_groups, self.adam_cfg, len(slots),
+                                       self.params_bf16, self.adam_ws)
+            slots.append((start, end))
+
+        if self.world_size > 1:
+            from .mesh import GradientReducer
+
+            reducer = GradientReducer(self.grads, self.pg, on_reduced=update)
+            self.backward(reduce_hook=reducer.launch)
+            reducer.finish(self.loss)
+        else:
+            self.backward(reduce_hook=update)
+        opt.wait_stream(compute)  # the (all-reduced) loss for the history row
+        with torch.cuda.stream(opt):
+            ops.adamw_end(len(slots), self.adam_cfg, self.step_dev, self.loss, self.history,
+                          self.adam_ws)
+        compute.wait_stream(opt)

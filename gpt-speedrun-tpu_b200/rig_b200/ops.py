@@ -71,7 +71,7 @@ def gemm(
 
     _cuda(a, b, out, bias, residual, aux, row_range, workspace)
     if kind == _lib.EPI_F32_SPLITK and workspace is None:
-        workspace = _scratch(gemm_workspace_size(m, n, k, kind), out.device)
+        workspace = splitk_workspace(gemm_workspace_size(m, n, k, kind), out.device)
     if a.dtype != BF16 or b.dtype != BF16:
         raise TypeError("GEMM operands must be bfloat16")
     lda, ldb, ldc = _row_major(a, "a"), _row_major(b, "b"), _row_major(out, "out")
@@ -109,6 +109,12 @@ def gemm(
 
 def gemm_workspace_size(m: int, n: int, k: int, kind: int) -> int:
     return int(_lib.load().gptb200_gemm_workspace_size(m, n, k, kind))
+
+
+def splitk_workspace(nbytes: int, device) -> torch.Tensor | None:
+    """Workspace of EPI_F32_SPLITK (the per-split partial slabs)."""
+
+    return torch.empty(max(int(nbytes), 16), dtype=torch.uint8, device=device) if nbytes else None
 
 
 def _scratch(nbytes: int, device) -> torch.Tensor | None:
@@ -387,6 +393,25 @@ def adamw_step(params, m, v, grads, groups_dev, n_groups, cfg, step, loss, histo
     call("gptb200_adamw_step", params.data_ptr(), m.data_ptr(), v.data_ptr(), grads.data_ptr(),
          params.numel(), groups_dev.data_ptr(), n_groups, ctypes.byref(cfg), step.data_ptr(),
          _ptr(loss), _ptr(history), _ptr(params_bf16), workspace.data_ptr(), _stream())
+
+
+def adamw_begin(cfg, step, workspace):
+    _cuda(step, workspace)
+    call("gptb200_adamw_begin", ctypes.byref(cfg), step.data_ptr(), workspace.data_ptr(), _stream())
+
+
+def adamw_update_range(params, m, v, grads, begin, end, groups_dev, n_groups, cfg, slot,
+                       params_bf16, workspace):
+    _cuda(params, m, v, grads, groups_dev, params_bf16, workspace)
+    call("gptb200_adamw_update_range", params.data_ptr(), m.data_ptr(), v.data_ptr(),
+         grads.data_ptr(), int(begin), int(end), groups_dev.data_ptr(), n_groups,
+         ctypes.byref(cfg), int(slot), _ptr(params_bf16), workspace.data_ptr(), _stream())
+
+
+def adamw_end(n_slots, cfg, step, loss, history, workspace):
+    _cuda(step, loss, history, workspace)
+    call("gptb200_adamw_end", int(n_slots), ctypes.byref(cfg), step.data_ptr(), _ptr(loss),
+         _ptr(history), workspace.data_ptr(), _stream())
 
 
 def device_error(clear: bool = True) -> int:

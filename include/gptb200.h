@@ -79,7 +79,8 @@ uint64_t gptb200_launch_count(void);
 #define GPTB200_EPI_F32_SPLITK 6 /* C fp32 += alpha*acc; K may be split across CTAs, each split
                                     writing its partial product to its own slab of `workspace`
                                     (gptb200_gemm_workspace_size bytes, 0 when K is not split),
-                                    the slabs then added in split order: bit-reproducible */
+                                    the slabs then added in split order: bit-reproducible.
+                                    Calls sharing a workspace must not overlap on the GPU. */
 
 typedef struct gptb200_epilogue {
   int kind;              /* GPTB200_EPI_* */
@@ -370,6 +371,31 @@ int gptb200_adamw_step(float* params, float* m, float* v, const float* grads, in
                        const gptb200_tensor_group* groups, int32_t n_groups,
                        const gptb200_adamw_config* cfg, int32_t* step, const float* loss,
                        float* history, void* params_bf16, void* workspace, void* stream);
+
+/* The same update in parts, so that each gradient bucket can be updated as
+ * soon as it is final (right after its all-reduce) while the backward pass
+ * goes on, for configurations without gradient clipping (grad_clip <= 0: the
+ * learning rate and bias corrections then do not depend on the global norm;
+ * GPTB200_EUNSUPPORTED otherwise). One step is:
+ *   gptb200_adamw_begin         advances *step, computes this step's scalars
+ *   gptb200_adamw_update_range  per bucket: elements [begin, end) (begin a
+ *                               multiple of 4); stores the bucket's squared
+ *                               gradient sums in slot `slot` (0 <= slot < 256,
+ *                               one slot per bucket)
+ *   gptb200_adamw_end           gradient norm from slots [0, n_slots) in slot
+ *                               order (deterministic), history row, and the
+ *                               non-finite flag.
+ * Same workspace as gptb200_adamw_step; the results equal its results except
+ * for the summation order of the logged gradient norm. Replaces the update
+ * of recipes/reference/train.py:1362-1457 like gptb200_adamw_step. */
+int gptb200_adamw_begin(const gptb200_adamw_config* cfg, int32_t* step, void* workspace,
+                        void* stream);
+int gptb200_adamw_update_range(float* params, float* m, float* v, const float* grads,
+                               int64_t begin, int64_t end, const gptb200_tensor_group* groups,
+                               int32_t n_groups, const gptb200_adamw_config* cfg, int32_t slot,
+                               void* params_bf16, void* workspace, void* stream);
+int gptb200_adamw_end(int32_t n_slots, const gptb200_adamw_config* cfg, const int32_t* step,
+                      const float* loss, float* history, void* workspace, void* stream);
 
 /* fp32 -> bf16 copy of n elements (the compute-dtype cast of train.py's
  * `weight.astype(dtype)`). */

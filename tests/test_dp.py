@@ -35,6 +35,43 @@ def _worker(rank, world, port, out):
         dist.destroy_process_group()
 
 
+def _worker_with_updates(rank, world, port, out):
+    """Each bucket's update is queued right behind its all-reduce (on_reduced)
+    and, after waiting on that work, sees the summed gradient of its range."""
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        grads = torch.arange(100, dtype=torch.float32) * (rank + 1)
+        params = torch.zeros(100)
+        seen = []
+
+        def update(start, end, work):
+            work.wait()
+            params[start:end] -= 0.5 * grads[start:end]
+            seen.append((start, end))
+
+        red = GradientReducer(grads, on_reduced=update)
+        for start, end in ((60, 100), (20, 60), (0, 20)):
+            red.launch(start, end)
+        red.finish(torch.tensor([1.0]))
+        out[rank] = (params.numpy().copy(), seen)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gradient_reducer_bucket_updates_gloo():
+    world = 2
+    port = _free_port()
+    manager = mp.Manager()
+    out = manager.dict()
+    mp.spawn(_worker_with_updates, args=(world, port, out), nprocs=world, join=True)
+    for r in range(world):
+        params, seen = out[r]
+        np.testing.assert_array_equal(params, -0.5 * 3.0 * np.arange(100, dtype=np.float32))
+        assert seen == [(60, 100), (20, 60), (0, 20)]
+
+
 def test_gradient_reducer_gloo():
     world = 2
     port = _free_port()

@@ -151,3 +151,38 @@ def test_cast(cuda, n):
     y = torch.empty(n, device=cuda, dtype=torch.bfloat16)
     ops.cast_bf16(x.to(cuda), y)
     assert torch.equal(y.cpu(), x.bfloat16())
+
+
+def test_apply_rotary_plugin_and_backward(cuda):
+    """rig_b200.nn.apply_rotary (rig/nn.py:36-52): forward equals the
+    restatement, and its gradient is the transpose rotation."""
+
+    from rig_b200 import nn
+
+    x = torch.randn(2, 300, 3, 64).bfloat16()
+    want = ref.apply_rotary(x)
+    xd = x.to(cuda).requires_grad_(True)
+    y = nn.apply_rotary(xd)
+    assert _rel(y.detach().cpu(), want) < 5e-3
+    dy = torch.randn_like(x)
+    y.backward(dy.to(cuda))
+    xx = x.float().requires_grad_(True)
+    ref.apply_rotary(xx).float().backward(dy.float())
+    assert _rel(xd.grad.cpu(), xx.grad) < 1e-2
+    with pytest.raises(ValueError):
+        nn.apply_rotary(torch.zeros(2, 3, 4, device=cuda))
+
+
+def test_device_error_flags(cuda):
+    """A token id outside the vocabulary reaches the gather: the embedding
+    family's flag is raised (and cleared by the read), nothing traps."""
+
+    from rig_b200 import _lib
+
+    assert _lib.load().gptb200_device_error_flags(1) == 0
+    table = torch.randn(100, 64, device=cuda).bfloat16()
+    tok = torch.tensor([3, 100, 5], dtype=torch.int32, device=cuda)
+    out = torch.empty(3, 64, device=cuda, dtype=torch.bfloat16)
+    ops.embedding_fwd(tok, table, out)
+    assert _lib.load().gptb200_device_error_flags(1) == _lib.DEVERR_TOKEN_RANGE
+    assert ops.device_error() == 0

@@ -92,20 +92,21 @@ def test_f32_splitk_ordered(cuda, m, n, k):
     equals the fp32 product and repeats bit for bit."""
 
     a, b, a_st, b_st = _operands(m, n, k, 1, 1, cuda, 7)
-    ws = ops.gemm_workspace_size(m, n, k, _lib.EPI_F32_SPLITK)
+    size = ops.gemm_workspace_size(m, n, k, _lib.EPI_F32_SPLITK)
     if k >= 4096 * 2:
-        assert ws >= 2 * m * n * 4  # K is split
+        assert size >= 2 * m * n * 4  # K is split
+    ws = ops.splitk_workspace(size, cuda)  # one workspace reused by every call below
     outs = []
-    for _ in range(2):
+    for _ in range(3):
         c = torch.ones(m, n, device=cuda)
         ops.gemm(a_st, b_st, c, a_mn_major=True, b_mn_major=True, m=m, n=n, k=k,
-                 kind=_lib.EPI_F32_SPLITK, alpha=0.5)
+                 kind=_lib.EPI_F32_SPLITK, alpha=0.5, workspace=ws)
         outs.append(c)
     torch.cuda.synchronize()
     assert ops.device_error() == 0
     ref = 1.0 + 0.5 * (a.float() @ b.float().t())
     assert _rel(outs[0], ref) < 1e-5
-    assert torch.equal(outs[0], outs[1])
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
 
 
 def test_f32_store_and_accumulate(cuda):

@@ -133,3 +133,56 @@ def test_step_is_bit_reproducible(cuda):
         runs.append((tr.grads.clone(), tr.params.clone(), tr.history[:3].clone()))
     for a, b in zip(*runs):
         assert torch.equal(a, b)
+
+
+def test_checked_metrics_raise_like_the_reference(cuda):
+    """GPTTrainer.checked_metrics: finite rows pass; a non-finite loss raises
+    FloatingPointError (rig/mesh.py:214-223) and the optimizer's non-finite
+    flag is reported."""
+
+    cfg = load_config("smoke_parity")
+    tr = GPTTrainer(cfg, cfg.batch_size, cuda)
+    tr.load_params(init_params(cfg, 0))
+    (x, y), = _batches(cfg, 1)
+    tr.train_step(torch.from_numpy(x).to(cuda), torch.from_numpy(y).to(cuda))
+    m = tr.checked_metrics(1)
+    assert set(m) == {"train_loss", "learning_rate", "grad_norm"} and m["train_loss"] > 0
+    tr.history[0, 0] = float("nan")
+    with pytest.raises(FloatingPointError):
+        tr.checked_metrics(1)
+    # a NaN gradient makes the AdamW kernel raise the non-finite flag
+    tr.forward()
+    tr.backward()
+    tr.grads[5] = float("nan")
+    tr.optimizer_step()
+    from rig_b200 import _lib
+
+    with pytest.raises(_lib.GptB200Error):
+        tr.checked_metrics(2)
+    assert ops.device_error() == 0  # the read cleared the flags
+
+
+def test_bucketed_optimizer_matches_single_update(cuda):
+    """Updating each gradient bucket on the optimizer stream as soon as it is
+    final gives the same parameters and moments, bit for bit, as one AdamW
+    pass after the backward; only the logged gradient norm is summed in
+    another order."""
+
+    cfg = load_config("smoke_parity")
+    params = init_params(cfg, 6)
+    batches = _batches(cfg, 3, seed=13)
+    runs = []
+    for overlap in (False, True):
+        tr = GPTTrainer(cfg, cfg.batch_size, cuda, overlap_optimizer=overlap)
+        tr.load_params(params)
+        for x, y in batches:
+            tr.train_step(torch.from_numpy(x).to(cuda), torch.from_numpy(y).to(cuda))
+        torch.cuda.synchronize()
+        runs.append(tr)
+    a, b = runs
+    assert b.overlap_optimizer and not a.overlap_optimizer
+    for name in ("params", "m", "v", "params_bf16"):
+        assert torch.equal(getattr(a, name), getattr(b, name)), name
+    assert torch.equal(a.history[:3, :2], b.history[:3, :2])
+    assert torch.allclose(a.history[:3, 2], b.history[:3, 2], rtol=1e-6)
+    assert int(b.step_dev.item()) == 3

@@ -15,7 +15,7 @@ import ctypes
 import pytest
 import torch
 
-from rig_b200 import _lib
+from rig_b200 import _lib, ops
 
 pytestmark = pytest.mark.gpu
 
@@ -66,6 +66,7 @@ def test_no_alloc_matches_workspace_entry_point_twice(cuda):
         want = _with_workspace(lib, h, e, t, sv, stream)
         got = _no_alloc(lib, h, e, t, sv, stream)
         torch.cuda.synchronize()
+        assert ops.device_error() == 0  # no GEMM wait ran out inside either call
         for a, b in zip(got[:2], want[:2]):
             ok = torch.isfinite(b)
             assert torch.equal(torch.isfinite(a), ok)
