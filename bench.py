@@ -454,6 +454,7 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--config", default="baseline_125m")
+    ap.add_argument("--tier", default=None, help="tier of the config (default: its default tier)")
     ap.add_argument("--seed", type=int, default=3)
     ap.add_argument("--batch", type=int, default=None,
                     help="global batch override (reduced cases for profiling; default: the "
@@ -478,7 +479,7 @@ def main() -> None:
     from rig_b200.config import load_config
     from rig_b200.mesh import initialize_distributed_runtime
 
-    cfg = load_config(args.config, batch_size=args.batch)
+    cfg = load_config(args.config, batch_size=args.batch, tier=args.tier)
     if args.impl == "reference":
         rank = int(os.environ.get("RANK", "0"))
         run_reference(args, cfg, rank, int(os.environ.get("WORLD_SIZE", "1")))

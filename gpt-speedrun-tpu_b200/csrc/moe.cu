@@ -25,100 +25,154 @@ constexpr int kDispatchBlock = 1024;  // assignments per dispatch block
 __host__ __device__ constexpr int moe_stat_width(int E) { return 2 * E + 3; }
 
 // ------------------------------------------------------------------ routing
-// One warp per token: logits = x(fp32) . W_router (fp32) -- the reference
-// promotes the bf16 activations to fp32 -- softmax probabilities, the top-k
-// logits (ties: lower expert first, like lax.top_k) and the gates (softmax of
-// the chosen logits). Block-level partial statistics, one atomic each.
+// logits = x(fp32) . W_router (fp32) -- the reference promotes the bf16
+// activations to fp32 -- softmax probabilities, the top-k logits (ties: lower
+// expert first, like lax.top_k) and the gates (softmax of the chosen logits).
+// A warp takes kRouteTok tokens at a time: lane l owns the 8-feature chunks
+// l, l + 32, ... of all of them, so each chunk of W (from shared memory) is
+// read once for kRouteTok tokens; the per-expert sums are then reduced across
+// the warp and lane e handles expert e of every token (softmax, entropy,
+// top-k by warp arg-max). Statistics are accumulated per lane, combined per
+// block in warp order and added to `stats` with one atomic per block.
+constexpr int kRouteTok = 4;
+
+__device__ __forceinline__ void warp_argmax(float& v, int& i) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, i, o);
+    if (ov > v || (ov == v && oi < i)) {
+      v = ov;
+      i = oi;
+    }
+  }
+}
+
 __global__ void __launch_bounds__(256) moe_route_kernel(
     const bf16* __restrict__ x, const float* __restrict__ w, int64_t n, int d, int E, int k,
     float* __restrict__ logits, int* __restrict__ chosen, float* __restrict__ gate,
     float* __restrict__ stats) {
-  extern __shared__ float wsm[];  // [E][d] router weights (transposed), then the block stats
-  float* bst = wsm + (size_t)d * E;
-  for (int i = threadIdx.x; i < d * E; i += blockDim.x) wsm[(i % E) * d + i / E] = w[i];
-  for (int i = threadIdx.x; i < moe_stat_width(E); i += blockDim.x) bst[i] = 0.f;
+  extern __shared__ float wsm[];  // [d / 8][E][8] router weights, then [8 warps][stat width]
+  const int width = moe_stat_width(E);
+  float* wst = wsm + (size_t)d * E;
+  const int nch = d / 8;
+  for (int i = threadIdx.x; i < d * E; i += blockDim.x) {
+    const int f = i / E, e = i - f * E;  // w is [d][E]
+    wsm[((f >> 3) * E + e) * 8 + (f & 7)] = w[i];
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  // per-lane statistics: lane e < E the probability sum and count of expert e;
+  // lane 0 the entropy, top-1 gate and squared-logit sums
+  float st_prob = 0.f, st_cnt = 0.f, st_ent = 0.f, st_top1 = 0.f, st_sq = 0.f;
   __syncthreads();
-  const int lane = threadIdx.x & 31;
-  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
-  for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < n;
-       t += warps) {
-    float acc[kMoeMaxE];
+  const int64_t groups = (n + kRouteTok - 1) / kRouteTok;
+  for (int64_t gi = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp; gi < groups;
+       gi += (int64_t)gridDim.x * (blockDim.x >> 5)) {
+    const int64_t t0 = gi * kRouteTok;
+    float acc[kRouteTok][kMoeMaxE];
 #pragma unroll
-    for (int e = 0; e < kMoeMaxE; ++e) acc[e] = 0.f;
-    const bf16* row = x + t * d;
-    for (int c = lane; c < d / 8; c += 32) {
-      const uint4 q = *reinterpret_cast<const uint4*>(row + c * 8);
-      const uint32_t* qw = &q.x;
-      float a[8];
+    for (int j = 0; j < kRouteTok; ++j)
 #pragma unroll
-      for (int j = 0; j < 4; ++j) unpack_bf16x2(qw[j], a[2 * j], a[2 * j + 1]);
+      for (int e = 0; e < kMoeMaxE; ++e) acc[j][e] = 0.f;
+    for (int c = lane; c < nch; c += 32) {
+      float a[kRouteTok][8];
+#pragma unroll
+      for (int j = 0; j < kRouteTok; ++j) {
+        const int64_t t = t0 + j < n ? t0 + j : n - 1;
+        const uint4 q = *reinterpret_cast<const uint4*>(x + t * d + c * 8);
+        const uint32_t* qw = &q.x;
+#pragma unroll
+        for (int h = 0; h < 4; ++h) unpack_bf16x2(qw[h], a[j][2 * h], a[j][2 * h + 1]);
+      }
 #pragma unroll
       for (int e = 0; e < kMoeMaxE; ++e) {
         if (e < E) {
-          const float4* we = reinterpret_cast<const float4*>(wsm + (size_t)e * d + c * 8);
+          const float4* we = reinterpret_cast<const float4*>(wsm + ((size_t)c * E + e) * 8);
           const float4 w0 = we[0], w1 = we[1];
-          acc[e] = fmaf(a[0], w0.x, fmaf(a[1], w0.y, fmaf(a[2], w0.z, fmaf(a[3], w0.w, acc[e]))));
-          acc[e] = fmaf(a[4], w1.x, fmaf(a[5], w1.y, fmaf(a[6], w1.z, fmaf(a[7], w1.w, acc[e]))));
+#pragma unroll
+          for (int j = 0; j < kRouteTok; ++j) {
+            float s = acc[j][e];
+            s = fmaf(a[j][0], w0.x, s);
+            s = fmaf(a[j][1], w0.y, s);
+            s = fmaf(a[j][2], w0.z, s);
+            s = fmaf(a[j][3], w0.w, s);
+            s = fmaf(a[j][4], w1.x, s);
+            s = fmaf(a[j][5], w1.y, s);
+            s = fmaf(a[j][6], w1.z, s);
+            s = fmaf(a[j][7], w1.w, s);
+            acc[j][e] = s;
+          }
         }
       }
     }
 #pragma unroll
-    for (int e = 0; e < kMoeMaxE; ++e)
-      if (e < E) acc[e] = warp_sum(acc[e]);
-    if (lane == 0) {
-      float mx = -INFINITY;
-      for (int e = 0; e < E; ++e) {
-        logits[t * E + e] = acc[e];
-        mx = fmaxf(mx, acc[e]);
+    for (int j = 0; j < kRouteTok; ++j) {
+      const int64_t t = t0 + j;
+      // every lane gets every expert's sum; lane e keeps expert e's logit
+      float lg = -INFINITY;
+#pragma unroll
+      for (int e = 0; e < kMoeMaxE; ++e) {
+        if (e < E) {
+          const float v = warp_sum(acc[j][e]);
+          if (lane == e) lg = v;
+        }
       }
-      float p[kMoeMaxE], z = 0.f, sq = 0.f;
-      for (int e = 0; e < E; ++e) {
-        p[e] = expf(acc[e] - mx);
-        z += p[e];
-        sq += acc[e] * acc[e];
+      if (t >= n) continue;  // warp-uniform
+      const bool live = lane < E;
+      if (live) logits[t * E + lane] = lg;
+      const float mx = warp_max(lg);
+      const float ex = live ? expf(lg - mx) : 0.f;
+      const float pr = ex / warp_sum(ex);
+      const float ent = warp_sum(live ? -pr * logf(pr + 1.0e-9f) : 0.f);
+      const float sq = warp_sum(live ? lg * lg : 0.f);
+      // top-k by repeated arg-max; the first (lowest) expert wins ties
+      float cur = live ? lg : -INFINITY;
+      float l0 = 0.f, gz = 0.f, mygate_logit = -INFINITY;
+      int mysel = -1;
+      for (int jj = 0; jj < k; ++jj) {
+        float v = cur;
+        int i = live ? lane : 1 << 30;
+        warp_argmax(v, i);
+        if (jj == 0) l0 = v;
+        gz += expf(v - l0);
+        if (lane == jj) {
+          mysel = i;
+          mygate_logit = v;
+        }
+        if (lane == i) cur = -INFINITY;
+        if (live && lane == i) st_cnt += 1.f;
       }
-      float ent = 0.f;
-      for (int e = 0; e < E; ++e) {
-        p[e] /= z;
-        ent -= p[e] * logf(p[e] + 1.0e-9f);
-        atomicAdd(&bst[e], p[e]);
+      // lanes 0..k-1 hold choice j = lane; the first choice has the largest gate
+      if (lane < k) {
+        const float g = expf(mygate_logit - l0) / gz;
+        chosen[t * k + lane] = mysel;
+        gate[t * k + lane] = g;
       }
-      // top-k by repeated arg-max; the first maximum wins ties
-      int sel[kMoeMaxK];
-      float lv[kMoeMaxK];
-      unsigned used = 0u;
-      for (int j = 0; j < k; ++j) {
-        int best = -1;
-        float bv = -INFINITY;
-        for (int e = 0; e < E; ++e)
-          if (!(used >> e & 1u) && (best < 0 || acc[e] > bv)) {
-            best = e;
-            bv = acc[e];
-          }
-        used |= 1u << best;
-        sel[j] = best;
-        lv[j] = bv;
+      if (live) st_prob += pr;
+      if (lane == 0) {
+        st_ent += ent;
+        st_top1 += 1.f / gz;  // the first gate, exp(0) / gz
+        st_sq += sq;
       }
-      float gz = 0.f, g[kMoeMaxK];
-      for (int j = 0; j < k; ++j) {
-        g[j] = expf(lv[j] - lv[0]);
-        gz += g[j];
-      }
-      float top1 = 0.f;
-      for (int j = 0; j < k; ++j) {
-        g[j] /= gz;
-        top1 = fmaxf(top1, g[j]);
-        chosen[t * k + j] = sel[j];
-        gate[t * k + j] = g[j];
-        atomicAdd(&bst[E + sel[j]], 1.f);
-      }
-      atomicAdd(&bst[2 * E], ent);
-      atomicAdd(&bst[2 * E + 1], top1);
-      atomicAdd(&bst[2 * E + 2], sq);
     }
   }
+  // block statistics: per warp, then the warps in order, one atomic per entry
+  float* mine = wst + warp * width;
+  if (lane < E) {
+    mine[lane] = st_prob;
+    mine[E + lane] = st_cnt;
+  }
+  if (lane == 0) {
+    mine[2 * E] = st_ent;
+    mine[2 * E + 1] = st_top1;
+    mine[2 * E + 2] = st_sq;
+  }
   __syncthreads();
-  for (int i = threadIdx.x; i < moe_stat_width(E); i += blockDim.x) atomicAdd(&stats[i], bst[i]);
+  for (int i = threadIdx.x; i < width; i += blockDim.x) {
+    float s = 0.f;
+    for (int w8 = 0; w8 < (int)(blockDim.x >> 5); ++w8) s += wst[w8 * width + i];
+    atomicAdd(&stats[i], s);
+  }
 }
 
 // ------------------------------------------------------------------ dispatch
@@ -310,87 +364,131 @@ __global__ void moe_zero_pad_kernel(const int* __restrict__ src, const int* __re
 // loss through the router probabilities (d prob_e = bal[e], the same for every
 // token); then d_x = bf16(bf16(sum_j d_grouped[pos(i,j)]) + bf16(d_logits . W^T))
 // and d_W += x^T d_logits. Tokens go in chunks of 64: the warps first form the
-// chunk's d_logits in shared memory (lane e = expert), then every thread owns a
-// few features (all E weights of them in registers) and walks the chunk's
-// tokens with coalesced row reads, accumulating its d_W entries in registers
-// (one atomic per entry per block at the end). One feature per thread up to
-// d = 1024 threads, two beyond.
+// chunk's d_logits in shared memory (lane e = expert); then thread (stream s,
+// group g) owns features [FPT g, FPT g + FPT) -- their weights and d_W
+// partials in registers -- and takes tokens s, s + S, ... of the chunk with
+// 8- or 16-byte row reads. At the end the S streams' d_W partials are added in
+// stream order in shared memory and the block adds them with one atomic each.
 constexpr int kRbChunk = 64;
-constexpr int kRbMaxF = 2;  // features per thread: d <= 2 * 1024
+constexpr int kRbMaxThreads = 512;  // 128 registers a thread
 
-template <int E>
-__global__ void __launch_bounds__(1024, 1) moe_route_bwd_kernel(
+template <int FPT>
+struct RbVec;
+template <>
+struct RbVec<8> {
+  using T = uint4;
+};
+template <>
+struct RbVec<4> {
+  using T = uint2;
+};
+template <>
+struct RbVec<2> {
+  using T = uint32_t;
+};
+
+template <int FPT>
+__device__ __forceinline__ void rb_unpack(const typename RbVec<FPT>::T& q, float* f) {
+  const uint32_t* w = reinterpret_cast<const uint32_t*>(&q);
+#pragma unroll
+  for (int h = 0; h < FPT / 2; ++h) unpack_bf16x2(w[h], f[2 * h], f[2 * h + 1]);
+}
+
+template <int E, int FPT>
+__global__ void __launch_bounds__(kRbMaxThreads, 1) moe_route_bwd_kernel(
     const bf16* __restrict__ x, const float* __restrict__ w, const float* __restrict__ logits,
     const int* __restrict__ chosen, const float* __restrict__ gate,
     const float* __restrict__ d_gate, const float* __restrict__ bal,
     const bf16* __restrict__ d_grouped, const int* __restrict__ pos, int64_t n, int d, int k,
-    float* __restrict__ d_w, bf16* __restrict__ d_x) {
+    int streams, float* __restrict__ d_w, bf16* __restrict__ d_x) {
+  using Vec = typename RbVec<FPT>::T;
+  extern __shared__ float dwsum[];  // [d][E] d_W partial of the block
   __shared__ float dl[kRbChunk][E];
   __shared__ int ps[kRbChunk][kMoeMaxK];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // features of this thread: f = tid + i * blockDim.x, i < kRbMaxF
-  float wreg[kRbMaxF][E], acc[kRbMaxF][E];
+  const int groups = d / FPT;
+  const int stream = threadIdx.x / groups, g = threadIdx.x - stream * groups;
+  const bool active = stream < streams;
+  const int f0 = g * FPT;
+  float wreg[FPT][E], acc[FPT][E];
 #pragma unroll
-  for (int i = 0; i < kRbMaxF; ++i) {
-    const int f = threadIdx.x + i * blockDim.x;
+  for (int i = 0; i < FPT; ++i)
 #pragma unroll
     for (int e = 0; e < E; ++e) {
-      wreg[i][e] = f < d ? w[(int64_t)f * E + e] : 0.f;
+      wreg[i][e] = active ? w[(int64_t)(f0 + i) * E + e] : 0.f;
       acc[i][e] = 0.f;
     }
-  }
   for (int64_t c0 = (int64_t)blockIdx.x * kRbChunk; c0 < n; c0 += (int64_t)gridDim.x * kRbChunk) {
     const int nt = (int)(n - c0 < kRbChunk ? n - c0 : kRbChunk);
     // (a) d_logits of the chunk: warp per token, lane e per expert
     for (int tt = warp; tt < nt; tt += blockDim.x >> 5) {
       const int64_t t = c0 + tt;
       const float lg = lane < E ? logits[t * E + lane] : -INFINITY;
-      float mx = lg;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      const float mx = warp_max(lg);
       const float ex = lane < E ? expf(lg - mx) : 0.f;
       const float z = warp_sum(ex);
       const float pr = ex / z;
       const float b = lane < E ? bal[lane] : 0.f;
       const float dot = warp_sum(pr * b);
-      float g = pr * (b - dot);
+      float gg = pr * (b - dot);
       float gd = 0.f;
       for (int j = 0; j < k; ++j) gd += gate[t * k + j] * d_gate[t * k + j];
       for (int j = 0; j < k; ++j)
-        if (chosen[t * k + j] == lane) g += gate[t * k + j] * (d_gate[t * k + j] - gd);
-      if (lane < E) dl[tt][lane] = g;
+        if (chosen[t * k + j] == lane) gg += gate[t * k + j] * (d_gate[t * k + j] - gd);
+      if (lane < E) dl[tt][lane] = gg;
       if (lane < k) ps[tt][lane] = pos[t * k + lane];
     }
     __syncthreads();
-    // (b) features: d_W accumulation and d_x
-    for (int tt = 0; tt < nt; ++tt) {
-      const int64_t t = c0 + tt;
+    // (b) d_W partials and d_x, FPT features of one token per step
+    if (active) {
+      for (int tt = stream; tt < nt; tt += streams) {
+        const int64_t t = c0 + tt;
+        float xv[FPT];
+        rb_unpack<FPT>(*reinterpret_cast<const Vec*>(x + t * d + f0), xv);
+        Vec gq = *reinterpret_cast<const Vec*>(d_grouped + (int64_t)ps[tt][0] * d + f0);
+        for (int j = 1; j < k; ++j) {
+          const Vec o = *reinterpret_cast<const Vec*>(d_grouped + (int64_t)ps[tt][j] * d + f0);
+          uint32_t* a32 = reinterpret_cast<uint32_t*>(&gq);
+          const uint32_t* o32 = reinterpret_cast<const uint32_t*>(&o);
 #pragma unroll
-      for (int i = 0; i < kRbMaxF; ++i) {
-        const int f = threadIdx.x + i * blockDim.x;
-        if (f >= d) break;
-        const float xv = __bfloat162float(x[t * d + f]);
-        float v = 0.f;
+          for (int h = 0; h < FPT / 2; ++h) a32[h] = hadd2_bf16(a32[h], o32[h]);
+        }
+        float v[FPT];
+#pragma unroll
+        for (int i = 0; i < FPT; ++i) v[i] = 0.f;
 #pragma unroll
         for (int e = 0; e < E; ++e) {
           const float de = dl[tt][e];
-          acc[i][e] = fmaf(xv, de, acc[i][e]);
-          v = fmaf(de, wreg[i][e], v);
+#pragma unroll
+          for (int i = 0; i < FPT; ++i) {
+            acc[i][e] = fmaf(xv[i], de, acc[i][e]);
+            v[i] = fmaf(de, wreg[i][e], v[i]);
+          }
         }
-        bf16 sg = d_grouped[(int64_t)ps[tt][0] * d + f];
-        for (int j = 1; j < k; ++j) sg = __hadd(sg, d_grouped[(int64_t)ps[tt][j] * d + f]);
-        d_x[t * d + f] = __hadd(sg, __float2bfloat16(v));
+        Vec out;
+        uint32_t* o32 = reinterpret_cast<uint32_t*>(&out);
+        const uint32_t* g32 = reinterpret_cast<const uint32_t*>(&gq);
+#pragma unroll
+        for (int h = 0; h < FPT / 2; ++h) o32[h] = hadd2_bf16(g32[h], pack_bf16x2(v[2 * h], v[2 * h + 1]));
+        *reinterpret_cast<Vec*>(d_x + t * d + f0) = out;
       }
     }
     __syncthreads();
   }
+  // d_W: the streams' partials added in stream order, then one atomic each
+  for (int s = 0; s < streams; ++s) {
+    if (active && stream == s) {
 #pragma unroll
-  for (int i = 0; i < kRbMaxF; ++i) {
-    const int f = threadIdx.x + i * blockDim.x;
-    if (f >= d) break;
+      for (int i = 0; i < FPT; ++i)
 #pragma unroll
-    for (int e = 0; e < E; ++e) atomicAdd(&d_w[(int64_t)f * E + e], acc[i][e]);
+        for (int e = 0; e < E; ++e) {
+          float* dst = &dwsum[(f0 + i) * E + e];
+          *dst = s == 0 ? acc[i][e] : *dst + acc[i][e];
+        }
+    }
+    __syncthreads();
   }
+  for (int i = threadIdx.x; i < d * E; i += blockDim.x) atomicAdd(&d_w[i], dwsum[i]);
 }
 
 // out[e][c] += sum of buf rows [seg[e].x, seg[e].x + seg[e].y), column c.
@@ -482,9 +580,9 @@ extern "C" int gptb200_moe_route(const void* x, const float* router_w, int64_t t
   if (!x || !router_w || !logits || !chosen || !gate || !stats || tokens <= 0) return GPTB200_EINVAL;
   if (experts < 1 || experts > kMoeMaxE || top_k < 1 || top_k > kMoeMaxK || top_k > experts)
     return GPTB200_EUNSUPPORTED;
-  if (d % 8 || d * experts * 4 + moe_stat_width(experts) * 4 > 200 * 1024) return GPTB200_ESHAPE;
+  if (d % 8 || d * experts * 4 + 8 * moe_stat_width(experts) * 4 > 200 * 1024) return GPTB200_ESHAPE;
   auto st = reinterpret_cast<cudaStream_t>(stream);
-  const size_t smem = (size_t)(d * experts + moe_stat_width(experts)) * 4;
+  const size_t smem = (size_t)(d * experts + 8 * moe_stat_width(experts)) * 4;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(moe_route_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -581,23 +679,39 @@ extern "C" int gptb200_moe_route_bwd(const void* x, const float* router_w, const
       !pos || !d_router_w || !d_x || tokens <= 0)
     return GPTB200_EINVAL;
   if (experts < 1 || experts > kMoeMaxE || top_k < 1 || top_k > kMoeMaxK) return GPTB200_EUNSUPPORTED;
-  if (d % 8 || d > kRbMaxF * 1024) return GPTB200_ESHAPE;
-  // the backward is instantiated for every expert count 1..16
+  if (d % 8 || d > 2048) return GPTB200_ESHAPE;
+  // Instantiated for every expert count 1..16 with 8, 4 or 2 features per
+  // thread (up to 4, 8, 16 experts) so that a thread's weights and partials
+  // (2 x features x experts floats) stay in registers.
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int threads = (int)std::min<int64_t>(1024, (d + 31) / 32 * 32);  // a feature per thread
-  const int blocks = (int)std::min<int64_t>((tokens + kRbChunk - 1) / kRbChunk, (int64_t)sms * 2);
+  const int fpt = experts <= 4 ? 8 : (experts <= 8 ? 4 : 2);
+  const int groups = (int)(d / fpt);
+  const int streams = std::max(1, std::min(8, kRbMaxThreads / groups));
+  const int threads = (groups * streams + 31) / 32 * 32;
+  const int blocks = (int)std::min<int64_t>((tokens + kRbChunk - 1) / kRbChunk, (int64_t)sms);
+  const size_t smem = (size_t)d * experts * sizeof(float);
   auto st = reinterpret_cast<cudaStream_t>(stream);
+  int status = GPTB200_OK;
   auto run = [&](auto kern) {
-    kern<<<blocks, threads, 0, st>>>(reinterpret_cast<const bf16*>(x), router_w, logits, chosen,
-                                     gate, d_gate, bal_grad,
-                                     reinterpret_cast<const bf16*>(d_grouped), pos, tokens,
-                                     (int)d, top_k, d_router_w, reinterpret_cast<bf16*>(d_x));
+    if (smem > 48 * 1024) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)smem);
+      if (e != cudaSuccess) {
+        status = -static_cast<int>(e);
+        return;
+      }
+    }
+    kern<<<blocks, threads, smem, st>>>(reinterpret_cast<const bf16*>(x), router_w, logits, chosen,
+                                        gate, d_gate, bal_grad,
+                                        reinterpret_cast<const bf16*>(d_grouped), pos, tokens,
+                                        (int)d, top_k, streams, d_router_w,
+                                        reinterpret_cast<bf16*>(d_x));
   };
   switch (experts) {
 #define GPTB200_ROUTE_BWD_CASE(E) \
-  case E: run(moe_route_bwd_kernel<E>); break;
+  case E: run(moe_route_bwd_kernel<E, (E <= 4 ? 8 : (E <= 8 ? 4 : 2))>); break;
     GPTB200_ROUTE_BWD_CASE(1) GPTB200_ROUTE_BWD_CASE(2) GPTB200_ROUTE_BWD_CASE(3)
     GPTB200_ROUTE_BWD_CASE(4) GPTB200_ROUTE_BWD_CASE(5) GPTB200_ROUTE_BWD_CASE(6)
     GPTB200_ROUTE_BWD_CASE(7) GPTB200_ROUTE_BWD_CASE(8) GPTB200_ROUTE_BWD_CASE(9)
@@ -607,6 +721,7 @@ extern "C" int gptb200_moe_route_bwd(const void* x, const float* router_w, const
 #undef GPTB200_ROUTE_BWD_CASE
     default: return GPTB200_EUNSUPPORTED;
   }
+  if (status) return status;
   GPTB200_CHECK_LAUNCH();
   return 0;
 }

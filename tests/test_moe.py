@@ -120,12 +120,15 @@ def test_moe_steps_train(cuda, tmp_path):
         np.testing.assert_allclose(log.values[:, c0:c0 + E].sum(1), 1.0, atol=1e-5)
 
 
-def test_routed_mlp_op(cuda):
+@pytest.mark.parametrize("experts", [4, 3, 8, 12, 16])
+def test_routed_mlp_op(cuda, experts):
     """One routed block on identical inputs: the forward output and the input,
     router, expert and bias gradients match the restatement's autograd (the
-    routing is identical here, so the bound is tight)."""
+    routing is identical here, so the bound is tight). Expert counts cover
+    every register layout of the router backward (8, 4 and 2 features a
+    thread) and counts that are not powers of two."""
 
-    cfg = _cfg().replace(layers=1)
+    cfg = _cfg().replace(layers=1, experts=experts)
     params = init_params(cfg, 2)
     n, d = cfg.batch_size * cfg.seq_len, cfg.d_model
     g = torch.Generator().manual_seed(9)
