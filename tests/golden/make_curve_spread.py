@@ -3,8 +3,10 @@ of the reference step (oracle/reference_step.py) moves away from its own
 200-step smoke history (loss_curve_smoke.npz) under perturbations far below
 any implementation difference:
 
-  ulp      one parameter element (token_embedding[0, 0]) changed by one fp32 ulp
-  threads  the same run with one CPU thread (matmul partial sums in another order)
+  bf16_ulp  one parameter element (token_embedding[0, 0]) moved to the next
+            bfloat16 value (the compute copy of the weights is bf16, so a
+            smaller change would not reach the forward pass)
+  threads   the same run with one CPU thread (matmul partial sums in another order)
 
 The spread of these runs measures how chaotic the trajectory is; the GPU
 curve test compares its own deviation with it.
@@ -43,8 +45,9 @@ def main(steps: int = 200) -> None:
     params = ref.init_params(cfg, 0)
     bumped = {k: v.copy() for k, v in params.items()}
     e = bumped["token_embedding"]
-    e[0, 0] = np.nextafter(e[0, 0], np.float32(np.inf))
-    out = {"ulp": run(cfg, bumped, 8), "threads": run(cfg, params, 1)}
+    b16 = torch.tensor(float(e[0, 0])).bfloat16()
+    e[0, 0] = float(torch.nextafter(b16, torch.tensor(1.0, dtype=torch.bfloat16)).float())
+    out = {"bf16_ulp": run(cfg, bumped, 8), "threads": run(cfg, params, 1)}
     path = pathlib.Path(__file__).resolve().parent / "loss_curve_spread.npz"
     np.savez_compressed(path, steps=steps, **out)
     print("wrote", path)
