@@ -336,6 +336,21 @@ GPTB200_DEV float2 fadd2(float2 a, float2 b) {
   return d;
 }
 
+GPTB200_DEV float2 fmul2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
+// L2 prefetch of the 128-byte line holding p.
+GPTB200_DEV void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
 GPTB200_DEV float bf16r(float x) { return __bfloat162float(__float2bfloat16(x)); }
 
 GPTB200_DEV uint32_t pack_bf16x2(float lo, float hi) {
@@ -384,6 +399,25 @@ GPTB200_DEV void gelu_tanh_fwd_grad(float x, float& g, float& gp) {
   const float hx = 0.5f * x;
   g = fmaf(hx, t, hx);
   gp = fmaf(0.5f, t, 0.5f) + hx * (1.0f - t * t) * (k0 * fmaf(3.0f * k1, x2, 1.0f));
+}
+
+// gelu_tanh and its derivative for two values at once with packed f32x2
+// arithmetic (half the FP32 issue slots of two gelu_tanh_fwd_grad calls):
+//   u = k0 x (1 + k1 x^2), t = tanh(u), g = x/2 (1 + t),
+//   g' = (1 + t)/2 + x/2 (1 - t^2) k0 (1 + 3 k1 x^2).
+GPTB200_DEV void gelu_tanh_fwd_grad2(float2 x, float2& g, float2& gp) {
+  const float2 k0 = make_float2(0.7978845608028654f, 0.7978845608028654f);
+  const float2 k1 = make_float2(0.044715f, 0.044715f);
+  const float2 k3 = make_float2(3.0f * 0.044715f, 3.0f * 0.044715f);
+  const float2 one = make_float2(1.0f, 1.0f), half = make_float2(0.5f, 0.5f);
+  const float2 x2 = fmul2(x, x);
+  const float2 inner = fmul2(fmul2(k0, x), ffma2(k1, x2, one));
+  const float2 t = make_float2(tanh_fast(inner.x), tanh_fast(inner.y));
+  const float2 hx = fmul2(half, x);
+  g = ffma2(hx, t, hx);
+  const float2 sech2 = ffma2(make_float2(-t.x, -t.y), t, one);  // 1 - t^2
+  const float2 dinner = fmul2(k0, ffma2(k3, x2, one));
+  gp = ffma2(fmul2(hx, sech2), dinner, ffma2(half, t, half));
 }
 
 // d/dx of gelu_tanh.
