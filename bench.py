@@ -58,6 +58,25 @@ def flops_per_token(cfg) -> int:
             + 12 * L * cfg.heads * cfg.seq_len * cfg.head_dim)
 
 
+def gemm_traffic_estimate(cfg, local_batch: int, launches: int):
+    """DRAM bytes per GEMM launch of the matmul family, from the committed ncu
+    capture of one reduced step (profiles/gemm_traffic_125m_batch16.md, the
+    JSON block), scaled by the tokens per GPU. Only for the dense 125M tier
+    with the captured launch count; (None, reason) otherwise."""
+
+    path = ROOT / "profiles" / "gemm_traffic_125m_batch16.md"
+    if cfg.experts or cfg.tier != "125m_768_tied" or not path.exists():
+        return None, "no committed capture of this configuration's GEMM traffic"
+    text = path.read_text()
+    block = json.loads(text.split("```json", 1)[1].split("```", 1)[0])
+    if launches != block["matmul_launches"]:
+        return None, f"launch count {launches} differs from the capture's {block['matmul_launches']}"
+    scale = local_batch * cfg.seq_len / block["tokens"]
+    per_launch = (block["dram_read_bytes"] + block["dram_write_bytes"]) / launches * scale
+    return per_launch, (f"ncu capture at {block['tokens']} tokens (profiles/gemm_traffic_125m_batch16.md) "
+                        f"scaled x{scale:g} to {local_batch * cfg.seq_len} tokens per GPU")
+
+
 def measured_peaks() -> dict:
     path = ROOT / "MEASURED_PEAKS.json"
     if path.exists():
@@ -578,20 +597,20 @@ def main() -> None:
     timed = ops.gemm_timer
     ops.gemm_timer = None
     trainer.graph = graph
-    gemm_ms = sum(s.elapsed_time(e) for s, e, _ in timed)
-    gemm_flops = sum(f for _, _, f in timed)
+    gemm_ms = sum(s.elapsed_time(e) for s, e, _, _ in timed)
+    gemm_flops = sum(f for _, _, f, _ in timed)
+    gemm_bytes = sum(b for _, _, _, b in timed)
     step_ms_instr = gstart.elapsed_time(gend)
     achieved = gemm_flops / (gemm_ms / 1000.0) / 1e12
+    traffic, traffic_note = gemm_traffic_estimate(cfg, local_batch, len(timed))
     roofline = {
         "bound": "tensor", "kernel": "gemm_tc_kernel (tcgen05 GEMM, all launches of one step)",
         "achieved": achieved, "peak": peaks["bf16_sustained"], "unit": "TFLOP/s",
         "frac": achieved / peaks["bf16_sustained"],
         "peak_source": f"{peaks['source']} sustained bf16 (kernel timed inside a long step)",
-        # DRAM read + write bytes per GEMM launch, averaged over one step's 144
-        # launches of the 1-GPU bench workload (one-pass ncu capture of
-        # dram__bytes_read.sum / dram__bytes_write.sum: 119.43 GB + 56.45 GB)
-        "traffic": (119.43e9 + 56.45e9) / 144 if world == 1 else None,
-        "traffic_unit": "bytes per launch (1-GPU workload, ncu capture)",
+        "traffic": traffic, "traffic_unit": "DRAM bytes read + written per launch",
+        "traffic_note": traffic_note,
+        "algorithmic_bytes_per_launch": gemm_bytes / max(len(timed), 1),
         "launches_per_step": len(timed), "share_of_step": gemm_ms / step_ms_instr,
         "algorithmic_flops_per_step": gemm_flops,
     }

@@ -10,6 +10,7 @@ from __future__ import annotations
 
 import concurrent.futures
 import os
+import re
 import pathlib
 import shutil
 import subprocess
@@ -82,5 +83,56 @@ def build(force: bool = False, verbose: bool = True) -> pathlib.Path:
     return LIB
 
 
+def ptxas_report(dest: pathlib.Path) -> None:
+    """Compiles every CUDA source once more with `-Xptxas -v` and writes, per
+    kernel instantiation, the registers per thread, spill bytes, stack frame and
+    static shared memory ptxas reports (one line each, names demangled)."""
+
+    import tempfile
+
+    rows = []
+    with tempfile.TemporaryDirectory() as tmp:
+        for src in _sources():
+            cmd = [_nvcc(), *ARCH, *NVCC_FLAGS, "-Xptxas", "-v", "-c", str(src),
+                   "-o", str(pathlib.Path(tmp) / (src.name + ".o"))]
+            if src.suffix == ".cpp":
+                cmd[1:1] = ["-x", "cu"]
+            log = subprocess.run(cmd, check=True, capture_output=True, text=True).stderr
+            name, props = None, {}
+            for line in log.splitlines():
+                m = re.search(r"Function properties for (\S+)", line)
+                if m:
+                    name, props = m.group(1), {}
+                    continue
+                m = re.search(r"(\d+) bytes stack frame, (\d+) bytes spill stores, (\d+) bytes spill loads", line)
+                if m and name:
+                    props.update(stack=int(m.group(1)), spill_st=int(m.group(2)), spill_ld=int(m.group(3)))
+                    continue
+                m = re.search(r"Used (\d+) registers", line)
+                if m and name:
+                    smem = re.search(r"(\d+) bytes smem", line)
+                    rows.append((src.name, name, int(m.group(1)), props.get("spill_st", 0),
+                                 props.get("spill_ld", 0), props.get("stack", 0),
+                                 int(smem.group(1)) if smem else 0))
+                    name = None
+    filt = shutil.which("c++filt")
+    names = [r[1] for r in rows]
+    if filt:
+        out = subprocess.run([filt], input="\n".join(names), capture_output=True, text=True, check=True)
+        names = out.stdout.splitlines()
+    lines = ["# ptxas resource usage of libgptb200 (sm_100a, -O3)", "",
+             "Command: python gpt-speedrun-tpu_b200/build.py --ptxas-report", "",
+             "file | registers/thread | spill stores B | spill loads B | stack B | static smem B | kernel",
+             "---|---|---|---|---|---|---"]
+    for (src, _m, regs, sst, sld, stk, smem), nm in zip(rows, names):
+        nm = re.sub(r"\s+", " ", nm)[:160]
+        lines.append(f"{src} | {regs} | {sst} | {sld} | {stk} | {smem} | `{nm}`")
+    dest.write_text("\n".join(lines) + "\n")
+    print(f"wrote {dest} ({len(rows)} kernels)")
+
+
 if __name__ == "__main__":
-    build(force="--force" in sys.argv)
+    if "--ptxas-report" in sys.argv:
+        ptxas_report(HERE.parent / "profiles" / "ptxas_resource_usage.md")
+    else:
+        build(force="--force" in sys.argv)

@@ -103,8 +103,29 @@ def gemm(
     if gemm_timer is not None and row_range is None:  # a range GEMM's work is device-side
         end = torch.cuda.Event(enable_timing=True)
         end.record()
-        gemm_timer.append((start, end, 2.0 * m * n * k))
+        gemm_timer.append((start, end, 2.0 * m * n * k,
+                           _gemm_algorithmic_bytes(m, n, k, kind, accumulate, bias, residual, aux)))
     return out
+
+
+def _gemm_algorithmic_bytes(m, n, k, kind, accumulate, bias, residual, aux) -> int:
+    """Bytes a GEMM launch must move at least: each operand read once, the
+    output written once (fp32 outputs that accumulate are read as well), plus
+    the epilogue's own inputs and outputs (bias, residual, GELU derivative)."""
+
+    nbytes = 2 * (m * k + n * k)
+    if kind in (_lib.EPI_F32, _lib.EPI_F32_ATOMIC, _lib.EPI_F32_SPLITK):
+        reads_c = kind != _lib.EPI_F32 or bool(accumulate)
+        nbytes += 4 * m * n * (2 if reads_c else 1)
+    else:
+        nbytes += 2 * m * n
+    if kind in (_lib.EPI_BIAS_GELU, _lib.EPI_DGELU):  # gelu' written / read
+        nbytes += 2 * m * n
+    if residual is not None:
+        nbytes += 2 * m * n
+    if bias is not None:
+        nbytes += 2 * n
+    return nbytes
 
 
 def gemm_workspace_size(m: int, n: int, k: int, kind: int) -> int:
@@ -123,8 +144,8 @@ def _scratch(nbytes: int, device) -> torch.Tensor | None:
     return torch.empty(max(int(nbytes), 16), dtype=torch.uint8, device=device) if nbytes else None
 
 
-# When set to a list, every gemm() call appends (start_event, end_event, flops)
-# recorded on the launching stream; the benchmark uses it to time the GEMM
+# When set to a list, every gemm() call appends (start_event, end_event, flops,
+# algorithmic bytes) recorded on the launching stream; the benchmark uses it to time the GEMM
 # launches inside its measured steps.
 gemm_timer: list | None = None
 
