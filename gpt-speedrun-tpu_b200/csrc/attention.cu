@@ -10,22 +10,25 @@
 // into bf16 P_x in TMEM, so the two tiles ping-pong: while one warpgroup
 // exponentiates, the tensor core runs the other tile's MMAs.
 // Backward (attn_bwd_tc): one CTA per (128-key tile, batch*head), looping over
-// 64-query tiles from the diagonal down. 19 warps: TMA (K, V once; Q/dO into a
+// 64-query tiles from the diagonal down. 23 warps: TMA (K, V once; Q/dO into a
 // 4-stage ring), a scores MMA thread (S^T = K Q^T and dP^T = V dO^T into one
 // of three 128-column TMEM buffers, as far ahead as the buffers allow), a
 // gradient MMA thread (dV += P^T dO and dK += dS^T Q with P^T / dS^T read
 // straight from TMEM; dQ = dS K per pair of tiles, dS^T read MN-major from a
-// shared-memory ring), and two softmax warpgroups taking alternate tiles
-// (thread = key row: P^T = exp2(S^T c - lse), dS^T = P^T (dP^T - delta),
-// written over the S^T columns as bf16 pairs). Two issuing threads keep the
-// tensor pipe fed while either waits on a barrier. dQ leaves TMEM through a
-// TMA reduce-add into an fp32 accumulator; dK, dV leave TMEM once at the end.
+// shared-memory ring), and 16 softmax warps that take every tile together
+// (thread = key row, 16 query columns per warp: P^T = exp2(S^T c - lse),
+// dS^T = P^T (dP^T - delta), written over the warp's own S^T columns as bf16
+// pairs), and four dQ warps. Two issuing threads keep the tensor pipe fed
+// while either waits on a barrier. The dQ warps read each pair's dQ out of
+// TMEM as soon as its MMA completes and reduce it into an fp32 accumulator by
+// TMA; dK, dV leave TMEM once at the end.
 // q and k arrive already rotated (RoPE runs in the QKV projection epilogue);
 // with RoPE tables the backward rotates dq and dk back so they are gradients
 // of the unrotated inputs.
 // Every mbarrier wait is bounded (common.cuh). Semantics follow
 // rig/kernels/tpu_flash_attention.py:171-207 (fp32 statistics, bf16 P).
 #include <algorithm>
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -460,9 +463,10 @@ constexpr int BQ = 64;                  // queries per inner tile
 constexpr int BT_BYTES = BT * 128;      // 128 rows x 64 bf16
 constexpr int BQ_BYTES = BQ * 128;      // 64 rows x 64 bf16
 constexpr int kQStages = 4;             // Q / dO tile ring
-constexpr int kBwdWgWarps = 8;          // per softmax warpgroup: two warps per TMEM lane quadrant
-constexpr int kBwdScoreWarp = 2 + 2 * kBwdWgWarps;  // issues the S^T / dP^T MMAs
-constexpr int kBwdThreads = 32 * (kBwdScoreWarp + 1);
+constexpr int kBwdSmWarps = 16;         // softmax warps: four per TMEM lane quadrant
+constexpr int kBwdScoreWarp = 2 + kBwdSmWarps;  // issues the S^T / dP^T MMAs
+constexpr int kBwdFlushWarp = kBwdScoreWarp + 1;  // first of four dQ read-out warps
+constexpr int kBwdThreads = 32 * (kBwdFlushWarp + 4);
 
 struct BwdSmem {
   static constexpr int K = 0;
@@ -470,8 +474,8 @@ struct BwdSmem {
   static constexpr int Q = V + BT_BYTES;                // kQStages tiles
   static constexpr int DO = Q + kQStages * BQ_BYTES;    // kQStages tiles
   static constexpr int DST = DO + kQStages * BQ_BYTES;  // ring of 4 dS^T tiles [128 keys x 64 queries]
-  static constexpr int DQS = DST + 4 * BT_BYTES;        // dQ staging: 8 warps x (32 x 32 fp32)
-  static constexpr int STAT = DQS + 8 * 4096;           // per warp: 32 lse*log2(e), delta, seg id
+  static constexpr int DQS = DST + 4 * BT_BYTES;        // dQ staging: 4 warps x 2 x (32 x 32 fp32)
+  static constexpr int STAT = DQS + 8 * 4096;           // per warp: 32 -lse*log2(e), -delta, seg id
   static constexpr int SEGTAB = STAT + 16 * 384;        // int2 per 64-position chunk from k0
   static constexpr int QLIST = SEGTAB + kMaxSegChunks * 8;  // query tiles this CTA visits
   static constexpr int BAR = QLIST + kMaxSegChunks * 4;
@@ -529,12 +533,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
     for (int s = 0; s < 3; ++s) {
       mbar_init(&s_full[s], 1);
-      mbar_init(&p_full[s], kBwdWgWarps);
+      mbar_init(&p_full[s], kBwdSmWarps);
     }
     for (int s = 0; s < 4; ++s) mbar_init(&done[s], 1);
     for (int s = 0; s < 2; ++s) {
       mbar_init(&dq_full[s], 1);
-      mbar_init(&dq_free[s], kBwdWgWarps);
+      mbar_init(&dq_free[s], 4);
     }
     mbar_init(fin, 1);
     *abort_flag = 0;
@@ -547,8 +551,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const int nq = counts[0];
   // TMEM columns: three tile buffers of 128 columns, then dV | dK. In buffer
   // b, columns [0, 64) receive S^T and [64, 128) dP^T (fp32, lane = key). The
-  // softmax writes P^T and dS^T as bf16 pairs over the S^T half (warp half hf
-  // owns columns 32 hf + [0, 16) for P^T and 32 hf + [16, 32) for dS^T); the
+  // softmax writes P^T and dS^T as bf16 pairs over the S^T half (query group
+  // cg = 16 queries: columns 16 cg + [0, 8) for P^T, 16 cg + [8, 16) for dS^T); the
   // dP^T half then holds dQ when the tile closes a query pair.
   const uint32_t tmem = *tmem_slot;
   const uint32_t tDV = tmem + 384, tDK = tmem + 448;
@@ -583,14 +587,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const uint32_t sQ = smem_u32(sm + BwdSmem::Q + s * BQ_BYTES);
         const uint32_t sDO = smem_u32(sm + BwdSmem::DO + s * BQ_BYTES);
         // dV += P^T dO and dK += dS^T Q with the A operands read from TMEM:
-        // queries 16k..16k+15 sit at column 32 (k/2) + 8 (k%2) of the buffer
-        // (P^T), 16 further on for dS^T.
+        // queries 16k..16k+15 sit at column 16k of the buffer (P^T, bf16
+        // pairs), 8 further on for dS^T.
 #pragma unroll
         for (int k = 0; k < BQ / 16; ++k) {
-          const uint32_t acol = tBuf(bb) + (k >> 1) * 32 + (k & 1) * 8;
+          const uint32_t acol = tBuf(bb) + k * 16;
           umma_bf16_ts(tDV, acol, umma_smem_desc(sDO + k * 2048, BQ_BYTES, 1024), idKN,
                        (it > 0 || k > 0));
-          umma_bf16_ts(tDK, acol + 16, umma_smem_desc(sQ + k * 2048, BQ_BYTES, 1024), idKN,
+          umma_bf16_ts(tDK, acol + 8, umma_smem_desc(sQ + k * 2048, BQ_BYTES, 1024), idKN,
                        (it > 0 || k > 0));
         }
         umma_commit(&q_empty[s]);
@@ -642,71 +646,49 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         umma_commit(&q_empty[s]);
       }
     }
-  } else if (warp < 2 + 2 * kBwdWgWarps) {
-    // Two softmax warpgroups take alternate query tiles (wg 0 even, wg 1 odd).
-    // Warp w reads TMEM lanes of quadrant w % 4 (key rows) and the query
-    // columns [32*hf, 32*hf + 32) of the tile. Warpgroup 0 also reads out dQ.
-    const int wg = (warp - 2) >> 3;
-    const int wl = (warp - 2) & 7;
+  } else if (warp < 2 + kBwdSmWarps) {
+    // All 16 softmax warps take every query tile together. Warp w reads TMEM
+    // lanes of quadrant w % 4 (key rows) and the 16 query columns
+    // [16 cg, 16 cg + 16) of the tile, cg = (w - 2) / 4, and writes P^T and
+    // dS^T (bf16 pairs) over exactly those S^T columns, so no warp overwrites
+    // scores another warp has yet to read.
     const int quad = warp & 3;
-    const int hf = wl >> 2;
+    const int cg = (warp - 2) >> 2;
     const int r = quad * 32 + lane;
     const int key = k0 + r;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const float c = p.scale * kLog2e;
     const float* Lg = p.lse + (int64_t)bh * p.T;
     const float* Dg = p.delta + (int64_t)bh * p.T;
-    uint8_t* stage = sm + BwdSmem::DQS + wl * 4096;  // dQ staging (warpgroup 0)
     float* stat = reinterpret_cast<float*>(sm + BwdSmem::STAT + (warp - 2) * 384);
     int* stat_seg = reinterpret_cast<int*>(stat + 64);
     // this key row's segment id (rows past T take an id no query has)
     const int sk = segrow ? (key < p.T ? segrow[key] : INT_MAX) : 0;
     const int2 krng = segrow ? seg_range(segtab, nch, 0, 2) : make_int2(0, 0);
-    // lane j fetches the statistics of query column j of list entry `it`
+    // lane j < 16 fetches the statistics of query column 16 cg + j of list entry `it`
     auto fetch = [&](int it, float& l2, float& d2, int& s2) {
-      const int t = k0 + qlist[it] * BQ + hf * 32 + lane;
+      const int t = k0 + qlist[it] * BQ + cg * 16 + (lane & 15);
       l2 = (t < p.T) ? Lg[t] * kLog2e : INFINITY;  // rows past T: P = 0
       d2 = (t < p.T) ? Dg[t] : 0.f;
       s2 = (segrow && t < p.T) ? segrow[t] : INT_MIN;
     };
     float nl = 0.f, nd = 0.f;
     int ns = 0;
-    if (wg < nq) fetch(wg, nl, nd, ns);
+    if (nq > 0) fetch(0, nl, nd, ns);
     bool ok = true;
-    // dQ rows of query pair j (list entries 2j, 2j+1; TMEM lane m is row m of
-    // the pair, quadrants 0-1 the first tile, 2-3 the second) from buffer bb:
-    // one 32x32 fp32 sub-tile per warp, reduced into dq_acc by a TMA reduce-add
-    // (rows past the sequence end are clipped by the map).
-    auto flush_dq = [&](int j, int bb) {
-      const int e = 2 * j + (quad >> 1);
-      if (e >= nq) return;  // a last pair of one tile (warp-uniform)
-      const int row0 = k0 + qlist[e] * BQ + (quad & 1) * 32;
-      float v[32];
-      tmem_ld32(tBuf(bb) + 64 + lane_off + hf * 32, v);
-      if (lane == 0) bulk_wait_read();  // the previous reduce has read the staging tile
-      __syncwarp();
-#pragma unroll
-      for (int ch = 0; ch < 8; ++ch)
-        *reinterpret_cast<float4*>(stage + lane * 128 + ((ch ^ (lane & 7)) << 4)) =
-            make_float4(v[4 * ch], v[4 * ch + 1], v[4 * ch + 2], v[4 * ch + 3]);
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) {
-        tma_reduce_add_3d(&tmDQ, stage, hf * 32, row0, bh);
-        bulk_commit();
-      }
-    };
-    for (int it = wg; it < nq && ok; it += 2) {
+    for (int it = 0; it < nq && ok; ++it) {
       const int bb = it % 3;
       const uint32_t tb = tBuf(bb);
       // this tile's statistics, broadcast to the warp through shared memory
       const int qt = qlist[it];  // query tile index (64 positions) past k0
       __syncwarp();
-      stat[lane] = nl;
-      stat[32 + lane] = nd;
-      stat_seg[lane] = ns;
+      if (lane < 16) {
+        stat[lane] = -nl;
+        stat[32 + lane] = -nd;
+        stat_seg[lane] = ns;
+      }
       __syncwarp();
-      if (it + 2 < nq) fetch(it + 2, nl, nd, ns);
+      if (it + 1 < nq) fetch(it + 1, nl, nd, ns);
       if (!mbar_wait(&s_full[bb], (it / 3) & 1, abort_flag, err)) {
         ok = false;
         break;
@@ -717,88 +699,88 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         break;
       }
       tc_fence_after();
-      uint32_t sraw[32], draw[32];
-      tmem_ld32_nw(tb + lane_off + hf * 32, sraw);
-      tmem_ld32_nw(tb + 64 + lane_off + hf * 32, draw);
+      uint32_t sraw[16], draw[16];
+      tmem_ld16_nw(tb + lane_off + cg * 16, sraw);
+      tmem_ld16_nw(tb + 64 + lane_off + cg * 16, draw);
       tmem_wait_ld();
-      const int qbase = qt * BQ + hf * 32;  // query index relative to k0
+      const int qbase = qt * BQ + cg * 16;  // query index relative to k0
       const bool diag = (qt < 2);           // key r > query masks only near the diagonal
       // per-element segment test unless this key tile and query tile share one id
       const bool segmask = segrow && !rng_single(seg_range(segtab, nch, qt, 1), krng);
-      uint32_t pk[16], dk[16];
+      // P^T = exp2(S^T c - lse log2e) and dS^T = P^T (dP^T - delta), two
+      // columns per packed f32x2 instruction (stat holds -lse log2e and
+      // -delta); the causal test runs only on the two diagonal tiles and the
+      // segment test only when the tiles' ids differ.
+      uint32_t pk[8], dk[8];
+      auto softmax_cols = [&](auto diag_tag) {
+        constexpr bool kDiag = decltype(diag_tag)::value;
+        const float2 c2 = make_float2(c, c);
 #pragma unroll
-      for (int j4 = 0; j4 < 8; ++j4) {
-        const float4 l4 = reinterpret_cast<const float4*>(stat)[j4];
-        const float4 d4 = reinterpret_cast<const float4*>(stat + 32)[j4];
-        const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
-        const float dl[4] = {d4.x, d4.y, d4.z, d4.w};
-        float pv[4], dv[4];
+        for (int j4 = 0; j4 < 4; ++j4) {
+          const float4 l4 = reinterpret_cast<const float4*>(stat)[j4];
+          const float4 d4 = reinterpret_cast<const float4*>(stat + 32)[j4];
+          const float2 x01 = ffma2(make_float2(__uint_as_float(sraw[4 * j4]),
+                                               __uint_as_float(sraw[4 * j4 + 1])),
+                                   c2, make_float2(l4.x, l4.y));
+          const float2 x23 = ffma2(make_float2(__uint_as_float(sraw[4 * j4 + 2]),
+                                               __uint_as_float(sraw[4 * j4 + 3])),
+                                   c2, make_float2(l4.z, l4.w));
+          float pv[4] = {ex2(x01.x), ex2(x01.y), ex2(x23.x), ex2(x23.y)};
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int j = 4 * j4 + u;
-          pv[u] = ex2(fmaf(__uint_as_float(sraw[j]), c, -lv[u]));
-          if (diag && r > qbase + j) pv[u] = 0.f;
-          if (segmask && stat_seg[j] != sk) pv[u] = 0.f;
-          dv[u] = pv[u] * (__uint_as_float(draw[j]) - dl[u]);
+          for (int u = 0; u < 4; ++u) {
+            const int j = 4 * j4 + u;
+            if (kDiag && r > qbase + j) pv[u] = 0.f;
+            if (SEG && segmask && stat_seg[j] != sk) pv[u] = 0.f;
+          }
+          const float2 g01 = fadd2(make_float2(__uint_as_float(draw[4 * j4]),
+                                               __uint_as_float(draw[4 * j4 + 1])),
+                                   make_float2(d4.x, d4.y));
+          const float2 g23 = fadd2(make_float2(__uint_as_float(draw[4 * j4 + 2]),
+                                               __uint_as_float(draw[4 * j4 + 3])),
+                                   make_float2(d4.z, d4.w));
+          const float2 dv01 = fmul2(make_float2(pv[0], pv[1]), g01);
+          const float2 dv23 = fmul2(make_float2(pv[2], pv[3]), g23);
+          pk[2 * j4] = pack_bf16x2(pv[0], pv[1]);
+          pk[2 * j4 + 1] = pack_bf16x2(pv[2], pv[3]);
+          dk[2 * j4] = pack_bf16x2(dv01.x, dv01.y);
+          dk[2 * j4 + 1] = pack_bf16x2(dv23.x, dv23.y);
         }
-        pk[2 * j4] = pack_bf16x2(pv[0], pv[1]);
-        pk[2 * j4 + 1] = pack_bf16x2(pv[2], pv[3]);
-        dk[2 * j4] = pack_bf16x2(dv[0], dv[1]);
-        dk[2 * j4 + 1] = pack_bf16x2(dv[2], dv[3]);
-      }
-      tmem_st8_nw(tb + lane_off + hf * 32, pk);
-      tmem_st8_nw(tb + lane_off + hf * 32 + 8, pk + 8);
-      tmem_st8_nw(tb + lane_off + hf * 32 + 16, dk);
-      tmem_st8_nw(tb + lane_off + hf * 32 + 24, dk + 8);
+      };
+      if (diag)
+        softmax_cols(std::integral_constant<bool, true>());
+      else
+        softmax_cols(std::integral_constant<bool, false>());
+      tmem_st8_nw(tb + lane_off + cg * 16, pk);
+      tmem_st8_nw(tb + lane_off + cg * 16 + 8, dk);
       uint8_t* sd = sm + BwdSmem::DST + (it & 3) * BT_BYTES;
 #pragma unroll
-      for (int g = 0; g < 4; ++g)
-        *reinterpret_cast<uint4*>(sd + swz128(r, hf * 4 + g)) =
+      for (int g = 0; g < 2; ++g)
+        *reinterpret_cast<uint4*>(sd + swz128(r, cg * 2 + g)) =
             make_uint4(dk[4 * g], dk[4 * g + 1], dk[4 * g + 2], dk[4 * g + 3]);
       tmem_wait_st();
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[bb]);
-      if (wg == 0 && it >= 2) {
-        // query pair j = (it-2, it-1) was closed by the previous tile of the
-        // other warpgroup; its dQ MMA has had a whole softmax tile to finish
-        const int j = (it >> 1) - 1;
-        if (!mbar_wait(&dq_full[j & 1], (j >> 1) & 1, abort_flag, err)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        flush_dq(j, (2 * j + 1) % 3);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&dq_free[j & 1]);
-      }
     }
-    if (wg == 0) {
-      // the last pair (closed by tile nq-1, which may be its only tile)
-      const int j = (nq - 1) >> 1;
-      if (ok && mbar_wait(&dq_full[j & 1], (j >> 1) & 1, abort_flag, err)) {
-        tc_fence_after();
-        flush_dq(j, (nq - 1) % 3);
-      }
-      if (lane == 0) bulk_wait_all();
-    }
+
     if (ok && mbar_wait(fin, 0, abort_flag, err)) {
       tc_fence_after();
-      // warpgroup 0 writes dK, warpgroup 1 dV; the warp-collective TMEM load
-      // stays outside the per-row guard
+      // warps with cg 0-1 write dK, cg 2-3 dV, 32 columns each; the
+      // warp-collective TMEM load stays outside the per-row guard
+      const bool is_k = cg < 2;
+      const int c0 = (cg & 1) * 32;
       float g[32];
-      tmem_ld32((wg == 0 ? tDK : tDV) + lane_off + hf * 32, g);
+      tmem_ld32((is_k ? tDK : tDV) + lane_off + c0, g);
       if (key < p.T) {
-        bf16* row = (wg == 0 ? p.dk : p.dv) + b * p.sb + h * p.sh + (int64_t)key * p.st + hf * 32;
+        bf16* row = (is_k ? p.dk : p.dv) + b * p.sb + h * p.sh + (int64_t)key * p.st + c0;
 #pragma unroll
         for (int q4 = 0; q4 < 4; ++q4) {
           float* gv = g + 8 * q4;
-          if (wg == 0) {
+          if (is_k) {
 #pragma unroll
             for (int i = 0; i < 8; ++i) gv[i] *= p.scale;
-            if (p.rcos) rope_back(gv, p.rcos, p.rsin, key, hf * 4 + q4);
+            if (p.rcos) rope_back(gv, p.rcos, p.rsin, key, c0 / 8 + q4);
           }
           uint4 o;
           o.x = pack_bf16x2(gv[0], gv[1]);
@@ -809,6 +791,55 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
       }
     }
+  } else {
+    // dQ read-out: warp kBwdFlushWarp + i serves TMEM lane quadrant
+    // (kBwdFlushWarp + i) % 4. For each query pair j (list entries 2j, 2j+1;
+    // TMEM lane m is row m of the pair, quadrants 0-1 the first tile, 2-3 the
+    // second) it loads its 32 rows x 64 fp32 columns as soon as the pair's dQ
+    // MMA has completed, releases the TMEM buffer, stages the rows in two
+    // 128-byte swizzled [32 x 32] boxes of its own and reduces them into
+    // dq_acc with TMA reduce-adds (rows past the sequence end are clipped by
+    // the map). The softmax warps never wait for this.
+    const int quad = warp & 3;
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    uint8_t* stage = sm + BwdSmem::DQS + (warp - kBwdFlushWarp) * 8192;
+    const int npairs = (nq + 1) >> 1;
+    for (int j = 0; j < npairs; ++j) {
+      if (!mbar_wait(&dq_full[j & 1], (j >> 1) & 1, abort_flag, err)) break;
+      tc_fence_after();
+      const int e = 2 * j + (quad >> 1);  // list entry of this warp's rows
+      const int bb = min(2 * j + 1, nq - 1) % 3;
+      if (e < nq) {
+        float v[64];
+        tmem_ld32(tBuf(bb) + 64 + lane_off, v);
+        tmem_ld32(tBuf(bb) + 96 + lane_off, v + 32);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&dq_free[j & 1]);
+        if (lane == 0) bulk_wait_read();  // the previous reduce has read the staging boxes
+        __syncwarp();
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+          for (int ch = 0; ch < 8; ++ch)
+            *reinterpret_cast<float4*>(stage + hh * 4096 + swz128(lane, ch)) =
+                make_float4(v[32 * hh + 4 * ch], v[32 * hh + 4 * ch + 1],
+                            v[32 * hh + 4 * ch + 2], v[32 * hh + 4 * ch + 3]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          const int row0 = k0 + qlist[e] * BQ + (quad & 1) * 32;
+          tma_reduce_add_3d(&tmDQ, stage, 0, row0, bh);
+          tma_reduce_add_3d(&tmDQ, stage + 4096, 32, row0, bh);
+          bulk_commit();
+        }
+      } else {  // a last pair of one tile: nothing in these rows
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&dq_free[j & 1]);
+      }
+    }
+    if (lane == 0) bulk_wait_all();
   }
   tc_fence_before();
   __syncthreads();

@@ -33,42 +33,73 @@ __device__ __forceinline__ void st8(bf16* p, const float* v) {
 
 // ------------------------------------------------------------------ RMSNorm
 // One warp per row; each lane keeps CH 8-element chunks of the row in
-// registers (CH = ceil(d / 256)), so x is read once.
+// registers (CH = ceil(d / 256)), so x is read once. A warp takes two rows
+// (r and r + warps) per iteration and issues both rows' loads before either
+// reduction, so twice as many bytes are in flight per warp.
 template <int CH>
-__global__ void __launch_bounds__(256) rms_fwd_kernel(const bf16* __restrict__ x,
+__global__ void __launch_bounds__(256, (CH <= 3 ? 4 : 1)) rms_fwd_kernel(const bf16* __restrict__ x,
                                                       const bf16* __restrict__ scale,
                                                       bf16* __restrict__ y,
                                                       float* __restrict__ rstd_out, int64_t rows,
                                                       int d) {
+  constexpr int R = CH <= 3 ? 2 : 1;  // wider rows already have enough bytes in flight
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
   const int nch = d >> 3;
-  for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows;
-       r += warps) {
-    const bf16* xr = x + r * d;
-    float v[CH][8];
-    float ss = 0.f;
+  for (int64_t r0 = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r0 < rows;
+       r0 += R * warps) {
+    uint4 xq[R][CH];
 #pragma unroll
-    for (int c = 0; c < CH; ++c) {
-      int ch = lane + 32 * c;
-      if (ch < nch) {
-        ld8(xr + ch * 8, v[c]);
+    for (int u = 0; u < R; ++u) {
+      const int64_t r = r0 + u * warps;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) ss += v[c][j] * v[c][j];
+      for (int c = 0; c < CH; ++c) {
+        const int ch = lane + 32 * c;
+        xq[u][c] = (r < rows && ch < nch)
+                       ? *reinterpret_cast<const uint4*>(x + r * d + ch * 8)
+                       : make_uint4(0, 0, 0, 0);
       }
     }
-    ss = warp_sum(ss);
-    const float rstd = rsqrtf(ss / (float)d + 1.0e-5f);
-    if (lane == 0) rstd_out[r] = rstd;
+    float ss[R];
 #pragma unroll
-    for (int c = 0; c < CH; ++c) {
-      int ch = lane + 32 * c;
-      if (ch < nch) {
-        float s[8], o[8];
-        ld8(scale + ch * 8, s);
+    for (int u = 0; u < R; ++u) {
+      ss[u] = 0.f;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) o[j] = bf16r(v[c][j] * rstd) * s[j];
-        st8(y + r * d + ch * 8, o);
+      for (int c = 0; c < CH; ++c) {
+        const uint32_t* w = &xq[u][c].x;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float a0, a1;
+          unpack_bf16x2(w[j], a0, a1);
+          ss[u] += a0 * a0;  // same fma order as a sequential sum over the row
+          ss[u] += a1 * a1;
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+      for (int u = 0; u < R; ++u) ss[u] += __shfl_xor_sync(0xffffffffu, ss[u], o);
+    }
+#pragma unroll
+    for (int u = 0; u < R; ++u) {
+      const int64_t r = r0 + u * warps;
+      if (r >= rows) break;  // warp-uniform
+      const float rstd = rsqrtf(ss[u] / (float)d + 1.0e-5f);
+      if (lane == 0) rstd_out[r] = rstd;
+#pragma unroll
+      for (int c = 0; c < CH; ++c) {
+        const int ch = lane + 32 * c;
+        if (ch < nch) {
+          float v[8], sc[8], o[8];
+          const uint32_t* w = &xq[u][c].x;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) unpack_bf16x2(w[j], v[2 * j], v[2 * j + 1]);
+          ld8(scale + ch * 8, sc);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) o[j] = bf16r(v[j] * rstd) * sc[j];
+          st8(y + r * d + ch * 8, o);
+        }
       }
     }
   }
@@ -80,8 +111,11 @@ __global__ void __launch_bounds__(256) rms_fwd_kernel(const bf16* __restrict__ x
 // the register count low enough for full occupancy (the kernel is latency-bound
 // on its three input streams); each warp accumulates its dscale partial in its
 // own shared-memory row instead of registers.
+// A warp takes two of its rows (r and r + warps) per iteration and loads both
+// before computing either, so twice the bytes are in flight; the rows still
+// enter the per-warp partials in the same order (r, r + warps, r + 2 warps ...).
 template <int CH>
-__global__ void __launch_bounds__(128, 6) rms_bwd_kernel(
+__global__ void __launch_bounds__(128, (CH <= 3 ? 4 : 1)) rms_bwd_kernel(
     const bf16* __restrict__ x, const bf16* __restrict__ scale, const float* __restrict__ rstd_in,
     const bf16* __restrict__ dy, const bf16* dx_in, bf16* dx_out, float* __restrict__ part,
     bool want_col, int64_t rows, int d) {
@@ -102,19 +136,34 @@ __global__ void __launch_bounds__(128, 6) rms_bwd_kernel(
     sc[c] = (ch < nch) ? *reinterpret_cast<const uint4*>(scale + ch * 8) : make_uint4(0, 0, 0, 0);
   }
 
-  for (int64_t r = (int64_t)blockIdx.x * wpb + wib; r < rows; r += warps) {
-    const float rstd = rstd_in[r];
-    uint4 xq[CH], gq[CH], pq[CH];
+  constexpr int R = CH <= 3 ? 2 : 1;
+  for (int64_t r0 = (int64_t)blockIdx.x * wpb + wib; r0 < rows; r0 += R * warps) {
+    uint4 xq2[R][CH], gq2[R][CH], pq2[R][CH];
+    float rstd2[R];
 #pragma unroll
-    for (int c = 0; c < CH; ++c) {
-      const int ch = lane + 32 * c;
-      if (ch < nch) {
-        xq[c] = *reinterpret_cast<const uint4*>(x + r * d + ch * 8);
-        gq[c] = *reinterpret_cast<const uint4*>(dy + r * d + ch * 8);
-        pq[c] = dx_in ? *reinterpret_cast<const uint4*>(dx_in + r * d + ch * 8)
-                      : make_uint4(0, 0, 0, 0);
+    for (int u = 0; u < R; ++u) {
+      const int64_t r = r0 + u * warps;
+      const bool live = r < rows;
+      rstd2[u] = live ? rstd_in[r] : 0.f;
+#pragma unroll
+      for (int c = 0; c < CH; ++c) {
+        const int ch = lane + 32 * c;
+        if (live && ch < nch) {
+          xq2[u][c] = *reinterpret_cast<const uint4*>(x + r * d + ch * 8);
+          gq2[u][c] = *reinterpret_cast<const uint4*>(dy + r * d + ch * 8);
+          pq2[u][c] = dx_in ? *reinterpret_cast<const uint4*>(dx_in + r * d + ch * 8)
+                            : make_uint4(0, 0, 0, 0);
+        }
       }
     }
+#pragma unroll
+    for (int u = 0; u < R; ++u) {
+    const int64_t r = r0 + u * warps;
+    if (r >= rows) break;  // warp-uniform
+    const float rstd = rstd2[u];
+    const uint4* xq = xq2[u];
+    const uint4* gq = gq2[u];
+    const uint4* pq = pq2[u];
     float dot = 0.f;
 #pragma unroll
     for (int c = 0; c < CH; ++c) {
@@ -177,6 +226,7 @@ __global__ void __launch_bounds__(128, 6) rms_bwd_kernel(
         }
       }
     }
+    }
   }
   // Reduce the per-warp partials inside the block (warp order) and store the
   // block's row: part[block][0][:] = dscale partial, part[block][1][:] = column
@@ -238,7 +288,7 @@ static int64_t rms_bwd_blocks(int64_t rows) {
 template <int CH>
 static int rms_fwd_launch(const bf16* x, const bf16* s, bf16* y, float* rstd, int64_t rows, int d,
                           cudaStream_t st) {
-  int64_t blocks = std::min<int64_t>((rows + 7) / 8, (int64_t)sms() * 8);
+  int64_t blocks = std::min<int64_t>((rows + 15) / 16, (int64_t)sms() * 4);
   rms_fwd_kernel<CH><<<(int)blocks, 256, 0, st>>>(x, s, y, rstd, rows, d);
   GPTB200_CHECK_LAUNCH();
   return 0;
