@@ -458,28 +458,52 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 }
 
 // ------------------------------------------------------------------ backward
-constexpr int BT = 128;                 // keys per CTA (TMEM lanes)
+// Persistent: one CTA per SM walks work items (key tile kt, batch*head bh),
+// item = kt * B*H + bh, taking items blockIdx.x, + gridDim.x, ... (heaviest
+// key tiles first, so the ends of the CTAs' lists are short items). Every role
+// walks the same item list and keeps running tile / query-pair counters across
+// items, so the rings (Q/dO stages, TMEM score buffers, dS^T slots, dQ pairs)
+// flow from one item into the next without draining: while the last tiles of
+// an item finish, the TMA warp already holds the next item's K/V (two K/V
+// slots) and the scores MMA thread computes its first scores.
+constexpr int BT = 128;                 // keys per item (TMEM lanes)
 constexpr int BQ = 64;                  // queries per inner tile
 constexpr int BT_BYTES = BT * 128;      // 128 rows x 64 bf16
 constexpr int BQ_BYTES = BQ * 128;      // 64 rows x 64 bf16
-constexpr int kQStages = 4;             // Q / dO tile ring
 constexpr int kBwdSmWarps = 16;         // softmax warps: four per TMEM lane quadrant
 constexpr int kBwdScoreWarp = 2 + kBwdSmWarps;  // issues the S^T / dP^T MMAs
 constexpr int kBwdFlushWarp = kBwdScoreWarp + 1;  // first of four dQ read-out warps
 constexpr int kBwdThreads = 32 * (kBwdFlushWarp + 4);
+// Arrivals that release an item slot: both MMA threads, the softmax warps and
+// the dQ warps.
+constexpr int kBwdItemUsers = 2 + kBwdSmWarps + 4;
 
+// Item slot written by the TMA warp: key tile, batch*head, number of 64-query
+// tiles (always even: an odd count gets one tile past the sequence end, whose
+// rows load as zeros and carry no probability, so query pairs never straddle
+// two items).
+struct BwdItem {
+  int kt, bh, nq, pad;
+};
+
+template <bool SEG>
 struct BwdSmem {
-  static constexpr int K = 0;
-  static constexpr int V = K + BT_BYTES;
-  static constexpr int Q = V + BT_BYTES;                // kQStages tiles
+  static constexpr int kQStages = SEG ? 2 : 3;          // Q / dO tile ring
+  static constexpr int KV = 0;                          // 2 slots x (K, V)
+  static constexpr int Q = KV + 4 * BT_BYTES;           // kQStages tiles
   static constexpr int DO = Q + kQStages * BQ_BYTES;    // kQStages tiles
   static constexpr int DST = DO + kQStages * BQ_BYTES;  // ring of 4 dS^T tiles [128 keys x 64 queries]
   static constexpr int DQS = DST + 4 * BT_BYTES;        // dQ staging: 4 warps x 2 x (32 x 32 fp32)
-  static constexpr int STAT = DQS + 8 * 4096;           // per warp: 32 -lse*log2(e), -delta, seg id
-  static constexpr int SEGTAB = STAT + 16 * 384;        // int2 per 64-position chunk from k0
-  static constexpr int QLIST = SEGTAB + kMaxSegChunks * 8;  // query tiles this CTA visits
-  static constexpr int BAR = QLIST + kMaxSegChunks * 4;
-  static constexpr int TOTAL = BAR + 256 + 1023;
+  // per Q/dO stage, the tile's query statistics copied in by the producer
+  // warp: 64 x lse, 64 x delta, 64 segment ids (zeros past the sequence end)
+  static constexpr int STAT = DQS + 8 * 4096;
+  static constexpr int ITEM = STAT + kQStages * 768;    // 2 BwdItem slots
+  // segment ids only: per slot, (min, max) id per 64-position chunk from k0
+  // and the list of query tiles that can see the key tile
+  static constexpr int SEGTAB = ITEM + 64;
+  static constexpr int QLIST = SEGTAB + (SEG ? 2 * kMaxSegChunks * 8 : 0);
+  static constexpr int BAR = QLIST + (SEG ? 2 * kMaxSegChunks * 4 : 0);
+  static constexpr int TOTAL = BAR + 512 + 1023;
 };
 
 template <bool SEG>
@@ -487,48 +511,55 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                 const __grid_constant__ CUtensorMap tmDQ, const AttnParams p) {
+  using L = BwdSmem<SEG>;
+  constexpr int kQS = L::kQStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                            ~static_cast<uintptr_t>(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + BwdSmem::BAR);
-  uint64_t* kv_full = bars + 0;
-  uint64_t* q_full = bars + 1;    // [4]
-  uint64_t* q_empty = bars + 5;   // [4]
-  uint64_t* s_full = bars + 9;    // [3]: S^T and dP^T of a tile are in TMEM buffer b
-  uint64_t* p_full = bars + 12;   // [3]: P^T, dS^T of a tile written (TMEM buffer b, smem ring)
-  uint64_t* done = bars + 15;     // [4]: every MMA issued up to the end of tile i has completed
-  uint64_t* dq_full = bars + 19;  // [2]: dQ of query pair j is in TMEM
-  uint64_t* dq_free = bars + 21;  // [2]: ... and has been read out
-  uint64_t* fin = bars + 23;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 24);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::BAR);
+  uint64_t* kv_full = bars + 0;       // [2] K/V slot loaded
+  uint64_t* kv_empty = bars + 2;      // [2] every MMA of the slot's item has completed
+  uint64_t* q_full = bars + 4;        // [3]
+  uint64_t* q_empty = bars + 7;       // [3]
+  uint64_t* s_full = bars + 10;       // [3]: S^T and dP^T of a tile are in TMEM buffer b
+  uint64_t* p_full = bars + 13;       // [3]: P^T, dS^T of a tile written (TMEM buffer b, smem ring)
+  uint64_t* done = bars + 16;         // [4]: every MMA issued up to the end of tile g has completed
+  uint64_t* dq_full = bars + 20;      // [2]: dQ of query pair J is in TMEM
+  uint64_t* dq_free = bars + 22;      // [2]: ... and has been read out
+  uint64_t* fin = bars + 24;          // an item's dK / dV are complete in TMEM
+  uint64_t* acc_free = bars + 25;     // ... and have been read out
+  uint64_t* item_full = bars + 26;    // [2]
+  uint64_t* item_empty = bars + 28;   // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 30);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  BwdItem* items = reinterpret_cast<BwdItem*>(sm + L::ITEM);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int kt = (int)blockIdx.x;
-  const int bh = blockIdx.y;
-  const int b = bh / p.H, h = bh - b * p.H;
-  const int k0 = kt * BT;
-  const int nq_all = (p.T - k0 + BQ - 1) / BQ;  // 64-query tiles from the diagonal to the end
-  const int* segrow = SEG ? p.seg + (int64_t)b * p.T : nullptr;  // null: causal only
-  int2* segtab = reinterpret_cast<int2*>(sm + BwdSmem::SEGTAB);  // chunk c at [c - 2 kt]
-  int* qlist = reinterpret_cast<int*>(sm + BwdSmem::QLIST);
-  int* counts = reinterpret_cast<int*>(bars + 26);
-  const int nch = (p.T + kSegChunk - 1) / kSegChunk - 2 * kt;
-  if (segrow) seg_chunk_ranges(segrow, p.T, 2 * kt, 2 * kt + nch, segtab);
-  __syncthreads();
+  const int BH = p.B * p.H;
+  const int n_items = ((p.T + BT - 1) / BT) * BH;
   int* err = &g_attn_error;
+  // query tile (64-position index past k0) of list entry `it` of the item in `slot`
+  auto qtile = [&](int slot, int it) -> int {
+    if constexpr (SEG)
+      return reinterpret_cast<const int*>(sm + L::QLIST)[slot * kMaxSegChunks + it];
+    else
+      return it;
+  };
+  auto segtab_of = [&](int slot) {
+    return reinterpret_cast<int2*>(sm + L::SEGTAB) + slot * kMaxSegChunks;
+  };
 
   if (threadIdx.x == 0) {
-    // The query tiles (one 64-position chunk each) that can see this key tile,
-    // in order; every role walks this list.
-    const int2 kr = segrow ? seg_range(segtab, nch, 0, 2) : make_int2(0, 0);
-    int n = 0;
-    for (int it = 0; it < nq_all; ++it)
-      if (!segrow || rng_meet(seg_range(segtab, nch, it, 1), kr)) qlist[n++] = it;
-    counts[0] = n;
-    mbar_init(kv_full, 1);
-    for (int s = 0; s < kQStages; ++s) {
-      mbar_init(&q_full[s], 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+      mbar_init(&item_full[s], 1);
+      mbar_init(&item_empty[s], kBwdItemUsers);
+      mbar_init(&dq_full[s], 1);
+      mbar_init(&dq_free[s], 4);
+    }
+    for (int s = 0; s < kQS; ++s) {
+      mbar_init(&q_full[s], 33);  // the Q/dO TMA and the 32 lanes' statistics copies
       mbar_init(&q_empty[s], 2);  // the scores MMAs and the gradient MMAs of the tile
     }
     for (int s = 0; s < 3; ++s) {
@@ -536,11 +567,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       mbar_init(&p_full[s], kBwdSmWarps);
     }
     for (int s = 0; s < 4; ++s) mbar_init(&done[s], 1);
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&dq_full[s], 1);
-      mbar_init(&dq_free[s], 4);
-    }
     mbar_init(fin, 1);
+    mbar_init(acc_free, 4);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -548,102 +576,202 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const int nq = counts[0];
   // TMEM columns: three tile buffers of 128 columns, then dV | dK. In buffer
   // b, columns [0, 64) receive S^T and [64, 128) dP^T (fp32, lane = key). The
   // softmax writes P^T and dS^T as bf16 pairs over the S^T half (query group
-  // cg = 16 queries: columns 16 cg + [0, 8) for P^T, 16 cg + [8, 16) for dS^T); the
-  // dP^T half then holds dQ when the tile closes a query pair.
+  // cg = 16 queries: columns 16 cg + [0, 8) for P^T, 16 cg + [8, 16) for
+  // dS^T); the dP^T half then holds dQ when the tile closes a query pair.
   const uint32_t tmem = *tmem_slot;
   const uint32_t tDV = tmem + 384, tDK = tmem + 448;
   auto tBuf = [&](int bb) { return tmem + 128 * bb; };
 
   if (warp == 0) {
-    if (lane == 0) {
-      mbar_arrive_expect_tx(kv_full, 2 * BT_BYTES);
-      tma_load_4d(sm + BwdSmem::K, &tmK, kv_full, 0, k0, h, b);
-      tma_load_4d(sm + BwdSmem::V, &tmV, kv_full, 0, k0, h, b);
-      for (int it = 0; it < nq; ++it) {
-        const int s = it % kQStages;
-        if (!mbar_wait(&q_empty[s], ((it / kQStages) & 1) ^ 1, abort_flag, err)) break;
-        mbar_arrive_expect_tx(&q_full[s], 2 * BQ_BYTES);
-        const int qq = k0 + qlist[it] * BQ;
-        tma_load_4d(sm + BwdSmem::Q + s * BQ_BYTES, &tmQ, &q_full[s], 0, qq, h, b);
-        tma_load_4d(sm + BwdSmem::DO + s * BQ_BYTES, &tmDO, &q_full[s], 0, qq, h, b);
+    // Item producer: publishes each item's slot (and, with segment ids, its
+    // chunk ranges and query-tile list), then loads its K/V and Q/dO tiles.
+    bool ok = true;
+    int g = 0, ii = 0;
+    for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x, ++ii) {
+      const int slot = ii & 1;
+      if (!(ok = mbar_wait(&item_empty[slot], ((ii >> 1) & 1) ^ 1, abort_flag, err))) break;
+      const int kt = item / BH, bh = item - kt * BH;
+      const int b = bh / p.H, h = bh - b * p.H;
+      const int k0 = kt * BT;
+      const int nq_all = (p.T - k0 + BQ - 1) / BQ;  // 64-query tiles from the diagonal on
+      int nq = nq_all;
+      if constexpr (SEG) {
+        // (min, max) segment id per 64-position chunk from k0, then the query
+        // tiles whose ids can meet this key tile's, in order
+        const int* segrow = p.seg + (int64_t)b * p.T;
+        int2* tab = segtab_of(slot);
+        const int nch = (p.T + kSegChunk - 1) / kSegChunk - 2 * kt;
+        for (int c = 0; c < nch; ++c) {
+          int mn = INT_MAX, mx = INT_MIN;
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int t = (2 * kt + c) * kSegChunk + u * 32 + lane;
+            if (t < p.T) {
+              const int v = segrow[t];
+              mn = min(mn, v);
+              mx = max(mx, v);
+            }
+          }
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) {
+            mn = min(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+            mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+          }
+          if (lane == 0) tab[c] = make_int2(mn, mx);
+        }
+        __syncwarp();
+        if (lane == 0) {
+          int* ql = reinterpret_cast<int*>(sm + L::QLIST) + slot * kMaxSegChunks;
+          const int2 kr = seg_range(tab, nch, 0, 2);
+          int n = 0;
+          for (int it = 0; it < nq_all; ++it)
+            if (rng_meet(seg_range(tab, nch, it, 1), kr)) ql[n++] = it;
+          if (n & 1) ql[n++] = nq_all;  // past the sequence end: no probability
+          nq = n;
+        }
+        nq = __shfl_sync(0xffffffffu, nq, 0);
+      } else {
+        nq += nq & 1;
+      }
+      if (lane == 0) {
+        items[slot] = BwdItem{kt, bh, nq, 0};
+        mbar_arrive(&item_full[slot]);
+        const int kvs = ii & 1;
+        ok = mbar_wait(&kv_empty[kvs], ((ii >> 1) & 1) ^ 1, abort_flag, err);
+        if (ok) {
+          uint8_t* kv = sm + L::KV + kvs * 2 * BT_BYTES;
+          mbar_arrive_expect_tx(&kv_full[kvs], 2 * BT_BYTES);
+          tma_load_4d(kv, &tmK, &kv_full[kvs], 0, k0, h, b);
+          tma_load_4d(kv + BT_BYTES, &tmV, &kv_full[kvs], 0, k0, h, b);
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, (int)ok, 0) != 0;
+      const float* Lg = p.lse + (int64_t)bh * p.T;
+      const float* Dg = p.delta + (int64_t)bh * p.T;
+      for (int it = 0; ok && it < nq; ++it, ++g) {
+        const int s = g % kQS;
+        const int qq = k0 + qtile(slot, it) * BQ;
+        if (lane == 0) {
+          ok = mbar_wait(&q_empty[s], ((g / kQS) & 1) ^ 1, abort_flag, err);
+          if (ok) {
+            mbar_arrive_expect_tx(&q_full[s], 2 * BQ_BYTES);
+            tma_load_4d(sm + L::Q + s * BQ_BYTES, &tmQ, &q_full[s], 0, qq, h, b);
+            tma_load_4d(sm + L::DO + s * BQ_BYTES, &tmDO, &q_full[s], 0, qq, h, b);
+          }
+        }
+        if (!(ok = __shfl_sync(0xffffffffu, (int)ok, 0) != 0)) break;
+        // the tile's statistics, copied asynchronously (each lane arrives on
+        // the stage's barrier once its copies have landed)
+        float* st = reinterpret_cast<float*>(sm + L::STAT + s * 768);
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int cidx = lane + 32 * u, t = qq + cidx;
+          const uint32_t nb = t < p.T ? 4u : 0u;
+          const int tc = min(t, p.T - 1);
+          cp_async_4(st + cidx, Lg + tc, nb);
+          cp_async_4(st + 64 + cidx, Dg + tc, nb);
+          if constexpr (SEG) cp_async_4(st + 128 + cidx, p.seg + (int64_t)b * p.T + tc, nb);
+        }
+        cp_async_mbar_arrive(&q_full[s]);
       }
     }
   } else if (warp == 1) {
-    // Gradient MMAs of tile `it` once its softmax is done. This thread and
-    // the scores thread (warp 18) issue independently: a thread that stops at
-    // a barrier leaves the tensor pipe to the other one.
+    // Gradient MMAs of tile g once its softmax is done. This thread and the
+    // scores thread (warp 18) issue independently: a thread that stops at a
+    // barrier leaves the tensor pipe to the other one.
     if (lane == 0) {
       constexpr uint32_t idKN = umma_idesc_bf16(128, 64, 0, 1);  // dV, dK: A in TMEM, B MN-major
       constexpr uint32_t idMN = umma_idesc_bf16(128, 64, 1, 1);  // dQ: A, B MN-major
-      const uint32_t sK = smem_u32(sm + BwdSmem::K);
-      for (int it = 0; it < nq; ++it) {
-        const int bb = it % 3, s = it % kQStages;
-        if (!mbar_wait(&p_full[bb], (it / 3) & 1, abort_flag, err)) break;
-        tc_fence_after();
-        const uint32_t sQ = smem_u32(sm + BwdSmem::Q + s * BQ_BYTES);
-        const uint32_t sDO = smem_u32(sm + BwdSmem::DO + s * BQ_BYTES);
-        // dV += P^T dO and dK += dS^T Q with the A operands read from TMEM:
-        // queries 16k..16k+15 sit at column 16k of the buffer (P^T, bf16
-        // pairs), 8 further on for dS^T.
+      bool ok = true;
+      int g = 0, ii = 0;
+      for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x, ++ii) {
+        const int slot = ii & 1, kvs = ii & 1;
+        if (!(ok = mbar_wait(&item_full[slot], (ii >> 1) & 1, abort_flag, err))) break;
+        const int nq = items[slot].nq;
+        // dV / dK of the previous item have been read out of TMEM
+        if (ii > 0 && !(ok = mbar_wait(acc_free, (ii - 1) & 1, abort_flag, err))) break;
+        const uint32_t sK = smem_u32(sm + L::KV + kvs * 2 * BT_BYTES);
+        for (int it = 0; it < nq; ++it, ++g) {
+          const int bb = g % 3, s = g % kQS;
+          if (!(ok = mbar_wait(&p_full[bb], (g / 3) & 1, abort_flag, err))) break;
+          tc_fence_after();
+          const uint32_t sQ = smem_u32(sm + L::Q + s * BQ_BYTES);
+          const uint32_t sDO = smem_u32(sm + L::DO + s * BQ_BYTES);
+          // dV += P^T dO and dK += dS^T Q with the A operands read from TMEM:
+          // queries 16k..16k+15 sit at column 16k of the buffer (P^T, bf16
+          // pairs), 8 further on for dS^T.
 #pragma unroll
-        for (int k = 0; k < BQ / 16; ++k) {
-          const uint32_t acol = tBuf(bb) + k * 16;
-          umma_bf16_ts(tDV, acol, umma_smem_desc(sDO + k * 2048, BQ_BYTES, 1024), idKN,
-                       (it > 0 || k > 0));
-          umma_bf16_ts(tDK, acol + 8, umma_smem_desc(sQ + k * 2048, BQ_BYTES, 1024), idKN,
-                       (it > 0 || k > 0));
-        }
-        umma_commit(&q_empty[s]);
-        if ((it & 1) || it == nq - 1) {
-          // dQ of query pair j (tiles 2j, 2j+1) = dS K into the dP^T half of
-          // this buffer: A = the pair's two dS^T tiles of the ring read
-          // MN-major (M = 128 queries, 16 KB apart), B = K tile MN-major.
-          const int j = it >> 1;
-          const uint32_t sd = smem_u32(sm + BwdSmem::DST + ((2 * j) & 3) * BT_BYTES);
+          for (int k = 0; k < BQ / 16; ++k) {
+            const uint32_t acol = tBuf(bb) + k * 16;
+            umma_bf16_ts(tDV, acol, umma_smem_desc(sDO + k * 2048, BQ_BYTES, 1024), idKN,
+                         (it > 0 || k > 0));
+            umma_bf16_ts(tDK, acol + 8, umma_smem_desc(sQ + k * 2048, BQ_BYTES, 1024), idKN,
+                         (it > 0 || k > 0));
+          }
+          umma_commit(&q_empty[s]);
+          if (it & 1) {
+            // dQ of query pair J (tiles g-1, g) = dS K into the dP^T half of
+            // this buffer: A = the pair's two dS^T tiles of the ring read
+            // MN-major (M = 128 queries, 16 KB apart), B = K tile MN-major.
+            const int J = g >> 1;
+            const uint32_t sd = smem_u32(sm + L::DST + ((g - 1) & 3) * BT_BYTES);
 #pragma unroll
-          for (int k = 0; k < BT / 16; ++k)
-            umma_bf16(tBuf(bb) + 64, umma_smem_desc(sd + k * 2048, BT_BYTES, 1024),
-                      umma_smem_desc(sK + k * 2048, BT_BYTES, 1024), idMN, k > 0);
-          umma_commit(&dq_full[j & 1]);
+            for (int k = 0; k < BT / 16; ++k)
+              umma_bf16(tBuf(bb) + 64, umma_smem_desc(sd + k * 2048, BT_BYTES, 1024),
+                        umma_smem_desc(sK + k * 2048, BT_BYTES, 1024), idMN, k > 0);
+            umma_commit(&dq_full[J & 1]);
+          }
+          umma_commit(&done[g & 3]);
         }
-        umma_commit(&done[it & 3]);
+        if (!ok) break;
+        umma_commit(fin);
+        umma_commit(&kv_empty[kvs]);
+        mbar_arrive(&item_empty[slot]);
       }
-      umma_commit(fin);
     }
   } else if (warp == kBwdScoreWarp) {
-    // S^T = K Q^T and dP^T = V dO^T of each tile into TMEM buffer it % 3, as
-    // far ahead as the buffers allow. The buffer last served tile it-3: read
-    // by that tile's dV / dK MMAs and, when it-3 closed a query pair, holding
-    // that pair's dQ until the softmax warps have read it out.
+    // S^T = K Q^T and dP^T = V dO^T of each tile into TMEM buffer g % 3, as
+    // far ahead as the buffers allow. The buffer last served tile g-3: read by
+    // that tile's dV / dK MMAs and, when g-3 closed a query pair, holding that
+    // pair's dQ until the dQ warps have read it out.
     if (lane == 0) {
       constexpr uint32_t idS = umma_idesc_bf16(128, BQ, 0, 0);
-      const uint32_t sK = smem_u32(sm + BwdSmem::K), sV = smem_u32(sm + BwdSmem::V);
-      bool ok = mbar_wait(kv_full, 0, abort_flag, err);
-      for (int it = 0; ok && it < nq; ++it) {
-        const int s = it % kQStages;
-        if (it >= 3) {
-          const int o = it - 3;
-          if (!mbar_wait(&done[o & 3], (o >> 2) & 1, abort_flag, err)) break;
-          if ((o & 1) && !mbar_wait(&dq_free[(o >> 1) & 1], (o >> 2) & 1, abort_flag, err)) break;
-        }
-        if (!mbar_wait(&q_full[s], (it / kQStages) & 1, abort_flag, err)) break;
-        tc_fence_after();
-        const uint32_t sQ = smem_u32(sm + BwdSmem::Q + s * BQ_BYTES);
-        const uint32_t sDO = smem_u32(sm + BwdSmem::DO + s * BQ_BYTES);
-        const uint32_t tb = tBuf(it % 3);
+      bool ok = true;
+      int g = 0, ii = 0;
+      for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x, ++ii) {
+        const int slot = ii & 1, kvs = ii & 1;
+        if (!(ok = mbar_wait(&item_full[slot], (ii >> 1) & 1, abort_flag, err))) break;
+        const int nq = items[slot].nq;
+        if (!(ok = mbar_wait(&kv_full[kvs], (ii >> 1) & 1, abort_flag, err))) break;
+        const uint32_t sK = smem_u32(sm + L::KV + kvs * 2 * BT_BYTES), sV = sK + BT_BYTES;
+        for (int it = 0; it < nq; ++it, ++g) {
+          const int s = g % kQS;
+          if (g >= 3) {
+            const int o = g - 3;
+            if (!(ok = mbar_wait(&done[o & 3], (o >> 2) & 1, abort_flag, err))) break;
+            if ((o & 1) && !(ok = mbar_wait(&dq_free[(o >> 1) & 1], (o >> 2) & 1, abort_flag, err)))
+              break;
+          }
+          if (!(ok = mbar_wait(&q_full[s], (g / kQS) & 1, abort_flag, err))) break;
+          tc_fence_after();
+          const uint32_t sQ = smem_u32(sm + L::Q + s * BQ_BYTES);
+          const uint32_t sDO = smem_u32(sm + L::DO + s * BQ_BYTES);
+          const uint32_t tb = tBuf(g % 3);
 #pragma unroll
-        for (int k = 0; k < HD / 16; ++k) {
-          umma_bf16(tb, umma_smem_desc(sK + k * 32, 16, 1024),
-                    umma_smem_desc(sQ + k * 32, 16, 1024), idS, k > 0);
-          umma_bf16(tb + 64, umma_smem_desc(sV + k * 32, 16, 1024),
-                    umma_smem_desc(sDO + k * 32, 16, 1024), idS, k > 0);
+          for (int k = 0; k < HD / 16; ++k) {
+            umma_bf16(tb, umma_smem_desc(sK + k * 32, 16, 1024),
+                      umma_smem_desc(sQ + k * 32, 16, 1024), idS, k > 0);
+            umma_bf16(tb + 64, umma_smem_desc(sV + k * 32, 16, 1024),
+                      umma_smem_desc(sDO + k * 32, 16, 1024), idS, k > 0);
+          }
+          umma_commit(&s_full[g % 3]);
+          umma_commit(&q_empty[s]);
         }
-        umma_commit(&s_full[it % 3]);
-        umma_commit(&q_empty[s]);
+        if (!ok) break;
+        mbar_arrive(&item_empty[slot]);
       }
     }
   } else if (warp < 2 + kBwdSmWarps) {
@@ -651,193 +779,220 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     // lanes of quadrant w % 4 (key rows) and the 16 query columns
     // [16 cg, 16 cg + 16) of the tile, cg = (w - 2) / 4, and writes P^T and
     // dS^T (bf16 pairs) over exactly those S^T columns, so no warp overwrites
-    // scores another warp has yet to read.
+    // scores another warp has yet to read. The tile's statistics come
+    // ready-made from the producer warp (shared memory of the Q/dO stage).
     const int quad = warp & 3;
     const int cg = (warp - 2) >> 2;
     const int r = quad * 32 + lane;
-    const int key = k0 + r;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const float c = p.scale * kLog2e;
-    const float* Lg = p.lse + (int64_t)bh * p.T;
-    const float* Dg = p.delta + (int64_t)bh * p.T;
-    float* stat = reinterpret_cast<float*>(sm + BwdSmem::STAT + (warp - 2) * 384);
-    int* stat_seg = reinterpret_cast<int*>(stat + 64);
-    // this key row's segment id (rows past T take an id no query has)
-    const int sk = segrow ? (key < p.T ? segrow[key] : INT_MAX) : 0;
-    const int2 krng = segrow ? seg_range(segtab, nch, 0, 2) : make_int2(0, 0);
-    // lane j < 16 fetches the statistics of query column 16 cg + j of list entry `it`
-    auto fetch = [&](int it, float& l2, float& d2, int& s2) {
-      const int t = k0 + qlist[it] * BQ + cg * 16 + (lane & 15);
-      l2 = (t < p.T) ? Lg[t] * kLog2e : INFINITY;  // rows past T: P = 0
-      d2 = (t < p.T) ? Dg[t] : 0.f;
-      s2 = (segrow && t < p.T) ? segrow[t] : INT_MIN;
-    };
-    float nl = 0.f, nd = 0.f;
-    int ns = 0;
-    if (nq > 0) fetch(0, nl, nd, ns);
     bool ok = true;
-    for (int it = 0; it < nq && ok; ++it) {
-      const int bb = it % 3;
-      const uint32_t tb = tBuf(bb);
-      // this tile's statistics, broadcast to the warp through shared memory
-      const int qt = qlist[it];  // query tile index (64 positions) past k0
-      __syncwarp();
-      if (lane < 16) {
-        stat[lane] = -nl;
-        stat[32 + lane] = -nd;
-        stat_seg[lane] = ns;
-      }
-      __syncwarp();
-      if (it + 1 < nq) fetch(it + 1, nl, nd, ns);
-      if (!mbar_wait(&s_full[bb], (it / 3) & 1, abort_flag, err)) {
-        ok = false;
-        break;
-      }
-      // The dS^T ring slot of this tile was last read by the dQ MMA of tile it-4.
-      if (it >= 4 && !mbar_wait(&done[(it - 3) & 3], ((it - 3) >> 2) & 1, abort_flag, err)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      uint32_t sraw[16], draw[16];
-      tmem_ld16_nw(tb + lane_off + cg * 16, sraw);
-      tmem_ld16_nw(tb + 64 + lane_off + cg * 16, draw);
-      tmem_wait_ld();
-      const int qbase = qt * BQ + cg * 16;  // query index relative to k0
-      const bool diag = (qt < 2);           // key r > query masks only near the diagonal
-      // per-element segment test unless this key tile and query tile share one id
-      const bool segmask = segrow && !rng_single(seg_range(segtab, nch, qt, 1), krng);
-      // P^T = exp2(S^T c - lse log2e) and dS^T = P^T (dP^T - delta), two
-      // columns per packed f32x2 instruction (stat holds -lse log2e and
-      // -delta); the causal test runs only on the two diagonal tiles and the
-      // segment test only when the tiles' ids differ.
-      uint32_t pk[8], dk[8];
-      auto softmax_cols = [&](auto diag_tag) {
-        constexpr bool kDiag = decltype(diag_tag)::value;
-        const float2 c2 = make_float2(c, c);
+    int g = 0, ii = 0;
+    for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x, ++ii) {
+      const int slot = ii & 1;
+      if (!(ok = mbar_wait(&item_full[slot], (ii >> 1) & 1, abort_flag, err))) break;
+      const BwdItem inf = items[slot];
+      const int nq = inf.nq;
+      const int b = inf.bh / p.H;
+      const int k0 = inf.kt * BT;
+      const int key = k0 + r;
+      const int* segrow = SEG ? p.seg + (int64_t)b * p.T : nullptr;
+      const int2* segtab = SEG ? segtab_of(slot) : nullptr;
+      const int nch = (p.T + kSegChunk - 1) / kSegChunk - 2 * inf.kt;
+      // this key row's segment id (rows past T take an id no query has)
+      const int sk = segrow ? (key < p.T ? segrow[key] : INT_MAX) : 0;
+      const int2 krng = segrow ? seg_range(segtab, nch, 0, 2) : make_int2(0, 0);
+      for (int it = 0; it < nq; ++it) {
+        const int gt = g + it;  // running tile index
+        const int bb = gt % 3;
+        const uint32_t tb = tBuf(bb);
+        const int qt = qtile(slot, it);  // query tile index (64 positions) past k0
+        // this warp's 16 columns of the stage's statistics; the scores of the
+        // tile exist only after its Q/dO stage (statistics included) was full
+        const float* stat = reinterpret_cast<const float*>(sm + L::STAT + (gt % kQS) * 768) + cg * 16;
+        const int* stat_seg = reinterpret_cast<const int*>(stat) + 128;
+        if (!(ok = mbar_wait(&s_full[bb], (gt / 3) & 1, abort_flag, err))) break;
+        if (!(ok = mbar_wait(&q_full[gt % kQS], (gt / kQS) & 1, abort_flag, err))) break;
+        // The dS^T ring slot of this tile was last read by the dQ MMA of the
+        // pair closed by tile gt-3.
+        if (gt >= 4 && !(ok = mbar_wait(&done[(gt - 3) & 3], ((gt - 3) >> 2) & 1, abort_flag, err)))
+          break;
+        tc_fence_after();
+        uint32_t sraw[16], draw[16];
+        tmem_ld16_nw(tb + lane_off + cg * 16, sraw);
+        tmem_ld16_nw(tb + 64 + lane_off + cg * 16, draw);
+        tmem_wait_ld();
+        const int qbase = qt * BQ + cg * 16;  // query index relative to k0
+        const bool diag = (qt < 2);           // key r > query masks only near the diagonal
+        const int tail = p.T - k0 - qbase;    // columns j >= tail lie past the sequence end
+        const bool mask = diag || tail < 16;
+        // per-element segment test unless this key tile and query tile share one id
+        const bool segmask = segrow && !rng_single(seg_range(segtab, nch, qt, 1), krng);
+        // P^T = exp2(S^T c - lse log2e) and dS^T = P^T (dP^T - delta), two
+        // columns per packed f32x2 instruction; the causal and end-of-sequence
+        // tests run only on tiles that need them and the segment test only
+        // when the tiles' ids differ.
+        uint32_t pk[8], dk[8];
+        auto softmax_cols = [&](auto mask_tag) {
+          constexpr bool kMask = decltype(mask_tag)::value;
+          const float2 c2 = make_float2(c, c);
+          const float2 nlog2e = make_float2(-kLog2e, -kLog2e);
+          const float2 m1 = make_float2(-1.f, -1.f);
 #pragma unroll
-        for (int j4 = 0; j4 < 4; ++j4) {
-          const float4 l4 = reinterpret_cast<const float4*>(stat)[j4];
-          const float4 d4 = reinterpret_cast<const float4*>(stat + 32)[j4];
-          const float2 x01 = ffma2(make_float2(__uint_as_float(sraw[4 * j4]),
-                                               __uint_as_float(sraw[4 * j4 + 1])),
-                                   c2, make_float2(l4.x, l4.y));
-          const float2 x23 = ffma2(make_float2(__uint_as_float(sraw[4 * j4 + 2]),
-                                               __uint_as_float(sraw[4 * j4 + 3])),
-                                   c2, make_float2(l4.z, l4.w));
-          float pv[4] = {ex2(x01.x), ex2(x01.y), ex2(x23.x), ex2(x23.y)};
+          for (int j4 = 0; j4 < 4; ++j4) {
+            const float4 l4 = reinterpret_cast<const float4*>(stat)[j4];
+            const float4 d4 = reinterpret_cast<const float4*>(stat + 64)[j4];
+            const float2 x01 = ffma2(make_float2(__uint_as_float(sraw[4 * j4]),
+                                                 __uint_as_float(sraw[4 * j4 + 1])),
+                                     c2, fmul2(make_float2(l4.x, l4.y), nlog2e));
+            const float2 x23 = ffma2(make_float2(__uint_as_float(sraw[4 * j4 + 2]),
+                                                 __uint_as_float(sraw[4 * j4 + 3])),
+                                     c2, fmul2(make_float2(l4.z, l4.w), nlog2e));
+            float pv[4] = {ex2(x01.x), ex2(x01.y), ex2(x23.x), ex2(x23.y)};
+            // dP^T - delta as fma(delta, -1, dP^T): one rounding, as a subtraction
+            const float2 g01 = ffma2(make_float2(d4.x, d4.y), m1,
+                                     make_float2(__uint_as_float(draw[4 * j4]),
+                                                 __uint_as_float(draw[4 * j4 + 1])));
+            const float2 g23 = ffma2(make_float2(d4.z, d4.w), m1,
+                                     make_float2(__uint_as_float(draw[4 * j4 + 2]),
+                                                 __uint_as_float(draw[4 * j4 + 3])));
+            float2 dv01 = fmul2(make_float2(pv[0], pv[1]), g01);
+            float2 dv23 = fmul2(make_float2(pv[2], pv[3]), g23);
+            float dvs[4] = {dv01.x, dv01.y, dv23.x, dv23.y};
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int j = 4 * j4 + u;
-            if (kDiag && r > qbase + j) pv[u] = 0.f;
-            if (SEG && segmask && stat_seg[j] != sk) pv[u] = 0.f;
+            for (int u = 0; u < 4; ++u) {
+              const int j = 4 * j4 + u;
+              bool off = false;
+              if (kMask) off = (diag && r > qbase + j) || j >= tail;
+              if (SEG && segmask && stat_seg[j] != sk) off = true;
+              if (off) pv[u] = dvs[u] = 0.f;
+            }
+            dv01 = make_float2(dvs[0], dvs[1]);
+            dv23 = make_float2(dvs[2], dvs[3]);
+            pk[2 * j4] = pack_bf16x2(pv[0], pv[1]);
+            pk[2 * j4 + 1] = pack_bf16x2(pv[2], pv[3]);
+            dk[2 * j4] = pack_bf16x2(dv01.x, dv01.y);
+            dk[2 * j4 + 1] = pack_bf16x2(dv23.x, dv23.y);
           }
-          const float2 g01 = fadd2(make_float2(__uint_as_float(draw[4 * j4]),
-                                               __uint_as_float(draw[4 * j4 + 1])),
-                                   make_float2(d4.x, d4.y));
-          const float2 g23 = fadd2(make_float2(__uint_as_float(draw[4 * j4 + 2]),
-                                               __uint_as_float(draw[4 * j4 + 3])),
-                                   make_float2(d4.z, d4.w));
-          const float2 dv01 = fmul2(make_float2(pv[0], pv[1]), g01);
-          const float2 dv23 = fmul2(make_float2(pv[2], pv[3]), g23);
-          pk[2 * j4] = pack_bf16x2(pv[0], pv[1]);
-          pk[2 * j4 + 1] = pack_bf16x2(pv[2], pv[3]);
-          dk[2 * j4] = pack_bf16x2(dv01.x, dv01.y);
-          dk[2 * j4 + 1] = pack_bf16x2(dv23.x, dv23.y);
-        }
-      };
-      if (diag)
-        softmax_cols(std::integral_constant<bool, true>());
-      else
-        softmax_cols(std::integral_constant<bool, false>());
-      tmem_st8_nw(tb + lane_off + cg * 16, pk);
-      tmem_st8_nw(tb + lane_off + cg * 16 + 8, dk);
-      uint8_t* sd = sm + BwdSmem::DST + (it & 3) * BT_BYTES;
+        };
+        if (mask)
+          softmax_cols(std::integral_constant<bool, true>());
+        else
+          softmax_cols(std::integral_constant<bool, false>());
+        tmem_st8_nw(tb + lane_off + cg * 16, pk);
+        tmem_st8_nw(tb + lane_off + cg * 16 + 8, dk);
+        uint8_t* sd = sm + L::DST + (gt & 3) * BT_BYTES;
 #pragma unroll
-      for (int g = 0; g < 2; ++g)
-        *reinterpret_cast<uint4*>(sd + swz128(r, cg * 2 + g)) =
-            make_uint4(dk[4 * g], dk[4 * g + 1], dk[4 * g + 2], dk[4 * g + 3]);
-      tmem_wait_st();
-      fence_proxy_async_smem();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[bb]);
-    }
-
-    if (ok && mbar_wait(fin, 0, abort_flag, err)) {
-      tc_fence_after();
-      // warps with cg 0-1 write dK, cg 2-3 dV, 32 columns each; the
-      // warp-collective TMEM load stays outside the per-row guard
-      const bool is_k = cg < 2;
-      const int c0 = (cg & 1) * 32;
-      float g[32];
-      tmem_ld32((is_k ? tDK : tDV) + lane_off + c0, g);
-      if (key < p.T) {
-        bf16* row = (is_k ? p.dk : p.dv) + b * p.sb + h * p.sh + (int64_t)key * p.st + c0;
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          float* gv = g + 8 * q4;
-          if (is_k) {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) gv[i] *= p.scale;
-            if (p.rcos) rope_back(gv, p.rcos, p.rsin, key, c0 / 8 + q4);
-          }
-          uint4 o;
-          o.x = pack_bf16x2(gv[0], gv[1]);
-          o.y = pack_bf16x2(gv[2], gv[3]);
-          o.z = pack_bf16x2(gv[4], gv[5]);
-          o.w = pack_bf16x2(gv[6], gv[7]);
-          *reinterpret_cast<uint4*>(row + 8 * q4) = o;
-        }
+        for (int q2 = 0; q2 < 2; ++q2)
+          *reinterpret_cast<uint4*>(sd + swz128(r, cg * 2 + q2)) =
+              make_uint4(dk[4 * q2], dk[4 * q2 + 1], dk[4 * q2 + 2], dk[4 * q2 + 3]);
+        tmem_wait_st();
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[bb]);
       }
+      if (!ok) break;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&item_empty[slot]);
+      g += nq;
     }
   } else {
     // dQ read-out: warp kBwdFlushWarp + i serves TMEM lane quadrant
-    // (kBwdFlushWarp + i) % 4. For each query pair j (list entries 2j, 2j+1;
-    // TMEM lane m is row m of the pair, quadrants 0-1 the first tile, 2-3 the
-    // second) it loads its 32 rows x 64 fp32 columns as soon as the pair's dQ
-    // MMA has completed, releases the TMEM buffer, stages the rows in two
-    // 128-byte swizzled [32 x 32] boxes of its own and reduces them into
-    // dq_acc with TMA reduce-adds (rows past the sequence end are clipped by
-    // the map). The softmax warps never wait for this.
+    // (kBwdFlushWarp + i) % 4. For each query pair (list entries 2j, 2j+1 of
+    // an item; TMEM lane m is row m of the pair, quadrants 0-1 the first tile,
+    // 2-3 the second) it loads its 32 rows x 64 fp32 columns as soon as the
+    // pair's dQ MMA has completed, releases the TMEM buffer, stages the rows
+    // in two 128-byte swizzled [32 x 32] boxes of its own and reduces them
+    // into dq_acc with TMA reduce-adds (rows past the sequence end are clipped
+    // by the map; a box that starts past it is skipped). At the end of an
+    // item the same warps write dK and dV. The softmax warps never wait for
+    // this.
     const int quad = warp & 3;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
-    uint8_t* stage = sm + BwdSmem::DQS + (warp - kBwdFlushWarp) * 8192;
-    const int npairs = (nq + 1) >> 1;
-    for (int j = 0; j < npairs; ++j) {
-      if (!mbar_wait(&dq_full[j & 1], (j >> 1) & 1, abort_flag, err)) break;
-      tc_fence_after();
-      const int e = 2 * j + (quad >> 1);  // list entry of this warp's rows
-      const int bb = min(2 * j + 1, nq - 1) % 3;
-      if (e < nq) {
+    uint8_t* stage = sm + L::DQS + (warp - kBwdFlushWarp) * 8192;
+    bool ok = true;
+    int g = 0, ii = 0;
+    for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x, ++ii) {
+      const int slot = ii & 1;
+      if (!(ok = mbar_wait(&item_full[slot], (ii >> 1) & 1, abort_flag, err))) break;
+      const BwdItem inf = items[slot];
+      const int k0 = inf.kt * BT;
+      for (int j = 0; j < inf.nq / 2; ++j) {
+        const int J = (g >> 1) + j;  // running pair index
+        if (!(ok = mbar_wait(&dq_full[J & 1], (J >> 1) & 1, abort_flag, err))) break;
+        tc_fence_after();
+        const int bb = (g + 2 * j + 1) % 3;  // buffer of the pair's closing tile
         float v[64];
         tmem_ld32(tBuf(bb) + 64 + lane_off, v);
         tmem_ld32(tBuf(bb) + 96 + lane_off, v + 32);
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&dq_free[j & 1]);
-        if (lane == 0) bulk_wait_read();  // the previous reduce has read the staging boxes
-        __syncwarp();
+        if (lane == 0) mbar_arrive(&dq_free[J & 1]);
+        const int row0 = k0 + qtile(slot, 2 * j + (quad >> 1)) * BQ + (quad & 1) * 32;
+        if (row0 < p.T) {  // warp-uniform
+          if (lane == 0) bulk_wait_read();  // the previous reduce has read the staging boxes
+          __syncwarp();
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh)
+          for (int hh = 0; hh < 2; ++hh)
 #pragma unroll
-          for (int ch = 0; ch < 8; ++ch)
-            *reinterpret_cast<float4*>(stage + hh * 4096 + swz128(lane, ch)) =
-                make_float4(v[32 * hh + 4 * ch], v[32 * hh + 4 * ch + 1],
-                            v[32 * hh + 4 * ch + 2], v[32 * hh + 4 * ch + 3]);
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          const int row0 = k0 + qlist[e] * BQ + (quad & 1) * 32;
-          tma_reduce_add_3d(&tmDQ, stage, 0, row0, bh);
-          tma_reduce_add_3d(&tmDQ, stage + 4096, 32, row0, bh);
-          bulk_commit();
+            for (int ch = 0; ch < 8; ++ch)
+              *reinterpret_cast<float4*>(stage + hh * 4096 + swz128(lane, ch)) =
+                  make_float4(v[32 * hh + 4 * ch], v[32 * hh + 4 * ch + 1],
+                              v[32 * hh + 4 * ch + 2], v[32 * hh + 4 * ch + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_reduce_add_3d(&tmDQ, stage, 0, row0, inf.bh);
+            tma_reduce_add_3d(&tmDQ, stage + 4096, 32, row0, inf.bh);
+            bulk_commit();
+          }
         }
-      } else {  // a last pair of one tile: nothing in these rows
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&dq_free[j & 1]);
       }
+      if (!ok) break;
+      // dK (times the softmax scale, rotated back by RoPE) and dV of the
+      // item's 128 keys, this warp's 32 rows, in four 32-column chunks; the
+      // next item's gradient MMAs may overwrite the accumulators once the
+      // last chunk has left TMEM.
+      if (!(ok = mbar_wait(fin, ii & 1, abort_flag, err))) break;
+      tc_fence_after();
+      {
+        const int key = k0 + quad * 32 + lane;
+        const int bi = inf.bh / p.H, hi = inf.bh - bi * p.H;
+#pragma unroll 1
+        for (int ci = 0; ci < 4; ++ci) {
+          const bool is_k = ci < 2;
+          const int c0 = (ci & 1) * 32;
+          float gv32[32];
+          tmem_ld32((is_k ? tDK : tDV) + lane_off + c0, gv32);
+          if (ci == 3) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_free);
+          }
+          if (key < p.T) {
+            bf16* row = (is_k ? p.dk : p.dv) + bi * p.sb + hi * p.sh + (int64_t)key * p.st + c0;
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4) {
+              float* gv = gv32 + 8 * q4;
+              if (is_k) {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) gv[i] *= p.scale;
+                if (p.rcos) rope_back(gv, p.rcos, p.rsin, key, c0 / 8 + q4);
+              }
+              uint4 o;
+              o.x = pack_bf16x2(gv[0], gv[1]);
+              o.y = pack_bf16x2(gv[2], gv[3]);
+              o.z = pack_bf16x2(gv[4], gv[5]);
+              o.w = pack_bf16x2(gv[6], gv[7]);
+              *reinterpret_cast<uint4*>(row + 8 * q4) = o;
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&item_empty[slot]);
+      g += inf.nq;
     }
     if (lane == 0) bulk_wait_all();
   }
@@ -1097,19 +1252,21 @@ extern "C" int gptb200_attention_bwd(const void* q, const void* k, const void* v
   cudaGetDevice(&dev);
   const int seg = segment_ids != nullptr;
   auto kern = seg ? attn_bwd_tc<true> : attn_bwd_tc<false>;
+  const int smem = seg ? BwdSmem<true>::TOTAL : BwdSmem<false>::TOTAL;
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (dev >= 64 || !cfg[dev][seg]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         BwdSmem::TOTAL);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return -static_cast<int>(e);
     if (dev < 64) cfg[dev][seg] = true;
   }
-  dim3 grid((unsigned)((seq + BT - 1) / BT), (unsigned)(batch * heads));
+  // persistent: one CTA per SM (or per item, when there are fewer items)
+  const int64_t items = (seq + BT - 1) / BT * batch * heads;
+  const unsigned grid = (unsigned)std::min<int64_t>(items, sms);
   CUtensorMap mdq;
   if (!make_dq_map(&mdq, dq_acc, B * H, T)) return GPTB200_ESHAPE;
-  kern<<<grid, kBwdThreads, BwdSmem::TOTAL, st>>>(mq, mk, mv, mdo, mdq, p);
+  kern<<<grid, kBwdThreads, smem, st>>>(mq, mk, mv, mdo, mdq, p);
   GPTB200_CHECK_LAUNCH();
-  int sms = 148;
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int64_t chunks = rows * (HD / 8);
   int blocks = (int)std::min<int64_t>((chunks + 255) / 256, (int64_t)sms * 8);
   attn_dq_store_kernel<<<blocks, 256, 0, st>>>(dq_acc, reinterpret_cast<bf16*>(dq), stride_b,

@@ -108,6 +108,20 @@ GPTB200_DEV void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, i
       : "memory");
 }
 
+// 4-byte asynchronous copy global -> shared; src_bytes 0 writes a zero instead
+// of reading (used for positions past the end of a row).
+GPTB200_DEV void cp_async_4(void* dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(dst)), "l"(src),
+               "r"(src_bytes)
+               : "memory");
+}
+// Arrive on an mbarrier once this thread's earlier cp.async copies have
+// landed (the arrival counts toward the barrier's expected count).
+GPTB200_DEV void cp_async_mbar_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
 // TMA tile store from shared memory (bulk-group completion).
 GPTB200_DEV void tma_store_2d(const CUtensorMap* map, const void* src, int c0, int c1) {
   asm volatile(
