@@ -488,7 +488,8 @@ struct BwdItem {
 
 template <bool SEG>
 struct BwdSmem {
-  static constexpr int kQStages = SEG ? 2 : 3;          // Q / dO tile ring
+  static constexpr int kQStages = SEG ? 2 : 4;          // Q / dO tile ring
+  static constexpr int kStatBytes = SEG ? 768 : 512;    // per stage: lse, delta (, segment ids)
   static constexpr int KV = 0;                          // 2 slots x (K, V)
   static constexpr int Q = KV + 4 * BT_BYTES;           // kQStages tiles
   static constexpr int DO = Q + kQStages * BQ_BYTES;    // kQStages tiles
@@ -497,13 +498,14 @@ struct BwdSmem {
   // per Q/dO stage, the tile's query statistics copied in by the producer
   // warp: 64 x lse, 64 x delta, 64 segment ids (zeros past the sequence end)
   static constexpr int STAT = DQS + 8 * 4096;
-  static constexpr int ITEM = STAT + kQStages * 768;    // 2 BwdItem slots
+  static constexpr int ITEM = STAT + kQStages * kStatBytes;  // 2 BwdItem slots
   // segment ids only: per slot, (min, max) id per 64-position chunk from k0
   // and the list of query tiles that can see the key tile
-  static constexpr int SEGTAB = ITEM + 64;
+  static constexpr int SEGTAB = ITEM + 32;
   static constexpr int QLIST = SEGTAB + (SEG ? 2 * kMaxSegChunks * 8 : 0);
   static constexpr int BAR = QLIST + (SEG ? 2 * kMaxSegChunks * 4 : 0);
-  static constexpr int TOTAL = BAR + 512 + 1023;
+  // the dynamic shared memory base is 1024-byte aligned (checked at entry)
+  static constexpr int TOTAL = BAR + 272;
 };
 
 template <bool SEG>
@@ -513,24 +515,27 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                 const __grid_constant__ CUtensorMap tmDQ, const AttnParams p) {
   using L = BwdSmem<SEG>;
   constexpr int kQS = L::kQStages;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                           ~static_cast<uintptr_t>(1023));
+  extern __shared__ __align__(1024) uint8_t smem_bwd[];
+  uint8_t* sm = smem_bwd;
+  if (smem_u32(sm) & 1023) {  // the layout needs 1024-byte aligned tiles: give up, flagged
+    if (threadIdx.x == 0) atomicCAS(&g_attn_error, 0, kErrSmemAlign);
+    return;
+  }
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::BAR);
   uint64_t* kv_full = bars + 0;       // [2] K/V slot loaded
   uint64_t* kv_empty = bars + 2;      // [2] every MMA of the slot's item has completed
-  uint64_t* q_full = bars + 4;        // [3]
-  uint64_t* q_empty = bars + 7;       // [3]
-  uint64_t* s_full = bars + 10;       // [3]: S^T and dP^T of a tile are in TMEM buffer b
-  uint64_t* p_full = bars + 13;       // [3]: P^T, dS^T of a tile written (TMEM buffer b, smem ring)
-  uint64_t* done = bars + 16;         // [4]: every MMA issued up to the end of tile g has completed
-  uint64_t* dq_full = bars + 20;      // [2]: dQ of query pair J is in TMEM
-  uint64_t* dq_free = bars + 22;      // [2]: ... and has been read out
-  uint64_t* fin = bars + 24;          // an item's dK / dV are complete in TMEM
-  uint64_t* acc_free = bars + 25;     // ... and have been read out
-  uint64_t* item_full = bars + 26;    // [2]
-  uint64_t* item_empty = bars + 28;   // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 30);
+  uint64_t* q_full = bars + 4;        // [4]
+  uint64_t* q_empty = bars + 8;       // [4]
+  uint64_t* s_full = bars + 12;       // [3]: S^T and dP^T of a tile are in TMEM buffer b
+  uint64_t* p_full = bars + 15;       // [3]: P^T, dS^T of a tile written (TMEM buffer b, smem ring)
+  uint64_t* done = bars + 18;         // [4]: every MMA issued up to the end of tile g has completed
+  uint64_t* dq_full = bars + 22;      // [2]: dQ of query pair J is in TMEM
+  uint64_t* dq_free = bars + 24;      // [2]: ... and has been read out
+  uint64_t* fin = bars + 26;          // an item's dK / dV are complete in TMEM
+  uint64_t* acc_free = bars + 27;     // ... and have been read out
+  uint64_t* item_full = bars + 28;    // [2]
+  uint64_t* item_empty = bars + 30;   // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 32);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   BwdItem* items = reinterpret_cast<BwdItem*>(sm + L::ITEM);
 
@@ -665,7 +670,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         if (!(ok = __shfl_sync(0xffffffffu, (int)ok, 0) != 0)) break;
         // the tile's statistics, copied asynchronously (each lane arrives on
         // the stage's barrier once its copies have landed)
-        float* st = reinterpret_cast<float*>(sm + L::STAT + s * 768);
+        float* st = reinterpret_cast<float*>(sm + L::STAT + s * L::kStatBytes);
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
           const int cidx = lane + 32 * u, t = qq + cidx;
@@ -809,7 +814,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const int qt = qtile(slot, it);  // query tile index (64 positions) past k0
         // this warp's 16 columns of the stage's statistics; the scores of the
         // tile exist only after its Q/dO stage (statistics included) was full
-        const float* stat = reinterpret_cast<const float*>(sm + L::STAT + (gt % kQS) * 768) + cg * 16;
+        const float* stat =
+            reinterpret_cast<const float*>(sm + L::STAT + (gt % kQS) * L::kStatBytes) + cg * 16;
         const int* stat_seg = reinterpret_cast<const int*>(stat) + 128;
         if (!(ok = mbar_wait(&s_full[bb], (gt / 3) & 1, abort_flag, err))) break;
         if (!(ok = mbar_wait(&q_full[gt % kQS], (gt / kQS) & 1, abort_flag, err))) break;
@@ -951,44 +957,64 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       if (!ok) break;
       // dK (times the softmax scale, rotated back by RoPE) and dV of the
-      // item's 128 keys, this warp's 32 rows, in four 32-column chunks; the
-      // next item's gradient MMAs may overwrite the accumulators once the
-      // last chunk has left TMEM.
+      // item's 128 keys, this warp's 32 rows. All four 32-column chunks leave
+      // TMEM first (dK parked in this warp's staging area, dV in registers) so
+      // the next item's gradient MMAs can start; then the rows are written.
       if (!(ok = mbar_wait(fin, ii & 1, abort_flag, err))) break;
       tc_fence_after();
       {
         const int key = k0 + quad * 32 + lane;
         const int bi = inf.bh / p.H, hi = inf.bh - bi * p.H;
-#pragma unroll 1
-        for (int ci = 0; ci < 4; ++ci) {
-          const bool is_k = ci < 2;
-          const int c0 = (ci & 1) * 32;
-          float gv32[32];
-          tmem_ld32((is_k ? tDK : tDV) + lane_off + c0, gv32);
-          if (ci == 3) {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(acc_free);
+        if (lane == 0) bulk_wait_read();  // the last dQ reduce has read the staging area
+        __syncwarp();
+        float* park = reinterpret_cast<float*>(stage);  // [32 rows][64] fp32, 16-byte chunks xor-swizzled
+        auto park_at = [&](int chunk) { return park + lane * 64 + ((chunk ^ (lane & 15)) << 2); };
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          float t32[32];
+          tmem_ld32(tDK + lane_off + hh * 32, t32);
+#pragma unroll
+          for (int c4 = 0; c4 < 8; ++c4)
+            *reinterpret_cast<float4*>(park_at(hh * 8 + c4)) =
+                make_float4(t32[4 * c4], t32[4 * c4 + 1], t32[4 * c4 + 2], t32[4 * c4 + 3]);
+        }
+        float dvv[64];
+        tmem_ld32_nw(tDV + lane_off, reinterpret_cast<uint32_t*>(dvv));
+        tmem_ld32_nw(tDV + lane_off + 32, reinterpret_cast<uint32_t*>(dvv) + 32);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(acc_free);
+        if (key < p.T) {
+          bf16* vrow = p.dv + bi * p.sb + hi * p.sh + (int64_t)key * p.st;
+          bf16* krow = p.dk + bi * p.sb + hi * p.sh + (int64_t)key * p.st;
+#pragma unroll
+          for (int q8 = 0; q8 < 8; ++q8) {
+            const float* gv = dvv + 8 * q8;
+            uint4 o;
+            o.x = pack_bf16x2(gv[0], gv[1]);
+            o.y = pack_bf16x2(gv[2], gv[3]);
+            o.z = pack_bf16x2(gv[4], gv[5]);
+            o.w = pack_bf16x2(gv[6], gv[7]);
+            *reinterpret_cast<uint4*>(vrow + 8 * q8) = o;
           }
-          if (key < p.T) {
-            bf16* row = (is_k ? p.dk : p.dv) + bi * p.sb + hi * p.sh + (int64_t)key * p.st + c0;
+#pragma unroll 2
+          for (int q8 = 0; q8 < 8; ++q8) {
+            const float4 a4 = *reinterpret_cast<const float4*>(park_at(2 * q8));
+            const float4 b4 = *reinterpret_cast<const float4*>(park_at(2 * q8 + 1));
+            float gv[8] = {a4.x, a4.y, a4.z, a4.w, b4.x, b4.y, b4.z, b4.w};
 #pragma unroll
-            for (int q4 = 0; q4 < 4; ++q4) {
-              float* gv = gv32 + 8 * q4;
-              if (is_k) {
-#pragma unroll
-                for (int i = 0; i < 8; ++i) gv[i] *= p.scale;
-                if (p.rcos) rope_back(gv, p.rcos, p.rsin, key, c0 / 8 + q4);
-              }
-              uint4 o;
-              o.x = pack_bf16x2(gv[0], gv[1]);
-              o.y = pack_bf16x2(gv[2], gv[3]);
-              o.z = pack_bf16x2(gv[4], gv[5]);
-              o.w = pack_bf16x2(gv[6], gv[7]);
-              *reinterpret_cast<uint4*>(row + 8 * q4) = o;
-            }
+            for (int i = 0; i < 8; ++i) gv[i] *= p.scale;
+            if (p.rcos) rope_back(gv, p.rcos, p.rsin, key, q8);
+            uint4 o;
+            o.x = pack_bf16x2(gv[0], gv[1]);
+            o.y = pack_bf16x2(gv[2], gv[3]);
+            o.z = pack_bf16x2(gv[4], gv[5]);
+            o.w = pack_bf16x2(gv[6], gv[7]);
+            *reinterpret_cast<uint4*>(krow + 8 * q8) = o;
           }
         }
+        __syncwarp();  // the park area is read before the next dQ staging writes
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&item_empty[slot]);

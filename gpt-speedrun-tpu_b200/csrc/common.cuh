@@ -24,6 +24,7 @@ enum {
   kErrTmemAlloc = 2,     // TMEM allocation returned an unexpected address
   kErrTokenRange = 3,    // a token id outside [0, vocab) reached the embedding gather
   kErrNonFinite = 4,     // the loss or the gradient norm is NaN or infinite
+  kErrSmemAlign = 5,     // a kernel found its dynamic shared memory misaligned
 };
 
 // Time limit of one mbarrier wait (nanoseconds of %globaltimer). Far above any
