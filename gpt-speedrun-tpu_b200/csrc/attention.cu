@@ -132,88 +132,95 @@ __device__ __forceinline__ int2 seg_range(const int2* tab, int nch, int c, int n
 }
 
 // ------------------------------------------------------------------ forward
-constexpr int FQ = 128;                 // queries per tile (TMEM lanes); two tiles per CTA
+// Persistent: one CTA per SM walks work items (pair of 128-query tiles pr,
+// batch*head bh), item = (npair-1-pr) * B*H + bh (heaviest pairs first),
+// taking items blockIdx.x, + gridDim.x, ... Every role keeps running
+// counters across items, so the K/V ring and the per-tile S/P/O handshakes
+// flow from one item into the next; Q tiles are double-buffered per item.
+constexpr int FQ = 128;                 // queries per tile (TMEM lanes); two tiles per item
 constexpr int FK = 128;                 // keys per K/V block
 constexpr int Q_BYTES = FQ * 128;       // 128 rows x 64 bf16
 constexpr int KV_BYTES = FK * 128;      // 128 rows x 64 bf16
-constexpr int kKvStages = 5;
+constexpr int kKvStages = 4;
 constexpr int kFwdMma1Warp = 10;       // MMA thread of tile 1 (warp 1 serves tile 0)
 constexpr int kFwdThreads = 32 * 11;
+constexpr int kFwdItemUsers = 2 + 8;   // both MMA threads, the 8 softmax warps
 
+// Item slot written by the TMA warp: pair, batch*head, key blocks the pair
+// visits (tile 0 the first n0 of them), whether tile 1 lies inside the sequence.
+struct FwdItem {
+  int pr, bh, nkv, n0, has1, pad0, pad1, pad2;
+};
+
+template <bool SEG>
 struct FwdSmem {
-  static constexpr int Q = 0;                             // 2 tiles
-  static constexpr int K = Q + 2 * Q_BYTES;               // kKvStages
-  static constexpr int V = K + kKvStages * KV_BYTES;      // kKvStages
-  static constexpr int SEGTAB = V + kKvStages * KV_BYTES; // int2 per 64-position chunk
-  static constexpr int BLOCKS = SEGTAB + kMaxSegChunks * 8;  // key blocks this CTA visits
-  static constexpr int KSEG = BLOCKS + kMaxSegChunks / 2 * 4;  // [tile][2][128] key ids
-  static constexpr int BAR = KSEG + 2 * 2 * FK * 4;
-  static constexpr int TOTAL = BAR + 256 + 1024;
+  static constexpr int Q = 0;                                 // 2 item slots x 2 tiles
+  static constexpr int K = Q + 4 * Q_BYTES;                   // kKvStages
+  static constexpr int V = K + kKvStages * KV_BYTES;          // kKvStages
+  static constexpr int ITEM = V + kKvStages * KV_BYTES;       // 2 FwdItem slots
+  // segment ids only: per slot, (min, max) id per 64-position chunk and the
+  // key blocks the pair visits; per tile, two buffers of a block's key ids
+  static constexpr int SEGTAB = ITEM + 64;
+  static constexpr int BLOCKS = SEGTAB + (SEG ? 2 * kMaxSegChunks * 8 : 0);
+  static constexpr int KSEG = BLOCKS + (SEG ? 2 * (kMaxSegChunks / 2) * 4 : 0);
+  static constexpr int BAR = KSEG + (SEG ? 2 * 2 * FK * 4 : 0);
+  // the dynamic shared memory base is 1024-byte aligned (checked at entry)
+  static constexpr int TOTAL = BAR + 256;
 };
 
 template <bool SEG>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                           ~static_cast<uintptr_t>(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + FwdSmem::BAR);
-  uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;                // [kKvStages]
+  using L = FwdSmem<SEG>;
+  extern __shared__ __align__(1024) uint8_t smem_fwd[];
+  uint8_t* sm = smem_fwd;
+  if (smem_u32(sm) & 1023) {  // the layout needs 1024-byte aligned tiles: give up, flagged
+    if (threadIdx.x == 0) atomicCAS(&g_attn_error, 0, kErrSmemAlign);
+    return;
+  }
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::BAR);
+  uint64_t* q_full = bars + 0;                 // [2 item slots]
+  uint64_t* q_empty = bars + 2;                // [2]
+  uint64_t* kv_full = bars + 4;                // [kKvStages]
   uint64_t* kv_empty = kv_full + kKvStages;    // [kKvStages]
   uint64_t* s_full = kv_empty + kKvStages;     // [2 tiles]: S of the current block is in TMEM
   uint64_t* p_full = s_full + 2;               // [2]: P written to TMEM
   uint64_t* pv_done = p_full + 2;              // [2]: the tile's P.V MMA has completed
   uint64_t* s_free = pv_done + 2;              // [2]: S has been loaded into registers
   uint64_t* kseg_full = s_free + 2;            // [2 tiles][2]: a block's key ids are in smem
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(kseg_full + 4);
+  uint64_t* item_full = kseg_full + 4;         // [2]
+  uint64_t* item_empty = item_full + 2;        // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(item_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  FwdItem* items = reinterpret_cast<FwdItem*>(sm + L::ITEM);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int BH = p.B * p.H;
   const int npair = (p.T + 2 * FQ - 1) / (2 * FQ);
-  const int pr = npair - 1 - (int)blockIdx.x;  // heaviest pairs first
-  const int bh = blockIdx.y;
-  const int b = bh / p.H, h = bh - b * p.H;
-  const int q0 = pr * 2 * FQ;
-  // Tile x's diagonal key block is d0 + x; tile 1 of the last pair may lie
-  // wholly past the sequence end.
-  const int d0 = q0 / FK;
-  const bool has1 = q0 + FQ < p.T;
-  const int dmax = has1 ? d0 + 1 : d0;
-  const int* segrow = SEG ? p.seg + (int64_t)b * p.T : nullptr;  // null: causal only
-  int2* segtab = reinterpret_cast<int2*>(sm + FwdSmem::SEGTAB);
-  int* blist = reinterpret_cast<int*>(sm + FwdSmem::BLOCKS);
-  int* counts = reinterpret_cast<int*>(tmem_slot + 2);  // [0] blocks, [1] of them <= d0
-  const int nch = min((p.T + kSegChunk - 1) / kSegChunk, 2 * (dmax + 1));
-  if (segrow) seg_chunk_ranges(segrow, p.T, 0, nch, segtab);
-  __syncthreads();
+  const int n_items = npair * BH;
   int* err = &g_attn_error;
+  auto segtab_of = [&](int slot) {
+    return reinterpret_cast<int2*>(sm + L::SEGTAB) + slot * kMaxSegChunks;
+  };
+  // key block of list entry j of the item in `slot`
+  auto kblock = [&](int slot, int j) -> int {
+    if constexpr (SEG)
+      return reinterpret_cast<const int*>(sm + L::BLOCKS)[slot * (kMaxSegChunks / 2) + j];
+    else
+      return j;
+  };
 
   if (threadIdx.x == 0) {
-    // The key blocks 0..dmax either query tile can see, in order. Both tiles
-    // walk this one list (tile 0 its prefix up to d0); a block only the other
-    // tile needs is fully masked for a tile, at most costing its exps.
-    const int2 qr0 = segrow ? seg_range(segtab, nch, 2 * d0, 2) : make_int2(0, 0);
-    const int2 qr1 = segrow ? seg_range(segtab, nch, 2 * d0 + 2, 2) : make_int2(0, 0);
-    int n = 0, n_le0 = 0;
-    for (int j = 0; j <= dmax; ++j) {
-      bool need = true;
-      if (segrow) {
-        const int2 kr = seg_range(segtab, nch, 2 * j, 2);
-        need = (j <= d0 && rng_meet(kr, qr0)) || (has1 && rng_meet(kr, qr1));
-      }
-      if (need) {
-        blist[n++] = j;
-        if (j <= d0) ++n_le0;
-      }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&q_full[s], 1);
+      mbar_init(&q_empty[s], 2);  // released by each tile's MMA thread
+      mbar_init(&item_full[s], 1);
+      mbar_init(&item_empty[s], kFwdItemUsers);
     }
-    counts[0] = n;
-    counts[1] = n_le0;
-    mbar_init(q_full, 1);
     for (int s = 0; s < kKvStages; ++s) {
       mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], has1 ? 2 : 1);  // released by each tile's MMA thread
+      mbar_init(&kv_empty[s], 2);  // released by each tile's MMA thread
     }
     for (int x = 0; x < 2; ++x) {
       mbar_init(&s_full[x], 1);
@@ -230,9 +237,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const int nkv = counts[0];
-  const int n0 = counts[1];
-  const int n1 = has1 ? nkv : 0;
   // TMEM columns: S[2] (128 fp32 each) | O[2] (64 fp32) | P[2] (128 keys as bf16 pairs)
   const uint32_t tmem = *tmem_slot;
   auto tS = [&](int x) { return tmem + 128 * x; };
@@ -240,61 +244,159 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   auto tP = [&](int x) { return tmem + 384 + 64 * x; };
 
   if (warp == 0) {
-    if (lane == 0) {
-      mbar_arrive_expect_tx(q_full, 2 * Q_BYTES);
-      tma_load_4d(sm + FwdSmem::Q, &tmQ, q_full, 0, q0, h, b);
-      tma_load_4d(sm + FwdSmem::Q + Q_BYTES, &tmQ, q_full, 0, q0 + FQ, h, b);
-      for (int j = 0; j < nkv; ++j) {
-        const int s = j % kKvStages;
-        if (!mbar_wait(&kv_empty[s], ((j / kKvStages) & 1) ^ 1, abort_flag, err)) break;
-        mbar_arrive_expect_tx(&kv_full[s], 2 * KV_BYTES);
-        const int key0 = blist[j] * FK;
-        tma_load_4d(sm + FwdSmem::K + s * KV_BYTES, &tmK, &kv_full[s], 0, key0, h, b);
-        tma_load_4d(sm + FwdSmem::V + s * KV_BYTES, &tmV, &kv_full[s], 0, key0, h, b);
+    // Item producer: publishes each item's slot (with segment ids also the
+    // chunk ranges and the key-block list), then loads its two Q tiles and its
+    // K/V blocks into the ring.
+    bool ok = true;
+    int gk = 0, ii = 0;
+    for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x, ++ii) {
+      const int slot = ii & 1;
+      if (!(ok = mbar_wait(&item_empty[slot], ((ii >> 1) & 1) ^ 1, abort_flag, err))) break;
+      const int pr = npair - 1 - item / BH, bh = item % BH;
+      const int b = bh / p.H, h = bh - b * p.H;
+      const int q0 = pr * 2 * FQ;
+      // tile x's diagonal key block is d0 + x; tile 1 of the last pair may lie
+      // wholly past the sequence end
+      const int d0 = q0 / FK;
+      const int has1 = q0 + FQ < p.T;
+      const int dmax = has1 ? d0 + 1 : d0;
+      int nkv = dmax + 1, n0 = d0 + 1;
+      if constexpr (SEG) {
+        // The key blocks 0..dmax either query tile can see, in order. Both
+        // tiles walk this one list (tile 0 its prefix up to d0); a block only
+        // the other tile needs is fully masked for a tile, at most costing its
+        // exps.
+        const int* segrow = p.seg + (int64_t)b * p.T;
+        int2* tab = segtab_of(slot);
+        const int nch = min((p.T + kSegChunk - 1) / kSegChunk, 2 * (dmax + 1));
+        for (int c = 0; c < nch; ++c) {
+          int mn = INT_MAX, mx = INT_MIN;
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int t = c * kSegChunk + u * 32 + lane;
+            if (t < p.T) {
+              const int v = segrow[t];
+              mn = min(mn, v);
+              mx = max(mx, v);
+            }
+          }
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) {
+            mn = min(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+            mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+          }
+          if (lane == 0) tab[c] = make_int2(mn, mx);
+        }
+        __syncwarp();
+        if (lane == 0) {
+          int* bl = reinterpret_cast<int*>(sm + L::BLOCKS) + slot * (kMaxSegChunks / 2);
+          const int2 qr0 = seg_range(tab, nch, 2 * d0, 2);
+          const int2 qr1 = seg_range(tab, nch, 2 * d0 + 2, 2);
+          int n = 0, n_le0 = 0;
+          for (int j = 0; j <= dmax; ++j) {
+            const int2 kr = seg_range(tab, nch, 2 * j, 2);
+            if ((j <= d0 && rng_meet(kr, qr0)) || (has1 && rng_meet(kr, qr1))) {
+              bl[n++] = j;
+              if (j <= d0) ++n_le0;
+            }
+          }
+          nkv = n;
+          n0 = n_le0;
+        }
+        nkv = __shfl_sync(0xffffffffu, nkv, 0);
+        n0 = __shfl_sync(0xffffffffu, n0, 0);
       }
+      if (lane == 0) {
+        items[slot] = FwdItem{pr, bh, nkv, n0, has1, 0, 0, 0};
+        mbar_arrive(&item_full[slot]);
+        if ((ok = mbar_wait(&q_empty[slot], ((ii >> 1) & 1) ^ 1, abort_flag, err))) {
+          uint8_t* qd = sm + L::Q + slot * 2 * Q_BYTES;
+          mbar_arrive_expect_tx(&q_full[slot], 2 * Q_BYTES);
+          tma_load_4d(qd, &tmQ, &q_full[slot], 0, q0, h, b);
+          tma_load_4d(qd + Q_BYTES, &tmQ, &q_full[slot], 0, q0 + FQ, h, b);
+        }
+        for (int j = 0; ok && j < nkv; ++j, ++gk) {
+          const int s = gk % kKvStages;
+          if (!(ok = mbar_wait(&kv_empty[s], ((gk / kKvStages) & 1) ^ 1, abort_flag, err))) break;
+          mbar_arrive_expect_tx(&kv_full[s], 2 * KV_BYTES);
+          const int key0 = kblock(slot, j) * FK;
+          tma_load_4d(sm + L::K + s * KV_BYTES, &tmK, &kv_full[s], 0, key0, h, b);
+          tma_load_4d(sm + L::V + s * KV_BYTES, &tmV, &kv_full[s], 0, key0, h, b);
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, (int)ok, 0) != 0;
     }
   } else if (warp == 1 || warp == kFwdMma1Warp) {
     // One MMA thread per tile: S_x = Q_x K_j^T (128 x 128 fp32) for the next
     // block as soon as the softmax holds S_x in registers, O_x += P_x V_j
-    // once P_x is in TMEM. The two tiles progress independently.
+    // once P_x is in TMEM. The two tiles progress independently; each walks
+    // every block of the item's list and releases the ones it does not use.
     const int x = warp == 1 ? 0 : 1;
-    const int nb = x == 0 ? n0 : n1;
-    if (lane == 0 && nb > 0) {
+    if (lane == 0) {
       constexpr uint32_t idS = umma_idesc_bf16(128, FK, 0, 0);
       constexpr uint32_t idO = umma_idesc_bf16(128, HD, 0, 1);  // A = P in TMEM, B = V MN-major
-      const uint32_t sQ = smem_u32(sm + FwdSmem::Q + x * Q_BYTES);
-      auto issue_s = [&](int j) {
-        const uint32_t sK = smem_u32(sm + FwdSmem::K + (j % kKvStages) * KV_BYTES);
+      bool ok = true;
+      int gk = 0, jx = 0, ii = 0;  // ring block, this tile's running block, item
+      for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x, ++ii) {
+        const int slot = ii & 1;
+        if (!(ok = mbar_wait(&item_full[slot], (ii >> 1) & 1, abort_flag, err))) break;
+        const FwdItem inf = items[slot];
+        const int nb = x == 0 ? inf.n0 : (inf.has1 ? inf.nkv : 0);
+        const uint32_t sQ = smem_u32(sm + L::Q + (slot * 2 + x) * Q_BYTES);
+        auto issue_s = [&](int s) {
+          const uint32_t sK = smem_u32(sm + L::K + s * KV_BYTES);
 #pragma unroll
-        for (int k = 0; k < HD / 16; ++k)
-          umma_bf16(tS(x), umma_smem_desc(sQ + k * 32, 16, 1024),
-                    umma_smem_desc(sK + k * 32, 16, 1024), idS, k > 0);
-        umma_commit(&s_full[x]);
-      };
-      bool ok = mbar_wait(q_full, 0, abort_flag, err) && mbar_wait(&kv_full[0], 0, abort_flag, err);
-      if (ok) {
-        tc_fence_after();
-        issue_s(0);
-      }
-      for (int j = 0; ok && j < nb; ++j) {
-        if (j + 1 < nb) {
-          if (!mbar_wait(&kv_full[(j + 1) % kKvStages], ((j + 1) / kKvStages) & 1, abort_flag,
-                         err) ||
-              !mbar_wait(&s_free[x], j & 1, abort_flag, err))
-            break;
+          for (int k = 0; k < HD / 16; ++k)
+            umma_bf16(tS(x), umma_smem_desc(sQ + k * 32, 16, 1024),
+                      umma_smem_desc(sK + k * 32, 16, 1024), idS, k > 0);
+          umma_commit(&s_full[x]);
+        };
+        if (nb > 0) {
+          // S of the item's first block: Q loaded, the block loaded, and the
+          // previous item's last S taken out of TMEM by the softmax
+          ok = mbar_wait(&q_full[slot], (ii >> 1) & 1, abort_flag, err) &&
+               mbar_wait(&kv_full[gk % kKvStages], (gk / kKvStages) & 1, abort_flag, err) &&
+               (jx == 0 || mbar_wait(&s_free[x], (jx - 1) & 1, abort_flag, err));
+          if (!ok) break;
           tc_fence_after();
-          issue_s(j + 1);
+          issue_s(gk % kKvStages);
         }
-        if (!mbar_wait(&p_full[x], j & 1, abort_flag, err)) break;
-        tc_fence_after();
-        const uint32_t sV = smem_u32(sm + FwdSmem::V + (j % kKvStages) * KV_BYTES);
-        // O_x += P_x V_j, P read from TMEM (keys 16k..16k+15 at column 8k)
+        for (int j = 0; ok && j < inf.nkv; ++j) {
+          const int s = (gk + j) % kKvStages;
+          if (j >= nb) {  // a block this tile skips: release it once it has arrived
+            if (!(ok = mbar_wait(&kv_full[s], ((gk + j) / kKvStages) & 1, abort_flag, err))) break;
+            mbar_arrive(&kv_empty[s]);
+            continue;
+          }
+          const int jj = jx + j;  // running block index of this tile
+          if (j + 1 < nb) {
+            const int s1 = (gk + j + 1) % kKvStages;
+            if (!(ok = mbar_wait(&kv_full[s1], ((gk + j + 1) / kKvStages) & 1, abort_flag, err)) ||
+                !(ok = mbar_wait(&s_free[x], jj & 1, abort_flag, err)))
+              break;
+            tc_fence_after();
+            issue_s(s1);
+          }
+          if (!(ok = mbar_wait(&p_full[x], jj & 1, abort_flag, err))) break;
+          tc_fence_after();
+          const uint32_t sV = smem_u32(sm + L::V + s * KV_BYTES);
+          // O_x += P_x V_j, P read from TMEM (keys 16k..16k+15 at column 8k)
 #pragma unroll
-        for (int k = 0; k < FK / 16; ++k)
-          umma_bf16_ts(tO(x), tP(x) + k * 8, umma_smem_desc(sV + k * 2048, KV_BYTES, 1024), idO,
-                       (j > 0 || k > 0));
-        umma_commit(&pv_done[x]);
-        umma_commit(&kv_empty[j % kKvStages]);
+          for (int k = 0; k < FK / 16; ++k)
+            umma_bf16_ts(tO(x), tP(x) + k * 8, umma_smem_desc(sV + k * 2048, KV_BYTES, 1024), idO,
+                         (j > 0 || k > 0));
+          umma_commit(&pv_done[x]);
+          umma_commit(&kv_empty[s]);
+        }
+        if (!ok) break;
+        // the item's Q tile is free once its last S MMA has completed
+        if (nb > 0)
+          umma_commit(&q_empty[slot]);
+        else
+          mbar_arrive(&q_empty[slot]);
+        mbar_arrive(&item_empty[slot]);
+        gk += inf.nkv;
+        jx += nb;
       }
     }
   } else if (warp < kFwdMma1Warp) {
@@ -306,147 +408,159 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const int x = (warp - 2) >> 2;
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
-    const int qrow = q0 + x * FQ + r;
-    const int nb = x == 0 ? n0 : n1;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const float c = p.scale * kLog2e;
-    float m_used = -INFINITY, l = 0.f;
-    // this row's segment id (rows past T take an id no key has)
-    const int sq = segrow ? (qrow < p.T ? segrow[qrow] : INT_MIN) : 0;
-    const int2 qrng = segrow ? seg_range(segtab, nch, 2 * (d0 + x), 2) : make_int2(0, 0);
-    int* kseg = reinterpret_cast<int*>(sm + FwdSmem::KSEG) + x * 2 * FK;
+    int* kseg = reinterpret_cast<int*>(sm + L::KSEG) + x * 2 * FK;
     int nseg = 0;  // blocks of this tile that needed the per-element test so far
     bool ok = true;
-    for (int j = 0; j < nb && ok; ++j) {
-      if (!mbar_wait(&s_full[x], j & 1, abort_flag, err)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const int jb = blist[j];
-      const bool diag = (jb == d0 + x);  // keys past the query (and past T) are masked
-      // Per-element segment test unless keys and queries all share one id;
-      // the block's key ids then come through shared memory (double-buffered,
-      // one mbarrier handshake across the warpgroup).
-      const bool segmask = segrow && !rng_single(seg_range(segtab, nch, 2 * jb, 2), qrng);
-      const int* ks = kseg + (nseg & 1) * FK;
-      if (segmask) {
-        const int key = jb * FK + r;
-        kseg[(nseg & 1) * FK + r] = key < p.T ? segrow[key] : INT_MAX;
-        mbar_arrive(&kseg_full[2 * x + (nseg & 1)]);
-        if (!mbar_wait(&kseg_full[2 * x + (nseg & 1)], (nseg >> 1) & 1, abort_flag, err)) {
-          ok = false;
-          break;
-        }
-        ++nseg;
-      }
-      // The whole 128-column S row in one batch of TMEM loads, then S_x is
-      // handed back so the next block's scores overlap this block's exps.
-      uint32_t v[FK];
-#pragma unroll
-      for (int cc = 0; cc < FK / 32; ++cc) tmem_ld32_nw(tS(x) + lane_off + cc * 32, v + 32 * cc);
-      tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_free[x]);
-      // Row max of the raw scores (c > 0 commutes with the max), eight
-      // independent chains; on the diagonal block keys past the query are out.
-      float m8[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) m8[u] = -INFINITY;
-      auto visible = [&](int i) { return (!diag || i <= r) && (!segmask || ks[i] == sq); };
-      if (diag || segmask) {
-#pragma unroll
-        for (int i = 0; i < FK; i += 2)
-          m8[(i >> 1) & 7] = fmax3(m8[(i >> 1) & 7], visible(i) ? __uint_as_float(v[i]) : -INFINITY,
-                                   visible(i + 1) ? __uint_as_float(v[i + 1]) : -INFINITY);
-      } else {
-#pragma unroll
-        for (int i = 0; i < FK; i += 2)
-          m8[(i >> 1) & 7] =
-              fmax3(m8[(i >> 1) & 7], __uint_as_float(v[i]), __uint_as_float(v[i + 1]));
-      }
-      const float mx =
-          fmaxf(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], fmaxf(m8[5], fmaxf(m8[6], m8[7])))) * c;
-      // The rescale decision is made per warp: the TMEM loads/stores of O are
-      // warp-collective and must not run in a divergent branch. Rows whose
-      // max did not move rescale by exactly 1.
-      const bool rescale = __any_sync(0xffffffffu, mx > m_used + 8.0f);
-      float alpha = 1.f;
-      if (rescale) {
-        // 0 on a row's first visible block (m_used = -inf); a row with no
-        // visible key yet (document masking) keeps its -inf max and alpha 1
-        const float m_new = fmaxf(m_used, mx);
-        alpha = m_new == -INFINITY ? 1.f : ex2(m_used - m_new);
-        m_used = m_new;
-      }
-      // P = exp2(s*c - m) packed to bf16 pairs in registers (the S registers
-      // die as P is produced); four packed partial row sums.
-      const float2 c2 = make_float2(c, c), nm2 = make_float2(-m_used, -m_used);
-      float2 acc[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) acc[u] = make_float2(0.f, 0.f);
-      uint32_t pk[FK / 2];
-#pragma unroll
-      for (int i = 0; i < FK; i += 2) {
-        const float2 t = ffma2(make_float2(__uint_as_float(v[i]), __uint_as_float(v[i + 1])), c2, nm2);
-        float p0 = ex2(t.x), p1 = ex2(t.y);
-        if (diag || segmask) {
-          if (!visible(i)) p0 = 0.f;
-          if (!visible(i + 1)) p1 = 0.f;
-        }
-        acc[(i >> 1) & 3] = fadd2(acc[(i >> 1) & 3], make_float2(p0, p1));
-        pk[i / 2] = pack_bf16x2(p0, p1);
-      }
-      const float2 s01 = fadd2(fadd2(acc[0], acc[1]), fadd2(acc[2], acc[3]));
-      const float sum = s01.x + s01.y;
-      // P and O of the previous block must have been consumed by its P.V MMA.
-      if (j > 0) {
-        if (!mbar_wait(&pv_done[x], (j - 1) & 1, abort_flag, err)) {
-          ok = false;
-          break;
-        }
+    int jx = 0, ii = 0;
+    for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x, ++ii) {
+      const int slot = ii & 1;
+      if (!(ok = mbar_wait(&item_full[slot], (ii >> 1) & 1, abort_flag, err))) break;
+      const FwdItem inf = items[slot];
+      const int nb = x == 0 ? inf.n0 : (inf.has1 ? inf.nkv : 0);
+      const int bh = inf.bh, b = bh / p.H, h = bh - b * p.H;
+      const int q0 = inf.pr * 2 * FQ;
+      const int d0 = q0 / FK;
+      const int qrow = q0 + x * FQ + r;
+      const int* segrow = SEG ? p.seg + (int64_t)b * p.T : nullptr;
+      const int2* segtab = SEG ? segtab_of(slot) : nullptr;
+      const int nch = min((p.T + kSegChunk - 1) / kSegChunk, 2 * (d0 + inf.has1 + 1));
+      // this row's segment id (rows past T take an id no key has)
+      const int sq = segrow ? (qrow < p.T ? segrow[qrow] : INT_MIN) : 0;
+      const int2 qrng = segrow ? seg_range(segtab, nch, 2 * (d0 + x), 2) : make_int2(0, 0);
+      float m_used = -INFINITY, l = 0.f;
+      for (int j = 0; j < nb && ok; ++j) {
+        const int jj = jx + j;
+        if (!(ok = mbar_wait(&s_full[x], jj & 1, abort_flag, err))) break;
         tc_fence_after();
-      }
+        const int jb = kblock(slot, j);
+        const bool diag = (jb == d0 + x);  // keys past the query (and past T) are masked
+        // Per-element segment test unless keys and queries all share one id;
+        // the block's key ids then come through shared memory (double-buffered,
+        // one mbarrier handshake across the warpgroup).
+        const bool segmask = segrow && !rng_single(seg_range(segtab, nch, 2 * jb, 2), qrng);
+        const int* ks = kseg + (nseg & 1) * FK;
+        if (segmask) {
+          const int key = jb * FK + r;
+          kseg[(nseg & 1) * FK + r] = key < p.T ? segrow[key] : INT_MAX;
+          mbar_arrive(&kseg_full[2 * x + (nseg & 1)]);
+          if (!(ok = mbar_wait(&kseg_full[2 * x + (nseg & 1)], (nseg >> 1) & 1, abort_flag, err)))
+            break;
+          ++nseg;
+        }
+        // The whole 128-column S row in one batch of TMEM loads, then S_x is
+        // handed back so the next block's scores overlap this block's exps.
+        uint32_t v[FK];
 #pragma unroll
-      for (int g = 0; g < FK / 16; ++g) tmem_st8_nw(tP(x) + lane_off + g * 8, pk + 8 * g);
-      l = l * alpha + sum;
-      if (rescale && j > 0) {
+        for (int cc = 0; cc < FK / 32; ++cc) tmem_ld32_nw(tS(x) + lane_off + cc * 32, v + 32 * cc);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_free[x]);
+        // Row max of the raw scores (c > 0 commutes with the max), eight
+        // independent chains; on the diagonal block keys past the query are out.
+        float m8[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) m8[u] = -INFINITY;
+        auto visible = [&](int i) { return (!diag || i <= r) && (!segmask || ks[i] == sq); };
+        if (diag || segmask) {
+#pragma unroll
+          for (int i = 0; i < FK; i += 2)
+            m8[(i >> 1) & 7] = fmax3(m8[(i >> 1) & 7], visible(i) ? __uint_as_float(v[i]) : -INFINITY,
+                                     visible(i + 1) ? __uint_as_float(v[i + 1]) : -INFINITY);
+        } else {
+#pragma unroll
+          for (int i = 0; i < FK; i += 2)
+            m8[(i >> 1) & 7] =
+                fmax3(m8[(i >> 1) & 7], __uint_as_float(v[i]), __uint_as_float(v[i + 1]));
+        }
+        const float mx =
+            fmaxf(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], fmaxf(m8[5], fmaxf(m8[6], m8[7])))) * c;
+        // The rescale decision is made per warp: the TMEM loads/stores of O are
+        // warp-collective and must not run in a divergent branch. Rows whose
+        // max did not move rescale by exactly 1.
+        const bool rescale = __any_sync(0xffffffffu, mx > m_used + 8.0f);
+        float alpha = 1.f;
+        if (rescale) {
+          // 0 on a row's first visible block (m_used = -inf); a row with no
+          // visible key yet (document masking) keeps its -inf max and alpha 1
+          const float m_new = fmaxf(m_used, mx);
+          alpha = m_new == -INFINITY ? 1.f : ex2(m_used - m_new);
+          m_used = m_new;
+        }
+        // P = exp2(s*c - m) packed to bf16 pairs in registers (the S registers
+        // die as P is produced); four packed partial row sums.
+        const float2 c2 = make_float2(c, c), nm2 = make_float2(-m_used, -m_used);
+        float2 acc[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) acc[u] = make_float2(0.f, 0.f);
+        uint32_t pk[FK / 2];
+#pragma unroll
+        for (int i = 0; i < FK; i += 2) {
+          const float2 t = ffma2(make_float2(__uint_as_float(v[i]), __uint_as_float(v[i + 1])), c2, nm2);
+          float p0 = ex2(t.x), p1 = ex2(t.y);
+          if (diag || segmask) {
+            if (!visible(i)) p0 = 0.f;
+            if (!visible(i + 1)) p1 = 0.f;
+          }
+          acc[(i >> 1) & 3] = fadd2(acc[(i >> 1) & 3], make_float2(p0, p1));
+          pk[i / 2] = pack_bf16x2(p0, p1);
+        }
+        const float2 s01 = fadd2(fadd2(acc[0], acc[1]), fadd2(acc[2], acc[3]));
+        const float sum = s01.x + s01.y;
+        // P and O of the previous block must have been consumed by its P.V
+        // MMA (the previous item's last block was waited for at its end).
+        if (j > 0) {
+          if (!(ok = mbar_wait(&pv_done[x], (jj - 1) & 1, abort_flag, err))) break;
+          tc_fence_after();
+        }
+#pragma unroll
+        for (int g = 0; g < FK / 16; ++g) tmem_st8_nw(tP(x) + lane_off + g * 8, pk + 8 * g);
+        l = l * alpha + sum;
+        if (rescale && j > 0) {
+          float o[32];
+#pragma unroll
+          for (int cc = 0; cc < HD / 32; ++cc) {
+            tmem_ld32(tO(x) + lane_off + cc * 32, o);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] *= alpha;
+            tmem_st32(tO(x) + lane_off + cc * 32, o);
+          }
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[x]);
+      }
+      if (ok && nb > 0) {
+        if (!(ok = mbar_wait(&pv_done[x], (jx + nb - 1) & 1, abort_flag, err))) break;
+        tc_fence_after();
+        const float inv = 1.f / l;
         float o[32];
+        bf16* orow = p.o + b * p.osb + h * p.osh + (int64_t)qrow * p.ost;
 #pragma unroll
         for (int cc = 0; cc < HD / 32; ++cc) {
           tmem_ld32(tO(x) + lane_off + cc * 32, o);
+          if (qrow < p.T) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] *= alpha;
-          tmem_st32(tO(x) + lane_off + cc * 32, o);
-        }
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[x]);
-    }
-    if (ok && nb > 0 && mbar_wait(&pv_done[x], (nb - 1) & 1, abort_flag, err)) {
-      tc_fence_after();
-      const float inv = 1.f / l;
-      float o[32];
-      bf16* orow = p.o + b * p.osb + h * p.osh + (int64_t)qrow * p.ost;
-#pragma unroll
-      for (int cc = 0; cc < HD / 32; ++cc) {
-        tmem_ld32(tO(x) + lane_off + cc * 32, o);
-        if (qrow < p.T) {
-#pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            uint4 q;
-            q.x = pack_bf16x2(o[8 * g] * inv, o[8 * g + 1] * inv);
-            q.y = pack_bf16x2(o[8 * g + 2] * inv, o[8 * g + 3] * inv);
-            q.z = pack_bf16x2(o[8 * g + 4] * inv, o[8 * g + 5] * inv);
-            q.w = pack_bf16x2(o[8 * g + 6] * inv, o[8 * g + 7] * inv);
-            *reinterpret_cast<uint4*>(orow + cc * 32 + 8 * g) = q;
+            for (int g = 0; g < 4; ++g) {
+              uint4 q;
+              q.x = pack_bf16x2(o[8 * g] * inv, o[8 * g + 1] * inv);
+              q.y = pack_bf16x2(o[8 * g + 2] * inv, o[8 * g + 3] * inv);
+              q.z = pack_bf16x2(o[8 * g + 4] * inv, o[8 * g + 5] * inv);
+              q.w = pack_bf16x2(o[8 * g + 6] * inv, o[8 * g + 7] * inv);
+              *reinterpret_cast<uint4*>(orow + cc * 32 + 8 * g) = q;
+            }
           }
         }
+        if (qrow < p.T) p.lse[(int64_t)bh * p.T + qrow] = (m_used + __log2f(l)) * kLn2;
       }
-      if (qrow < p.T) p.lse[(int64_t)bh * p.T + qrow] = (m_used + __log2f(l)) * kLn2;
+      if (!ok) break;
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&item_empty[slot]);
+      jx += nb;
     }
   }
   tc_fence_before();
@@ -1202,15 +1316,18 @@ extern "C" int gptb200_attention_fwd(const void* q, const void* k, const void* v
   cudaGetDevice(&dev);
   const int seg = segment_ids != nullptr;
   auto kern = seg ? attn_fwd_tc<true> : attn_fwd_tc<false>;
+  const int smem = seg ? FwdSmem<true>::TOTAL : FwdSmem<false>::TOTAL;
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (dev >= 64 || !cfg[dev][seg]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         FwdSmem::TOTAL);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return -static_cast<int>(e);
     if (dev < 64) cfg[dev][seg] = true;
   }
-  dim3 grid((unsigned)((seq + 2 * FQ - 1) / (2 * FQ)), (unsigned)(batch * heads));
-  kern<<<grid, kFwdThreads, FwdSmem::TOTAL, reinterpret_cast<cudaStream_t>(stream)>>>(mq, mk, mv,
-                                                                                      p);
+  // persistent: one CTA per SM (or per item, when there are fewer items)
+  const int64_t items = (seq + 2 * FQ - 1) / (2 * FQ) * batch * heads;
+  const unsigned grid = (unsigned)std::min<int64_t>(items, sms);
+  kern<<<grid, kFwdThreads, smem, reinterpret_cast<cudaStream_t>(stream)>>>(mq, mk, mv, p);
   GPTB200_CHECK_LAUNCH();
   return 0;
 }
