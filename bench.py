@@ -3,7 +3,7 @@
 MFU of the 125M tier, bf16, seq 1024, global batch 128, at 1/2/4/8 GPUs).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-    python bench.py --op attention|lce|gelu_gemm   (op configurations, 1 GPU)
+    python bench.py --op attention|lce|gemm|gelu_gemm   (op configurations, 1 GPU)
 
 One process per GPU (torchrun for N > 1). A "step" is one full training step
 (forward, backward, gradient all-reduce, AdamW) over the rank's share of the
@@ -223,6 +223,8 @@ def run_op(args) -> None:
     * lce: config 2 -- hidden [65536, 768] bf16 ~ N(0, 1), embedding
       [50304, 768] bf16 ~ N(0, 0.02), Zipf(1.1) labels (seed 1); one step = mean
       loss + dH + dE; algorithmic FLOPs 6 N V D = 1.519e13 per step.
+    * gemm: the MLP down projection of the step (M = 131072, K = 3072,
+      N = 768) with the plain bf16 epilogue.
     * gelu_gemm: the MLP up projection of the step (M = 131072, K = 768,
       N = 3072) with the bias + GELU epilogue (writes g and gelu').
     Each timed iteration is bracketed by CUDA events on the launching stream;
@@ -270,6 +272,14 @@ def run_op(args) -> None:
         parts = {"fwd": (fwd, 2.0 * n * vocab * d), "bwd": (bwd, 4.0 * n * vocab * d)}
         config = {"workload": "config 2: tied linear cross-entropy loss + dH + dE", "tokens": n,
                   "vocab": vocab, "d_model": d}
+    elif args.op == "gemm":
+        m, kk, nn = 131072, 3072, 768
+        x = torch.randn(m, kk, generator=gen(0)).bfloat16().to(dev)
+        w = (0.02 * torch.randn(kk, nn, generator=gen(1))).bfloat16().to(dev)
+        out = torch.empty(m, nn, dtype=torch.bfloat16, device=dev)
+        run = lambda: ops.matmul(x, w, out=out)  # noqa: E731
+        parts = {"gemm": (run, 2.0 * m * nn * kk)}
+        config = {"workload": "MLP down projection, plain bf16 epilogue", "M": m, "K": kk, "N": nn}
     elif args.op == "gelu_gemm":
         m, kk, nn = 131072, 768, 3072
         x = torch.randn(m, kk, generator=gen(0)).bfloat16().to(dev)
@@ -484,7 +494,7 @@ def main() -> None:
                     help="one AdamW pass after the backward instead of per-bucket updates")
     ap.add_argument("--atomic-wgrad", action="store_true",
                     help="fp32 atomics for split-K weight gradients (not bit-reproducible)")
-    ap.add_argument("--op", choices=["step", "attention", "lce", "gelu_gemm", "kernels"],
+    ap.add_argument("--op", choices=["step", "attention", "lce", "gemm", "gelu_gemm", "kernels"],
                     default="step",
                     help="op-level configuration instead of the training step (1 GPU)")
     args = ap.parse_args()

@@ -1083,14 +1083,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         __syncwarp();
         float* park = reinterpret_cast<float*>(stage);  // [32 rows][64] fp32, 16-byte chunks xor-swizzled
         auto park_at = [&](int chunk) { return park + lane * 64 + ((chunk ^ (lane & 15)) << 2); };
+        {
+          float t64[64];
+          tmem_ld32_nw(tDK + lane_off, reinterpret_cast<uint32_t*>(t64));
+          tmem_ld32_nw(tDK + lane_off + 32, reinterpret_cast<uint32_t*>(t64) + 32);
+          tmem_wait_ld();
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          float t32[32];
-          tmem_ld32(tDK + lane_off + hh * 32, t32);
-#pragma unroll
-          for (int c4 = 0; c4 < 8; ++c4)
-            *reinterpret_cast<float4*>(park_at(hh * 8 + c4)) =
-                make_float4(t32[4 * c4], t32[4 * c4 + 1], t32[4 * c4 + 2], t32[4 * c4 + 3]);
+          for (int c4 = 0; c4 < 16; ++c4)
+            *reinterpret_cast<float4*>(park_at(c4)) =
+                make_float4(t64[4 * c4], t64[4 * c4 + 1], t64[4 * c4 + 2], t64[4 * c4 + 3]);
         }
         float dvv[64];
         tmem_ld32_nw(tDV + lane_off, reinterpret_cast<uint32_t*>(dvv));
