@@ -1,33 +1,40 @@
 // Causal flash attention (head_dim 64) on the Blackwell tensor cores.
 //
-// Forward (attn_fwd_tc): one CTA per (pair of 128-query tiles, batch*head),
-// 10 warps, all of TMEM: warp 0 loads both Q tiles once and 128-key K/V blocks
-// into a 3-stage ring (4-D tensor maps over (e, t, h, b), so any [b, t, h, e]
-// strides work and rows past the sequence end arrive as zeros); one thread of
-// warp 1 issues the MMAs, S_x = Q_x K^T (128x128 fp32 in TMEM) and
-// O_x += P_x V (P_x read from TMEM, V an MN-major shared operand); two softmax
-// warpgroups own one tile each (thread = query row = TMEM lane) and turn S_x
-// into bf16 P_x in TMEM, so the two tiles ping-pong: while one warpgroup
-// exponentiates, the tensor core runs the other tile's MMAs.
-// Backward (attn_bwd_tc): one CTA per (128-key tile, batch*head), looping over
-// 64-query tiles from the diagonal down. 23 warps: TMA (K, V once; Q/dO into a
-// 4-stage ring), a scores MMA thread (S^T = K Q^T and dP^T = V dO^T into one
+// Both kernels are persistent: one CTA per SM walks a list of work items and
+// keeps its shared-memory rings and TMEM handshakes running from one item into
+// the next (see the item comments at each kernel).
+// Forward (attn_fwd_tc): work item = (pair of 128-query tiles, batch*head).
+// 11 warps, all of TMEM: warp 0 loads both Q tiles of an item (two item
+// slots) and 128-key K/V blocks into a 4-stage ring (4-D tensor maps over
+// (e, t, h, b), so any [b, t, h, e] strides work and rows past the sequence
+// end arrive as zeros); one MMA thread per tile issues S_x = Q_x K^T (128x128
+// fp32 in TMEM) and O_x += P_x V (P_x read from TMEM, V an MN-major shared
+// operand); two softmax warpgroups own one tile each (thread = query row =
+// TMEM lane) and turn S_x into bf16 P_x in TMEM, so the two tiles ping-pong:
+// while one warpgroup exponentiates, the tensor core runs the other tile's
+// MMAs.
+// Backward (attn_bwd_tc): work item = (128-key tile, batch*head), looping over
+// 64-query tiles from the diagonal down. 23 warps: TMA (K, V per item in two
+// slots; Q/dO into a 4-stage ring with the tile's lse/delta copied in by
+// cp.async), a scores MMA thread (S^T = K Q^T and dP^T = V dO^T into one
 // of three 128-column TMEM buffers, as far ahead as the buffers allow), a
 // gradient MMA thread (dV += P^T dO and dK += dS^T Q with P^T / dS^T read
 // straight from TMEM; dQ = dS K per pair of tiles, dS^T read MN-major from a
-// shared-memory ring), and 16 softmax warps that take every tile together
+// shared-memory ring), 16 softmax warps that take every tile together
 // (thread = key row, 16 query columns per warp: P^T = exp2(S^T c - lse),
 // dS^T = P^T (dP^T - delta), written over the warp's own S^T columns as bf16
 // pairs), and four dQ warps. Two issuing threads keep the tensor pipe fed
 // while either waits on a barrier. The dQ warps read each pair's dQ out of
 // TMEM as soon as its MMA completes and reduce it into an fp32 accumulator by
-// TMA; dK, dV leave TMEM once at the end.
+// TMA; at the end of an item they also write dK and dV.
 // q and k arrive already rotated (RoPE runs in the QKV projection epilogue);
 // with RoPE tables the backward rotates dq and dk back so they are gradients
 // of the unrotated inputs.
 // Every mbarrier wait is bounded (common.cuh). Semantics follow
 // rig/kernels/tpu_flash_attention.py:171-207 (fp32 statistics, bf16 P).
 #include <algorithm>
+#include <atomic>
+#include <mutex>
 #include <type_traits>
 
 #include "common.cuh"
@@ -57,6 +64,7 @@ struct AttnParams {
   const bf16* rcos;    // RoPE tables [T, 32] or null
   const bf16* rsin;
   const int* seg;      // document segment ids [B, T] or null (causal only)
+  unsigned* sched;     // this launch's work counter {next item, finished CTAs}
 };
 
 __device__ __forceinline__ uint32_t swz128(int row, int chunk) {
@@ -131,10 +139,39 @@ __device__ __forceinline__ int2 seg_range(const int2* tab, int nch, int c, int n
   return r;
 }
 
+// Dynamic work distribution of the persistent kernels: the TMA warp of each
+// CTA takes the next item index from a per-launch counter (the items are laid
+// out head by head, heaviest first within a head, so the items in flight at
+// once cover a few heads whose K/V or Q/dO tiles come from DRAM about once and
+// are then served from L2, and a CTA that finishes early takes more work).
+// The counters live in a small device array of slots; each launch gets its own
+// slot (so launches that overlap on the GPU do not share one) and the last CTA
+// to finish puts the slot back to zero.
+constexpr int kSchedSlots = 64;
+__device__ unsigned g_attn_sched[2][kSchedSlots][2];
+
+// Called by the whole producer warp: the next item index (lane 0 fetches).
+__device__ __forceinline__ int next_item(unsigned* sched, int lane) {
+  int v = 0;
+  if (lane == 0) v = (int)atomicAdd(sched, 1u);
+  return __shfl_sync(0xffffffffu, v, 0);
+}
+
+// Called by thread 0 of each CTA after all of the CTA's work: the last CTA
+// resets the launch's counter slot.
+__device__ __forceinline__ void sched_finish(unsigned* sched) {
+  __threadfence();
+  if (atomicAdd(sched + 1, 1u) == gridDim.x - 1) {
+    sched[0] = 0;
+    sched[1] = 0;
+    __threadfence();
+  }
+}
+
 // ------------------------------------------------------------------ forward
 // Persistent: one CTA per SM walks work items (pair of 128-query tiles pr,
-// batch*head bh), item = (npair-1-pr) * B*H + bh (heaviest pairs first),
-// taking items blockIdx.x, + gridDim.x, ... Every role keeps running
+// batch*head bh), item = bh * npair + (npair-1-pr), handed out by next_item.
+// Every role keeps running
 // counters across items, so the K/V ring and the per-tile S/P/O handshakes
 // flow from one item into the next; Q tiles are double-buffered per item.
 constexpr int FQ = 128;                 // queries per tile (TMEM lanes); two tiles per item
@@ -176,7 +213,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   extern __shared__ __align__(1024) uint8_t smem_fwd[];
   uint8_t* sm = smem_fwd;
   if (smem_u32(sm) & 1023) {  // the layout needs 1024-byte aligned tiles: give up, flagged
-    if (threadIdx.x == 0) atomicCAS(&g_attn_error, 0, kErrSmemAlign);
+    if (threadIdx.x == 0) {
+      atomicCAS(&g_attn_error, 0, kErrSmemAlign);
+      sched_finish(p.sched);
+    }
     return;
   }
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::BAR);
@@ -198,7 +238,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int BH = p.B * p.H;
   const int npair = (p.T + 2 * FQ - 1) / (2 * FQ);
-  const int n_items = npair * BH;
+  const int n_items = npair * BH;  // item = bh * npair + (npair - 1 - pair)
   int* err = &g_attn_error;
   auto segtab_of = [&](int slot) {
     return reinterpret_cast<int2*>(sm + L::SEGTAB) + slot * kMaxSegChunks;
@@ -248,11 +288,19 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     // chunk ranges and the key-block list), then loads its two Q tiles and its
     // K/V blocks into the ring.
     bool ok = true;
-    int gk = 0, ii = 0;
-    for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x, ++ii) {
+    int gk = 0;
+    for (int ii = 0; ok; ++ii) {
       const int slot = ii & 1;
+      const int item = next_item(p.sched, lane);
       if (!(ok = mbar_wait(&item_empty[slot], ((ii >> 1) & 1) ^ 1, abort_flag, err))) break;
-      const int pr = npair - 1 - item / BH, bh = item % BH;
+      if (item >= n_items) {  // no more work: an empty slot ends every role's loop
+        if (lane == 0) {
+          items[slot].nkv = -1;
+          mbar_arrive(&item_full[slot]);
+        }
+        break;
+      }
+      const int bh = item / npair, pr = npair - 1 - (item - bh * npair);
       const int b = bh / p.H, h = bh - b * p.H;
       const int q0 = pr * 2 * FQ;
       // tile x's diagonal key block is d0 + x; tile 1 of the last pair may lie
@@ -337,10 +385,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       constexpr uint32_t idO = umma_idesc_bf16(128, HD, 0, 1);  // A = P in TMEM, B = V MN-major
       bool ok = true;
       int gk = 0, jx = 0, ii = 0;  // ring block, this tile's running block, item
-      for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x, ++ii) {
+      for (; ok; ++ii) {
         const int slot = ii & 1;
         if (!(ok = mbar_wait(&item_full[slot], (ii >> 1) & 1, abort_flag, err))) break;
         const FwdItem inf = items[slot];
+        if (inf.nkv < 0) break;  // no more items
         const int nb = x == 0 ? inf.n0 : (inf.has1 ? inf.nkv : 0);
         const uint32_t sQ = smem_u32(sm + L::Q + (slot * 2 + x) * Q_BYTES);
         auto issue_s = [&](int s) {
@@ -414,10 +463,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     int nseg = 0;  // blocks of this tile that needed the per-element test so far
     bool ok = true;
     int jx = 0, ii = 0;
-    for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x, ++ii) {
+    for (; ok; ++ii) {
       const int slot = ii & 1;
       if (!(ok = mbar_wait(&item_full[slot], (ii >> 1) & 1, abort_flag, err))) break;
       const FwdItem inf = items[slot];
+      if (inf.nkv < 0) break;  // no more items
       const int nb = x == 0 ? inf.n0 : (inf.has1 ? inf.nkv : 0);
       const int bh = inf.bh, b = bh / p.H, h = bh - b * p.H;
       const int q0 = inf.pr * 2 * FQ;
@@ -569,12 +619,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
+  if (threadIdx.x == 0) sched_finish(p.sched);
 }
 
 // ------------------------------------------------------------------ backward
 // Persistent: one CTA per SM walks work items (key tile kt, batch*head bh),
-// item = kt * B*H + bh, taking items blockIdx.x, + gridDim.x, ... (heaviest
-// key tiles first, so the ends of the CTAs' lists are short items). Every role
+// item = bh * nkt + kt, handed out by next_item. Every role
 // walks the same item list and keeps running tile / query-pair counters across
 // items, so the rings (Q/dO stages, TMEM score buffers, dS^T slots, dQ pairs)
 // flow from one item into the next without draining: while the last tiles of
@@ -632,7 +682,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   extern __shared__ __align__(1024) uint8_t smem_bwd[];
   uint8_t* sm = smem_bwd;
   if (smem_u32(sm) & 1023) {  // the layout needs 1024-byte aligned tiles: give up, flagged
-    if (threadIdx.x == 0) atomicCAS(&g_attn_error, 0, kErrSmemAlign);
+    if (threadIdx.x == 0) {
+      atomicCAS(&g_attn_error, 0, kErrSmemAlign);
+      sched_finish(p.sched);
+    }
     return;
   }
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::BAR);
@@ -655,7 +708,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int BH = p.B * p.H;
-  const int n_items = ((p.T + BT - 1) / BT) * BH;
+  const int n_items = ((p.T + BT - 1) / BT) * BH;  // item = bh * nkt + kt
   int* err = &g_attn_error;
   // query tile (64-position index past k0) of list entry `it` of the item in `slot`
   auto qtile = [&](int slot, int it) -> int {
@@ -708,11 +761,20 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     // Item producer: publishes each item's slot (and, with segment ids, its
     // chunk ranges and query-tile list), then loads its K/V and Q/dO tiles.
     bool ok = true;
-    int g = 0, ii = 0;
-    for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x, ++ii) {
+    int g = 0;
+    for (int ii = 0; ok; ++ii) {
       const int slot = ii & 1;
+      const int item = next_item(p.sched, lane);
       if (!(ok = mbar_wait(&item_empty[slot], ((ii >> 1) & 1) ^ 1, abort_flag, err))) break;
-      const int kt = item / BH, bh = item - kt * BH;
+      if (item >= n_items) {  // no more work: an empty slot ends every role's loop
+        if (lane == 0) {
+          items[slot].nq = -1;
+          mbar_arrive(&item_full[slot]);
+        }
+        break;
+      }
+      const int nkt = (p.T + BT - 1) / BT;
+      const int bh = item / nkt, kt = item - bh * nkt;
       const int b = bh / p.H, h = bh - b * p.H;
       const int k0 = kt * BT;
       const int nq_all = (p.T - k0 + BQ - 1) / BQ;  // 64-query tiles from the diagonal on
@@ -806,10 +868,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       constexpr uint32_t idMN = umma_idesc_bf16(128, 64, 1, 1);  // dQ: A, B MN-major
       bool ok = true;
       int g = 0, ii = 0;
-      for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x, ++ii) {
+      for (; ok; ++ii) {
         const int slot = ii & 1, kvs = ii & 1;
         if (!(ok = mbar_wait(&item_full[slot], (ii >> 1) & 1, abort_flag, err))) break;
         const int nq = items[slot].nq;
+        if (nq < 0) break;  // no more items
         // dV / dK of the previous item have been read out of TMEM
         if (ii > 0 && !(ok = mbar_wait(acc_free, (ii - 1) & 1, abort_flag, err))) break;
         const uint32_t sK = smem_u32(sm + L::KV + kvs * 2 * BT_BYTES);
@@ -860,10 +923,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       constexpr uint32_t idS = umma_idesc_bf16(128, BQ, 0, 0);
       bool ok = true;
       int g = 0, ii = 0;
-      for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x, ++ii) {
+      for (; ok; ++ii) {
         const int slot = ii & 1, kvs = ii & 1;
         if (!(ok = mbar_wait(&item_full[slot], (ii >> 1) & 1, abort_flag, err))) break;
         const int nq = items[slot].nq;
+        if (nq < 0) break;  // no more items
         if (!(ok = mbar_wait(&kv_full[kvs], (ii >> 1) & 1, abort_flag, err))) break;
         const uint32_t sK = smem_u32(sm + L::KV + kvs * 2 * BT_BYTES), sV = sK + BT_BYTES;
         for (int it = 0; it < nq; ++it, ++g) {
@@ -907,10 +971,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const float c = p.scale * kLog2e;
     bool ok = true;
     int g = 0, ii = 0;
-    for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x, ++ii) {
+    for (; ok; ++ii) {
       const int slot = ii & 1;
       if (!(ok = mbar_wait(&item_full[slot], (ii >> 1) & 1, abort_flag, err))) break;
       const BwdItem inf = items[slot];
+      if (inf.nq < 0) break;  // no more items
       const int nq = inf.nq;
       const int b = inf.bh / p.H;
       const int k0 = inf.kt * BT;
@@ -1033,10 +1098,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     uint8_t* stage = sm + L::DQS + (warp - kBwdFlushWarp) * 8192;
     bool ok = true;
     int g = 0, ii = 0;
-    for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x, ++ii) {
+    for (; ok; ++ii) {
       const int slot = ii & 1;
       if (!(ok = mbar_wait(&item_full[slot], (ii >> 1) & 1, abort_flag, err))) break;
       const BwdItem inf = items[slot];
+      if (inf.nq < 0) break;  // no more items
       const int k0 = inf.kt * BT;
       for (int j = 0; j < inf.nq / 2; ++j) {
         const int J = (g >> 1) + j;  // running pair index
@@ -1143,6 +1209,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
+  if (threadIdx.x == 0) sched_finish(p.sched);
 }
 
 // delta[bh, t] = sum_e dO * O, and zero the dQ accumulator row. Eight lanes
@@ -1218,6 +1285,27 @@ int attention_read_error(int clear) {
 }
 
 // ------------------------------------------------------------------ host
+// A counter slot of g_attn_sched for one launch of kernel `which` (0 forward,
+// 1 backward) on the current device: slots rotate per device, so up to
+// kSchedSlots launches may be in flight at once.
+static unsigned* sched_slot(int which) {
+  static unsigned* base[64] = {};
+  static std::atomic<unsigned> next[64][2];
+  static std::mutex mu;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 64) return nullptr;
+  if (!base[dev]) {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!base[dev]) {
+      void* ptr = nullptr;
+      if (cudaGetSymbolAddress(&ptr, g_attn_sched) != cudaSuccess) return nullptr;
+      base[dev] = reinterpret_cast<unsigned*>(ptr);
+    }
+  }
+  const unsigned k = next[dev][which].fetch_add(1) % kSchedSlots;
+  return base[dev] + ((size_t)which * kSchedSlots + k) * 2;
+}
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
@@ -1312,6 +1400,8 @@ extern "C" int gptb200_attention_fwd(const void* q, const void* k, const void* v
   p.ost = o_stride_t;
   p.lse = lse;
   p.seg = segment_ids;
+  p.sched = sched_slot(0);
+  if (!p.sched) return GPTB200_EUNSUPPORTED;
   static bool cfg[64][2] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1391,6 +1481,8 @@ extern "C" int gptb200_attention_bwd(const void* q, const void* k, const void* v
   p.rcos = reinterpret_cast<const bf16*>(rope_cos);
   p.rsin = reinterpret_cast<const bf16*>(rope_sin);
   p.seg = segment_ids;
+  p.sched = sched_slot(1);
+  if (!p.sched) return GPTB200_EUNSUPPORTED;
   static bool cfg[64][2] = {};
   int dev = 0;
   cudaGetDevice(&dev);
