@@ -52,14 +52,19 @@ __global__ void __launch_bounds__(256) moe_route_kernel(
     const bf16* __restrict__ x, const float* __restrict__ w, int64_t n, int d, int E, int k,
     float* __restrict__ logits, int* __restrict__ chosen, float* __restrict__ gate,
     float* __restrict__ stats) {
-  extern __shared__ float wsm[];  // [d / 8][E][8] router weights, then [8 warps][stat width]
+  // Router weights as float4 [E][2][d / 8]: expert e's features 8c..8c+3 at
+  // [e][0][c], 8c+4..8c+7 at [e][1][c], so the 32 lanes of a warp (chunks c,
+  // c+1, ...) read 32 consecutive 16-byte words (no bank conflicts); then
+  // [8 warps][stat width] statistics.
+  extern __shared__ float wsm[];
   const int width = moe_stat_width(E);
   float* wst = wsm + (size_t)d * E;
   const int nch = d / 8;
   for (int i = threadIdx.x; i < d * E; i += blockDim.x) {
     const int f = i / E, e = i - f * E;  // w is [d][E]
-    wsm[((f >> 3) * E + e) * 8 + (f & 7)] = w[i];
+    wsm[(((size_t)e * 2 + ((f >> 2) & 1)) * nch + (f >> 3)) * 4 + (f & 3)] = w[i];
   }
+  const float4* w4 = reinterpret_cast<const float4*>(wsm);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   // per-lane statistics: lane e < E the probability sum and count of expert e;
   // lane 0 the entropy, top-1 gate and squared-logit sums
@@ -87,8 +92,7 @@ __global__ void __launch_bounds__(256) moe_route_kernel(
 #pragma unroll
       for (int e = 0; e < kMoeMaxE; ++e) {
         if (e < E) {
-          const float4* we = reinterpret_cast<const float4*>(wsm + ((size_t)c * E + e) * 8);
-          const float4 w0 = we[0], w1 = we[1];
+          const float4 w0 = w4[(size_t)(e * 2) * nch + c], w1 = w4[(size_t)(e * 2 + 1) * nch + c];
 #pragma unroll
           for (int j = 0; j < kRouteTok; ++j) {
             float s = acc[j][e];
@@ -371,6 +375,9 @@ __global__ void moe_zero_pad_kernel(const int* __restrict__ src, const int* __re
 // stream order in shared memory and the block adds them with one atomic each.
 constexpr int kRbChunk = 64;
 constexpr int kRbMaxThreads = 512;  // 128 registers a thread
+// tokens whose row reads a thread has in flight (fewer for wider rows, so the
+// weights and partials stay in registers)
+__host__ __device__ constexpr int rb_unroll(int fpt) { return fpt == 2 ? 4 : (fpt == 4 ? 3 : 2); }
 
 template <int FPT>
 struct RbVec;
@@ -439,38 +446,60 @@ __global__ void __launch_bounds__(kRbMaxThreads, 1) moe_route_bwd_kernel(
       if (lane < k) ps[tt][lane] = pos[t * k + lane];
     }
     __syncthreads();
-    // (b) d_W partials and d_x, FPT features of one token per step
+    // (b) d_W partials and d_x, FPT features of one token per step; a thread
+    // issues the row reads of rb_unroll(FPT) of its tokens before their math (the
+    // tokens still enter the partials in order s, s + S, s + 2S, ...)
     if (active) {
-      for (int tt = stream; tt < nt; tt += streams) {
-        const int64_t t = c0 + tt;
-        float xv[FPT];
-        rb_unpack<FPT>(*reinterpret_cast<const Vec*>(x + t * d + f0), xv);
-        Vec gq = *reinterpret_cast<const Vec*>(d_grouped + (int64_t)ps[tt][0] * d + f0);
-        for (int j = 1; j < k; ++j) {
-          const Vec o = *reinterpret_cast<const Vec*>(d_grouped + (int64_t)ps[tt][j] * d + f0);
-          uint32_t* a32 = reinterpret_cast<uint32_t*>(&gq);
-          const uint32_t* o32 = reinterpret_cast<const uint32_t*>(&o);
+      for (int tb = stream; tb < nt; tb += streams * rb_unroll(FPT)) {
+        constexpr int U = rb_unroll(FPT);
+        Vec xq[U], gq[U][kMoeMaxK];
 #pragma unroll
-          for (int h = 0; h < FPT / 2; ++h) a32[h] = hadd2_bf16(a32[h], o32[h]);
-        }
-        float v[FPT];
+        for (int u = 0; u < U; ++u) {
+          const int tt = tb + u * streams;
+          if (tt < nt) {
+            const int64_t t = c0 + tt;
+            xq[u] = *reinterpret_cast<const Vec*>(x + t * d + f0);
 #pragma unroll
-        for (int i = 0; i < FPT; ++i) v[i] = 0.f;
-#pragma unroll
-        for (int e = 0; e < E; ++e) {
-          const float de = dl[tt][e];
-#pragma unroll
-          for (int i = 0; i < FPT; ++i) {
-            acc[i][e] = fmaf(xv[i], de, acc[i][e]);
-            v[i] = fmaf(de, wreg[i][e], v[i]);
+            for (int j = 0; j < kMoeMaxK; ++j)
+              if (j < k) gq[u][j] = *reinterpret_cast<const Vec*>(d_grouped + (int64_t)ps[tt][j] * d + f0);
           }
         }
-        Vec out;
-        uint32_t* o32 = reinterpret_cast<uint32_t*>(&out);
-        const uint32_t* g32 = reinterpret_cast<const uint32_t*>(&gq);
 #pragma unroll
-        for (int h = 0; h < FPT / 2; ++h) o32[h] = hadd2_bf16(g32[h], pack_bf16x2(v[2 * h], v[2 * h + 1]));
-        *reinterpret_cast<Vec*>(d_x + t * d + f0) = out;
+        for (int u = 0; u < U; ++u) {
+          const int tt = tb + u * streams;
+          if (tt >= nt) break;
+          const int64_t t = c0 + tt;
+          float xv[FPT];
+          rb_unpack<FPT>(xq[u], xv);
+          Vec g0 = gq[u][0];
+#pragma unroll
+          for (int j = 1; j < kMoeMaxK; ++j) {
+            if (j >= k) break;
+            uint32_t* a32 = reinterpret_cast<uint32_t*>(&g0);
+            const uint32_t* o32 = reinterpret_cast<const uint32_t*>(&gq[u][j]);
+#pragma unroll
+            for (int h = 0; h < FPT / 2; ++h) a32[h] = hadd2_bf16(a32[h], o32[h]);
+          }
+          float v[FPT];
+#pragma unroll
+          for (int i = 0; i < FPT; ++i) v[i] = 0.f;
+#pragma unroll
+          for (int e = 0; e < E; ++e) {
+            const float de = dl[tt][e];
+#pragma unroll
+            for (int i = 0; i < FPT; ++i) {
+              acc[i][e] = fmaf(xv[i], de, acc[i][e]);
+              v[i] = fmaf(de, wreg[i][e], v[i]);
+            }
+          }
+          Vec out;
+          uint32_t* o32 = reinterpret_cast<uint32_t*>(&out);
+          const uint32_t* g32 = reinterpret_cast<const uint32_t*>(&g0);
+#pragma unroll
+          for (int h = 0; h < FPT / 2; ++h)
+            o32[h] = hadd2_bf16(g32[h], pack_bf16x2(v[2 * h], v[2 * h + 1]));
+          *reinterpret_cast<Vec*>(d_x + t * d + f0) = out;
+        }
       }
     }
     __syncthreads();
@@ -492,17 +521,53 @@ __global__ void __launch_bounds__(kRbMaxThreads, 1) moe_route_bwd_kernel(
 }
 
 // out[e][c] += sum of buf rows [seg[e].x, seg[e].x + seg[e].y), column c.
-__global__ void moe_seg_colsum_kernel(const bf16* __restrict__ buf, const int2* __restrict__ seg,
-                                      int w, float* __restrict__ out) {
+// A thread owns 8 consecutive columns (16-byte row reads, four rows in flight)
+// of one of gridDim.z row chunks of the segment; the chunk's sums (rows added
+// in order) go to `out` with one atomic per column. width % 8 == 0.
+__global__ void __launch_bounds__(128) moe_seg_colsum_kernel(const bf16* __restrict__ buf,
+                                                             const int2* __restrict__ seg, int w,
+                                                             float* __restrict__ out) {
   const int e = blockIdx.y;
-  const int col = blockIdx.x * blockDim.x + threadIdx.x;
-  if (col >= w) return;
+  const int c0 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (c0 >= w) return;
   const int2 sg = seg[e];
   const int chunk = (sg.y + gridDim.z - 1) / gridDim.z;
   const int r0 = sg.x + blockIdx.z * chunk, r1 = min(sg.x + sg.y, r0 + chunk);
-  float s = 0.f;
-  for (int r = r0; r < r1; ++r) s += __bfloat162float(buf[(int64_t)r * w + col]);
-  if (r1 > r0) atomicAdd(&out[(int64_t)e * w + col], s);
+  float s[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) s[j] = 0.f;
+  int r = r0;
+  for (; r + 4 <= r1; r += 4) {
+    uint4 q[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) q[u] = *reinterpret_cast<const uint4*>(buf + (int64_t)(r + u) * w + c0);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const uint32_t* qw = &q[u].x;
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        float a, b;
+        unpack_bf16x2(qw[h], a, b);
+        s[2 * h] += a;
+        s[2 * h + 1] += b;
+      }
+    }
+  }
+  for (; r < r1; ++r) {
+    const uint4 q = *reinterpret_cast<const uint4*>(buf + (int64_t)r * w + c0);
+    const uint32_t* qw = &q.x;
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      float a, b;
+      unpack_bf16x2(qw[h], a, b);
+      s[2 * h] += a;
+      s[2 * h + 1] += b;
+    }
+  }
+  if (r1 > r0) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) atomicAdd(&out[(int64_t)e * w + c0 + j], s[j]);
+  }
 }
 
 // ------------------------------------------------------------------ statistics
@@ -730,8 +795,9 @@ extern "C" int gptb200_moe_segment_colsum(const void* buf, const int32_t* seg, i
                                           int64_t width, float* out, void* stream) {
   if (!buf || !seg || !out || width <= 0) return GPTB200_EINVAL;
   if (experts < 1 || experts > kMoeMaxE) return GPTB200_EUNSUPPORTED;
-  dim3 grid((unsigned)((width + 255) / 256), (unsigned)experts, 128);
-  moe_seg_colsum_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  if (width % 8 || (reinterpret_cast<uintptr_t>(buf) & 15)) return GPTB200_ESHAPE;
+  dim3 grid((unsigned)((width / 8 + 127) / 128), (unsigned)experts, 128);
+  moe_seg_colsum_kernel<<<grid, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<const bf16*>(buf), reinterpret_cast<const int2*>(seg), (int)width, out);
   GPTB200_CHECK_LAUNCH();
   return 0;

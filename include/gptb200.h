@@ -256,8 +256,9 @@ int gptb200_moe_route_bwd(const void* x, const float* router_w, const float* log
                           const float* bal_grad, const void* d_grouped, const int32_t* pos,
                           int64_t tokens, int64_t d, int32_t experts, int32_t top_k,
                           float* d_router_w, void* d_x, void* stream);
-/* out fp32 [E, width] += column sums of buf (bf16 [rows, width]) over each
- * expert's segment (per-expert bias gradients). */
+/* out fp32 [E, width] += column sums of buf (bf16 [rows, width], 16-byte
+ * aligned, width % 8 == 0) over each expert's segment (per-expert bias
+ * gradients). */
 int gptb200_moe_segment_colsum(const void* buf, const int32_t* seg, int32_t experts,
                                int64_t width, float* out, void* stream);
 /* From the (rank-summed) stats of all layers: balance loss per layer, the
