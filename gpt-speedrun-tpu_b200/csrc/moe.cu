@@ -367,8 +367,8 @@ __global__ void moe_zero_pad_kernel(const int* __restrict__ src, const int* __re
 // d_logits from the gates (softmax of the chosen logits) and from the balance
 // loss through the router probabilities (d prob_e = bal[e], the same for every
 // token); then d_x = bf16(bf16(sum_j d_grouped[pos(i,j)]) + bf16(d_logits . W^T))
-// and d_W += x^T d_logits. Tokens go in chunks of 64: the warps first form the
-// chunk's d_logits in shared memory (lane e = expert); then thread (stream s,
+// and d_W += x^T d_logits. Tokens go in chunks of 64: the first 64 threads
+// form the chunk's d_logits in shared memory (a thread per token); then thread (stream s,
 // group g) owns features [FPT g, FPT g + FPT) -- their weights and d_W
 // partials in registers -- and takes tokens s, s + S, ... of the chunk with
 // 8- or 16-byte row reads. At the end the S streams' d_W partials are added in
@@ -412,7 +412,6 @@ __global__ void __launch_bounds__(kRbMaxThreads, 1) moe_route_bwd_kernel(
   extern __shared__ float dwsum[];  // [d][E] d_W partial of the block
   __shared__ float dl[kRbChunk][E];
   __shared__ int ps[kRbChunk][kMoeMaxK];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int groups = d / FPT;
   const int stream = threadIdx.x / groups, g = threadIdx.x - stream * groups;
   const bool active = stream < streams;
@@ -427,23 +426,49 @@ __global__ void __launch_bounds__(kRbMaxThreads, 1) moe_route_bwd_kernel(
     }
   for (int64_t c0 = (int64_t)blockIdx.x * kRbChunk; c0 < n; c0 += (int64_t)gridDim.x * kRbChunk) {
     const int nt = (int)(n - c0 < kRbChunk ? n - c0 : kRbChunk);
-    // (a) d_logits of the chunk: warp per token, lane e per expert
-    for (int tt = warp; tt < nt; tt += blockDim.x >> 5) {
+    // (a) d_logits of the chunk: one thread per token, all experts in registers
+    for (int tt = threadIdx.x; tt < nt; tt += blockDim.x) {
       const int64_t t = c0 + tt;
-      const float lg = lane < E ? logits[t * E + lane] : -INFINITY;
-      const float mx = warp_max(lg);
-      const float ex = lane < E ? expf(lg - mx) : 0.f;
-      const float z = warp_sum(ex);
-      const float pr = ex / z;
-      const float b = lane < E ? bal[lane] : 0.f;
-      const float dot = warp_sum(pr * b);
-      float gg = pr * (b - dot);
+      float lg[E], pr[E];
+      float mx = -INFINITY;
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        lg[e] = logits[t * E + e];
+        mx = fmaxf(mx, lg[e]);
+      }
+      float z = 0.f;
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        pr[e] = expf(lg[e] - mx);
+        z += pr[e];
+      }
+      float dot = 0.f;
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        pr[e] = pr[e] / z;
+        dot += pr[e] * bal[e];
+      }
+      float gt[kMoeMaxK], dgt[kMoeMaxK];
+      int ch[kMoeMaxK];
       float gd = 0.f;
-      for (int j = 0; j < k; ++j) gd += gate[t * k + j] * d_gate[t * k + j];
-      for (int j = 0; j < k; ++j)
-        if (chosen[t * k + j] == lane) gg += gate[t * k + j] * (d_gate[t * k + j] - gd);
-      if (lane < E) dl[tt][lane] = gg;
-      if (lane < k) ps[tt][lane] = pos[t * k + lane];
+#pragma unroll
+      for (int j = 0; j < kMoeMaxK; ++j) {
+        if (j < k) {
+          gt[j] = gate[t * k + j];
+          dgt[j] = d_gate[t * k + j];
+          ch[j] = chosen[t * k + j];
+          ps[tt][j] = pos[t * k + j];
+          gd += gt[j] * dgt[j];
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        float gg = pr[e] * (bal[e] - dot);
+#pragma unroll
+        for (int j = 0; j < kMoeMaxK; ++j)
+          if (j < k && ch[j] == e) gg += gt[j] * (dgt[j] - gd);
+        dl[tt][e] = gg;
+      }
     }
     __syncthreads();
     // (b) d_W partials and d_x, FPT features of one token per step; a thread
