@@ -28,17 +28,21 @@ __host__ __device__ constexpr int moe_stat_width(int E) { return 2 * E + 3; }
 // logits = x(fp32) . W_router (fp32) -- the reference promotes the bf16
 // activations to fp32 -- softmax probabilities, the top-k logits (ties: lower
 // expert first, like lax.top_k) and the gates (softmax of the chosen logits).
-// A warp takes kRouteTok tokens at a time: lane l owns the 8-feature chunks
-// l, l + 32, ... of all of them, so each chunk of W (from shared memory) is
-// read once for kRouteTok tokens; the per-expert sums are then reduced across
-// the warp and lane e handles expert e of every token (softmax, entropy,
-// top-k by warp arg-max). Statistics are accumulated per lane, combined per
-// block in warp order and added to `stats` with one atomic per block.
-constexpr int kRouteTok = 4;
+// EP = E rounded up to a power of two (at least 4), TPG = 32 / EP tokens per
+// warp step. Lane l owns the 8-feature chunks l, l + 32, ... of the step's
+// TPG tokens and accumulates all TPG x EP dot products (each chunk of W read
+// once from shared memory for the whole step); one transposing butterfly
+// reduction (31 shuffles) then leaves lane l with the logit of token l / EP,
+// expert l % EP, so each group of EP lanes finishes one token (softmax,
+// entropy, top-k by group arg-max) with shuffles inside the group.
+// Statistics are accumulated per lane, combined per block in warp order and
+// added to `stats` with one atomic per block.
 
-__device__ __forceinline__ void warp_argmax(float& v, int& i) {
+// Arg-max over the aligned groups of `width` lanes; ties go to the lower index.
+template <int width>
+__device__ __forceinline__ void group_argmax(float& v, int& i) {
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
+  for (int o = width / 2; o > 0; o >>= 1) {
     const float ov = __shfl_xor_sync(0xffffffffu, v, o);
     const int oi = __shfl_xor_sync(0xffffffffu, i, o);
     if (ov > v || (ov == v && oi < i)) {
@@ -47,42 +51,56 @@ __device__ __forceinline__ void warp_argmax(float& v, int& i) {
     }
   }
 }
+template <int width>
+__device__ __forceinline__ float group_sum(float v) {
+#pragma unroll
+  for (int o = width / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+template <int width>
+__device__ __forceinline__ float group_max(float v) {
+#pragma unroll
+  for (int o = width / 2; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
 
+template <int EP>
 __global__ void __launch_bounds__(256) moe_route_kernel(
     const bf16* __restrict__ x, const float* __restrict__ w, int64_t n, int d, int E, int k,
     float* __restrict__ logits, int* __restrict__ chosen, float* __restrict__ gate,
     float* __restrict__ stats) {
-  // Router weights as float4 [E][2][d / 8]: expert e's features 8c..8c+3 at
-  // [e][0][c], 8c+4..8c+7 at [e][1][c], so the 32 lanes of a warp (chunks c,
-  // c+1, ...) read 32 consecutive 16-byte words (no bank conflicts); then
-  // [8 warps][stat width] statistics.
+  constexpr int TPG = 32 / EP;
+  // Router weights as float4 [EP][2][d / 8] (experts past E are zero): expert
+  // e's features 8c..8c+3 at [e][0][c], 8c+4..8c+7 at [e][1][c], so the 32
+  // lanes of a warp (chunks c, c+1, ...) read 32 consecutive 16-byte words;
+  // then [8 warps][stat width] statistics.
   extern __shared__ float wsm[];
   const int width = moe_stat_width(E);
-  float* wst = wsm + (size_t)d * E;
   const int nch = d / 8;
-  for (int i = threadIdx.x; i < d * E; i += blockDim.x) {
-    const int f = i / E, e = i - f * E;  // w is [d][E]
-    wsm[(((size_t)e * 2 + ((f >> 2) & 1)) * nch + (f >> 3)) * 4 + (f & 3)] = w[i];
+  float* wst = wsm + (size_t)d * EP;
+  for (int i = threadIdx.x; i < d * EP; i += blockDim.x) {
+    const int f = i / EP, e = i - f * EP;
+    wsm[(((size_t)e * 2 + ((f >> 2) & 1)) * nch + (f >> 3)) * 4 + (f & 3)] =
+        e < E ? w[(size_t)f * E + e] : 0.f;
   }
   const float4* w4 = reinterpret_cast<const float4*>(wsm);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  // per-lane statistics: lane e < E the probability sum and count of expert e;
-  // lane 0 the entropy, top-1 gate and squared-logit sums
+  const int my_e = lane % EP, my_j = lane / EP;
+  // per-lane statistics: expert my_e's probability sum and count; the entropy,
+  // top-1 gate and squared-logit sums in the lanes with my_e == 0
   float st_prob = 0.f, st_cnt = 0.f, st_ent = 0.f, st_top1 = 0.f, st_sq = 0.f;
   __syncthreads();
-  const int64_t groups = (n + kRouteTok - 1) / kRouteTok;
+  const int64_t groups = (n + TPG - 1) / TPG;
   for (int64_t gi = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp; gi < groups;
        gi += (int64_t)gridDim.x * (blockDim.x >> 5)) {
-    const int64_t t0 = gi * kRouteTok;
-    float acc[kRouteTok][kMoeMaxE];
+    const int64_t t0 = gi * TPG;
+    float acc[TPG * EP];
 #pragma unroll
-    for (int j = 0; j < kRouteTok; ++j)
-#pragma unroll
-      for (int e = 0; e < kMoeMaxE; ++e) acc[j][e] = 0.f;
+    for (int i = 0; i < TPG * EP; ++i) acc[i] = 0.f;
     for (int c = lane; c < nch; c += 32) {
-      float a[kRouteTok][8];
+      float a[TPG][8];
 #pragma unroll
-      for (int j = 0; j < kRouteTok; ++j) {
+      for (int j = 0; j < TPG; ++j) {
         const int64_t t = t0 + j < n ? t0 + j : n - 1;
         const uint4 q = *reinterpret_cast<const uint4*>(x + t * d + c * 8);
         const uint32_t* qw = &q.x;
@@ -90,77 +108,86 @@ __global__ void __launch_bounds__(256) moe_route_kernel(
         for (int h = 0; h < 4; ++h) unpack_bf16x2(qw[h], a[j][2 * h], a[j][2 * h + 1]);
       }
 #pragma unroll
-      for (int e = 0; e < kMoeMaxE; ++e) {
-        if (e < E) {
-          const float4 w0 = w4[(size_t)(e * 2) * nch + c], w1 = w4[(size_t)(e * 2 + 1) * nch + c];
+      for (int e = 0; e < EP; ++e) {
+        const float4 w0 = w4[(size_t)(e * 2) * nch + c], w1 = w4[(size_t)(e * 2 + 1) * nch + c];
 #pragma unroll
-          for (int j = 0; j < kRouteTok; ++j) {
-            float s = acc[j][e];
-            s = fmaf(a[j][0], w0.x, s);
-            s = fmaf(a[j][1], w0.y, s);
-            s = fmaf(a[j][2], w0.z, s);
-            s = fmaf(a[j][3], w0.w, s);
-            s = fmaf(a[j][4], w1.x, s);
-            s = fmaf(a[j][5], w1.y, s);
-            s = fmaf(a[j][6], w1.z, s);
-            s = fmaf(a[j][7], w1.w, s);
-            acc[j][e] = s;
-          }
+        for (int j = 0; j < TPG; ++j) {
+          float s = acc[j * EP + e];
+          s = fmaf(a[j][0], w0.x, s);
+          s = fmaf(a[j][1], w0.y, s);
+          s = fmaf(a[j][2], w0.z, s);
+          s = fmaf(a[j][3], w0.w, s);
+          s = fmaf(a[j][4], w1.x, s);
+          s = fmaf(a[j][5], w1.y, s);
+          s = fmaf(a[j][6], w1.z, s);
+          s = fmaf(a[j][7], w1.w, s);
+          acc[j * EP + e] = s;
         }
       }
     }
+    // transposing butterfly: after the step with offset o, a lane keeps the
+    // half of its values whose index bit o matches its own lane bit
 #pragma unroll
-    for (int j = 0; j < kRouteTok; ++j) {
-      const int64_t t = t0 + j;
-      // every lane gets every expert's sum; lane e keeps expert e's logit
-      float lg = -INFINITY;
+    for (int o = 16; o > 0; o >>= 1) {
+      const bool upper = (lane & o) != 0;
 #pragma unroll
-      for (int e = 0; e < kMoeMaxE; ++e) {
-        if (e < E) {
-          const float v = warp_sum(acc[j][e]);
-          if (lane == e) lg = v;
-        }
+      for (int i = 0; i < o; ++i) {
+        const float send = upper ? acc[i] : acc[i + o];
+        const float keep = upper ? acc[i + o] : acc[i];
+        acc[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
       }
-      if (t >= n) continue;  // warp-uniform
-      const bool live = lane < E;
-      if (live) logits[t * E + lane] = lg;
-      const float mx = warp_max(lg);
-      const float ex = live ? expf(lg - mx) : 0.f;
-      const float pr = ex / warp_sum(ex);
-      const float ent = warp_sum(live ? -pr * logf(pr + 1.0e-9f) : 0.f);
-      const float sq = warp_sum(live ? lg * lg : 0.f);
-      // top-k by repeated arg-max; the first (lowest) expert wins ties
-      float cur = live ? lg : -INFINITY;
-      float l0 = 0.f, gz = 0.f, mygate_logit = -INFINITY;
-      int mysel = -1;
-      for (int jj = 0; jj < k; ++jj) {
-        float v = cur;
-        int i = live ? lane : 1 << 30;
-        warp_argmax(v, i);
-        if (jj == 0) l0 = v;
-        gz += expf(v - l0);
-        if (lane == jj) {
-          mysel = i;
-          mygate_logit = v;
-        }
-        if (lane == i) cur = -INFINITY;
-        if (live && lane == i) st_cnt += 1.f;
+    }
+    const int64_t t = t0 + my_j;
+    const bool tok = t < n;
+    const bool live = tok && my_e < E;
+    const float lg = live ? acc[0] : -INFINITY;
+    if (live) logits[t * E + my_e] = lg;
+    const float mx = group_max<EP>(lg);
+    const float ex = live ? expf(lg - mx) : 0.f;
+    const float z = group_sum<EP>(ex);
+    const float pr = tok ? ex / z : 0.f;
+    const float ent = group_sum<EP>(live ? -pr * logf(pr + 1.0e-9f) : 0.f);
+    const float sq = group_sum<EP>(live ? lg * lg : 0.f);
+    // top-k by repeated group arg-max; the first (lowest) expert wins ties
+    float cur = lg;
+    float l0 = 0.f, gz = 0.f, mygate_logit = -INFINITY;
+    int mysel = -1;
+    for (int jj = 0; jj < k; ++jj) {
+      float v = cur;
+      int i = live ? my_e : 1 << 30;
+      group_argmax<EP>(v, i);
+      if (jj == 0) l0 = v;
+      gz += expf(v - l0);
+      if (my_e == jj) {
+        mysel = i;
+        mygate_logit = v;
       }
-      // lanes 0..k-1 hold choice j = lane; the first choice has the largest gate
-      if (lane < k) {
-        const float g = expf(mygate_logit - l0) / gz;
-        chosen[t * k + lane] = mysel;
-        gate[t * k + lane] = g;
+      if (my_e == i) {
+        cur = -INFINITY;
+        if (live) st_cnt += 1.f;
       }
-      if (live) st_prob += pr;
-      if (lane == 0) {
-        st_ent += ent;
-        st_top1 += 1.f / gz;  // the first gate, exp(0) / gz
-        st_sq += sq;
-      }
+    }
+    // lanes my_e = 0..k-1 hold choice my_e; the first choice has the largest gate
+    if (tok && my_e < k) {
+      chosen[t * k + my_e] = mysel;
+      gate[t * k + my_e] = expf(mygate_logit - l0) / gz;
+    }
+    if (live) st_prob += pr;
+    if (tok && my_e == 0) {
+      st_ent += ent;
+      st_top1 += 1.f / gz;  // the first gate, exp(0) / gz
+      st_sq += sq;
     }
   }
-  // block statistics: per warp, then the warps in order, one atomic per entry
+  // lanes with the same expert combine, then per warp, then the warps in order
+#pragma unroll
+  for (int o = EP; o < 32; o <<= 1) {
+    st_prob += __shfl_xor_sync(0xffffffffu, st_prob, o);
+    st_cnt += __shfl_xor_sync(0xffffffffu, st_cnt, o);
+    st_ent += __shfl_xor_sync(0xffffffffu, st_ent, o);
+    st_top1 += __shfl_xor_sync(0xffffffffu, st_top1, o);
+    st_sq += __shfl_xor_sync(0xffffffffu, st_sq, o);
+  }
   float* mine = wst + warp * width;
   if (lane < E) {
     mine[lane] = st_prob;
@@ -670,21 +697,28 @@ extern "C" int gptb200_moe_route(const void* x, const float* router_w, int64_t t
   if (!x || !router_w || !logits || !chosen || !gate || !stats || tokens <= 0) return GPTB200_EINVAL;
   if (experts < 1 || experts > kMoeMaxE || top_k < 1 || top_k > kMoeMaxK || top_k > experts)
     return GPTB200_EUNSUPPORTED;
-  if (d % 8 || d * experts * 4 + 8 * moe_stat_width(experts) * 4 > 200 * 1024) return GPTB200_ESHAPE;
+  const int ep = experts <= 4 ? 4 : (experts <= 8 ? 8 : 16);
+  const size_t smem = (size_t)(d * ep + 8 * moe_stat_width(experts)) * 4;
+  if (d % 8 || smem > 200 * 1024) return GPTB200_ESHAPE;
+  if (reinterpret_cast<uintptr_t>(x) & 15) return GPTB200_ESHAPE;
   auto st = reinterpret_cast<cudaStream_t>(stream);
-  const size_t smem = (size_t)(d * experts + 8 * moe_stat_width(experts)) * 4;
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(moe_route_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return -static_cast<int>(e);
-  }
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int blocks = (int)std::min<int64_t>((tokens + 7) / 8, (int64_t)sms * 4);
-  moe_route_kernel<<<blocks, 256, smem, st>>>(reinterpret_cast<const bf16*>(x), router_w, tokens,
-                                               (int)d, experts, top_k, logits, chosen, gate,
-                                               stats);
+  const int tpg = 32 / ep;
+  const int blocks = (int)std::min<int64_t>((tokens + 8 * tpg - 1) / (8 * tpg), (int64_t)sms * 4);
+  auto run = [&](auto kern) -> int {
+    if (smem > 48 * 1024) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return -static_cast<int>(e);
+    }
+    kern<<<blocks, 256, smem, st>>>(reinterpret_cast<const bf16*>(x), router_w, tokens, (int)d,
+                                    experts, top_k, logits, chosen, gate, stats);
+    return 0;
+  };
+  const int status = ep == 4 ? run(moe_route_kernel<4>)
+                             : (ep == 8 ? run(moe_route_kernel<8>) : run(moe_route_kernel<16>));
+  if (status) return status;
   GPTB200_CHECK_LAUNCH();
   return 0;
 }
