@@ -334,59 +334,88 @@ __global__ void moe_combine_kernel(const bf16* __restrict__ out, const int* __re
 
 // Backward of the combine: d_mlp = bf16(alpha * dx); d_out[pos(i,j)] =
 // bf16(d_mlp * bf16(gate)); d_gate(i,j) = bf16-rounded sum_d d_mlp * out.
-// One warp per token. Padding rows of d_out are zeroed by moe_zero_pad_kernel.
-__global__ void moe_combine_bwd_kernel(const bf16* __restrict__ dx, float alpha,
-                                       const bf16* __restrict__ out, const int* __restrict__ pos,
-                                       const float* __restrict__ gate, int64_t n, int d, int k,
-                                       bf16* __restrict__ d_out, float* __restrict__ d_gate) {
+// One warp per token; a lane owns the 8-column chunks lane, lane + 32, ...,
+// taken kCbChunks at a time with all their row reads issued before the math.
+// Padding rows of d_out are zeroed by moe_zero_pad_kernel.
+constexpr int kCbChunks = 3;
+__global__ void __launch_bounds__(256) moe_combine_bwd_kernel(
+    const bf16* __restrict__ dx, float alpha, const bf16* __restrict__ out,
+    const int* __restrict__ pos, const float* __restrict__ gate, int64_t n, int d, int k,
+    bf16* __restrict__ d_out, float* __restrict__ d_gate) {
   const int lane = threadIdx.x & 31;
+  const int nch = d / 8;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
   const uint32_t al = pack_bf16x2(alpha, alpha);
   for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < n;
        t += warps) {
+    int64_t r[kMoeMaxK];
+    uint32_t gb[kMoeMaxK];
     float dg[kMoeMaxK];
-    for (int j = 0; j < k; ++j) dg[j] = 0.f;
-    for (int c = lane; c < d / 8; c += 32) {
-      const uint4 q = *reinterpret_cast<const uint4*>(dx + t * d + c * 8);
-      const uint32_t* qw = &q.x;
+#pragma unroll
+    for (int j = 0; j < kMoeMaxK; ++j) {
+      dg[j] = 0.f;
+      if (j < k) {
+        r[j] = pos[t * k + j];
+        const float g = gate[t * k + j];
+        gb[j] = pack_bf16x2(g, g);
+      }
+    }
+    for (int cb = 0; cb < nch; cb += 32 * kCbChunks) {
+    uint4 q[kCbChunks], o[kCbChunks][kMoeMaxK];
+#pragma unroll
+    for (int i = 0; i < kCbChunks; ++i) {
+      const int c = cb + lane + 32 * i;
+      if (c < nch) {
+        q[i] = *reinterpret_cast<const uint4*>(dx + t * d + c * 8);
+#pragma unroll
+        for (int j = 0; j < kMoeMaxK; ++j)
+          if (j < k) o[i][j] = *reinterpret_cast<const uint4*>(out + r[j] * d + c * 8);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kCbChunks; ++i) {
+      const int c = cb + lane + 32 * i;
+      if (c >= nch) break;
+      const uint32_t* qw = &q[i].x;
       uint32_t dm[4];
 #pragma unroll
       for (int q4 = 0; q4 < 4; ++q4) dm[q4] = hmul2_bf16(qw[q4], al);
-      for (int j = 0; j < k; ++j) {
-        const int64_t r = pos[t * k + j];
-        const float g = gate[t * k + j];
-        const uint32_t gb = pack_bf16x2(g, g);
-        const uint4 o = *reinterpret_cast<const uint4*>(out + r * d + c * 8);
-        const uint32_t* ow = &o.x;
+#pragma unroll
+      for (int j = 0; j < kMoeMaxK; ++j) {
+        if (j >= k) break;
+        const uint32_t* ow = &o[i][j].x;
         uint4 w;
         uint32_t* ww = &w.x;
 #pragma unroll
         for (int q4 = 0; q4 < 4; ++q4) {
-          ww[q4] = hmul2_bf16(dm[q4], gb);
+          ww[q4] = hmul2_bf16(dm[q4], gb[j]);
           float a0, a1, b0, b1;
           unpack_bf16x2(dm[q4], a0, a1);
           unpack_bf16x2(ow[q4], b0, b1);
           dg[j] = fmaf(a0, b0, fmaf(a1, b1, dg[j]));
         }
-        *reinterpret_cast<uint4*>(d_out + r * d + c * 8) = w;
+        *reinterpret_cast<uint4*>(d_out + r[j] * d + c * 8) = w;
       }
     }
-    for (int j = 0; j < k; ++j) {
+    }
+#pragma unroll
+    for (int j = 0; j < kMoeMaxK; ++j) {
+      if (j >= k) break;
       const float s = warp_sum(dg[j]);
       if (lane == 0) d_gate[t * k + j] = bf16r(s);
     }
   }
 }
 
+// Zeroes the padding rows (src < 0) of a grouped buffer: one thread per row.
 __global__ void moe_zero_pad_kernel(const int* __restrict__ src, const int* __restrict__ total,
                                     int d, bf16* __restrict__ buf) {
   const int64_t rows = *total;
-  const int nch = d / 8;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < rows * nch;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / nch;
-    if (src[r] < 0)
-      *reinterpret_cast<uint4*>(buf + r * d + (i - r * nch) * 8) = make_uint4(0u, 0u, 0u, 0u);
+  for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < rows;
+       r += (int64_t)gridDim.x * blockDim.x) {
+    if (src[r] >= 0) continue;
+    uint4* row = reinterpret_cast<uint4*>(buf + r * d);
+    for (int c = 0; c < d / 8; ++c) row[c] = make_uint4(0u, 0u, 0u, 0u);
   }
 }
 
