@@ -635,6 +635,11 @@ constexpr int BQ = 64;                  // queries per inner tile
 constexpr int BT_BYTES = BT * 128;      // 128 rows x 64 bf16
 constexpr int BQ_BYTES = BQ * 128;      // 64 rows x 64 bf16
 constexpr int kBwdSmWarps = 16;         // softmax warps: four per TMEM lane quadrant
+// The softmax warps form GROUPS groups (a kernel template parameter) that take
+// alternate tiles; a warp of a group covers 64 / (group warps / 4) query
+// columns of its tile. One group (every warp on every tile) has the shortest
+// latency per tile and wins at T = 1024, where items are a few tiles long;
+// two groups overlap consecutive tiles and win on long sequences.
 constexpr int kBwdScoreWarp = 2 + kBwdSmWarps;  // issues the S^T / dP^T MMAs
 constexpr int kBwdFlushWarp = kBwdScoreWarp + 1;  // first of four dQ read-out warps
 constexpr int kBwdThreads = 32 * (kBwdFlushWarp + 4);
@@ -672,13 +677,16 @@ struct BwdSmem {
   static constexpr int TOTAL = BAR + 272;
 };
 
-template <bool SEG>
+template <bool SEG, int GROUPS>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                 const __grid_constant__ CUtensorMap tmDQ, const AttnParams p) {
   using L = BwdSmem<SEG>;
   constexpr int kQS = L::kQStages;
+  constexpr int kBwdSmGroups = GROUPS;
+  constexpr int kBwdGroupWarps = kBwdSmWarps / kBwdSmGroups;
+  constexpr int kBwdWarpCols = 64 / (kBwdGroupWarps / 4);
   extern __shared__ __align__(1024) uint8_t smem_bwd[];
   uint8_t* sm = smem_bwd;
   if (smem_u32(sm) & 1023) {  // the layout needs 1024-byte aligned tiles: give up, flagged
@@ -736,7 +744,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
     for (int s = 0; s < 3; ++s) {
       mbar_init(&s_full[s], 1);
-      mbar_init(&p_full[s], kBwdSmWarps);
+      mbar_init(&p_full[s], kBwdGroupWarps);
     }
     for (int s = 0; s < 4; ++s) mbar_init(&done[s], 1);
     mbar_init(fin, 1);
@@ -958,14 +966,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
     }
   } else if (warp < 2 + kBwdSmWarps) {
-    // All 16 softmax warps take every query tile together. Warp w reads TMEM
-    // lanes of quadrant w % 4 (key rows) and the 16 query columns
-    // [16 cg, 16 cg + 16) of the tile, cg = (w - 2) / 4, and writes P^T and
-    // dS^T (bf16 pairs) over exactly those S^T columns, so no warp overwrites
-    // scores another warp has yet to read. The tile's statistics come
-    // ready-made from the producer warp (shared memory of the Q/dO stage).
+    // Softmax group wg takes the tiles it = wg, wg + kBwdSmGroups, ... of
+    // each item. Warp w reads TMEM lanes of quadrant w % 4 (key rows) and
+    // kBwdWarpCols query columns of the tile, in 16-column groups cg, and
+    // writes P^T and dS^T (bf16 pairs) over exactly those S^T columns, so no
+    // warp overwrites scores another warp has yet to read. The tile's
+    // statistics come from the shared memory of its Q/dO stage (cp.async).
     const int quad = warp & 3;
-    const int cg = (warp - 2) >> 2;
+    const int wg = (warp - 2) / kBwdGroupWarps;
+    const int cg0 = (((warp - 2) % kBwdGroupWarps) >> 2) * (kBwdWarpCols / 16);
     const int r = quad * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const float c = p.scale * kLog2e;
@@ -986,16 +995,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       // this key row's segment id (rows past T take an id no query has)
       const int sk = segrow ? (key < p.T ? segrow[key] : INT_MAX) : 0;
       const int2 krng = segrow ? seg_range(segtab, nch, 0, 2) : make_int2(0, 0);
-      for (int it = 0; it < nq; ++it) {
+      for (int it = wg; it < nq; it += kBwdSmGroups) {
         const int gt = g + it;  // running tile index
         const int bb = gt % 3;
         const uint32_t tb = tBuf(bb);
         const int qt = qtile(slot, it);  // query tile index (64 positions) past k0
-        // this warp's 16 columns of the stage's statistics; the scores of the
-        // tile exist only after its Q/dO stage (statistics included) was full
-        const float* stat =
-            reinterpret_cast<const float*>(sm + L::STAT + (gt % kQS) * L::kStatBytes) + cg * 16;
-        const int* stat_seg = reinterpret_cast<const int*>(stat) + 128;
         if (!(ok = mbar_wait(&s_full[bb], (gt / 3) & 1, abort_flag, err))) break;
         if (!(ok = mbar_wait(&q_full[gt % kQS], (gt / kQS) & 1, abort_flag, err))) break;
         // The dS^T ring slot of this tile was last read by the dQ MMA of the
@@ -1003,6 +1007,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         if (gt >= 4 && !(ok = mbar_wait(&done[(gt - 3) & 3], ((gt - 3) >> 2) & 1, abort_flag, err)))
           break;
         tc_fence_after();
+        uint8_t* sd = sm + L::DST + (gt & 3) * BT_BYTES;
+#pragma unroll
+        for (int sub = 0; sub < kBwdWarpCols / 16; ++sub) {
+        const int cg = cg0 + sub;
+        // this 16-column group's statistics; the scores of the tile exist only
+        // after its Q/dO stage (statistics included) was full
+        const float* stat =
+            reinterpret_cast<const float*>(sm + L::STAT + (gt % kQS) * L::kStatBytes) + cg * 16;
+        const int* stat_seg = reinterpret_cast<const int*>(stat) + 128;
         uint32_t sraw[16], draw[16];
         tmem_ld16_nw(tb + lane_off + cg * 16, sraw);
         tmem_ld16_nw(tb + 64 + lane_off + cg * 16, draw);
@@ -1066,11 +1079,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           softmax_cols(std::integral_constant<bool, false>());
         tmem_st8_nw(tb + lane_off + cg * 16, pk);
         tmem_st8_nw(tb + lane_off + cg * 16 + 8, dk);
-        uint8_t* sd = sm + L::DST + (gt & 3) * BT_BYTES;
 #pragma unroll
         for (int q2 = 0; q2 < 2; ++q2)
           *reinterpret_cast<uint4*>(sd + swz128(r, cg * 2 + q2)) =
               make_uint4(dk[4 * q2], dk[4 * q2 + 1], dk[4 * q2 + 2], dk[4 * q2 + 3]);
+        }
         tmem_wait_st();
         fence_proxy_async_smem();
         tc_fence_before();
@@ -1483,18 +1496,21 @@ extern "C" int gptb200_attention_bwd(const void* q, const void* k, const void* v
   p.seg = segment_ids;
   p.sched = sched_slot(1);
   if (!p.sched) return GPTB200_EUNSUPPORTED;
-  static bool cfg[64][2] = {};
+  static bool cfg[64][4] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   const int seg = segment_ids != nullptr;
-  auto kern = seg ? attn_bwd_tc<true> : attn_bwd_tc<false>;
+  const int groups = seq >= 2048 ? 2 : 1;
+  auto kern = seg ? (groups == 2 ? attn_bwd_tc<true, 2> : attn_bwd_tc<true, 1>)
+                  : (groups == 2 ? attn_bwd_tc<false, 2> : attn_bwd_tc<false, 1>);
   const int smem = seg ? BwdSmem<true>::TOTAL : BwdSmem<false>::TOTAL;
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  if (dev >= 64 || !cfg[dev][seg]) {
+  const int ci = seg * 2 + (groups - 1);
+  if (dev >= 64 || !cfg[dev][ci]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return -static_cast<int>(e);
-    if (dev < 64) cfg[dev][seg] = true;
+    if (dev < 64) cfg[dev][ci] = true;
   }
   // persistent: one CTA per SM (or per item, when there are fewer items)
   const int64_t items = (seq + BT - 1) / BT * batch * heads;
