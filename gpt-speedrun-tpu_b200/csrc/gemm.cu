@@ -35,8 +35,9 @@ static __device__ int g_gemm_error;
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int kEpiWarps = 16;                  // four per TMEM lane quadrant
-constexpr int kThreads = 64 + 32 * kEpiWarps;  // TMA warp + MMA warp + epilogue
+// Epilogue warps: 16 (four per TMEM lane quadrant, a quarter of the tile's
+// columns each) or 8 (two per quadrant, half the columns each, in two passes);
+// a kernel has 64 + 32 x that many threads (TMA warp + MMA warp + epilogue).
 
 template <int BN, int STAGES>
 struct GemmSmem {
@@ -320,8 +321,8 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int row, int
 }
 
 // ------------------------------------------------------------------ kernel
-template <int BN, int STAGES, int EPI, int A_MN, int B_MN>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int BN, int STAGES, int EPIW, int EPI, int A_MN, int B_MN>
+__global__ void __launch_bounds__(64 + 32 * EPIW, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ EpiMaps maps, const GemmParams p) {
   using L = GemmSmem<BN, STAGES>;
@@ -345,7 +346,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], kEpiWarps);
+      mbar_init(&tempty[a], EPIW);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -470,8 +471,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     // loads are issued before one wait, and the accumulator is handed back to
     // the MMA warp as soon as it is in registers.
     constexpr int COLS = BN / 4;
+    constexpr int PASSES = 16 / EPIW;  // column quarters a warp takes in turn
+    static_assert(PASSES == 1 || EPI != EPI_LCE_FWD_, "the LCE forward needs 16 epilogue warps");
     const int quad = warp & 3;
-    const int part = (warp - 2) >> 2;
+    const int wpart = (warp - 2) >> 2;
     const int r_in_tile = quad * 32 + lane;
     float2* red = reinterpret_cast<float2*>(smem + L::RED_OFFSET);  // [4][128] LCE partials
     int acc = 0;
@@ -481,6 +484,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       int kb0, kb1;
       if (!unit_kb(tc, kb0, kb1)) continue;
       const int row = m_off + tc.tm * BM + r_in_tile;
+      for (int vp = 0; vp < PASSES; ++vp) {
+      const int part = wpart * PASSES + vp;
       const int n0 = tc.tn * BN + part * COLS;
       if constexpr (EPI == EPI_BF16_) {
         // The residual rows of this thread's slice of the NEXT tile go to L2
@@ -500,8 +505,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, err)) break;
-      tc_fence_after();
+      if (vp == 0) {
+        if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, err)) goto epi_done;
+        tc_fence_after();
+      }
       int target = -1;
       float lse = 0.f, cot = 0.f;
       if constexpr (EPI == EPI_LCE_FWD_ || EPI == EPI_LCE_BWD_) {
@@ -519,9 +526,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int c = 0; c < COLS / 32; ++c) tmem_ld32_nw(taddr + c * 32, raw + c * 32);
       tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (vp == PASSES - 1) {  // the whole slice is in registers: hand the accumulator back
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[acc]);
+      }
       EpilogueRowState<EPI> st;
       if constexpr (kStagedEpi<EPI>) {
         // bf16 outputs: 32x32 sub-tiles through the warp's swizzled staging
@@ -576,7 +585,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if constexpr (EPI == EPI_LCE_FWD_) {
         // combine the four column quarters of each row, one partial per tile
         red[part * BM + r_in_tile] = make_float2(st.run_max, st.run_sum);
-        named_bar_sync(1, 32 * kEpiWarps);
+        named_bar_sync(1, 32 * EPIW);
         if (part == 0 && row < p.M) {
           const float kLog2e = 1.4426950408889634f;
           float m = -INFINITY, sum = 0.f;
@@ -590,8 +599,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           p.partial[(int64_t)row * p.tiles_n + tc.tn] = make_float2(m, sum);
         }
-        named_bar_sync(1, 32 * kEpiWarps);
+        named_bar_sync(1, 32 * EPIW);
       }
+      }  // passes
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1;
@@ -599,6 +609,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
+epi_done:
   if constexpr (kStagedEpi<EPI>) {
     if (warp >= 2 && lane == 0) bulk_wait_all();
   }
@@ -700,11 +711,19 @@ static int sm_count() {
   return n;
 }
 
+// Epilogue warps by kind: the heavy per-element epilogues (GELU and its
+// derivative, RoPE, the cross-entropy G tile) use 8, the others 16.
+template <int EPI>
+constexpr int kEpiWarpsFor =
+    (EPI == EPI_BIAS_GELU_ || EPI == EPI_DGELU_ || EPI == EPI_BIAS_ROPE_ || EPI == EPI_LCE_BWD_) ? 8
+                                                                                                 : 16;
+
 template <int BN, int STAGES, int EPI, int A_MN, int B_MN>
 static int launch_variant(const CUtensorMap& ta, const CUtensorMap& tb, const EpiMaps& em,
                           const GemmParams& p, cudaStream_t stream) {
   using L = GemmSmem<BN, STAGES>;
-  auto kern = gemm_tc_kernel<BN, STAGES, EPI, A_MN, B_MN>;
+  constexpr int EPIW = kEpiWarpsFor<EPI>;
+  auto kern = gemm_tc_kernel<BN, STAGES, EPIW, EPI, A_MN, B_MN>;
   static bool configured[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -714,7 +733,7 @@ static int launch_variant(const CUtensorMap& ta, const CUtensorMap& tb, const Ep
     if (dev < 64) configured[dev] = true;
   }
   int grid = std::min<int64_t>(p.num_units, sm_count());
-  kern<<<grid, kThreads, L::TOTAL, stream>>>(ta, tb, em, p);
+  kern<<<grid, 64 + 32 * EPIW, L::TOTAL, stream>>>(ta, tb, em, p);
   GPTB200_CHECK_LAUNCH();
   return GPTB200_OK;
 }
