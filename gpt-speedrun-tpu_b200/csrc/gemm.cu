@@ -472,7 +472,6 @@ __global__ void __launch_bounds__(64 + 32 * EPIW, 1)
     // the MMA warp as soon as it is in registers.
     constexpr int COLS = BN / 4;
     constexpr int PASSES = 16 / EPIW;  // column quarters a warp takes in turn
-    static_assert(PASSES == 1 || EPI != EPI_LCE_FWD_, "the LCE forward needs 16 epilogue warps");
     const int quad = warp & 3;
     const int wpart = (warp - 2) >> 2;
     const int r_in_tile = quad * 32 + lane;
@@ -582,11 +581,12 @@ __global__ void __launch_bounds__(64 + 32 * EPIW, 1)
           epilogue_chunk<EPI>(p, row, n0 + c * 32, tc.ks, v, st, target, lse, cot);
         }
       }
+      if constexpr (EPI == EPI_LCE_FWD_) red[part * BM + r_in_tile] = make_float2(st.run_max, st.run_sum);
+      }  // passes
       if constexpr (EPI == EPI_LCE_FWD_) {
         // combine the four column quarters of each row, one partial per tile
-        red[part * BM + r_in_tile] = make_float2(st.run_max, st.run_sum);
         named_bar_sync(1, 32 * EPIW);
-        if (part == 0 && row < p.M) {
+        if (wpart == 0 && row < p.M) {
           const float kLog2e = 1.4426950408889634f;
           float m = -INFINITY, sum = 0.f;
 #pragma unroll
@@ -601,7 +601,6 @@ __global__ void __launch_bounds__(64 + 32 * EPIW, 1)
         }
         named_bar_sync(1, 32 * EPIW);
       }
-      }  // passes
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1;
@@ -712,11 +711,12 @@ static int sm_count() {
 }
 
 // Epilogue warps by kind: the heavy per-element epilogues (GELU and its
-// derivative, RoPE, the cross-entropy G tile) use 8, the others 16.
+// derivative, RoPE, the two cross-entropy epilogues) use 8, the others 16.
 template <int EPI>
-constexpr int kEpiWarpsFor =
-    (EPI == EPI_BIAS_GELU_ || EPI == EPI_DGELU_ || EPI == EPI_BIAS_ROPE_ || EPI == EPI_LCE_BWD_) ? 8
-                                                                                                 : 16;
+constexpr int kEpiWarpsFor = (EPI == EPI_BIAS_GELU_ || EPI == EPI_DGELU_ || EPI == EPI_BIAS_ROPE_ ||
+                              EPI == EPI_LCE_BWD_ || EPI == EPI_LCE_FWD_)
+                                 ? 8
+                                 : 16;
 
 template <int BN, int STAGES, int EPI, int A_MN, int B_MN>
 static int launch_variant(const CUtensorMap& ta, const CUtensorMap& tb, const EpiMaps& em,
