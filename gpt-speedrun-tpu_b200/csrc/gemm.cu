@@ -835,15 +835,30 @@ int gemm_launch(const void* a, int a_mn, int64_t lda, const void* b, int b_mn, i
 int gemm_tile_n() { return kBN; }
 
 static int gemm_split_request(int64_t M, int64_t N, int64_t K) {
-  // Split K until there are about three units per SM, keeping >= 32 k-blocks
-  // (2048 of K) per unit: every unit ends in a BM x BN fp32 write-out (atomics
-  // or a partial slab), which a shorter main loop no longer hides.
+  // The split count with the shortest main-loop critical path, in k-blocks
+  // per CTA: waves of units over the SMs x k-blocks per unit. Ties go to the
+  // fewer splits (less fp32 partial traffic: every unit ends in a BM x BN
+  // slab write that the ordered reduction reads back). A unit keeps >= 32
+  // k-blocks (2048 of K) so its write-out hides behind the next unit's loop,
+  // and at most 256 (16,384 of K): the accumulation error of the fp32 TMEM
+  // accumulator grows with the length it runs over (measured relative error
+  // ~1.1e-9 x K per unit), while the slabs are added in exact fp32.
   const int64_t tiles = ((M + BM - 1) / BM) * ((N + kBN - 1) / kBN);
   const int64_t num_kb = (K + BK - 1) / BK;
-  const int64_t target = 3 * (int64_t)sm_count();
-  int splits = 1;
-  while (tiles * splits < target && num_kb / (splits * 2) >= 32) splits *= 2;
-  return splits;
+  const int64_t sms = sm_count();
+  int s0 = 1;
+  while (s0 < 64 && (num_kb + s0 - 1) / s0 > 256) s0 *= 2;
+  int best_s = s0;
+  int64_t best = INT64_MAX;
+  for (int s = s0; s <= 64 && (s == s0 || num_kb / s >= 32); s *= 2) {
+    const int64_t waves = (tiles * s + sms - 1) / sms;
+    const int64_t cost = waves * ((num_kb + s - 1) / s);
+    if (cost < best) {
+      best = cost;
+      best_s = s;
+    }
+  }
+  return best_s;
 }
 
 // Splits that actually run: k-blocks are dealt in runs of ceil(num_kb / request).
