@@ -554,7 +554,7 @@ def main() -> None:
     clocks = ClockSampler(local)
     for i in range(args.warmup):
         trainer.train_step(*dev_batches[i])
-        if i == 0 and world == 1 and not args.eager:
+        if i == 0 and not args.eager:
             trainer.capture()  # after one eager step; replays the same launches
     clocks.wait_ready()
     barrier()
@@ -660,6 +660,11 @@ def main() -> None:
                                 "sample": sample}
     if rank == 0:
         print(json.dumps(line), flush=True)
+    # The captured step holds references to the NCCL communicator: release it
+    # before the process group goes away.
+    trainer.graph = None
+    del graph
+    torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

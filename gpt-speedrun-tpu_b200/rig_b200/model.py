@@ -183,6 +183,10 @@ class _Block:
             self.router_w32 = trainer.param_view(f"blocks/{b}/router_w")
 
 
+# Parts the tail gradient bucket is all-reduced and updated in (see backward).
+TAIL_PARTS = 4
+
+
 class GPTTrainer:
     """Holds the model state on one GPU and runs the training step."""
 
@@ -566,7 +570,16 @@ class GPTTrainer:
                 reduce_hook(*self.layout.block_ranges[l])
         ops.embedding_bwd(self.tokens.view(-1), dx, self.g_tok_emb, workspace=self.scratch)
         if reduce_hook is not None:
-            reduce_hook(*self.layout.tail_range)
+            # The tail bucket (final norm + embeddings, about a third of the
+            # parameters) is final only after the last backward kernel, so it
+            # goes in parts: each part's update overlaps the next part's
+            # all-reduce instead of waiting for the whole bucket.
+            start, end = self.layout.tail_range
+            parts = TAIL_PARTS if end - start >= TAIL_PARTS * 4096 else 1
+            for i in range(parts):
+                a = start + (end - start) * i // parts // 1024 * 1024
+                b = end if i == parts - 1 else start + (end - start) * (i + 1) // parts // 1024 * 1024
+                reduce_hook(max(a, start), b)
 
     def optimizer_step(self) -> None:
         ops.adamw_step(self.params, self.m, self.v, self.grads, self.groups_dev, self.n_groups,
@@ -580,11 +593,13 @@ class GPTTrainer:
         warm-up step (which also sets every kernel's shared-memory attribute)
         the graph replays the identical launch sequence; the batch is read from
         `self.tokens` / `self.targets` and the step counter lives on the device.
-        Single-process only: with data parallelism the step runs eagerly.
+        With data parallelism the bucketed NCCL all-reduces and the optimizer
+        stream's per-bucket updates are recorded with the kernels (every rank
+        records the same sequence, so replays stay matched across ranks).
+        Release the graph (`self.graph = None`) before the process group is
+        destroyed.
         """
 
-        if self.world_size != 1:
-            raise ValueError("graph capture is used for the single-GPU step only")
         side = torch.cuda.Stream(self.device)
         side.wait_stream(torch.cuda.current_stream(self.device))
         graph = torch.cuda.CUDAGraph()
