@@ -187,6 +187,16 @@ class _Block:
 TAIL_PARTS = 4
 
 
+def tail_parts(start: int, end: int, parts: int = TAIL_PARTS) -> list[tuple[int, int]]:
+    """[start, end) cut into `parts` contiguous ranges whose inner boundaries
+    are start + multiples of 1024 elements (one range if it is too short)."""
+
+    if end - start < parts * 4096:
+        return [(start, end)]
+    cuts = [start + (end - start) * i // parts // 1024 * 1024 for i in range(parts)] + [end]
+    return [(cuts[i], cuts[i + 1]) for i in range(parts)]
+
+
 class GPTTrainer:
     """Holds the model state on one GPU and runs the training step."""
 
@@ -574,12 +584,8 @@ class GPTTrainer:
             # parameters) is final only after the last backward kernel, so it
             # goes in parts: each part's update overlaps the next part's
             # all-reduce instead of waiting for the whole bucket.
-            start, end = self.layout.tail_range
-            parts = TAIL_PARTS if end - start >= TAIL_PARTS * 4096 else 1
-            for i in range(parts):
-                a = start + (end - start) * i // parts // 1024 * 1024
-                b = end if i == parts - 1 else start + (end - start) * (i + 1) // parts // 1024 * 1024
-                reduce_hook(max(a, start), b)
+            for part in tail_parts(*self.layout.tail_range):
+                reduce_hook(*part)
 
     def optimizer_step(self) -> None:
         ops.adamw_step(self.params, self.m, self.v, self.grads, self.groups_dev, self.n_groups,

@@ -107,3 +107,21 @@ def test_finite_metric_raises_like_the_reference():
             finite_metric("loss", bad)
     with pytest.raises(FloatingPointError):
         finite_metric("tokens_per_second", 0.0, positive=True)
+
+
+def test_tail_parts_cover_the_bucket():
+    """The tail bucket is reduced and updated in contiguous parts that tile it
+    exactly, with inner boundaries 1024-element aligned (the AdamW range entry
+    point needs multiples of 4)."""
+
+    from rig_b200.config import load_config
+    from rig_b200.model import ParamLayout, tail_parts
+
+    layout = ParamLayout(load_config("baseline_125m"))
+    start, end = layout.tail_range
+    parts = tail_parts(start, end)
+    assert len(parts) == 4 and parts[0][0] == start and parts[-1][1] == end
+    assert all(a < b for a, b in parts)
+    assert all(parts[i][1] == parts[i + 1][0] for i in range(len(parts) - 1))
+    assert all((b - start) % 1024 == 0 for _, b in parts[:-1]) and start % 4 == 0
+    assert tail_parts(100, 200) == [(100, 200)]
